@@ -1,0 +1,290 @@
+"""fusion-pcu_b200: B200-native (sm_100a) strict-tensor CUDA provider for Fusion-PCU.
+
+Python front end over the C ABI in include/pcu_b200.h (libpcu_b200.so, built in-tree by
+fusion-pcu_b200/build.py).  PyTorch is used only as plumbing: CUDA device memory, streams
+and torch.distributed.  There is no CPU fallback: if the shared library is missing or no
+CUDA device is present the calls raise ProviderUnavailable.
+
+Fault lifting mirrors the reference's per-node decoding (paths relative to the Fusion-PCU
+checkout): Profile::fault of Crates/backends/cuda/tensor/strict_matmul/strict_matmul.rs:191-215,
+strict_sgd.rs:198-219, strict_mse.rs:189-222 and the element faults of relu_backward.rs:259-281,
+producing the TensorError variants of Crates/core/dialect/tensor.rs:234-251.
+"""
+import ctypes
+import os
+
+import numpy as np
+
+__all__ = [
+    "ProviderUnavailable", "TensorError", "ArithmeticFault", "CompoundArithmeticFault", "ProviderFailure",
+    "library", "POLICY", "OPS", "STATUS_OK", "new_status", "decode_status", "strict_matmul", "strict_sgd",
+    "strict_mse", "checked_binary", "checked_relu", "checked_relu_backward", "matmul_fault", "sgd_fault",
+    "mse_fault", "element_fault",
+]
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIBRARY = os.path.join(_HERE, "libpcu_b200.so")
+STATUS_OK = (1 << 64) - 1
+POLICY = {"IeeeAfterRounding": 0, "RejectSubnormalResult": 1, "AllowGradualUnderflow": 2}
+OPS = {"add": 0, "sub": 1, "mul": 2, "div": 3}
+KIND_NAMES = {1: "DivideByZero", 2: "SignedDivisionOverflow", 3: "ArithmeticOverflow", 4: "ArithmeticUnderflow",
+              5: "InvalidFloatingOperand"}
+WATCHDOG = 7
+
+
+class ProviderUnavailable(RuntimeError):
+    """The CUDA provider cannot run here (library not built, or no CUDA device)."""
+
+
+class ProviderFailure(RuntimeError):
+    """A host-side error code from the C ABI or a malformed / watchdog status word."""
+
+
+class TensorError(Exception):
+    pass
+
+
+class ArithmeticFault(TensorError):
+    """TensorError::ArithmeticFault { value, element_index, kind }."""
+
+    def __init__(self, value, element_index, kind):
+        super().__init__(f"ArithmeticFault(value={value}, element_index={element_index}, kind={kind})")
+        self.value, self.element_index, self.kind = value, element_index, kind
+
+
+class CompoundArithmeticFault(TensorError):
+    """TensorError::CompoundArithmeticFault { value, element_index, reduction_index, step, kind }."""
+
+    def __init__(self, value, element_index, reduction_index, step, kind):
+        super().__init__(f"CompoundArithmeticFault(value={value}, element_index={element_index}, "
+                         f"reduction_index={reduction_index}, step={step}, kind={kind})")
+        self.value, self.element_index, self.reduction_index = value, element_index, reduction_index
+        self.step, self.kind = step, kind
+
+
+_lib = None
+
+
+def library():
+    """Load libpcu_b200.so (raises ProviderUnavailable; never substitutes another path)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIBRARY):
+            raise ProviderUnavailable(f"{LIBRARY} is not built (run fusion-pcu_b200/build.py)")
+        lib = ctypes.CDLL(LIBRARY)
+        _declare(lib)
+        _lib = lib
+    return _lib
+
+
+def _declare(L):
+    i32, u32, u64, vp, sz = ctypes.c_int, ctypes.c_uint32, ctypes.c_uint64, ctypes.c_void_p, ctypes.c_size_t
+    L.pcu_b200_abi_version.restype = i32
+    L.pcu_b200_error_string.argtypes = [i32]
+    L.pcu_b200_error_string.restype = ctypes.c_char_p
+    L.pcu_b200_last_cuda_error.restype = i32
+    L.pcu_b200_status_reset.argtypes = [vp, u64, vp]
+    L.pcu_b200_strict_matmul_workspace_size.argtypes = [u64, u64, u64]
+    L.pcu_b200_strict_matmul_workspace_size.restype = sz
+    L.pcu_b200_strict_matmul.argtypes = [i32, i32, vp, vp, vp, u64, u64, u64, u64, u64, i32, i32, vp, sz, vp, vp]
+    L.pcu_b200_strict_sgd.argtypes = [i32, i32, vp, vp, vp, u64, u32, vp, vp]
+    L.pcu_b200_strict_mse_workspace_size.argtypes = [i32, u64]
+    L.pcu_b200_strict_mse_workspace_size.restype = sz
+    L.pcu_b200_strict_mse.argtypes = [i32, i32, vp, vp, vp, u64, vp, sz, vp, vp]
+    L.pcu_b200_checked_binary.argtypes = [i32, i32, i32, vp, vp, vp, u64, i32, i32, vp, vp]
+    L.pcu_b200_checked_relu.argtypes = [i32, i32, vp, vp, u64, vp, vp]
+    L.pcu_b200_checked_relu_backward.argtypes = [i32, i32, vp, vp, vp, u64, vp, vp]
+
+
+def _torch():
+    import torch
+
+    if not torch.cuda.is_available():
+        raise ProviderUnavailable("no CUDA device: the strict provider has no CPU fallback")
+    return torch
+
+
+def _check(rc):
+    if rc != 0:
+        L = library()
+        msg = L.pcu_b200_error_string(rc).decode()
+        raise ProviderFailure(f"pcu_b200 error {rc}: {msg} (cuda error {L.pcu_b200_last_cuda_error()})")
+
+
+def _dtype_code(t):
+    torch = _torch()
+    if t.dtype == torch.float32:
+        return 0
+    if t.dtype == torch.float64:
+        return 1
+    raise TypeError(f"strict provider handles float32/float64, got {t.dtype}")
+
+
+def _stream(stream):
+    torch = _torch()
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def new_status(count=1, device=None, stream=None):
+    """Device status words initialised to the no-fault sentinel (int64 storage, read as unsigned)."""
+    torch = _torch()
+    return torch.full((count,), -1, dtype=torch.int64, device=device or "cuda")
+
+
+def decode_status(word):
+    """Unsigned status word -> None (no fault) or (event, kind)."""
+    word = int(word) & STATUS_OK
+    if word == STATUS_OK:
+        return None
+    return word >> 3, word & 7
+
+
+def _kind(kind):
+    if kind not in KIND_NAMES:
+        raise ProviderFailure("device watchdog expired" if kind == WATCHDOG else f"malformed status kind {kind}")
+    return KIND_NAMES[kind]
+
+
+def matmul_fault(word, inner, cells, value=None):
+    """Profile::fault for MatMul (strict_matmul.rs:191-215)."""
+    d = decode_status(word)
+    if d is None:
+        return None
+    event, kind = d
+    pair = event // 2
+    if inner == 0 or pair // inner >= cells:
+        raise ProviderFailure(f"status {word:#x} outside the MatMul event domain")
+    return CompoundArithmeticFault(value, pair // inner, pair % inner, "Multiply" if event % 2 == 0 else "Add",
+                                   _kind(kind))
+
+
+def sgd_fault(word, count, value=None):
+    d = decode_status(word)
+    if d is None:
+        return None
+    event, kind = d
+    if event // 2 >= count:
+        raise ProviderFailure(f"status {word:#x} outside the SGD event domain")
+    return CompoundArithmeticFault(value, event // 2, 0, "Multiply" if event % 2 == 0 else "Subtract", _kind(kind))
+
+
+def mse_fault(word, count, value=None):
+    d = decode_status(word)
+    if d is None:
+        return None
+    event, kind = d
+    if event > 3 * count:
+        raise ProviderFailure(f"status {word:#x} outside the MSE event domain")
+    if event == 3 * count:
+        return CompoundArithmeticFault(value, 0, count, "Divide", _kind(kind))
+    return CompoundArithmeticFault(value, 0, event // 3, ("Subtract", "Multiply", "Add")[event % 3], _kind(kind))
+
+
+def element_fault(word, count, value=None):
+    d = decode_status(word)
+    if d is None:
+        return None
+    event, kind = d
+    if event >= count:
+        raise ProviderFailure(f"status {word:#x} outside the element domain")
+    return ArithmeticFault(value, event, _kind(kind))
+
+
+# ------------------------------------------------------------------ kernel-level calls
+# Each returns the output tensor; faults stay in `status` (device) until the caller reads it,
+# exactly like the reference's one-status-word-per-node protocol.
+
+def strict_matmul(left, right, transpose_left=False, transpose_right=False, policy=0, out=None, status=None,
+                  workspace=None, stream=None):
+    torch = _torch()
+    assert left.dim() == 2 and right.dim() == 2 and left.dtype == right.dtype
+    assert left.stride(1) == 1 and right.stride(1) == 1, "operands must be row-major"
+    rows, inner = (left.shape[1], left.shape[0]) if transpose_left else (left.shape[0], left.shape[1])
+    inner2, cols = (right.shape[1], right.shape[0]) if transpose_right else (right.shape[0], right.shape[1])
+    if inner != inner2:
+        raise ValueError(f"MatMulShape {tuple(left.shape)} {tuple(right.shape)}")
+    L = library()
+    if out is None:
+        out = torch.empty((rows, cols), dtype=left.dtype, device=left.device)
+    if status is None:
+        status = new_status(device=left.device)
+    need = L.pcu_b200_strict_matmul_workspace_size(rows, inner, cols)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=left.device)
+    _check(L.pcu_b200_strict_matmul(_dtype_code(left), policy, _ptr(left), _ptr(right), _ptr(out), rows, inner,
+                                    cols, left.stride(0), right.stride(0), int(transpose_left),
+                                    int(transpose_right), _ptr(workspace), workspace.numel(), _ptr(status),
+                                    _stream(stream)))
+    return out
+
+
+def strict_sgd(weights, gradient, rate, policy=0, out=None, status=None, stream=None):
+    torch = _torch()
+    assert weights.is_contiguous() and gradient.is_contiguous() and weights.numel() == gradient.numel()
+    if out is None:
+        out = torch.empty_like(weights)
+    if status is None:
+        status = new_status(device=weights.device)
+    rate_bits = int(np.array([rate], dtype=np.float32).view(np.uint32)[0])
+    _check(library().pcu_b200_strict_sgd(_dtype_code(weights), policy, _ptr(weights), _ptr(gradient), _ptr(out),
+                                         weights.numel(), rate_bits, _ptr(status), _stream(stream)))
+    return out
+
+
+def strict_mse(prediction, target, policy=0, out=None, status=None, workspace=None, stream=None):
+    torch = _torch()
+    assert prediction.is_contiguous() and target.is_contiguous() and prediction.numel() == target.numel()
+    L = library()
+    n = prediction.numel()
+    if out is None:
+        out = torch.empty((), dtype=prediction.dtype, device=prediction.device)
+    if status is None:
+        status = new_status(device=prediction.device)
+    need = L.pcu_b200_strict_mse_workspace_size(_dtype_code(prediction), n)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=prediction.device)
+    _check(L.pcu_b200_strict_mse(_dtype_code(prediction), policy, _ptr(prediction), _ptr(target), _ptr(out), n,
+                                 _ptr(workspace), workspace.numel(), _ptr(status), _stream(stream)))
+    return out
+
+
+def checked_binary(op, left, right, policy=0, left_uniform=False, right_uniform=False, out=None, status=None,
+                   stream=None):
+    torch = _torch()
+    n = max(1 if left_uniform else left.numel(), 1 if right_uniform else right.numel())
+    shape = right.shape if left_uniform else left.shape
+    if out is None:
+        out = torch.empty(shape, dtype=left.dtype, device=left.device)
+    if status is None:
+        status = new_status(device=left.device)
+    _check(library().pcu_b200_checked_binary(_dtype_code(left), policy, OPS.get(op, op), _ptr(left), _ptr(right),
+                                             _ptr(out), n, int(left_uniform), int(right_uniform), _ptr(status),
+                                             _stream(stream)))
+    return out
+
+
+def checked_relu(x, policy=0, out=None, status=None, stream=None):
+    torch = _torch()
+    if out is None:
+        out = torch.empty_like(x)
+    if status is None:
+        status = new_status(device=x.device)
+    _check(library().pcu_b200_checked_relu(_dtype_code(x), policy, _ptr(x), _ptr(out), x.numel(), _ptr(status),
+                                           _stream(stream)))
+    return out
+
+
+def checked_relu_backward(x, upstream, policy=0, out=None, status=None, stream=None):
+    torch = _torch()
+    if out is None:
+        out = torch.empty_like(x)
+    if status is None:
+        status = new_status(device=x.device)
+    _check(library().pcu_b200_checked_relu_backward(_dtype_code(x), policy, _ptr(x), _ptr(upstream), _ptr(out),
+                                                    x.numel(), _ptr(status), _stream(stream)))
+    return out

@@ -1,0 +1,603 @@
+// strict_matmul.cu -- ordered-K checked F32/F64 MatMul for sm_100a.
+//
+// Semantics (paths relative to the Fusion-PCU checkout): every output cell folds k = 0..K-1 in
+// increasing order from +0, rounding the multiply, then the add, each checked under the
+// node's underflow policy (Crates/core/dialect/tensor/reference/strict_matmul/strict_matmul.rs:22-73,
+// CPU order Crates/backends/cpu/prepared_tensor/execution/execution.rs:243-281).  The first
+// fault is the lowest event (cell*K + k)*2 + {Multiply 0, Add 1}
+// (Crates/core/dialect/tensor/fault_domain/fault_domain.rs:131-142), recorded with atomicMin as
+// the reference kernel does (Crates/backends/cuda/tensor/strict_matmul/strict_matmul.rs:253-256).
+//
+// B200 design.  The strict contract forbids FMA and reassociation, so tensor cores cannot be
+// used: the kernel is bound by the FP32 (FP64) CUDA-core issue rate, one FMUL and one FADD
+// per (cell, k).  Everything else is organised to keep other instructions off the issue ports:
+//   * TMA (cp.async.bulk.tensor, no multicast) stages A and B tiles into a 4-stage shared
+//     memory ring driven by one producer thread and mbarriers; K-major tiles use the 128-byte
+//     swizzle so the consumers' 16-byte fragment loads are bank-conflict free.
+//   * 256 consumer threads each own an 8x8 (F32) or 8x4 (F64) register block of cells and run
+//     __fmul_rn/__fadd_rn on 16-byte shared-memory fragments: 4 LDS.128 per 128 FP32 ops.
+//   * Fault detection costs nothing in the loop.  Overflow and invalid operands are sticky
+//     through IEEE add/multiply, so a finite final sum proves neither happened.  A tiny
+//     (underflowing) product is only possible when the smallest nonzero operand exponents of
+//     the cell's row of op(A) and column of op(B) add up below the format's limit; a prescan
+//     kernel computes those minima once per call.  Cells that fail either test re-walk their
+//     K range with the exact checked law (checked_law.cuh) to find the first fault; all other
+//     cells are bit-identical to the law because no step faulted.
+//   * Shapes whose strides or base addresses TMA cannot describe use a plain tiled kernel
+//     with the same epilogue.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+#include "pcu_b200.h"
+
+namespace pcu {
+
+template <typename T> struct MatmulParams {
+    const T *left;
+    const T *right;
+    T *out;
+    uint64_t rows, inner, columns, left_stride, right_stride;
+    int transpose_left, transpose_right, policy, threshold;
+    const int *row_minexp;  // null when no product can be rejected for underflow (gradual policy)
+    const int *col_minexp;
+    unsigned long long *status;
+    int vector_out;  // out is 16-byte aligned and columns is a multiple of the 16-byte vector
+};
+
+// "no nonzero finite element" marker of the exponent prescan (also the memset byte pattern)
+constexpr int kNoExponent = 0x10101010;
+
+template <typename T> __device__ __forceinline__ int min_exponent_of(T x);
+
+template <> __device__ __forceinline__ int min_exponent_of<float>(float x) {
+    uint32_t u = __float_as_uint(x);
+    uint32_t e = (u >> 23) & 0xffu;
+    if (e == 0xffu || (u << 1) == 0) return kNoExponent;
+    if (e) return (int)e - 127;
+    return (31 - __clz(u & 0x7fffffu)) - 149;
+}
+
+template <> __device__ __forceinline__ int min_exponent_of<double>(double x) {
+    uint64_t u = (uint64_t)__double_as_longlong(x);
+    uint32_t e = (uint32_t)((u >> 52) & 0x7ffu);
+    if (e == 0x7ffu || (u << 1) == 0) return kNoExponent;
+    if (e) return (int)e - 1023;
+    return (63 - __clzll((long long)(u & 0x000fffffffffffffull))) - 1074;
+}
+
+// min exponent along each row of a rows x cols row-major matrix (one warp per row)
+template <typename T>
+__global__ void __launch_bounds__(256) minexp_rows_kernel(const T *x, uint64_t rows, uint64_t cols, uint64_t ld,
+                                                          int *out) {
+    const uint64_t warps = (uint64_t)gridDim.x * (blockDim.x / 32);
+    const uint64_t warp = (uint64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+    for (uint64_t r = warp; r < rows; r += warps) {
+        const T *row = x + r * ld;
+        int m = kNoExponent;
+        for (uint64_t c = lane; c < cols; c += 32) m = min(m, min_exponent_of<T>(__ldg(row + c)));
+#pragma unroll
+        for (int o = 16; o; o >>= 1) m = min(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (lane == 0) out[r] = m;
+    }
+}
+
+// min exponent down each column; blockIdx.y takes a slab of rows, atomicMin merges slabs
+template <typename T>
+__global__ void __launch_bounds__(256) minexp_cols_kernel(const T *x, uint64_t rows, uint64_t cols, uint64_t ld,
+                                                          uint64_t rows_per_slab, int *out) {
+    const uint64_t c = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= cols) return;
+    const uint64_t r0 = (uint64_t)blockIdx.y * rows_per_slab;
+    const uint64_t r1 = r0 + rows_per_slab < rows ? r0 + rows_per_slab : rows;
+    int m = kNoExponent;
+    for (uint64_t r = r0; r < r1; ++r) m = min(m, min_exponent_of<T>(__ldg(x + r * ld + c)));
+    if (m != kNoExponent) atomicMin(out + c, m);
+}
+
+template <typename T>
+__device__ __forceinline__ T load_a(const MatmulParams<T> &p, uint64_t r, uint64_t k) {
+    return p.transpose_left ? p.left[k * p.left_stride + r] : p.left[r * p.left_stride + k];
+}
+
+template <typename T>
+__device__ __forceinline__ T load_b(const MatmulParams<T> &p, uint64_t k, uint64_t c) {
+    return p.transpose_right ? p.right[c * p.right_stride + k] : p.right[k * p.right_stride + c];
+}
+
+// Exact ordered walk of one cell with the checked law; records its first fault.
+template <typename T>
+__device__ __noinline__ void exact_cell(const MatmulParams<T> &p, uint64_t r, uint64_t c) {
+    const uint64_t cell = r * p.columns + c;
+    const uint64_t base = cell * p.inner * 2;
+    if (fault_precedes(p.status, base)) return;
+    T acc = T(0);
+    for (uint64_t k = 0; k < p.inner; ++k) {
+        T prod;
+        unsigned kind = checked_mul<T>(load_a(p, r, k), load_b(p, k, c), p.policy, prod);
+        if (kind) { record_fault(p.status, base + 2 * k, kind); return; }
+        kind = checked_add<T>(acc, prod, p.policy, acc);
+        if (kind) { record_fault(p.status, base + 2 * k + 1, kind); return; }
+        if ((k & 1023) == 1023 && fault_precedes(p.status, base + 2 * k)) return;
+    }
+    p.out[cell] = acc;
+}
+
+// Does the fast result of cell (r, c) need the exact walk?
+template <typename T>
+__device__ __forceinline__ bool needs_exact(const MatmulParams<T> &p, T acc, int rmin, int cmin) {
+    return nonfinite_bits<T>(Fmt<T>::bits(acc)) || (p.row_minexp && rmin + cmin < p.threshold);
+}
+
+// ------------------------------------------------------------------ TMA / mbarrier helpers
+__device__ __forceinline__ uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// Bounded wait: false after kWaitLimitNs (the caller reports kWatchdog).
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = global_ns();
+    for (;;) {
+#pragma unroll 1
+        for (int i = 0; i < 64; ++i)
+            if (mbar_try_wait(bar, parity)) return true;
+        if (global_ns() - t0 > kWaitLimitNs) return false;
+    }
+}
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::
+            "r"(smem_addr(dst)),
+        "l"(map), "r"(smem_addr(bar)), "r"(x), "r"(y)
+        : "memory");
+}
+
+template <typename T> struct Tile;
+template <> struct Tile<float> {
+    static constexpr int TM = 8, TN = 8, BK = 32, STAGES = 4;
+};
+template <> struct Tile<double> {
+    static constexpr int TM = 8, TN = 4, BK = 16, STAGES = 4;
+};
+
+template <typename T, int V> struct SVec;
+template <> struct SVec<float, 4> { using type = float4; };
+template <> struct SVec<double, 2> { using type = double2; };
+
+template <typename T> struct TileShape {
+    static constexpr int V = 16 / sizeof(T);  // elements per 16-byte fragment
+    static constexpr int TM = Tile<T>::TM, TN = Tile<T>::TN, BK = Tile<T>::BK, STAGES = Tile<T>::STAGES;
+    static constexpr int BM = 16 * TM, BN = 16 * TN;
+    static constexpr int A_BYTES = BM * BK * (int)sizeof(T);
+    static constexpr int B_BYTES = BN * BK * (int)sizeof(T);
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 2 * STAGES * 8 + 1024;  // + barriers + align slack
+    static_assert(BK * sizeof(T) == 128, "K-major tiles are one 128-byte swizzle row per M/N index");
+};
+
+constexpr int kConsumerWarps = 8;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+
+// A_KMAJOR: op(A) rows are contiguous in k (left not transposed).
+// B_KMAJOR: op(B) columns are contiguous in k (right transposed).
+template <typename T, bool A_KMAJOR, bool B_KMAJOR>
+__global__ void __launch_bounds__(kThreads, 1)
+    strict_matmul_tma_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                             const __grid_constant__ MatmulParams<T> p) {
+    using S = TileShape<T>;
+    constexpr int V = S::V, TM = S::TM, TN = S::TN, BK = S::BK, BM = S::BM, BN = S::BN, STAGES = S::STAGES;
+    using VT = typename SVec<T, V>::type;
+    using F = Fmt<T>;
+
+    extern __shared__ unsigned char smem_raw[];
+    const uintptr_t base = (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023);
+    T *const tiles = reinterpret_cast<T *>(base);
+    uint64_t *const full = reinterpret_cast<uint64_t *>(base + STAGES * S::STAGE_BYTES);
+    uint64_t *const empty = full + STAGES;
+    __shared__ int abort_flag;
+    __shared__ int consumed_tiles;
+
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const uint64_t m0 = (uint64_t)blockIdx.y * BM, n0 = (uint64_t)blockIdx.x * BN;
+    const int KT = (int)((p.inner + BK - 1) / BK);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumerWarps);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        abort_flag = 0;
+        consumed_tiles = 0;
+    }
+    __syncthreads();
+
+    if (warp == kConsumerWarps) {
+        // ---------------------------------------------------------------- producer
+        int issued = 0;
+        if (lane == 0) {
+            for (int kt = 0; kt < KT; ++kt) {
+                const int s = kt % STAGES;
+                if (!mbar_wait(&empty[s], ((kt / STAGES) & 1) ^ 1)) {
+                    record_fault(p.status, 0, kWatchdog);
+                    abort_flag = 1;
+                    break;
+                }
+                if (*(volatile int *)&abort_flag) break;
+                T *sa = tiles + (size_t)s * (S::STAGE_BYTES / sizeof(T));
+                T *sb = sa + S::A_BYTES / sizeof(T);
+                mbar_expect_tx(&full[s], S::STAGE_BYTES);
+                const int k0 = kt * BK;
+                if (A_KMAJOR) tma_load_2d(sa, &map_a, &full[s], k0, (int)m0);
+                else tma_load_2d(sa, &map_a, &full[s], (int)m0, k0);
+                if (B_KMAJOR) tma_load_2d(sb, &map_b, &full[s], k0, (int)n0);
+                else tma_load_2d(sb, &map_b, &full[s], (int)n0, k0);
+                ++issued;
+            }
+        }
+        __syncwarp();
+        __syncthreads();
+        // Never leave the CTA with a bulk copy still writing into its shared memory.
+        if (lane == 0) {
+            for (int kt = consumed_tiles; kt < issued; ++kt)
+                if (!mbar_wait(&full[kt % STAGES], (kt / STAGES) & 1)) break;
+        }
+        return;
+    }
+
+    // -------------------------------------------------------------------- consumers
+    const int ty = (warp >> 1) * 4 + (lane >> 3);  // 0..15 along M
+    const int tx = (warp & 1) * 8 + (lane & 7);    // 0..15 along N
+
+    // M (N) offsets of this thread's cells inside the tile.  K-major tiles use a stride of 16
+    // (rows ty, ty+16, ...) so the 128-byte swizzle spreads a warp over distinct banks;
+    // MN-major tiles use runs of V contiguous elements for 16-byte fragment loads.
+    auto row_of = [&](int i) -> int { return A_KMAJOR ? ty + 16 * i : (i / V) * (16 * V) + ty * V + (i % V); };
+    auto col_of = [&](int j) -> int { return B_KMAJOR ? tx + 16 * j : (j / V) * (16 * V) + tx * V + (j % V); };
+
+    T acc[TM][TN];
+#pragma unroll
+    for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < TN; ++j) acc[i][j] = T(0);
+
+    int kt = 0;
+    for (; kt < KT; ++kt) {
+        const int s = kt % STAGES;
+        if (!mbar_wait(&full[s], (kt / STAGES) & 1)) {
+            record_fault(p.status, 0, kWatchdog);
+            abort_flag = 1;
+            break;
+        }
+        const T *sa = tiles + (size_t)s * (S::STAGE_BYTES / sizeof(T));
+        const T *sb = sa + S::A_BYTES / sizeof(T);
+#pragma unroll
+        for (int g = 0; g < BK / V; ++g) {
+            T a[TM][V];
+            T b[V][TN];
+            if (A_KMAJOR) {
+                const int chunk = g ^ (ty & 7);
+#pragma unroll
+                for (int i = 0; i < TM; ++i) {
+                    VT v = *reinterpret_cast<const VT *>(sa + row_of(i) * BK + chunk * V);
+                    const T *e = reinterpret_cast<const T *>(&v);
+#pragma unroll
+                    for (int kv = 0; kv < V; ++kv) a[i][kv] = e[kv];
+                }
+            } else {
+#pragma unroll
+                for (int kv = 0; kv < V; ++kv)
+#pragma unroll
+                    for (int ig = 0; ig < TM / V; ++ig) {
+                        VT v = *reinterpret_cast<const VT *>(sa + (g * V + kv) * BM + ig * 16 * V + ty * V);
+                        const T *e = reinterpret_cast<const T *>(&v);
+#pragma unroll
+                        for (int q = 0; q < V; ++q) a[ig * V + q][kv] = e[q];
+                    }
+            }
+            if (B_KMAJOR) {
+                const int chunk = g ^ (tx & 7);
+#pragma unroll
+                for (int j = 0; j < TN; ++j) {
+                    VT v = *reinterpret_cast<const VT *>(sb + col_of(j) * BK + chunk * V);
+                    const T *e = reinterpret_cast<const T *>(&v);
+#pragma unroll
+                    for (int kv = 0; kv < V; ++kv) b[kv][j] = e[kv];
+                }
+            } else {
+#pragma unroll
+                for (int kv = 0; kv < V; ++kv)
+#pragma unroll
+                    for (int jg = 0; jg < TN / V; ++jg) {
+                        VT v = *reinterpret_cast<const VT *>(sb + (g * V + kv) * BN + jg * 16 * V + tx * V);
+                        const T *e = reinterpret_cast<const T *>(&v);
+#pragma unroll
+                        for (int q = 0; q < V; ++q) b[kv][jg * V + q] = e[q];
+                    }
+            }
+#pragma unroll
+            for (int kv = 0; kv < V; ++kv)
+#pragma unroll
+                for (int i = 0; i < TM; ++i)
+#pragma unroll
+                    for (int j = 0; j < TN; ++j) acc[i][j] = F::add(acc[i][j], F::mul(a[i][kv], b[kv][j]));
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    if (threadIdx.x == 0) consumed_tiles = kt;
+    __syncwarp();
+    __syncthreads();  // pairs with the producer warp's barrier
+    if (*(volatile int *)&abort_flag) return;
+
+    // -------------------------------------------------------------------- epilogue
+    int rmin[TM], cmin[TN];
+#pragma unroll
+    for (int i = 0; i < TM; ++i) {
+        const uint64_t r = m0 + row_of(i);
+        rmin[i] = (p.row_minexp && r < p.rows) ? p.row_minexp[r] : 0;
+    }
+#pragma unroll
+    for (int j = 0; j < TN; ++j) {
+        const uint64_t c = n0 + col_of(j);
+        cmin[j] = (p.col_minexp && c < p.columns) ? p.col_minexp[c] : 0;
+    }
+    const bool vec_store = !B_KMAJOR && p.vector_out;
+#pragma unroll
+    for (int i = 0; i < TM; ++i) {
+        const uint64_t r = m0 + row_of(i);
+        if (r >= p.rows) continue;
+        if (vec_store) {
+#pragma unroll
+            for (int jg = 0; jg < TN / V; ++jg) {
+                const uint64_t c = n0 + col_of(jg * V);
+                if (c >= p.columns) continue;
+                bool exact = false;
+#pragma unroll
+                for (int q = 0; q < V; ++q) exact |= needs_exact(p, acc[i][jg * V + q], rmin[i], cmin[jg * V + q]);
+                if (!exact) {
+                    VT v;
+                    T *e = reinterpret_cast<T *>(&v);
+#pragma unroll
+                    for (int q = 0; q < V; ++q) e[q] = acc[i][jg * V + q];
+                    *reinterpret_cast<VT *>(p.out + r * p.columns + c) = v;
+                } else {
+#pragma unroll
+                    for (int q = 0; q < V; ++q) {
+                        if (needs_exact(p, acc[i][jg * V + q], rmin[i], cmin[jg * V + q])) exact_cell(p, r, c + q);
+                        else p.out[r * p.columns + c + q] = acc[i][jg * V + q];
+                    }
+                }
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < TN; ++j) {
+                const uint64_t c = n0 + col_of(j);
+                if (c >= p.columns) continue;
+                if (needs_exact(p, acc[i][j], rmin[i], cmin[j])) exact_cell(p, r, c);
+                else p.out[r * p.columns + c] = acc[i][j];
+            }
+        }
+    }
+}
+
+// Plain tiled kernel for operands TMA cannot describe (unaligned base or stride): 16x16
+// threads, one cell each, 16-deep K slabs through shared memory, same epilogue.
+template <typename T>
+__global__ void __launch_bounds__(256) strict_matmul_generic_kernel(const __grid_constant__ MatmulParams<T> p) {
+    using F = Fmt<T>;
+    __shared__ T sa[16][17];
+    __shared__ T sb[16][17];
+    const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+    const uint64_t r = (uint64_t)blockIdx.y * 16 + ty, c = (uint64_t)blockIdx.x * 16 + tx;
+    T acc = T(0);
+    for (uint64_t k0 = 0; k0 < p.inner; k0 += 16) {
+        const uint64_t ka = k0 + tx, kb = k0 + ty;
+        const uint64_t ar = (uint64_t)blockIdx.y * 16 + ty, bc = (uint64_t)blockIdx.x * 16 + tx;
+        sa[ty][tx] = (ar < p.rows && ka < p.inner) ? load_a(p, ar, ka) : T(0);
+        sb[ty][tx] = (bc < p.columns && kb < p.inner) ? load_b(p, kb, bc) : T(0);
+        __syncthreads();
+        const int kk_end = (p.inner - k0) < 16 ? (int)(p.inner - k0) : 16;
+        for (int kk = 0; kk < kk_end; ++kk) acc = F::add(acc, F::mul(sa[ty][kk], sb[kk][tx]));
+        __syncthreads();
+    }
+    if (r >= p.rows || c >= p.columns) return;
+    const int rmin = p.row_minexp ? p.row_minexp[r] : 0;
+    const int cmin = p.col_minexp ? p.col_minexp[c] : 0;
+    if (needs_exact(p, acc, rmin, cmin)) exact_cell(p, r, c);
+    else p.out[r * p.columns + c] = acc;
+}
+
+}  // namespace pcu
+
+// ============================================================================ host side
+namespace {
+
+using namespace pcu;
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static std::once_flag once;
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    std::call_once(once, [] {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    });
+    return fn;
+}
+
+// 2-D tile map over a row-major matrix of `outer` rows x `inner_dim` elements with row
+// stride `ld` elements; box = box_inner x box_outer elements.
+template <typename T>
+bool make_map(CUtensorMap *map, const T *base, uint64_t inner_dim, uint64_t outer, uint64_t ld, uint32_t box_inner,
+              uint32_t box_outer, bool swizzle128) {
+    auto encode = tensor_map_encoder();
+    if (!encode) return false;
+    if (!pcu_host::aligned(base, 16) || (ld * sizeof(T)) % 16 != 0) return false;
+    if (inner_dim == 0 || outer == 0 || inner_dim >= (1ull << 31) || outer >= (1ull << 31)) return false;
+    if (ld * sizeof(T) >= (1ull << 40)) return false;
+    cuuint64_t dims[2] = {inner_dim, outer};
+    cuuint64_t strides[1] = {ld * sizeof(T)};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t estrides[2] = {1, 1};
+    CUresult r = encode(map, sizeof(T) == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT64, 2,
+                        const_cast<T *>(base), dims, strides, box, estrides, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+template <typename T, bool AK, bool BK>
+int launch_tma(const CUtensorMap &ma, const CUtensorMap &mb, const MatmulParams<T> &p, cudaStream_t stream) {
+    using S = TileShape<T>;
+    static std::mutex lock;
+    static bool configured[64] = {false};
+    int device = 0;
+    cudaGetDevice(&device);
+    {
+        std::lock_guard<std::mutex> guard(lock);
+        if (device >= 0 && device < 64 && !configured[device]) {
+            cudaError_t e = cudaFuncSetAttribute(strict_matmul_tma_kernel<T, AK, BK>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM_BYTES);
+            if (e != cudaSuccess) return pcu_host::set_cuda_error(e);
+            configured[device] = true;
+        }
+    }
+    dim3 grid((unsigned)((p.columns + S::BN - 1) / S::BN), (unsigned)((p.rows + S::BM - 1) / S::BM));
+    strict_matmul_tma_kernel<T, AK, BK><<<grid, kThreads, S::SMEM_BYTES, stream>>>(ma, mb, p);
+    return pcu_host::launch_status();
+}
+
+template <typename T>
+int run_matmul(int policy, const T *left, const T *right, T *out, uint64_t rows, uint64_t inner, uint64_t columns,
+               uint64_t lda, uint64_t ldb, int tl, int tr, void *workspace, size_t workspace_bytes,
+               unsigned long long *status, cudaStream_t stream) {
+    MatmulParams<T> p{left, right, out,     rows,    inner,   columns, lda,
+                      ldb,  tl,    tr,      policy, 0,       nullptr, nullptr, status,
+                      pcu_host::aligned(out, 16) && columns % (16 / sizeof(T)) == 0};
+    if (policy != kPolicyGradual && inner > 0) {
+        size_t need = pcu_b200_strict_matmul_workspace_size(rows, inner, columns);
+        if (!workspace || workspace_bytes < need) return PCU_B200_ERROR_WORKSPACE;
+        int *row_min = reinterpret_cast<int *>(workspace);
+        int *col_min = reinterpret_cast<int *>(reinterpret_cast<char *>(workspace) + ((rows * 4 + 255) / 256) * 256);
+        cudaError_t e = cudaMemsetAsync(workspace, 0x10, need, stream);
+        if (e != cudaSuccess) return pcu_host::set_cuda_error(e);
+        const int sms = pcu_host::sm_count();
+        auto rows_pass = [&](const T *x, uint64_t r, uint64_t c, uint64_t ld, int *dst) {
+            uint64_t blocks = (r + 7) / 8;
+            if (blocks > (uint64_t)sms * 16) blocks = (uint64_t)sms * 16;
+            minexp_rows_kernel<T><<<(unsigned)blocks, 256, 0, stream>>>(x, r, c, ld, dst);
+        };
+        auto cols_pass = [&](const T *x, uint64_t r, uint64_t c, uint64_t ld, int *dst) {
+            uint64_t col_blocks = (c + 255) / 256;
+            uint64_t slabs = ((uint64_t)sms * 8 + col_blocks - 1) / col_blocks;
+            if (slabs > r) slabs = r;
+            if (slabs > 65535) slabs = 65535;
+            uint64_t per = (r + slabs - 1) / slabs;
+            slabs = (r + per - 1) / per;
+            minexp_cols_kernel<T><<<dim3((unsigned)col_blocks, (unsigned)slabs), 256, 0, stream>>>(x, r, c, ld, per,
+                                                                                                 dst);
+        };
+        if (!tl) rows_pass(left, rows, inner, lda, row_min);
+        else cols_pass(left, inner, rows, lda, row_min);
+        if (!tr) cols_pass(right, inner, columns, ldb, col_min);
+        else rows_pass(right, columns, inner, ldb, col_min);
+        int rc = pcu_host::launch_status();
+        if (rc) return rc;
+        p.row_minexp = row_min;
+        p.col_minexp = col_min;
+        // A product below 2^(threshold) may be tiny (IEEE policy); under RejectSubnormalResult
+        // every intermediate is a multiple of 2^(emin_a + emin_b - 2*frac), which must stay normal.
+        const int frac = sizeof(T) == 4 ? 23 : 52;
+        const int emin = sizeof(T) == 4 ? -126 : -1022;
+        p.threshold = policy == kPolicyIeee ? emin : emin + 2 * frac;
+    }
+    using S = TileShape<T>;
+    CUtensorMap ma, mb;
+    bool tma = inner > 0;
+    if (tma) {
+        tma = tl ? make_map<T>(&ma, left, rows, inner, lda, S::BM, S::BK, false)
+                 : make_map<T>(&ma, left, inner, rows, lda, S::BK, S::BM, true);
+    }
+    if (tma) {
+        tma = tr ? make_map<T>(&mb, right, inner, columns, ldb, S::BK, S::BN, true)
+                 : make_map<T>(&mb, right, columns, inner, ldb, S::BN, S::BK, false);
+    }
+    if (tma && (rows + S::BM - 1) / S::BM <= 65535) {
+        if (!tl && !tr) return launch_tma<T, true, false>(ma, mb, p, stream);
+        if (!tl && tr) return launch_tma<T, true, true>(ma, mb, p, stream);
+        if (tl && !tr) return launch_tma<T, false, false>(ma, mb, p, stream);
+        return launch_tma<T, false, true>(ma, mb, p, stream);
+    }
+    if ((rows + 15) / 16 > 65535) return PCU_B200_ERROR_SIZE_OVERFLOW;
+    dim3 grid((unsigned)((columns + 15) / 16), (unsigned)((rows + 15) / 16));
+    strict_matmul_generic_kernel<T><<<grid, 256, 0, stream>>>(p);
+    return pcu_host::launch_status();
+}
+
+}  // namespace
+
+extern "C" size_t pcu_b200_strict_matmul_workspace_size(uint64_t rows, uint64_t inner, uint64_t columns) {
+    (void)inner;
+    return ((rows * 4 + 255) / 256) * 256 + ((columns * 4 + 255) / 256) * 256;
+}
+
+extern "C" int pcu_b200_strict_matmul(int dtype, int policy, const void *left, const void *right, void *out,
+                                      uint64_t rows, uint64_t inner, uint64_t columns, uint64_t left_stride,
+                                      uint64_t right_stride, int transpose_left, int transpose_right,
+                                      void *workspace, size_t workspace_bytes, uint64_t *status, void *stream) {
+    if ((dtype != PCU_B200_F32 && dtype != PCU_B200_F64) || policy < 0 || policy > 2 || !status)
+        return PCU_B200_ERROR_INVALID_ARGUMENT;
+    if (rows == 0 || columns == 0) return PCU_B200_OK;
+    if (!out || (inner > 0 && (!left || !right))) return PCU_B200_ERROR_INVALID_ARGUMENT;
+    // left is rows x inner (or inner x rows); right is inner x columns (or columns x inner)
+    const uint64_t left_row_len = transpose_left ? rows : inner;
+    const uint64_t right_row_len = transpose_right ? inner : columns;
+    if (inner > 0 && (left_stride < left_row_len || right_stride < right_row_len))
+        return PCU_B200_ERROR_INVALID_ARGUMENT;
+    // rows*columns*inner*2 <= 2^60 (strict_matmul.rs:121-127)
+    unsigned __int128 events = (unsigned __int128)rows * columns;
+    events *= (inner ? inner : 1);
+    events *= 2;
+    if (events > ((unsigned __int128)1 << 60)) return PCU_B200_ERROR_SIZE_OVERFLOW;
+    auto *st = reinterpret_cast<unsigned long long *>(status);
+    cudaStream_t s = pcu_host::as_stream(stream);
+    if (dtype == PCU_B200_F32)
+        return run_matmul<float>(policy, (const float *)left, (const float *)right, (float *)out, rows, inner, columns,
+                                 left_stride, right_stride, transpose_left != 0, transpose_right != 0, workspace,
+                                 workspace_bytes, st, s);
+    return run_matmul<double>(policy, (const double *)left, (const double *)right, (double *)out, rows, inner,
+                              columns, left_stride, right_stride, transpose_left != 0, transpose_right != 0,
+                              workspace, workspace_bytes, st, s);
+}

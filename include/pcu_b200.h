@@ -1,0 +1,162 @@
+/*
+ * pcu_b200.h -- C ABI of the B200 (sm_100a) strict-tensor CUDA provider for Fusion-PCU.
+ *
+ * Each entry point replaces one per-node executor of the reference's CUDA provider
+ * (paths relative to the Fusion-PCU checkout):
+ *
+ *   pcu_b200_strict_matmul          CudaTensorAssessor::execute_strict_matmul
+ *                                   Crates/backends/cuda/tensor/strict_matmul/strict_matmul.rs:278-332
+ *   pcu_b200_strict_sgd             execute_strict_sgd        tensor/strict_sgd/strict_sgd.rs:234-289
+ *   pcu_b200_strict_mse             execute_strict_mse        tensor/strict_mse/strict_mse.rs:234-291
+ *   pcu_b200_checked_binary         execute_elementwise       tensor/tensor.rs:5657 (checked Add/Sub/Mul/Div,
+ *                                   uniform operands as in the scalar mask of tensor.rs:4813-4826)
+ *   pcu_b200_checked_relu           ReLU node                 tensor/tensor.rs:4944 (helper
+ *                                   codegen/lower/checked_float/checked_float.rs:606-626)
+ *   pcu_b200_checked_relu_backward  execute_admitted_relu_backward tensor/relu_backward/relu_backward.rs:298
+ *
+ * Contract shared by all entry points (the reference's fusion_kernel ABI,
+ * strict_matmul.rs:335-343, owned_dispatch/owned_dispatch.rs:20-22,70-109):
+ *   - Every data pointer is DEVICE memory owned by the caller; the library never frees it.
+ *   - `status` points to one device uint64 that the caller initialised to UINT64_MAX
+ *     (pcu_b200_status_reset).  A checked arithmetic fault is reported ONLY there, as
+ *     (event << 3) | kind with kinds 1 DivideByZero, 2 SignedDivisionOverflow,
+ *     3 ArithmeticOverflow, 4 ArithmeticUnderflow, 5 InvalidFloatingOperand; the lowest
+ *     event wins (atomicMin).  Event ordinals are the reference's fault domains
+ *     (Crates/core/dialect/tensor/fault_domain/fault_domain.rs:122-171):
+ *       matmul  (cell * inner + k) * 2 + {0 Multiply, 1 Add},   cell = row * columns + column
+ *       sgd     index * 2 + {0 Multiply, 1 Subtract}
+ *       mse     index * 3 + {0 Subtract, 1 Multiply, 2 Add};  3 * count = Divide
+ *       elementwise / relu / relu_backward: the element index
+ *     Kind 7 (PCU_B200_STATUS_WATCHDOG) means a device wait gave up; it is a provider
+ *     failure, never an arithmetic fault, and the reference decoder rejects it as malformed.
+ *   - Outputs are written even when a fault is recorded; a caller publishes them only
+ *     after reading the sentinel back (nothing is published on fault).
+ *   - The int return is PCU_B200_OK or a host-side error (argument validation, shape or
+ *     event-domain overflow, CUDA launch failure).  Calls are asynchronous on `stream`
+ *     (a cudaStream_t, NULL = legacy default stream), never synchronise the host, and are
+ *     reentrant per (device, stream).
+ *   - dtype: PCU_B200_F32 or PCU_B200_F64.  policy: the checked-float underflow policy
+ *     (Crates/core/scalar_float_underflow.rs:47-56).
+ */
+#ifndef PCU_B200_H
+#define PCU_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PCU_B200_ABI_VERSION 1
+
+/* element types (PcuScalarType::F32 / F64) */
+#define PCU_B200_F32 0
+#define PCU_B200_F64 1
+
+/* PcuFloatUnderflowPolicy */
+#define PCU_B200_IEEE_AFTER_ROUNDING 0
+#define PCU_B200_REJECT_SUBNORMAL_RESULT 1
+#define PCU_B200_ALLOW_GRADUAL_UNDERFLOW 2
+
+/* checked binary op tags (PcuDispatchFloatBinaryOp, checked_float.rs:230-235) */
+#define PCU_B200_ADD 0
+#define PCU_B200_SUB 1
+#define PCU_B200_MUL 2
+#define PCU_B200_DIV 3
+
+/* status word */
+#define PCU_B200_STATUS_OK UINT64_MAX
+#define PCU_B200_KIND_DIVIDE_BY_ZERO 1
+#define PCU_B200_KIND_SIGNED_DIVISION_OVERFLOW 2
+#define PCU_B200_KIND_OVERFLOW 3
+#define PCU_B200_KIND_UNDERFLOW 4
+#define PCU_B200_KIND_INVALID 5
+#define PCU_B200_STATUS_WATCHDOG 7
+
+/* host return codes */
+#define PCU_B200_OK 0
+#define PCU_B200_ERROR_INVALID_ARGUMENT 1
+#define PCU_B200_ERROR_SIZE_OVERFLOW 2
+#define PCU_B200_ERROR_WORKSPACE 3
+#define PCU_B200_ERROR_CUDA 4
+#define PCU_B200_ERROR_UNSUPPORTED 5
+
+/* ------------------------------------------------------------------ library */
+
+/* PCU_B200_ABI_VERSION of the loaded library. */
+int pcu_b200_abi_version(void);
+
+/* Static description of a host return code. */
+const char *pcu_b200_error_string(int code);
+
+/* The cudaError_t behind the calling thread's last PCU_B200_ERROR_CUDA (0 if none). */
+int pcu_b200_last_cuda_error(void);
+
+/* Fill `count` status words with UINT64_MAX (owned_scratch::submit's reset,
+ * Crates/backends/cuda/owned_dispatch/fault_word.rs:17-31). */
+int pcu_b200_status_reset(uint64_t *status, uint64_t count, void *stream);
+
+/* ------------------------------------------------------------------ strict MatMul */
+
+/* Device workspace bytes pcu_b200_strict_matmul needs for this shape (row/column
+ * operand-exponent minima used to prove that no product can underflow). */
+size_t pcu_b200_strict_matmul_workspace_size(uint64_t rows, uint64_t inner, uint64_t columns);
+
+/* out[rows x columns] (dense, row-major) = op(left) . op(right), each cell folding k = 0..inner-1
+ * in increasing order from +0 with a separately rounded, checked multiply then add
+ * (reference: Crates/core/dialect/tensor/reference/strict_matmul/strict_matmul.rs:22-73).
+ * left is stored row-major as rows x inner (or inner x rows when transpose_left) with row
+ * stride left_stride elements; right as inner x columns (or columns x inner when
+ * transpose_right) with row stride right_stride.  inner may be 0 (out = +0).
+ * Rejects rows*columns*inner*2 > 2^60 (the reference's packed event bound,
+ * strict_matmul.rs:121-127) with PCU_B200_ERROR_SIZE_OVERFLOW. */
+int pcu_b200_strict_matmul(int dtype, int policy, const void *left, const void *right, void *out,
+                           uint64_t rows, uint64_t inner, uint64_t columns, uint64_t left_stride,
+                           uint64_t right_stride, int transpose_left, int transpose_right, void *workspace,
+                           size_t workspace_bytes, uint64_t *status, void *stream);
+
+/* ------------------------------------------------------------------ strict SGD */
+
+/* out[i] = weights[i] - rate * gradient[i] with the multiply and the subtract separately
+ * rounded and checked (reference/strict_sgd/strict_sgd.rs:20-46).  The rate is a finite
+ * binary32 pattern; for F64 it is widened exactly (reference.rs:507-517).  out may alias
+ * weights (in-place update). */
+int pcu_b200_strict_sgd(int dtype, int policy, const void *weights, const void *gradient, void *out,
+                        uint64_t count, uint32_t rate_bits_f32, uint64_t *status, void *stream);
+
+/* ------------------------------------------------------------------ strict MSE */
+
+/* Device workspace bytes pcu_b200_strict_mse needs for `count` elements. */
+size_t pcu_b200_strict_mse_workspace_size(int dtype, uint64_t count);
+
+/* out[0] = (sum over i ascending of (prediction[i] - target[i])^2) / count, every subtract,
+ * square, accumulate and the final divide separately rounded and checked, the running sum
+ * starting at +0 (reference/strict_mse/strict_mse.rs:22-59; the divisor is count rounded to
+ * nearest-even, constants/constants.rs:18-27).  count must be >= 1. */
+int pcu_b200_strict_mse(int dtype, int policy, const void *prediction, const void *target, void *out,
+                        uint64_t count, void *workspace, size_t workspace_bytes, uint64_t *status,
+                        void *stream);
+
+/* ------------------------------------------------------------------ checked elementwise */
+
+/* out[i] = op(left[i], right[i]); a nonzero *_uniform flag broadcasts element 0 of that
+ * operand (the reference's UniformScalar representation).  out may alias a non-uniform input. */
+int pcu_b200_checked_binary(int dtype, int policy, int op, const void *left, const void *right, void *out,
+                            uint64_t count, int left_uniform, int right_uniform, uint64_t *status,
+                            void *stream);
+
+/* out[i] = checked ReLU(input[i]): non-finite -> Invalid, negative or signed zero -> +0,
+ * RejectSubnormalResult rejects a subnormal result (scalar_checked_float.rs:273-309). */
+int pcu_b200_checked_relu(int dtype, int policy, const void *input, void *out, uint64_t count,
+                          uint64_t *status, void *stream);
+
+/* out[i] = input[i] > 0 ? upstream[i] : +0, both operands required finite
+ * (scalar_checked_float.rs:634-652). */
+int pcu_b200_checked_relu_backward(int dtype, int policy, const void *input, const void *upstream, void *out,
+                                   uint64_t count, uint64_t *status, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

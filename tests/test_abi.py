@@ -1,0 +1,73 @@
+"""The C ABI library loads on a machine without a GPU and exports every declared symbol.
+
+Only host-side argument validation is exercised here (those paths return before any CUDA
+call); compute calls are in the gpu-marked tests.
+"""
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared():
+    names = set()
+    for header in os.listdir(os.path.join(ROOT, "include")):
+        if header.endswith(".h"):
+            text = open(os.path.join(ROOT, "include", header)).read()
+            names.update(re.findall(r"\b(pcu_b200_\w+)\s*\(", text))
+    return sorted(names)
+
+
+def test_header_declares_the_node_executors():
+    names = _declared()
+    for required in ("pcu_b200_strict_matmul", "pcu_b200_strict_sgd", "pcu_b200_strict_mse",
+                     "pcu_b200_checked_binary", "pcu_b200_checked_relu", "pcu_b200_checked_relu_backward",
+                     "pcu_b200_status_reset"):
+        assert required in names
+
+
+def test_library_exports_every_declared_symbol(provider):
+    lib = provider.library()
+    missing = [n for n in _declared() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_library_links_no_driver_at_load_time():
+    out = os.popen(f"ldd {os.path.join(ROOT, 'fusion-pcu_b200', 'libpcu_b200.so')}").read()
+    assert "libcuda.so" not in out and "not found" not in out, out
+
+
+def test_host_validation_rejects_bad_arguments(provider):
+    lib = provider.library()
+    status = ctypes.c_uint64(0)
+    sp = ctypes.byref(status)
+    # bad dtype / policy / op, missing status: all rejected before any device work
+    assert lib.pcu_b200_checked_binary(7, 0, 0, None, None, None, 0, 0, 0, sp, None) == 1
+    assert lib.pcu_b200_checked_binary(0, 9, 0, None, None, None, 0, 0, 0, sp, None) == 1
+    assert lib.pcu_b200_checked_binary(0, 0, 9, None, None, None, 0, 0, 0, sp, None) == 1
+    assert lib.pcu_b200_strict_sgd(0, 0, None, None, None, 4, 0x3F000000, None, None) == 1
+    # a non-finite learning rate is rejected (the capture-time rule of Graph::sgd_update)
+    assert lib.pcu_b200_strict_sgd(0, 0, ctypes.c_void_p(16), ctypes.c_void_p(16), ctypes.c_void_p(16), 4,
+                                   0x7FC00000, sp, None) == 1
+    # MSE of zero elements has no fault domain (fault_domain.rs:99-104)
+    assert lib.pcu_b200_strict_mse(0, 0, ctypes.c_void_p(16), ctypes.c_void_p(16), ctypes.c_void_p(16), 0, None,
+                                   0, sp, None) == 1
+    # the packed event bound rows*columns*inner*2 <= 2^60 (strict_matmul.rs:121-127)
+    big = 1 << 21
+    assert lib.pcu_b200_strict_matmul(0, 2, ctypes.c_void_p(16), ctypes.c_void_p(16), ctypes.c_void_p(16), big,
+                                      big, big, big, big, 0, 0, None, 0, sp, None) == 2
+    # empty outputs are a successful no-op
+    assert lib.pcu_b200_strict_matmul(0, 0, None, None, None, 0, 5, 5, 5, 5, 0, 0, None, 0, sp, None) == 0
+    assert lib.pcu_b200_abi_version() == 1
+    assert lib.pcu_b200_error_string(3).decode().startswith("workspace")
+
+
+@pytest.mark.parametrize("rows,inner,columns", [(1, 1, 1), (8192, 8192, 8192), (3, 0, 5)])
+def test_workspace_sizes(provider, rows, inner, columns):
+    lib = provider.library()
+    need = lib.pcu_b200_strict_matmul_workspace_size(rows, inner, columns)
+    assert need >= 4 * (rows + columns) and need % 256 == 0
+    assert lib.pcu_b200_strict_mse_workspace_size(0, 1 << 28) >= 4 << 28
