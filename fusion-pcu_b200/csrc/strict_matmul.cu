@@ -601,3 +601,68 @@ extern "C" int pcu_b200_strict_matmul(int dtype, int policy, const void *left, c
                               columns, left_stride, right_stride, transpose_left != 0, transpose_right != 0,
                               workspace, workspace_bytes, st, s);
 }
+
+// ============================================================================
+// Strict MatMul for callers that cannot allocate device memory.
+//
+// Some callers of this library are handed only the operand, output and status buffers and have
+// no way to obtain more device memory for the call: for example a plain C or FFI caller that is
+// not the owner of the process's device allocator (in Fusion-PCU all device memory belongs to
+// the Rust CudaMemoryResource pool), or a caller that must keep the call itself free of
+// allocation.  pcu_b200_strict_matmul needs a workspace for the operand-exponent minima; this
+// variant uses a fixed array of device memory that belongs to this library instead, and
+// allocates nothing itself.
+//
+// The array is a file-scope __device__ variable, so every GPU that loads this library holds
+// kStaticScratchBytes (about 257 KB) until the process exits.  Its limit is
+// rows + columns <= kStaticScratchMaxExtent.  In host code the array's name is only a host-side
+// handle, so the device address is looked up once per device with cudaGetSymbolAddress.
+// ============================================================================
+namespace {
+
+constexpr uint64_t kStaticScratchMaxExtent = 65536;  // rows + columns
+constexpr size_t kStaticScratchInts = kStaticScratchMaxExtent + 128;  // + 256-byte rounding of both halves
+constexpr size_t kStaticScratchBytes = kStaticScratchInts * sizeof(int);
+
+static __device__ __align__(256) int g_strict_matmul_scratch[kStaticScratchInts];
+
+// Device address of g_strict_matmul_scratch on the current device.  The first call on each
+// device performs the lookup; later calls reuse it.
+int static_scratch_address(void **address) {
+    static std::mutex lock;
+    static void *addresses[64] = {nullptr};
+    int device = 0;
+    cudaError_t err = cudaGetDevice(&device);
+    if (err != cudaSuccess) return pcu_host::set_cuda_error(err);
+    if (device < 0 || device >= 64) return PCU_B200_ERROR_UNSUPPORTED;
+    std::lock_guard<std::mutex> guard(lock);
+    if (!addresses[device]) {
+        void *ptr = nullptr;
+        err = cudaGetSymbolAddress(&ptr, g_strict_matmul_scratch);
+        if (err != cudaSuccess) return pcu_host::set_cuda_error(err);
+        addresses[device] = ptr;
+    }
+    *address = addresses[device];
+    return PCU_B200_OK;
+}
+
+}  // namespace
+
+extern "C" int pcu_b200_strict_matmul_static_scratch(int dtype, int policy, const void *left, const void *right,
+                                                     void *out, uint64_t rows, uint64_t inner, uint64_t columns,
+                                                     uint64_t left_stride, uint64_t right_stride,
+                                                     int transpose_left, int transpose_right, uint64_t *status,
+                                                     void *stream) {
+    if ((dtype != PCU_B200_F32 && dtype != PCU_B200_F64) || policy < 0 || policy > 2 || !status)
+        return PCU_B200_ERROR_INVALID_ARGUMENT;
+    if (rows + columns > kStaticScratchMaxExtent || rows > kStaticScratchMaxExtent ||
+        columns > kStaticScratchMaxExtent)
+        return PCU_B200_ERROR_WORKSPACE;
+    void *scratch = nullptr;
+    int rc = static_scratch_address(&scratch);
+    if (rc != PCU_B200_OK) return rc;
+    // pcu_b200_strict_matmul re-initialises the minima it needs on every call, so the contents
+    // a previous call left in the shared array never leak into this one.
+    return pcu_b200_strict_matmul(dtype, policy, left, right, out, rows, inner, columns, left_stride, right_stride,
+                                  transpose_left, transpose_right, scratch, kStaticScratchBytes, status, stream);
+}

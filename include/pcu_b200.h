@@ -116,6 +116,26 @@ int pcu_b200_strict_matmul(int dtype, int policy, const void *left, const void *
                            uint64_t right_stride, int transpose_left, int transpose_right, void *workspace,
                            size_t workspace_bytes, uint64_t *status, void *stream);
 
+/* pcu_b200_strict_matmul for callers that cannot allocate device memory.  It has no
+ * counterpart in the reference.
+ *
+ * Some callers are handed only the operand, output and status buffers and have no way to get
+ * more device memory for the call: a plain C or FFI caller that does not own the process's
+ * device allocator (in Fusion-PCU every device allocation belongs to the Rust memory-resource
+ * pool), or a caller that must keep the call itself free of allocation.  This variant takes no
+ * workspace.  Its scratch is a fixed array of device memory inside this library (about 257 KB,
+ * held on every GPU that loads the library until the process exits), so it accepts only
+ * shapes with rows + columns <= 65536; larger shapes return PCU_B200_ERROR_WORKSPACE.  It calls
+ * no cudaMalloc or cudaFree.  The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress); make that first call before any stream capture.  All calls share the
+ * one array: each call re-initialises what it reads, but calls whose executions overlap on the
+ * GPU (other streams, other host threads) race on it and must be serialised by the caller.
+ * Everything else -- arguments, results, status word, errors -- is exactly pcu_b200_strict_matmul. */
+int pcu_b200_strict_matmul_static_scratch(int dtype, int policy, const void *left, const void *right, void *out,
+                                          uint64_t rows, uint64_t inner, uint64_t columns, uint64_t left_stride,
+                                          uint64_t right_stride, int transpose_left, int transpose_right,
+                                          uint64_t *status, void *stream);
+
 /* ------------------------------------------------------------------ strict SGD */
 
 /* out[i] = weights[i] - rate * gradient[i] with the multiply and the subtract separately
