@@ -1,0 +1,89 @@
+"""Run one provider kernel on a fixed seeded case, for profilers (ncu) and quick timing.
+
+  python fusion-pcu_b200/profile_cases.py matmul --m 8192 --n 8192 --k 1024 [--dtype f32|f64]
+         [--layout nn|tn|nt|tt] [--policy 0|1|2] [--repeat R]
+  python fusion-pcu_b200/profile_cases.py sgd --count 67108864 [--repeat R]
+  python fusion-pcu_b200/profile_cases.py mse --count 67108864 [--repeat R]
+
+Each run prints the CUDA-event time per call; it checks that the status word stayed clean.
+"""
+import argparse
+import importlib
+import os
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.dirname(HERE))
+
+
+def dyadic(torch, shape, seed, dtype):
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    frac = 23 if dtype == torch.float32 else 52
+    hi = 1 << min(frac, 30)
+    k = torch.randint(-hi, hi, shape, generator=g, device="cuda", dtype=torch.int64)
+    return (k.to(torch.float64) / hi).to(dtype)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("case", choices=["matmul", "sgd", "mse", "binary"])
+    ap.add_argument("--m", type=int, default=8192)
+    ap.add_argument("--n", type=int, default=8192)
+    ap.add_argument("--k", type=int, default=1024)
+    ap.add_argument("--count", type=int, default=1 << 26)
+    ap.add_argument("--dtype", default="f32", choices=["f32", "f64"])
+    ap.add_argument("--layout", default="nn", choices=["nn", "tn", "nt", "tt"])
+    ap.add_argument("--policy", type=int, default=0)
+    ap.add_argument("--repeat", type=int, default=2)
+    args = ap.parse_args()
+
+    import torch
+
+    pcu = importlib.import_module("fusion-pcu_b200")
+    dt = torch.float32 if args.dtype == "f32" else torch.float64
+    status = pcu.new_status()
+    if args.case == "matmul":
+        tl, tr = args.layout[0] == "t", args.layout[1] == "t"
+        a = dyadic(torch, (args.k, args.m) if tl else (args.m, args.k), 1, dt)
+        b = dyadic(torch, (args.n, args.k) if tr else (args.k, args.n), 2, dt)
+        out = torch.empty((args.m, args.n), dtype=dt, device="cuda")
+        ws = torch.empty(pcu.library().pcu_b200_strict_matmul_workspace_size(args.m, args.k, args.n),
+                         dtype=torch.uint8, device="cuda")
+        call = lambda: pcu.strict_matmul(a, b, tl, tr, args.policy, out=out, status=status, workspace=ws)  # noqa
+        work, unit = 2.0 * args.m * args.n * args.k, "TFLOP/s"
+    elif args.case == "sgd":
+        w, g = dyadic(torch, (args.count,), 1, dt), dyadic(torch, (args.count,), 2, dt)
+        out = torch.empty_like(w)
+        call = lambda: pcu.strict_sgd(w, g, 0.01, args.policy, out=out, status=status)  # noqa
+        work, unit = 3.0 * args.count * w.element_size(), "GB/s"
+    elif args.case == "binary":
+        x, y = dyadic(torch, (args.count,), 1, dt), dyadic(torch, (args.count,), 2, dt)
+        out = torch.empty_like(x)
+        call = lambda: pcu.checked_binary("add", x, y, args.policy, out=out, status=status)  # noqa
+        work, unit = 3.0 * args.count * x.element_size(), "GB/s"
+    else:
+        p, t = dyadic(torch, (args.count,), 1, dt), dyadic(torch, (args.count,), 2, dt)
+        out = torch.empty((), dtype=dt, device="cuda")
+        ws = torch.empty(pcu.library().pcu_b200_strict_mse_workspace_size(0 if dt == torch.float32 else 1,
+                                                                           args.count),
+                         dtype=torch.uint8, device="cuda")
+        call = lambda: pcu.strict_mse(p, t, args.policy, out=out, status=status, workspace=ws)  # noqa
+        work, unit = 2.0 * args.count * p.element_size(), "GB/s"
+    call()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.repeat):
+        call()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.repeat
+    word = int(status.cpu().item()) & ((1 << 64) - 1)
+    assert word == pcu.STATUS_OK, hex(word)
+    scale = 1e12 if unit == "TFLOP/s" else 1e9
+    print(f"{args.case} {args.dtype} {ms:.3f} ms/call  {work / (ms * 1e-3) / scale:.2f} {unit}")
+
+
+if __name__ == "__main__":
+    main()
