@@ -34,6 +34,17 @@
 #include "common.cuh"
 #include "pcu_b200.h"
 
+// Tuning knobs (defaults are the measured best; override with -D for sweeps).
+#ifndef PCU_MM_UNROLL_F32
+#define PCU_MM_UNROLL_F32 2
+#endif
+#ifndef PCU_MM_UNROLL_F64
+#define PCU_MM_UNROLL_F64 8
+#endif
+#ifndef PCU_MM_LOOKAHEAD
+#define PCU_MM_LOOKAHEAD 2
+#endif
+
 namespace pcu {
 
 template <typename T> struct MatmulParams {
@@ -182,11 +193,13 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, u
 }
 
 template <typename T> struct Tile;
+// GROUP_UNROLL: 16-byte K groups folded per loop iteration (measured best on B200:
+// 2 for binary32, whose group body is 512 FP instructions; 8 for binary64, 128 per group).
 template <> struct Tile<float> {
-    static constexpr int TM = 8, TN = 8, BK = 32, STAGES = 4;
+    static constexpr int TM = 8, TN = 8, BK = 32, STAGES = 4, GROUP_UNROLL = PCU_MM_UNROLL_F32;
 };
 template <> struct Tile<double> {
-    static constexpr int TM = 8, TN = 4, BK = 16, STAGES = 4;
+    static constexpr int TM = 8, TN = 4, BK = 16, STAGES = 4, GROUP_UNROLL = PCU_MM_UNROLL_F64;
 };
 
 template <typename T, int V> struct SVec;
@@ -204,8 +217,14 @@ template <typename T> struct TileShape {
     static_assert(BK * sizeof(T) == 128, "K-major tiles are one 128-byte swizzle row per M/N index");
 };
 
+// Eight warps, two per SM sub-partition: a ninth (producer) warp would put three warps on one
+// sub-partition and cap every thread at 168 registers.  Thread 0 issues the TMA copies instead.
 constexpr int kConsumerWarps = 8;
-constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kThreads = kConsumerWarps * 32;
+// Stages in flight beyond the one being folded.  Thread 0 refills the slot of stage kt-2 while
+// folding stage kt, so it practically never waits for a slower warp to release a slot.
+constexpr int kLookahead = PCU_MM_LOOKAHEAD;
+static_assert(kLookahead >= 1 && kLookahead < 4, "lookahead must leave a slot free");
 
 // A_KMAJOR: op(A) rows are contiguous in k (left not transposed).
 // B_KMAJOR: op(B) columns are contiguous in k (right transposed).
@@ -224,7 +243,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t *const full = reinterpret_cast<uint64_t *>(base + STAGES * S::STAGE_BYTES);
     uint64_t *const empty = full + STAGES;
     __shared__ int abort_flag;
-    __shared__ int consumed_tiles;
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const uint64_t m0 = (uint64_t)blockIdx.y * BM, n0 = (uint64_t)blockIdx.x * BN;
@@ -237,42 +255,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         abort_flag = 0;
-        consumed_tiles = 0;
     }
     __syncthreads();
 
-    if (warp == kConsumerWarps) {
-        // ---------------------------------------------------------------- producer
-        int issued = 0;
-        if (lane == 0) {
-            for (int kt = 0; kt < KT; ++kt) {
-                const int s = kt % STAGES;
-                if (!mbar_wait(&empty[s], ((kt / STAGES) & 1) ^ 1)) {
-                    record_fault(p.status, 0, kWatchdog);
-                    abort_flag = 1;
-                    break;
-                }
-                if (*(volatile int *)&abort_flag) break;
-                T *sa = tiles + (size_t)s * (S::STAGE_BYTES / sizeof(T));
-                T *sb = sa + S::A_BYTES / sizeof(T);
-                mbar_expect_tx(&full[s], S::STAGE_BYTES);
-                const int k0 = kt * BK;
-                if (A_KMAJOR) tma_load_2d(sa, &map_a, &full[s], k0, (int)m0);
-                else tma_load_2d(sa, &map_a, &full[s], (int)m0, k0);
-                if (B_KMAJOR) tma_load_2d(sb, &map_b, &full[s], k0, (int)n0);
-                else tma_load_2d(sb, &map_b, &full[s], (int)n0, k0);
-                ++issued;
-            }
+    // Thread 0 only: copy stage `kt` into its slot once every warp has released the slot.
+    int issued = 0;
+    auto issue = [&](int kt) -> bool {
+        const int s = kt % STAGES;
+        if (!mbar_wait(&empty[s], ((kt / STAGES) & 1) ^ 1)) {
+            record_fault(p.status, 0, kWatchdog);
+            abort_flag = 1;
+            return false;
         }
-        __syncwarp();
-        __syncthreads();
-        // Never leave the CTA with a bulk copy still writing into its shared memory.
-        if (lane == 0) {
-            for (int kt = consumed_tiles; kt < issued; ++kt)
-                if (!mbar_wait(&full[kt % STAGES], (kt / STAGES) & 1)) break;
-        }
-        return;
-    }
+        T *sa = tiles + (size_t)s * (S::STAGE_BYTES / sizeof(T));
+        T *sb = sa + S::A_BYTES / sizeof(T);
+        mbar_expect_tx(&full[s], S::STAGE_BYTES);
+        const int k0 = kt * BK;
+        if (A_KMAJOR) tma_load_2d(sa, &map_a, &full[s], k0, (int)m0);
+        else tma_load_2d(sa, &map_a, &full[s], (int)m0, k0);
+        if (B_KMAJOR) tma_load_2d(sb, &map_b, &full[s], k0, (int)n0);
+        else tma_load_2d(sb, &map_b, &full[s], (int)n0, k0);
+        ++issued;
+        return true;
+    };
+    if (threadIdx.x == 0)
+        for (int kt = 0; kt < kLookahead && kt < KT; ++kt)
+            if (!issue(kt)) break;
 
     // -------------------------------------------------------------------- consumers
     const int ty = (warp >> 1) * 4 + (lane >> 3);  // 0..15 along M
@@ -293,6 +301,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     int kt = 0;
     for (; kt < KT; ++kt) {
         const int s = kt % STAGES;
+        if (threadIdx.x == 0 && kt + kLookahead < KT && !*(volatile int *)&abort_flag) issue(kt + kLookahead);
+        __syncwarp();
         if (!mbar_wait(&full[s], (kt / STAGES) & 1)) {
             record_fault(p.status, 0, kWatchdog);
             abort_flag = 1;
@@ -300,10 +310,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const T *sa = tiles + (size_t)s * (S::STAGE_BYTES / sizeof(T));
         const T *sb = sa + S::A_BYTES / sizeof(T);
-#pragma unroll
-        for (int g = 0; g < BK / V; ++g) {
-            T a[TM][V];
-            T b[V][TN];
+        // One group = V k-steps of 16-byte fragments; a stage holds BK / V = 8 groups.
+        auto load_group = [&](int g, T (&a)[TM][V], T (&b)[V][TN]) {
             if (A_KMAJOR) {
                 const int chunk = g ^ (ty & 7);
 #pragma unroll
@@ -344,20 +352,38 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int q = 0; q < V; ++q) b[kv][jg * V + q] = e[q];
                     }
             }
+        };
+        // k ascending inside the group: kv is the outer loop, so every cell sees its K in order
+        auto fold_group = [&](const T (&a)[TM][V], const T (&b)[V][TN]) {
 #pragma unroll
             for (int kv = 0; kv < V; ++kv)
 #pragma unroll
                 for (int i = 0; i < TM; ++i)
 #pragma unroll
                     for (int j = 0; j < TN; ++j) acc[i][j] = F::add(acc[i][j], F::mul(a[i][kv], b[kv][j]));
+        };
+        // Unrolling all BK / V groups of a stage makes the body larger than the instruction
+        // cache (measured: the no_instruction stall dominates); Tile<T>::GROUP_UNROLL groups
+        // per loop iteration keep it resident.
+        constexpr int kUnroll = Tile<T>::GROUP_UNROLL;
+#pragma unroll kUnroll
+        for (int g = 0; g < BK / V; ++g) {
+            T a[TM][V], b[V][TN];
+            load_group(g, a, b);
+            fold_group(a, b);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
     }
-    if (threadIdx.x == 0) consumed_tiles = kt;
-    __syncwarp();
-    __syncthreads();  // pairs with the producer warp's barrier
-    if (*(volatile int *)&abort_flag) return;
+    // Never leave the CTA with a bulk copy still writing into its shared memory: after a
+    // watchdog abort thread 0 waits (bounded) for every copy it issued but nobody folded.
+    __syncthreads();
+    if (*(volatile int *)&abort_flag) {
+        if (threadIdx.x == 0)
+            for (int t = kt; t < issued; ++t)
+                if (!mbar_wait(&full[t % STAGES], (t / STAGES) & 1)) break;
+        return;
+    }
 
     // -------------------------------------------------------------------- epilogue
     int rmin[TM], cmin[TN];
