@@ -1,116 +1,728 @@
-// strict_mse.cu -- ordered strict mean squared error.
+// strict_mse.cu -- ordered strict mean squared error at HBM speed, bit-exact.
 //
 // Semantics (paths relative to the Fusion-PCU checkout): for i ascending, d = sub(p, t),
 // q = mul(d, d), s = add(s, q) from s = +0, then mean = div(s, count rounded to nearest-even);
-// each step separately rounded and checked; events i*3 + {Subtract 0, Multiply 1, Add 2} and
-// 3n for Divide (Crates/core/dialect/tensor/reference/strict_mse/strict_mse.rs:22-59,
+// each step separately rounded and checked; events i*3 + {Subtract 0, Multiply 1, Add 2} and 3n
+// for Divide (Crates/core/dialect/tensor/reference/strict_mse/strict_mse.rs:22-59,
 // Crates/core/dialect/tensor/fault_domain/fault_domain.rs:148-158).  The reference CUDA
-// provider runs this on one lane (Crates/backends/cuda/tensor/strict_mse/strict_mse.rs:144-188).
+// provider runs the whole reduction on one lane (tensor/strict_mse/strict_mse.rs:144-188).
 //
-// This provider splits the work:
-//   phase 1 (all SMs, HBM-bound): every element's subtract and square with their checks,
-//            writing the squares q[i] to the workspace plus a per-block maximum;
-//   phase 2 (one warp): the ordered running sum.  The running sum of squares is monotone,
-//            so a block whose largest square is below half an ulp of the current sum cannot
-//            change it and is skipped whole; overflow (the only fault an Add of nonnegative
-//            finite squares can raise, fault_domain.rs:207-214) is sticky, so it is checked per
-//            block and located exactly only when it happened.
+// Exact parallel algorithm.  Write the running sum as s = x * u with u = 2^k its ulp (k = e - P
+// for s in the binade [2^e, 2^(e+1)), P = 23 or 52 fraction bits; below the top of the
+// smallest normal binade the spacing is the minimum, k = KMIN).  While s stays inside its
+// binade, one step is x' = x + y rounded to the nearest integer, ties to even, y = q / u.  That
+// equals x + RN_half_up(y) unless y is an exact half-integer (a tie), where the result is the
+// even neighbour and so depends on x's parity.  A run of squares therefore acts on the state as
+//                     x  ->  x + D[x mod 2]
+// for two integers D[0], D[1] (they differ only through ties), valid while the final state stays
+// below 2^(P+1) (every intermediate exact sum is then inside the binade).  Such maps compose:
+// D12[p] = D1[p] + D2[(p + D1[p]) mod 2].  Squares are >= 0, so s is monotone and only ever
+// moves up through the binades.
+//
+//   phase 1 (mse_chunk_kernel, all SMs, HBM bound): per CHUNK elements, the subtract and the
+//     square (a cheap test of the square selects the exact checked path for the rare suspects),
+//     then D for every binade k in the window [k_hi - W + 1, k_hi], k_hi = exponent(max q) + 1
+//     (above it every y < 1/2: identity):
+//       * q in fixed point Q = floor(q / 2^(k_lo - 1)) plus a sticky bit; the half-up
+//         increment at binade k is (Q + 2^(j-1)) >> j, j = k - k_lo + 1, so its chunk sum is
+//         W_j + cnt[j-1] with W_j = 2 W_(j+1) + cnt[j] from per-bit population counts cnt[b]
+//         (vertical bit-plane counters, then warp reductions);
+//       * the parity of a half-up increment is bit j of R = Q ^ (Q << 1), so one exclusive
+//         prefix-XOR of R gives, for every binade at once, the parity of the half-up running
+//         increment in front of each element;
+//       * a tie at binade k is an element whose lowest set bit (and no sticky) is bit j-1.  Only
+//         binades where the chunk's sum can fit in one binade are kept (below them the map is
+//         never applied, and every square is a tie at the binade of its own lowest bit); those
+//         ties are rare and give the exact corrections for an even and an odd start.
+//   phase 2 (mse_block_kernel): compose the chunk maps of each BLOCK of 64 chunks.
+//   phase 3 (mse_walk_kernel, one CTA): from s = +0, apply block maps in order, descending to
+//     chunk maps when a block map cannot be applied.  A chunk whose map cannot be applied (the
+//     state crosses a binade inside it, a Subtract/Multiply fault lies in it, or it had too
+//     many ties) is resolved in parallel: its squares are recomputed, the half-up increments
+//     at the current binade are prefix-summed, every element before the first tie or binade
+//     crossing is applied at once, and that one element is added exactly with the IEEE add.
+//     The only fault an Add of nonnegative finite squares can raise is overflow
+//     (fault_domain.rs:207-214); a map is never applied when its result would leave the
+//     binade, so overflow is always met by the exact add.  Then the checked divide.
 #include <cstring>
+#include <type_traits>
 
 #include "common.cuh"
 #include "pcu_b200.h"
 
 namespace pcu {
 
-constexpr int kMseBlock = 1024;  // elements per phase-2 skip block
+template <typename T> struct MseTraits;
+template <> struct MseTraits<float> {
+    using Fix = uint32_t;     // fixed-point square (W bits) + sticky in the top bit
+    using D = uint32_t;       // map increment: a valid one is below 2^24
+    static constexpr int EPT = 32;               // elements per thread
+    static constexpr int CHUNK = 256 * EPT;      // 8192
+    static constexpr int W = 27;                 // binades per window
+    static constexpr int P = 23;                 // fraction bits
+    static constexpr int KMIN = -149;            // smallest ulp exponent
+    static constexpr int PLANES = 6;             // vertical counter planes: counts up to 63
+    static constexpr uint64_t SAT = 1ull << 40;  // no valid increment comes near this
+};
+template <> struct MseTraits<double> {
+    using Fix = uint64_t;
+    using D = uint64_t;       // a valid increment is below 2^53
+    static constexpr int EPT = 16;
+    static constexpr int CHUNK = 256 * EPT;      // 4096
+    static constexpr int W = 56;
+    static constexpr int P = 52;
+    static constexpr int KMIN = -1074;
+    static constexpr int PLANES = 5;
+    static constexpr uint64_t SAT = 1ull << 62;
+};
+
+constexpr int kBlockChunks = 64;
+constexpr int kMaxTies = 256;
+
+enum : int { kHeadZero = 1, kHeadExact = 2, kHeadFault = 4 };
+
+struct MseHead {
+    int32_t k_lo;      // window [k_lo, k_lo + W - 1]
+    int32_t flags;     // kHeadZero: every square is +0; kHeadExact: resolve element by element
+    uint32_t fault;    // first Subtract/Multiply fault (chunk- or block-relative) if kHeadFault
+    uint32_t pad;
+};
+
+template <typename T> __device__ __forceinline__ typename MseTraits<T>::D no_map() {
+    return (typename MseTraits<T>::D)~0ull;
+}
+
+template <typename T> __device__ __forceinline__ typename MseTraits<T>::D sat_d(uint64_t v) {
+    return v >= MseTraits<T>::SAT ? no_map<T>() : (typename MseTraits<T>::D)v;
+}
+
+template <typename T> __device__ __forceinline__ int exponent_of(typename Fmt<T>::Bits b) {
+    using F = Fmt<T>;
+    const int field = (int)((b & F::kExpMask) >> F::kFrac);
+    if (field) return field - F::kBias;
+    typename F::Bits f = b & F::kFracMask;
+    const int top = sizeof(T) == 4 ? 31 - __clz((int)f) : 63 - __clzll((long long)f);
+    return top + F::kMinExp - F::kFrac;
+}
+
+// x (state in ulps) and k (ulp exponent) of a running sum s >= 0.
+template <typename T>
+__device__ __forceinline__ void state_of(T s, uint64_t &x, int &k) {
+    using F = Fmt<T>;
+    using Tr = MseTraits<T>;
+    typename F::Bits b = F::bits(s);
+    const int field = (int)((b & F::kExpMask) >> F::kFrac);
+    const uint64_t frac = (uint64_t)(b & F::kFracMask);
+    if (field <= 1) {  // subnormal or smallest normal binade: spacing is the minimum ulp
+        k = Tr::KMIN;
+        x = field ? (frac | (1ull << Tr::P)) : frac;
+    } else {
+        k = field - F::kBias - Tr::P;
+        x = frac | (1ull << Tr::P);
+    }
+}
 
 template <typename T>
-__global__ void __launch_bounds__(256) mse_squares_kernel(const T *prediction, const T *target, uint64_t n,
-                                                          T *squares, T *block_max, int policy,
-                                                          unsigned long long *status) {
-    // one CTA of 256 threads covers kMseBlock elements per iteration
-    __shared__ T warp_max[8];
-    for (uint64_t blk = blockIdx.x; blk * kMseBlock < n; blk += gridDim.x) {
-        T local = T(0);
-        bool stop = false;
-        for (int e = threadIdx.x; e < kMseBlock; e += 256) {
-            const uint64_t i = blk * kMseBlock + e;
-            if (i >= n || stop) break;
-            T d, q;
-            unsigned kind = checked_sub<T>(prediction[i], target[i], policy, d);
-            if (kind) { record_fault(status, i * 3, kind); stop = true; break; }
-            kind = checked_mul<T>(d, d, policy, q);
-            if (kind) { record_fault(status, i * 3 + 1, kind); stop = true; break; }
-            squares[i] = q;
-            local = local > q ? local : q;
-        }
+__device__ __forceinline__ T value_of(uint64_t x, int k) {
+    using F = Fmt<T>;
+    using Tr = MseTraits<T>;
+    if (k == Tr::KMIN) return F::value((typename F::Bits)x);  // field 0 or 1 encodes x directly
+    return F::value(((typename F::Bits)(k + Tr::P + F::kBias) << F::kFrac) |
+                    ((typename F::Bits)x & F::kFracMask));
+}
+
+// Half-up increment of a square at ulp 2^k (saturating) and whether it is a tie there.
+template <typename T>
+__device__ __forceinline__ uint64_t half_up_increment(T q, int k, bool &tie) {
+    using F = Fmt<T>;
+    using Tr = MseTraits<T>;
+    const typename F::Bits b = F::bits(q);
+    tie = false;
+    if (!b) return 0;
+    const int field = (int)((b & F::kExpMask) >> F::kFrac);
+    const uint64_t m = (uint64_t)(b & F::kFracMask) | (field ? (1ull << F::kFrac) : 0);
+    const int e = (field ? field : 1) - F::kBias - F::kFrac;  // q = m * 2^e
+    const int sh = e - k;
+    if (sh >= 0) return sh + Tr::P + 1 >= 62 ? Tr::SAT : min((uint64_t)Tr::SAT, m << sh);
+    const int d = -sh;
+    if (d > Tr::P + 2) return 0;  // y < 1/2
+    const uint64_t half = 1ull << (d - 1);
+    tie = (m & ((half << 1) - 1)) == half;
+    return (m + half) >> d;
+}
+
+struct Tie {
+    uint32_t index;   // chunk-relative element
+    uint16_t j;       // binade offset: k = k_lo + j - 1
+    uint8_t mpar;     // parity of floor(q / 2^k)
+    uint8_t pi;       // parity of the half-up increments in front of it
+};
+
+template <typename T> __device__ __forceinline__ typename Fmt<T>::Bits warp_max_bits(typename Fmt<T>::Bits v) {
+    if constexpr (sizeof(T) == 4) {
+        return __reduce_max_sync(0xffffffffu, (unsigned)v);
+    } else {
 #pragma unroll
         for (int o = 16; o; o >>= 1) {
-            T other = __shfl_xor_sync(0xffffffffu, local, o);
-            local = local > other ? local : other;
+            unsigned long long other = __shfl_xor_sync(0xffffffffu, (unsigned long long)v, o);
+            v = other > v ? other : v;
         }
-        if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = local;
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            T m = warp_max[0];
-            for (int w = 1; w < 8; ++w) m = m > warp_max[w] ? m : warp_max[w];
-            block_max[blk] = m;
-        }
-        __syncthreads();
+        return v;
     }
 }
 
+template <typename X> __device__ __forceinline__ X shfl_up_x(X v, int o) {
+    if constexpr (sizeof(X) == 4) return __shfl_up_sync(0xffffffffu, (unsigned)v, o);
+    else return __shfl_up_sync(0xffffffffu, (unsigned long long)v, o);
+}
+
+template <typename X> __device__ __forceinline__ X shfl_x(X v, int src) {
+    if constexpr (sizeof(X) == 4) return __shfl_sync(0xffffffffu, (unsigned)v, src);
+    else return __shfl_sync(0xffffffffu, (unsigned long long)v, src);
+}
+
+// Element layout of a chunk: warp w owns a contiguous span of 32*V*ROWS elements; in row r
+// lane l owns V consecutive elements (one 16-byte load per row, coalesced across the warp).
+template <typename T> struct ChunkMap {
+    static constexpr int V = 16 / sizeof(T);
+    static constexpr int ROWS = MseTraits<T>::EPT / V;
+    static constexpr int WARP_SPAN = 32 * V * ROWS;
+    __device__ static __forceinline__ int index(int warp, int row, int lane, int e) {
+        return warp * WARP_SPAN + row * 32 * V + lane * V + e;
+    }
+};
+
+// a[idx] = v for a register array and a run-time index, without demoting the array to memory
+template <typename X, int N> __device__ __forceinline__ void set_at(X (&a)[N], int idx, X v) {
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+        if (i == idx) a[i] = v;
+}
+
+// The square of one element with the reference's checked subtract and multiply (first fault
+// recorded); used only for the rare elements the fast test flags.
 template <typename T>
-__device__ __forceinline__ T half_ulp(T s) {
-    using F = Fmt<T>;
-    typename F::Bits b = F::bits(s);
-    const int64_t field = (int64_t)((b & F::kExpMask) >> F::kFrac);
-    // half an ulp of a normal s is 2^(field - bias - frac - 1), i.e. biased field - frac - 1;
-    // near the bottom of the range (or for subnormal s) never skip
-    if (field - F::kFrac - 1 <= 0) return T(0);
-    return F::value((typename F::Bits)(field - F::kFrac - 1) << F::kFrac);
+__device__ __noinline__ bool checked_square(T p, T t, uint64_t i, int policy, unsigned long long *status, T &q) {
+    T d;
+    unsigned kind = checked_sub<T>(p, t, policy, d);
+    if (kind) { record_fault(status, i * 3, kind); return false; }
+    kind = checked_mul<T>(d, d, policy, q);
+    if (kind) { record_fault(status, i * 3 + 1, kind); return false; }
+    return true;
 }
 
 template <typename T>
-__global__ void mse_sum_kernel(const T *squares, const T *block_max, uint64_t n, T denominator, int policy, T *out,
-                               unsigned long long *status) {
-    if (threadIdx.x != 0) return;
+__global__ void __launch_bounds__(256) mse_chunk_kernel(const T *prediction, const T *target, uint64_t n,
+                                                        int policy, MseHead *heads,
+                                                        typename MseTraits<T>::D *deltas,
+                                                        unsigned long long *status) {
+    using Tr = MseTraits<T>;
     using F = Fmt<T>;
-    T s = T(0);
-    const uint64_t blocks = (n + kMseBlock - 1) / kMseBlock;
-    for (uint64_t blk = 0; blk < blocks; ++blk) {
-        const uint64_t i0 = blk * kMseBlock;
-        const uint64_t i1 = i0 + kMseBlock < n ? i0 + kMseBlock : n;
-        // a subtract/multiply fault at or before this block ends the ordered walk
-        if (fault_precedes(status, i1 * 3)) {
-            // the walk may still own an earlier Add overflow inside [i0, i1)
-            const unsigned long long st = read_status(status);
-            const uint64_t first = (st >> 3) / 3;  // element of the earlier fault
-            for (uint64_t i = i0; i < first && i < i1; ++i) {
-                T t = F::add(s, squares[i]);
-                if (nonfinite_bits<T>(F::bits(t))) { record_fault(status, i * 3 + 2, kOverflow); return; }
-                s = t;
+    using B = typename F::Bits;
+    using Fix = typename Tr::Fix;
+    using CM = ChunkMap<T>;
+    constexpr int EPT = Tr::EPT, W = Tr::W, V = CM::V, ROWS = CM::ROWS;
+    constexpr int FIXBITS = sizeof(Fix) * 8;
+    constexpr Fix kSticky = (Fix)1 << (FIXBITS - 1);
+    using VT = typename std::conditional<sizeof(T) == 4, float4, double2>::type;
+
+    __shared__ unsigned int s_fault;
+    __shared__ unsigned long long s_qmax;
+    __shared__ unsigned int s_cnt[W];
+    __shared__ Fix s_warp_xor[8];
+    __shared__ unsigned int s_tie_count;
+    __shared__ int s_jmin;
+    __shared__ Tie s_ties[kMaxTies];
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint64_t chunk0 = (uint64_t)blockIdx.x * Tr::CHUNK;
+    if (tid == 0) {
+        s_fault = 0xffffffffu;
+        s_qmax = 0;
+        s_tie_count = 0;
+    }
+    if (tid < W) s_cnt[tid] = 0;
+    __syncthreads();
+
+    // ---- squares.  Fast test: a non-finite square means an invalid operand or an overflow in
+    // one of the two steps; a square at or below the smallest normal of a nonzero difference
+    // may hide an underflow decision (and under RejectSubnormalResult a subnormal difference
+    // always squares into that range).  Flagged threads redo their elements with the checked
+    // law, in order, and stop at their first fault (their later events cannot win).
+    Fix qf[EPT];  // q's bits first, its fixed-point form later; qf[row * V + e]
+    bool suspect = false;
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r) {
+        const uint64_t i0 = chunk0 + CM::index(warp, r, lane, 0);
+        T pv[V], tv[V];
+        if (i0 + V <= n) {
+            const VT a = __ldcs(reinterpret_cast<const VT *>(prediction + i0));
+            const VT b = __ldcs(reinterpret_cast<const VT *>(target + i0));
+#pragma unroll
+            for (int e = 0; e < V; ++e) {
+                pv[e] = reinterpret_cast<const T *>(&a)[e];
+                tv[e] = reinterpret_cast<const T *>(&b)[e];
             }
+        } else {
+#pragma unroll
+            for (int e = 0; e < V; ++e) {
+                pv[e] = i0 + e < n ? prediction[i0 + e] : T(0);
+                tv[e] = i0 + e < n ? target[i0 + e] : T(0);
+            }
+        }
+#pragma unroll
+        for (int e = 0; e < V; ++e) {
+            const T d = F::sub(pv[e], tv[e]);
+            const B qb = F::bits(F::mul(d, d));
+            suspect |= nonfinite_bits<T>(qb) ||
+                       (policy != kPolicyGradual && qb <= F::kMinNormalBits && (F::bits(d) << 1) != 0);
+            qf[r * V + e] = (Fix)qb;
+        }
+    }
+    if (suspect) {  // rare: reload and redo this thread's elements with the checked law
+        bool stopped = false;
+#pragma unroll 1
+        for (int r = 0; r < ROWS; ++r)
+#pragma unroll 1
+            for (int e = 0; e < V; ++e) {
+                const int c = CM::index(warp, r, lane, e);
+                const uint64_t i = chunk0 + c;
+                T q = T(0);
+                if (!stopped && i < n && !checked_square<T>(prediction[i], target[i], i, policy, status, q)) {
+                    atomicMin(&s_fault, (unsigned)c);
+                    stopped = true;
+                }
+                if (i < n) set_at(qf, r * V + e, stopped ? (Fix)0 : (Fix)F::bits(q));
+            }
+    }
+    B local_max = 0;
+#pragma unroll
+    for (int e = 0; e < EPT; ++e) local_max = (B)qf[e] > local_max ? (B)qf[e] : local_max;
+    local_max = warp_max_bits<T>(local_max);
+    if (lane == 0) atomicMax(&s_qmax, (unsigned long long)local_max);
+    __syncthreads();
+
+    MseHead head;
+    head.pad = 0;
+    head.fault = s_fault;
+    head.flags = s_fault != 0xffffffffu ? kHeadFault : 0;
+    const B qmax = (B)s_qmax;
+    if (qmax == 0) {  // every square is +0 (or faulted): the identity at every binade
+        if (tid == 0) {
+            head.k_lo = 0;
+            head.flags |= kHeadZero;
+            heads[blockIdx.x] = head;
+        }
+        return;
+    }
+    const int k_hi = exponent_of<T>(qmax) + 1;
+    const int k_lo = max(k_hi - (W - 1), Tr::KMIN);
+    const int L0 = k_lo - 1;  // fixed-point unit 2^L0
+
+    // ---- fixed point (branch-free), vertical bit counters, per-row XOR of R = Q ^ (Q << 1)
+    Fix planes[Tr::PLANES];
+#pragma unroll
+    for (int pl = 0; pl < Tr::PLANES; ++pl) planes[pl] = 0;
+    Fix row_xor[ROWS];
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r) {
+        row_xor[r] = 0;
+#pragma unroll
+        for (int e = 0; e < V; ++e) {
+            const B qb = (B)qf[r * V + e];
+            const int field = (int)((qb & F::kExpMask) >> F::kFrac);
+            const Fix m = (Fix)(qb & F::kFracMask) | (field ? ((Fix)1 << F::kFrac) : (Fix)0);
+            // q = m * 2^(field' - bias - frac), field' = max(field, 1); Q = m * 2^sh, sh <= 3
+            const int sh = (field ? field : 1) - F::kBias - F::kFrac - L0;
+            const int up = sh > 0 ? sh : 0;
+            const int dn = sh < 0 ? min(-sh, FIXBITS - 1) : 0;
+            const Fix mm = m << up;
+            const Fix Q = mm >> dn;
+            const Fix sticky = (mm & (((Fix)1 << dn) - 1)) ? kSticky : (Fix)0;
+            qf[r * V + e] = Q | sticky;
+            Fix carry = Q;
+#pragma unroll
+            for (int pl = 0; pl < Tr::PLANES; ++pl) {
+                const Fix t = planes[pl] & carry;
+                planes[pl] ^= carry;
+                carry = t;
+            }
+            row_xor[r] ^= Q ^ (Q << 1);
+        }
+    }
+    // per-bit counts: planes -> counts, warp reduce, block accumulate
+#pragma unroll
+    for (int b = 0; b < W; ++b) {
+        unsigned c = 0;
+#pragma unroll
+        for (int pl = 0; pl < Tr::PLANES; ++pl) c |= (unsigned)((planes[pl] >> b) & 1) << pl;
+        c = __reduce_add_sync(0xffffffffu, c);
+        if (lane == 0 && c) atomicAdd(&s_cnt[b], c);
+    }
+    // exclusive prefix XOR in element order: row by row across lanes, then across warps
+    Fix lane_ex[ROWS];
+    Fix warp_total = 0;
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r) {
+        Fix incl = row_xor[r];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const Fix v = shfl_up_x(incl, o);
+            if (lane >= o) incl ^= v;
+        }
+        lane_ex[r] = warp_total ^ incl ^ row_xor[r];  // rows before r, then lanes before this one
+        warp_total ^= shfl_x(incl, 31);
+    }
+    if (lane == 0) s_warp_xor[warp] = warp_total;
+    __syncthreads();
+    Fix warp_prefix = 0;
+    for (int w = 0; w < warp; ++w) warp_prefix ^= s_warp_xor[w];
+    // Lowest binade offset whose half-up sum could still fit inside one binade (< 2^(P+1)).
+    if (tid == 0) {
+        int jmin = W + 1;
+        uint64_t Wj = 0;
+        for (int j = W; j >= 1; --j) {
+            if (j < W) Wj = 2 * Wj + s_cnt[j];
+            if (Wj >= Tr::SAT || Wj + s_cnt[j - 1] >= (2ull << Tr::P)) break;  // sums only grow as j falls
+            jmin = j;
+        }
+        s_jmin = jmin;
+    }
+    __syncthreads();
+    const int jmin = s_jmin;
+
+    // ---- ties at the usable binades, with the parity of the half-up increments in front
+    const Fix qmask = (Fix)~kSticky;
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r) {
+        Fix prefix = warp_prefix ^ lane_ex[r];
+#pragma unroll
+        for (int e = 0; e < V; ++e) {
+            const Fix qs = qf[r * V + e];
+            const Fix Q = qs & qmask;
+            const int j = sizeof(Fix) == 4 ? __ffs((int)Q) : __ffsll((long long)Q);  // lowest bit + 1
+            if (Q && !(qs & kSticky) && j >= jmin && j <= W) {
+                const unsigned slot = atomicAdd(&s_tie_count, 1u);
+                if (slot < (unsigned)kMaxTies) {
+                    Tie t;
+                    t.index = (uint32_t)CM::index(warp, r, lane, e);
+                    t.j = (uint16_t)j;
+                    t.mpar = (uint8_t)((j < FIXBITS) ? ((Q >> j) & 1) : 0);
+                    t.pi = (uint8_t)((j < FIXBITS) ? ((prefix >> j) & 1) : 0);
+                    s_ties[slot] = t;
+                }
+            }
+            prefix ^= Q ^ (Q << 1);
+        }
+    }
+    __syncthreads();
+
+    const unsigned ties = s_tie_count;
+    if (tid == 0) {
+        head.k_lo = k_lo;
+        if (ties > (unsigned)kMaxTies) head.flags |= kHeadExact;
+        heads[blockIdx.x] = head;
+    }
+    // ---- one thread per binade: half-up sum from the counts, then the tie corrections
+    if (tid < W) {
+        const int j = tid + 1;  // binade k = k_lo + tid
+        uint64_t Wj = 0;
+        for (int b = W - 1; b >= j; --b) {
+            Wj = 2 * Wj + s_cnt[b];
+            if (Wj >= Tr::SAT) { Wj = Tr::SAT; break; }
+        }
+        const bool usable = Wj < Tr::SAT && j >= jmin;
+        const uint64_t half_up = usable ? Wj + s_cnt[j - 1] : Tr::SAT;
+        int64_t corr[2] = {0, 0};
+        if (usable && ties <= (unsigned)kMaxTies) {
+            // this binade's ties in element order (few): repeated minimum selection
+            uint32_t last = 0;
+            bool first_pick = true;
+            for (;;) {
+                uint32_t best = 0xffffffffu;
+                int bi = -1;
+                for (unsigned t = 0; t < ties; ++t) {
+                    const Tie c = s_ties[t];
+                    if (c.j == j && (first_pick || c.index > last) && c.index < best) {
+                        best = c.index;
+                        bi = (int)t;
+                    }
+                }
+                if (bi < 0) break;
+                last = best;
+                first_pick = false;
+                const Tie t = s_ties[bi];
+#pragma unroll
+                for (int p0 = 0; p0 < 2; ++p0) {
+                    // state parity in front of the tie: start + half-up prefix + corrections so far
+                    const int parity = (p0 + t.pi + (int)(corr[p0] & 1)) & 1;
+                    // round to even: up iff (state + floor(q/u)) is odd; half-up assumed up
+                    if (((parity + t.mpar) & 1) == 0) corr[p0] -= 1;
+                }
+            }
+        }
+        typename Tr::D *d = deltas + ((size_t)blockIdx.x * W + tid) * 2;
+        d[0] = usable ? sat_d<T>((uint64_t)((int64_t)half_up + corr[0])) : no_map<T>();
+        d[1] = usable ? sat_d<T>((uint64_t)((int64_t)half_up + corr[1])) : no_map<T>();
+    }
+}
+
+// Compose the maps of kBlockChunks consecutive chunks into one block map per binade.
+template <typename T>
+__global__ void __launch_bounds__(64) mse_block_kernel(const MseHead *heads, const typename MseTraits<T>::D *deltas,
+                                                       uint64_t chunks, MseHead *bheads,
+                                                       typename MseTraits<T>::D *bdeltas) {
+    using Tr = MseTraits<T>;
+    constexpr int W = Tr::W;
+    const uint64_t c0 = (uint64_t)blockIdx.x * kBlockChunks;
+    const uint64_t c1 = c0 + kBlockChunks < chunks ? c0 + kBlockChunks : chunks;
+    __shared__ int s_khi;
+    __shared__ int s_flags;
+    __shared__ unsigned s_fault;
+    if (threadIdx.x == 0) {
+        int khi = INT_MIN, flags = kHeadZero;
+        unsigned fault = 0xffffffffu;
+        for (uint64_t c = c0; c < c1; ++c) {
+            const MseHead h = heads[c];
+            if (h.flags & kHeadFault) {
+                flags |= kHeadFault;
+                fault = min(fault, (unsigned)((c - c0) * Tr::CHUNK + h.fault));
+            }
+            if (h.flags & kHeadExact) flags |= kHeadExact;
+            if (!(h.flags & kHeadZero)) {
+                flags &= ~kHeadZero;
+                khi = max(khi, h.k_lo + W - 1);
+            }
+        }
+        s_khi = khi;
+        s_flags = flags;
+        s_fault = fault;
+    }
+    __syncthreads();
+    const int flags = s_flags;
+    MseHead bh;
+    bh.pad = 0;
+    bh.flags = flags;
+    bh.fault = s_fault;
+    bh.k_lo = (flags & kHeadZero) ? 0 : max(s_khi - (W - 1), Tr::KMIN);
+    if (threadIdx.x == 0) bheads[blockIdx.x] = bh;
+    if ((flags & kHeadZero) || threadIdx.x >= W) return;
+    const int k = bh.k_lo + threadIdx.x;
+    uint64_t D[2] = {0, 0};
+    bool valid = !(flags & (kHeadExact | kHeadFault));
+    for (uint64_t c = c0; c < c1 && valid; ++c) {
+        const MseHead h = heads[c];
+        if (h.flags & kHeadZero) continue;
+        if (k > h.k_lo + W - 1) continue;  // every square of the chunk is below half an ulp
+        if (k < h.k_lo) { valid = false; break; }
+        const typename Tr::D *d = deltas + ((size_t)c * W + (k - h.k_lo)) * 2;
+        const typename Tr::D d0 = d[0], d1 = d[1];
+        if (d0 == no_map<T>() || d1 == no_map<T>()) { valid = false; break; }
+        const uint64_t n0 = D[0] + ((D[0] & 1) ? d1 : d0);
+        const uint64_t n1 = D[1] + (((1 + D[1]) & 1) ? d1 : d0);
+        D[0] = n0;
+        D[1] = n1;
+        if (D[0] >= (2ull << Tr::P) || D[1] >= (2ull << Tr::P)) valid = false;  // cannot fit a binade
+    }
+    typename Tr::D *out = bdeltas + ((size_t)blockIdx.x * W + threadIdx.x) * 2;
+    out[0] = valid ? sat_d<T>(D[0]) : no_map<T>();
+    out[1] = valid ? sat_d<T>(D[1]) : no_map<T>();
+}
+
+// Apply a map to s if the binade's window covers s and the result stays inside the binade.
+template <typename T>
+__device__ __forceinline__ bool apply_map(const MseHead &h, const typename MseTraits<T>::D *deltas, T &s) {
+    using Tr = MseTraits<T>;
+    constexpr int W = Tr::W;
+    if (h.flags & (kHeadExact | kHeadFault)) return false;
+    if (h.flags & kHeadZero) return true;
+    uint64_t x;
+    int k;
+    state_of<T>(s, x, k);
+    if (k > h.k_lo + W - 1) return true;  // identity: every square < half an ulp
+    if (k < h.k_lo) return false;
+    const typename Tr::D d = deltas[(size_t)(k - h.k_lo) * 2 + (x & 1)];
+    if (d == no_map<T>()) return false;
+    const uint64_t nx = x + d;
+    if (nx >= (2ull << Tr::P)) return false;  // would leave the binade (or overflow)
+    s = value_of<T>(nx, k);
+    return true;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) mse_walk_kernel(const T *prediction, const T *target, uint64_t n,
+                                                       const MseHead *heads, const typename MseTraits<T>::D *deltas,
+                                                       const MseHead *bheads, const typename MseTraits<T>::D *bdeltas,
+                                                       uint64_t chunks, uint64_t blocks, T denominator, int policy,
+                                                       T *out, unsigned long long *status) {
+    using Tr = MseTraits<T>;
+    using F = Fmt<T>;
+    constexpr int W = Tr::W;
+    constexpr int PER = Tr::CHUNK / 256;
+    __shared__ T sq[Tr::CHUNK];
+    __shared__ uint64_t s_walk;   // chunk to resolve element by element (or ~0)
+    __shared__ int s_done;        // 1: ordered end reached, 2: overflow recorded
+    __shared__ T s_sum;
+    __shared__ uint64_t s_x;
+    __shared__ int s_k;
+    __shared__ unsigned s_pos, s_stop;
+    __shared__ uint64_t s_warp_sum[8];
+    __shared__ uint64_t s_xstop;
+
+    // every Subtract/Multiply fault is already in the status word; the walk stops in front of
+    // the earliest one, so only earlier Adds can still report (their events are smaller)
+    const unsigned long long st0 = read_status(status);
+    const uint64_t stop = st0 == kStatusOk ? n : ((st0 >> 3) / 3 < n ? (st0 >> 3) / 3 : n);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+    if (tid == 0) {
+        s_sum = T(0);
+        s_done = 0;
+    }
+    __syncthreads();
+    uint64_t blk = 0, chunk = 0;
+    bool in_block = false;  // thread 0's cursor: descending into block `blk`
+    for (;;) {
+        if (tid == 0) {
+            s_walk = ~0ull;
+            T s = s_sum;
+            while (!s_done) {
+                if (!in_block) {
+                    if (blk >= blocks || blk * kBlockChunks * (uint64_t)Tr::CHUNK >= stop) { s_done = 1; break; }
+                    const uint64_t bend = (blk + 1) * kBlockChunks * (uint64_t)Tr::CHUNK;
+                    if (bend <= stop && apply_map<T>(bheads[blk], bdeltas + (size_t)blk * W * 2, s)) {
+                        ++blk;
+                        continue;
+                    }
+                    in_block = true;
+                    chunk = blk * kBlockChunks;
+                }
+                const uint64_t cend = blk * kBlockChunks + kBlockChunks < chunks ? blk * kBlockChunks + kBlockChunks
+                                                                                 : chunks;
+                if (chunk >= cend) {
+                    in_block = false;
+                    ++blk;
+                    continue;
+                }
+                if (chunk * Tr::CHUNK >= stop) { s_done = 1; break; }
+                if ((chunk + 1) * Tr::CHUNK <= stop && apply_map<T>(heads[chunk], deltas + (size_t)chunk * W * 2, s)) {
+                    ++chunk;
+                    continue;
+                }
+                s_walk = chunk;  // resolve this chunk element by element
+                ++chunk;
+                break;
+            }
+            s_sum = s;
+        }
+        __syncthreads();
+        const uint64_t walk = s_walk;
+        if (walk == ~0ull) break;
+        // recompute the chunk's squares (all fault-free in front of `stop`)
+        const uint64_t i0 = walk * Tr::CHUNK;
+        const unsigned len = (unsigned)((i0 + Tr::CHUNK < stop ? i0 + Tr::CHUNK : stop) - i0);
+        for (unsigned c = tid; c < len; c += 256) {
+            const T d = F::sub(prediction[i0 + c], target[i0 + c]);
+            sq[c] = F::mul(d, d);
+        }
+        if (tid == 0) s_pos = 0;
+        __syncthreads();
+        // Resolve [pos, len): apply every element in front of the first tie or binade crossing
+        // at once (prefix sums of half-up increments), then add that element exactly.
+        for (;;) {
+            const unsigned pos = s_pos;
+            if (pos >= len) break;
+            if (tid == 0) {
+                uint64_t x;
+                int k;
+                state_of<T>(s_sum, x, k);
+                s_x = x;
+                s_k = k;
+                s_stop = len;
+            }
+            __syncthreads();
+            const uint64_t x = s_x;
+            const int k = s_k;
+            const unsigned c0 = pos + (unsigned)tid * PER;
+            uint64_t inc[PER];
+            uint64_t local = 0;
+            unsigned first_tie = len;
+#pragma unroll
+            for (int e = 0; e < PER; ++e) {
+                const unsigned c = c0 + e;
+                bool tie = false;
+                inc[e] = c < len ? half_up_increment<T>(sq[c], k, tie) : 0;
+                if (tie && c < len && first_tie == len) first_tie = c;
+                local = min(local + inc[e], (uint64_t)Tr::SAT);
+            }
+            // exclusive prefix sum of thread totals (element order = thread order)
+            uint64_t incl = local;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint64_t v = __shfl_up_sync(0xffffffffu, (unsigned long long)incl, o);
+                if (lane >= o) incl = min(incl + v, (uint64_t)Tr::SAT);
+            }
+            if (lane == 31) s_warp_sum[warp] = incl;
+            __syncthreads();
+            // exclusive prefix from the previous lane (not incl - local: both may be saturated
+            // when this thread's own range holds the element that saturates)
+            uint64_t before = __shfl_up_sync(0xffffffffu, (unsigned long long)incl, 1);
+            if (lane == 0) before = 0;
+            for (int w = 0; w < warp; ++w) before = min(before + s_warp_sum[w], (uint64_t)Tr::SAT);
+            // first element whose half-up result may leave the binade, or the first tie
+            uint64_t run = x + before;
+            unsigned mine = first_tie;
+#pragma unroll
+            for (int e = 0; e < PER; ++e) {
+                const unsigned c = c0 + e;
+                if (c < len && c < mine && run + inc[e] >= (2ull << Tr::P)) mine = c;
+                run = min(run + inc[e], (uint64_t)Tr::SAT);
+            }
+            if (mine < len) atomicMin(&s_stop, mine);
+            __syncthreads();
+            const unsigned cut = s_stop;
+            // the owner of `cut` (or the last thread) publishes the state in front of it
+            if (cut >= c0 && cut < c0 + PER) {
+                uint64_t r = x + before;
+#pragma unroll
+                for (int e = 0; e < PER; ++e)
+                    if (c0 + e < cut) r += inc[e];
+                s_xstop = r;
+            } else if (cut == len && tid == 255) {
+                s_xstop = x + before + local;
+            }
+            __syncthreads();
+            if (tid == 0) {
+                T s = value_of<T>(s_xstop, k);
+                if (cut < len) {
+                    const T t = F::add(s, sq[cut]);
+                    if (nonfinite_bits<T>(F::bits(t))) {
+                        record_fault(status, (i0 + cut) * 3 + 2, kOverflow);
+                        s_done = 2;
+                        s_pos = len;
+                    } else {
+                        s = t;
+                        s_pos = cut + 1;
+                    }
+                } else {
+                    s_pos = len;
+                }
+                s_sum = s;
+            }
+            __syncthreads();
+        }
+        if (s_done == 2) return;
+    }
+    if (tid == 0) {
+        if (stop < n || fault_precedes(status, n * 3)) return;
+        T mean;
+        const unsigned kind = checked_div<T>(s_sum, denominator, policy, mean);
+        if (kind) {
+            record_fault(status, n * 3, kind);
             return;
         }
-        if (block_max[blk] < half_ulp<T>(s)) continue;  // every step rounds back to s
-        T t = s;
-#pragma unroll 8
-        for (uint64_t i = i0; i < i1; ++i) t = F::add(t, squares[i]);
-        if (nonfinite_bits<T>(F::bits(t))) {
-            for (uint64_t i = i0; i < i1; ++i) {
-                T u = F::add(s, squares[i]);
-                if (nonfinite_bits<T>(F::bits(u))) { record_fault(status, i * 3 + 2, kOverflow); return; }
-                s = u;
-            }
-        }
-        s = t;
+        out[0] = mean;
     }
-    if (fault_precedes(status, n * 3)) return;
-    T mean;
-    unsigned kind = checked_div<T>(s, denominator, policy, mean);
-    if (kind) { record_fault(status, n * 3, kind); return; }
-    out[0] = mean;
 }
 
 // binary32/binary64 encoding of an element count, nearest-even (constants/constants.rs:18-27)
@@ -141,28 +753,51 @@ template <typename T> T count_value(uint64_t n) {
     return v;
 }
 
+template <typename T> struct MseLayout {
+    uint64_t chunks, blocks;
+    size_t heads_off, deltas_off, bheads_off, bdeltas_off, bytes;
+    explicit MseLayout(uint64_t n) {
+        using Tr = MseTraits<T>;
+        auto up = [](size_t v) { return (v + 255) / 256 * 256; };
+        const size_t dsz = Tr::W * 2 * sizeof(typename Tr::D);
+        chunks = (n + Tr::CHUNK - 1) / Tr::CHUNK;
+        blocks = (chunks + kBlockChunks - 1) / kBlockChunks;
+        heads_off = 0;
+        deltas_off = up(chunks * sizeof(MseHead));
+        bheads_off = deltas_off + up(chunks * dsz);
+        bdeltas_off = bheads_off + up(blocks * sizeof(MseHead));
+        bytes = bdeltas_off + up(blocks * dsz);
+    }
+};
+
 template <typename T>
 int run_mse(int policy, const T *p, const T *t, T *out, uint64_t n, void *workspace, size_t workspace_bytes,
             unsigned long long *status, cudaStream_t stream) {
-    const uint64_t blocks = (n + kMseBlock - 1) / kMseBlock;
-    size_t need = pcu_b200_strict_mse_workspace_size(sizeof(T) == 4 ? PCU_B200_F32 : PCU_B200_F64, n);
-    if (!workspace || workspace_bytes < need) return PCU_B200_ERROR_WORKSPACE;
-    T *squares = reinterpret_cast<T *>(workspace);
-    T *block_max = reinterpret_cast<T *>(reinterpret_cast<char *>(workspace) + ((n * sizeof(T) + 255) / 256) * 256);
-    uint64_t grid = blocks < (uint64_t)pcu_host::sm_count() * 8 ? blocks : (uint64_t)pcu_host::sm_count() * 8;
-    mse_squares_kernel<T><<<(unsigned)grid, 256, 0, stream>>>(p, t, n, squares, block_max, policy, status);
+    using D = typename MseTraits<T>::D;
+    MseLayout<T> lay(n);
+    if (!workspace || workspace_bytes < lay.bytes) return PCU_B200_ERROR_WORKSPACE;
+    if (lay.chunks > 0x7fffffffull) return PCU_B200_ERROR_SIZE_OVERFLOW;
+    char *ws = reinterpret_cast<char *>(workspace);
+    auto *heads = reinterpret_cast<MseHead *>(ws + lay.heads_off);
+    auto *deltas = reinterpret_cast<D *>(ws + lay.deltas_off);
+    auto *bheads = reinterpret_cast<MseHead *>(ws + lay.bheads_off);
+    auto *bdeltas = reinterpret_cast<D *>(ws + lay.bdeltas_off);
+    mse_chunk_kernel<T><<<(unsigned)lay.chunks, 256, 0, stream>>>(p, t, n, policy, heads, deltas, status);
     int rc = pcu_host::launch_status();
     if (rc) return rc;
-    mse_sum_kernel<T><<<1, 32, 0, stream>>>(squares, block_max, n, count_value<T>(n), policy, out, status);
+    mse_block_kernel<T><<<(unsigned)lay.blocks, 64, 0, stream>>>(heads, deltas, lay.chunks, bheads, bdeltas);
+    rc = pcu_host::launch_status();
+    if (rc) return rc;
+    mse_walk_kernel<T><<<1, 256, 0, stream>>>(p, t, n, heads, deltas, bheads, bdeltas, lay.chunks, lay.blocks,
+                                              count_value<T>(n), policy, out, status);
     return pcu_host::launch_status();
 }
 
 }  // namespace pcu
 
 extern "C" size_t pcu_b200_strict_mse_workspace_size(int dtype, uint64_t count) {
-    const size_t elem = dtype == PCU_B200_F64 ? 8 : 4;
-    const uint64_t blocks = (count + pcu::kMseBlock - 1) / pcu::kMseBlock;
-    return ((count * elem + 255) / 256) * 256 + ((blocks * elem + 255) / 256) * 256;
+    if (dtype == PCU_B200_F64) return pcu::MseLayout<double>(count).bytes;
+    return pcu::MseLayout<float>(count).bytes;
 }
 
 extern "C" int pcu_b200_strict_mse(int dtype, int policy, const void *prediction, const void *target, void *out,

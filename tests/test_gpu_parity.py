@@ -326,6 +326,59 @@ def test_mse_random(provider, width, policy):
                 assert bits(to_host(out).reshape(1))[0] == bits(o_o)[0]
 
 
+def _mse_case(provider, p, t, policy=0):
+    s_o, o_o = oracle.mse(p, t, policy)
+    status = provider.new_status()
+    out = provider.strict_mse(to_device(p), to_device(t), policy, status=status)
+    _sync()
+    word = status_word(status)
+    assert word == s_o, (p.size, oracle.decode(word), oracle.decode(s_o))
+    if s_o == oracle.STATUS_OK:
+        assert bits(to_host(out).reshape(1))[0] == bits(o_o)[0], (p.size, to_host(out), o_o)
+
+
+@pytest.mark.parametrize("width", [32, 64])
+def test_mse_tie_heavy_and_wide_range(provider, width):
+    """Squares with few significant bits make round-to-even ties at many binades of the running
+    sum; powers of two spread the squares over many exponents; partial chunks at the end."""
+    rng = np.random.default_rng(900 + width)
+    ft = FT[width]
+    for n in (5000, 8192 * 3 + 17, 1 << 19, (1 << 21) + 333):
+        # small integers scaled by a power of two: d^2 has at most ~12 significant bits
+        p = (rng.integers(-64, 64, size=n) * 2.0 ** -3).astype(ft)
+        t = (rng.integers(-64, 64, size=n) * 2.0 ** -3).astype(ft)
+        _mse_case(provider, p, t)
+        # powers of two over a wide exponent range: every square is a tie somewhere
+        e = rng.integers(-30, 30, size=n)
+        p2 = (2.0 ** e * rng.choice([-1.0, 1.0], size=n)).astype(ft)
+        _mse_case(provider, p2, np.zeros(n, ft), policy=2)
+        # mostly tiny with rare large values (sum dominated by a few elements)
+        p3 = dyadic_uniform(rng, n, width) * ft(2.0 ** -12)
+        p3[rng.integers(0, n, size=5)] = ft(1000.0)
+        _mse_case(provider, p3, np.zeros(n, ft), policy=2)
+    # exactly representable halves: q = 0.25 everywhere -> ties whenever the sum's ulp is 0.5
+    n = 1 << 20
+    _mse_case(provider, np.full(n, ft(0.5)), np.zeros(n, ft))
+    _mse_case(provider, np.full(n, ft(1.5)), np.zeros(n, ft))
+
+
+@pytest.mark.parametrize("width", [32, 64])
+def test_mse_late_faults(provider, width):
+    rng = np.random.default_rng(950 + width)
+    ft = FT[width]
+    n = (1 << 20) + 11
+    p = dyadic_uniform(rng, n, width)
+    t = dyadic_uniform(rng, n, width)
+    big = np.sqrt(np.finfo(ft).max / 4).astype(ft)
+    for where in (0, 8191, 8192, 700001, n - 1):
+        q = p.copy()
+        q[where] = np.nan
+        _mse_case(provider, q, t)
+        q = p.copy()
+        q[where:where + 8] = big  # the running sum overflows a few elements after `where`
+        _mse_case(provider, q, t)
+
+
 def test_mse_overflow_and_tiny_mean(provider):
     import torch
 
