@@ -549,6 +549,48 @@ __device__ __forceinline__ bool apply_map(const MseHead &h, const typename MseTr
     return true;
 }
 
+// Summaries the walker stages in shared memory: one head and W increment pairs per map.
+template <typename T> struct WalkSmem {
+    using Tr = MseTraits<T>;
+    using D = typename Tr::D;
+    static constexpr int BATCH = 32;  // block maps staged per batch
+    static constexpr size_t MAP_BYTES = sizeof(MseHead) + (size_t)Tr::W * 2 * sizeof(D);
+    static constexpr size_t SQ_OFF = 0;
+    static constexpr size_t BLOCKS_OFF = SQ_OFF + (size_t)Tr::CHUNK * sizeof(T);
+    static constexpr size_t CHUNKS_OFF = BLOCKS_OFF + BATCH * MAP_BYTES;
+    static constexpr size_t BYTES = CHUNKS_OFF + (size_t)kBlockChunks * MAP_BYTES;
+};
+
+// Copy `count` maps (heads and increment rows) starting at `first` into shared memory.
+template <typename T>
+__device__ __forceinline__ void stage_maps(const MseHead *heads, const typename MseTraits<T>::D *deltas,
+                                           uint64_t first, unsigned count, unsigned char *dst) {
+    using Tr = MseTraits<T>;
+    using D = typename Tr::D;
+    auto *h = reinterpret_cast<MseHead *>(dst);
+    auto *d = reinterpret_cast<D *>(dst + count * sizeof(MseHead));  // rows follow the heads
+    for (unsigned i = threadIdx.x; i < count; i += blockDim.x) h[i] = heads[first + i];
+    // at most kBlockChunks rows: a fixed, unrolled trip count keeps every load in flight at once
+    const unsigned words = count * Tr::W * 2;
+    constexpr unsigned kMaxWords = (unsigned)kBlockChunks * Tr::W * 2;
+#pragma unroll
+    for (unsigned r = 0; r < (kMaxWords + 255) / 256; ++r) {
+        const unsigned i = threadIdx.x + r * 256;
+        if (i < words) d[i] = deltas[first * Tr::W * 2 + i];
+    }
+}
+
+template <typename T>
+__device__ __forceinline__ bool apply_staged(const unsigned char *base, unsigned count, unsigned i, T &s) {
+    using Tr = MseTraits<T>;
+    using D = typename Tr::D;
+    const auto *h = reinterpret_cast<const MseHead *>(base);
+    const auto *d = reinterpret_cast<const D *>(base + count * sizeof(MseHead));
+    return apply_map<T>(h[i], d + (size_t)i * Tr::W * 2, s);
+}
+
+enum : int { kReqDone = 0, kReqBlocks = 1, kReqChunks = 2, kReqResolve = 3 };
+
 template <typename T>
 __global__ void __launch_bounds__(256) mse_walk_kernel(const T *prediction, const T *target, uint64_t n,
                                                        const MseHead *heads, const typename MseTraits<T>::D *deltas,
@@ -557,11 +599,17 @@ __global__ void __launch_bounds__(256) mse_walk_kernel(const T *prediction, cons
                                                        T *out, unsigned long long *status) {
     using Tr = MseTraits<T>;
     using F = Fmt<T>;
-    constexpr int W = Tr::W;
+    using SM = WalkSmem<T>;
     constexpr int PER = Tr::CHUNK / 256;
-    __shared__ T sq[Tr::CHUNK];
-    __shared__ uint64_t s_walk;   // chunk to resolve element by element (or ~0)
-    __shared__ int s_done;        // 1: ordered end reached, 2: overflow recorded
+    constexpr uint64_t BLOCK_ELEMS = (uint64_t)kBlockChunks * Tr::CHUNK;
+    extern __shared__ __align__(16) unsigned char walk_smem[];
+    T *sq = reinterpret_cast<T *>(walk_smem + SM::SQ_OFF);
+    unsigned char *staged_blocks = walk_smem + SM::BLOCKS_OFF;
+    unsigned char *staged_chunks = walk_smem + SM::CHUNKS_OFF;
+    __shared__ int s_req;
+    __shared__ uint64_t s_arg;
+    __shared__ unsigned s_arg_count;
+    __shared__ int s_done;  // 2: overflow recorded
     __shared__ T s_sum;
     __shared__ uint64_t s_x;
     __shared__ int s_k;
@@ -580,55 +628,91 @@ __global__ void __launch_bounds__(256) mse_walk_kernel(const T *prediction, cons
         s_done = 0;
     }
     __syncthreads();
-    uint64_t blk = 0, chunk = 0;
-    bool in_block = false;  // thread 0's cursor: descending into block `blk`
+    // thread 0's cursor
+    uint64_t blk = 0, chunk = 0, batch0 = 0;
+    unsigned batch_count = 0;
+    bool in_block = false, chunks_staged = false;
     for (;;) {
         if (tid == 0) {
-            s_walk = ~0ull;
             T s = s_sum;
-            while (!s_done) {
+            int req = kReqDone;
+            for (;;) {
                 if (!in_block) {
-                    if (blk >= blocks || blk * kBlockChunks * (uint64_t)Tr::CHUNK >= stop) { s_done = 1; break; }
-                    const uint64_t bend = (blk + 1) * kBlockChunks * (uint64_t)Tr::CHUNK;
-                    if (bend <= stop && apply_map<T>(bheads[blk], bdeltas + (size_t)blk * W * 2, s)) {
+                    if (blk >= blocks || blk * BLOCK_ELEMS >= stop) break;  // done
+                    if (blk >= batch0 + batch_count) {  // stage the next batch of block maps
+                        batch0 = blk;
+                        batch_count = (unsigned)min((uint64_t)SM::BATCH, blocks - blk);
+                        req = kReqBlocks;
+                        s_arg = batch0;
+                        s_arg_count = batch_count;
+                        break;
+                    }
+                    if ((blk + 1) * BLOCK_ELEMS <= stop &&
+                        apply_staged<T>(staged_blocks, batch_count, (unsigned)(blk - batch0), s)) {
                         ++blk;
                         continue;
                     }
                     in_block = true;
+                    chunks_staged = false;
                     chunk = blk * kBlockChunks;
                 }
-                const uint64_t cend = blk * kBlockChunks + kBlockChunks < chunks ? blk * kBlockChunks + kBlockChunks
-                                                                                 : chunks;
+                const uint64_t cfirst = blk * kBlockChunks;
+                const uint64_t cend = cfirst + kBlockChunks < chunks ? cfirst + kBlockChunks : chunks;
+                if (!chunks_staged) {
+                    chunks_staged = true;
+                    req = kReqChunks;
+                    s_arg = cfirst;
+                    s_arg_count = (unsigned)(cend - cfirst);
+                    break;
+                }
                 if (chunk >= cend) {
                     in_block = false;
                     ++blk;
                     continue;
                 }
-                if (chunk * Tr::CHUNK >= stop) { s_done = 1; break; }
-                if ((chunk + 1) * Tr::CHUNK <= stop && apply_map<T>(heads[chunk], deltas + (size_t)chunk * W * 2, s)) {
+                if (chunk * Tr::CHUNK >= stop) break;  // done
+                if ((chunk + 1) * Tr::CHUNK <= stop &&
+                    apply_staged<T>(staged_chunks, (unsigned)(cend - cfirst), (unsigned)(chunk - cfirst), s)) {
                     ++chunk;
                     continue;
                 }
-                s_walk = chunk;  // resolve this chunk element by element
+                req = kReqResolve;  // resolve this chunk element by element
+                s_arg = chunk;
                 ++chunk;
                 break;
             }
             s_sum = s;
+            s_req = req;
         }
         __syncthreads();
-        const uint64_t walk = s_walk;
-        if (walk == ~0ull) break;
-        // recompute the chunk's squares (all fault-free in front of `stop`)
-        const uint64_t i0 = walk * Tr::CHUNK;
+        const int req = s_req;
+        if (req == kReqDone) break;
+        if (req == kReqBlocks) {
+            stage_maps<T>(bheads, bdeltas, s_arg, s_arg_count, staged_blocks);
+            __syncthreads();
+            continue;
+        }
+        if (req == kReqChunks) {
+            stage_maps<T>(heads, deltas, s_arg, s_arg_count, staged_chunks);
+            __syncthreads();
+            continue;
+        }
+        // ---- resolve one chunk: recompute its squares (all fault-free in front of `stop`)
+        const uint64_t i0 = s_arg * Tr::CHUNK;
         const unsigned len = (unsigned)((i0 + Tr::CHUNK < stop ? i0 + Tr::CHUNK : stop) - i0);
-        for (unsigned c = tid; c < len; c += 256) {
-            const T d = F::sub(prediction[i0 + c], target[i0 + c]);
-            sq[c] = F::mul(d, d);
+        // fixed trip count, unrolled: all of a thread's loads are in flight together
+#pragma unroll
+        for (int e = 0; e < PER; ++e) {
+            const unsigned c = (unsigned)tid + (unsigned)e * 256;
+            if (c < len) {
+                const T d = F::sub(prediction[i0 + c], target[i0 + c]);
+                sq[c] = F::mul(d, d);
+            }
         }
         if (tid == 0) s_pos = 0;
         __syncthreads();
-        // Resolve [pos, len): apply every element in front of the first tie or binade crossing
-        // at once (prefix sums of half-up increments), then add that element exactly.
+        // Apply every element in front of the first tie or binade crossing at once (prefix sums of
+        // half-up increments), then add that element exactly; repeat.
         for (;;) {
             const unsigned pos = s_pos;
             if (pos >= len) break;
@@ -651,7 +735,7 @@ __global__ void __launch_bounds__(256) mse_walk_kernel(const T *prediction, cons
             for (int e = 0; e < PER; ++e) {
                 const unsigned c = c0 + e;
                 bool tie = false;
-                inc[e] = c < len ? half_up_increment<T>(sq[c], k, tie) : 0;
+                inc[e] = c < len ? half_up_increment<T>(sq[c < len ? c : 0], k, tie) : 0;
                 if (tie && c < len && first_tie == len) first_tie = c;
                 local = min(local + inc[e], (uint64_t)Tr::SAT);
             }
@@ -788,8 +872,18 @@ int run_mse(int policy, const T *p, const T *t, T *out, uint64_t n, void *worksp
     mse_block_kernel<T><<<(unsigned)lay.blocks, 64, 0, stream>>>(heads, deltas, lay.chunks, bheads, bdeltas);
     rc = pcu_host::launch_status();
     if (rc) return rc;
-    mse_walk_kernel<T><<<1, 256, 0, stream>>>(p, t, n, heads, deltas, bheads, bdeltas, lay.chunks, lay.blocks,
-                                              count_value<T>(n), policy, out, status);
+    static bool configured[64] = {false};
+    int device = 0;
+    cudaGetDevice(&device);
+    if (device >= 0 && device < 64 && !configured[device]) {
+        cudaError_t e = cudaFuncSetAttribute(mse_walk_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)WalkSmem<T>::BYTES);
+        if (e != cudaSuccess) return pcu_host::set_cuda_error(e);
+        configured[device] = true;
+    }
+    mse_walk_kernel<T><<<1, 256, WalkSmem<T>::BYTES, stream>>>(p, t, n, heads, deltas, bheads, bdeltas, lay.chunks,
+                                                               lay.blocks,
+                                                               count_value<T>(n), policy, out, status);
     return pcu_host::launch_status();
 }
 
