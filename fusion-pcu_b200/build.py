@@ -15,7 +15,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(ROOT, "_build", "provider")
 LIBRARY = os.path.join(HERE, "libpcu_b200.so")
-SOURCES = ["abi.cu", "streaming.cu", "strict_matmul.cu", "strict_mse.cu"]
+SOURCES = ["abi.cu", "streaming.cu", "strict_matmul.cu", "strict_mse.cu", "tensor_graph.cu"]
 HEADERS = ["checked_law.cuh", "common.cuh"]
 
 NVCC = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
@@ -34,7 +34,8 @@ def _stale(target, deps):
 
 def _compile(src, verbose):
     obj = os.path.join(BUILD, src.replace(".cu", ".o"))
-    deps = [os.path.join(CSRC, src), os.path.join(ROOT, "include", "pcu_b200.h"), __file__] + \
+    deps = [os.path.join(CSRC, src), os.path.join(ROOT, "include", "pcu_b200.h"),
+            os.path.join(ROOT, "include", "pcu_b200_graph.h"), __file__] + \
         [os.path.join(CSRC, h) for h in HEADERS]
     if not _stale(obj, deps):
         return obj, ""

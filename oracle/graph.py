@@ -95,7 +95,17 @@ class Graph:
 
     # ---------------------------------------------------------------- reverse mode
     def gradient(self, loss, target, name=None):
-        """Graph::backward_mse_for_targets(loss, [target]) for one target."""
+        """Graph::backward_mse_for(loss, target) (gradients.rs:279-287)."""
+        result = self.gradients(loss, [target])[0]
+        if name is not None:
+            # give the final gradient value the requested name as an alias
+            self.index[name] = self.index[result]
+        return result
+
+    def gradients(self, loss, targets):
+        """Graph::backward_mse_for_targets(loss, targets): one shared reverse sweep (gradients.rs:289-303)."""
+        if not targets:
+            raise ValueError("EmptyOutputs")
         root = self.nodes[self.index[loss]]
         if root.op != "mse":
             raise ValueError("GradientRootNotMse")
@@ -114,15 +124,16 @@ class Graph:
             if node.op in ("div", "relu_backward"):
                 raise ValueError("UnsupportedGradient")
             pending.extend(self.index[a] for a in node.args)
-        t_i = self.index[target]
-        if not visited[t_i]:
-            raise ValueError("UnsupportedGradient")
         needed = [False] * n_orig
-        needed[t_i] = True
+        for target in targets:
+            t_i = self.index[target]
+            if not visited[t_i]:
+                raise ValueError("UnsupportedGradient")
+            needed[t_i] = True
         for i in range(loss_i + 1):
             needed[i] = needed[i] or any(needed[self.index[a]] for a in self.nodes[i].args)
         grads = [None] * n_orig
-        if target == loss:
+        if any(self.index[t] == loss_i for t in targets):
             grads[loss_i] = self.uniform((), self._one())
         else:
             self._mse_grad(grads, root.args[0], root.args[1], needed)
@@ -132,13 +143,10 @@ class Graph:
                 continue
             node = self.nodes[i]
             self._node_grad(grads, node, g, needed)
-        result = grads[t_i]
-        if result is None:
+        results = [grads[self.index[t]] for t in targets]
+        if any(r is None for r in results):
             raise ValueError("UnsupportedGradient")
-        if name is not None:
-            # give the final gradient value the requested name as an alias
-            self.index[name] = self.index[result]
-        return result
+        return results
 
     def _one(self):
         return 0x3F800000 if self.width == 32 else 0x3FF0000000000000
@@ -222,7 +230,10 @@ class Graph:
             if ig is not None:
                 self._accumulate(grads, upd, ig)
         elif op == "mse":
-            raise ValueError("UnsupportedGradient (nested MSE)")
+            # only the root reaches here (nested MSE is rejected up front): an explicit
+            # d loss / d loss seeds the root with Uniform(1), then the MSE rule runs
+            # (gradients.rs:123-125, 384-397)
+            self._mse_grad(grads, args[0], args[1], needed)
         else:
             raise ValueError(f"UnsupportedGradient ({op})")
 
@@ -246,12 +257,15 @@ class Graph:
                 close(i)
         return [i for i, s in enumerate(selected) if s]
 
-    def evaluate(self, inputs, outputs, policy=0):
-        """Returns ({output: array}, None) or (None, fault dict) for the first faulting node."""
+    def evaluate(self, inputs, outputs, policy=0, fast=False):
+        """Returns ({output: array}, None) or (None, fault dict) for the first faulting node.
+
+        fast=True evaluates MatMul nodes with the multi-threaded hardware-IEEE checker
+        (exact soft-float fallback), which the oracle tests hold to the scalar law."""
         values = {}
         for i in self.plan(outputs):
             node = self.nodes[i]
-            status, value, fault = self._run(node, values, inputs, policy)
+            status, value, fault = self._run(node, values, inputs, policy, fast)
             if status != STATUS_OK:
                 return None, fault
             values[node.name] = value
@@ -261,7 +275,7 @@ class Graph:
         bits = np.array([node.value], dtype=np.uint32 if self.width == 32 else np.uint64)
         return np.broadcast_to(bits.view(self.dtype), node.shape if node.shape else (1,)).copy()
 
-    def _run(self, node, values, inputs, policy):
+    def _run(self, node, values, inputs, policy, fast=False):
         op = node.op
         if op == "input":
             return STATUS_OK, np.ascontiguousarray(inputs[node.name], dtype=self.dtype).reshape(node.shape), None
@@ -278,7 +292,7 @@ class Graph:
             status, out = relu_backward(args[0].ravel(), args[1].ravel(), policy)
             out = out.reshape(node.shape)
         elif op == "matmul":
-            status, out = matmul(args[0], args[1], node.tl, node.tr, policy)
+            status, out = matmul(args[0], args[1], node.tl, node.tr, policy, fast=fast)
         elif op == "mse":
             status, out = mse(args[0].ravel(), args[1].ravel(), policy)
             out = out.reshape(())
