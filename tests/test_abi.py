@@ -70,4 +70,9 @@ def test_workspace_sizes(provider, rows, inner, columns):
     lib = provider.library()
     need = lib.pcu_b200_strict_matmul_workspace_size(rows, inner, columns)
     assert need >= 4 * (rows + columns) and need % 256 == 0
-    assert lib.pcu_b200_strict_mse_workspace_size(0, 1 << 28) >= 4 << 28
+    # strict MSE keeps one ordered-sum map per chunk (F32: 8192 elements -> a 16-byte head and
+    # 2 x 27 u32 deltas; F64: 4096 elements -> a head and 2 x 56 u64 deltas), plus one per block
+    for dtype, chunk, per_chunk in ((0, 8192, 16 + 2 * 27 * 4), (1, 4096, 16 + 2 * 56 * 8)):
+        got = lib.pcu_b200_strict_mse_workspace_size(dtype, 1 << 28)
+        assert got >= ((1 << 28) // chunk) * per_chunk and got % 256 == 0
+        assert got < ((1 << 28) // chunk) * per_chunk * 1.1
