@@ -18,7 +18,7 @@ import numpy as np
 __all__ = [
     "ProviderUnavailable", "TensorError", "ArithmeticFault", "CompoundArithmeticFault", "ProviderFailure",
     "library", "POLICY", "OPS", "STATUS_OK", "new_status", "decode_status", "strict_matmul", "strict_sgd",
-    "strict_mse", "checked_binary", "checked_relu", "checked_relu_backward", "matmul_fault", "sgd_fault",
+    "strict_mse", "mse_workspace", "strict_mse_segment_prepare", "strict_mse_segment_walk", "checked_binary", "checked_relu", "checked_relu_backward", "matmul_fault", "sgd_fault",
     "mse_fault", "element_fault",
 ]
 
@@ -91,6 +91,8 @@ def _declare(L):
     L.pcu_b200_strict_mse_workspace_size.argtypes = [i32, u64]
     L.pcu_b200_strict_mse_workspace_size.restype = sz
     L.pcu_b200_strict_mse.argtypes = [i32, i32, vp, vp, vp, u64, vp, sz, vp, vp]
+    L.pcu_b200_strict_mse_segment_prepare.argtypes = [i32, i32, vp, vp, u64, u64, vp, sz, vp, vp]
+    L.pcu_b200_strict_mse_segment_walk.argtypes = [i32, i32, vp, vp, u64, u64, u64, vp, vp, vp, vp, sz, vp, vp]
     L.pcu_b200_checked_binary.argtypes = [i32, i32, i32, vp, vp, vp, u64, i32, i32, vp, vp]
     L.pcu_b200_checked_relu.argtypes = [i32, i32, vp, vp, u64, vp, vp]
     L.pcu_b200_checked_relu_backward.argtypes = [i32, i32, vp, vp, vp, u64, vp, vp]
@@ -250,6 +252,37 @@ def strict_mse(prediction, target, policy=0, out=None, status=None, workspace=No
         workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=prediction.device)
     _check(L.pcu_b200_strict_mse(_dtype_code(prediction), policy, _ptr(prediction), _ptr(target), _ptr(out), n,
                                  _ptr(workspace), workspace.numel(), _ptr(status), _stream(stream)))
+    return out
+
+
+def mse_workspace(prediction):
+    """A device workspace sized for strict_mse / the segment calls over `prediction`."""
+    torch = _torch()
+    need = library().pcu_b200_strict_mse_workspace_size(_dtype_code(prediction), prediction.numel())
+    return torch.empty(max(need, 1), dtype=torch.uint8, device=prediction.device)
+
+
+def strict_mse_segment_prepare(prediction, target, first_index, policy=0, status=None, workspace=None, stream=None):
+    """Bandwidth-bound phase of one segment [first_index, first_index + n) of a split strict MSE."""
+    assert prediction.is_contiguous() and target.is_contiguous() and prediction.numel() == target.numel()
+    if status is None:
+        status = new_status(device=prediction.device)
+    if workspace is None:
+        workspace = mse_workspace(prediction)
+    _check(library().pcu_b200_strict_mse_segment_prepare(
+        _dtype_code(prediction), policy, _ptr(prediction), _ptr(target), prediction.numel(), first_index,
+        _ptr(workspace), workspace.numel(), _ptr(status), _stream(stream)))
+    return status, workspace
+
+
+def strict_mse_segment_walk(prediction, target, first_index, total_count, carry, workspace, status, policy=0,
+                            out=None, stream=None):
+    """Ordered walk of one segment: `carry` (a device scalar) holds the running sum entering the
+    segment and receives the sum after it; for the last segment `out` receives the checked mean."""
+    _check(library().pcu_b200_strict_mse_segment_walk(
+        _dtype_code(prediction), policy, _ptr(prediction), _ptr(target), prediction.numel(), first_index,
+        total_count, _ptr(carry), _ptr(carry), _ptr(out), _ptr(workspace), workspace.numel(), _ptr(status),
+        _stream(stream)))
     return out
 
 

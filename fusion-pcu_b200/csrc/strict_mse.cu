@@ -213,7 +213,7 @@ __device__ __noinline__ bool checked_square(T p, T t, uint64_t i, int policy, un
 
 template <typename T>
 __global__ void __launch_bounds__(256) mse_chunk_kernel(const T *prediction, const T *target, uint64_t n,
-                                                        int policy, MseHead *heads,
+                                                        uint64_t base, int policy, MseHead *heads,
                                                         typename MseTraits<T>::D *deltas,
                                                         unsigned long long *status) {
     using Tr = MseTraits<T>;
@@ -288,7 +288,7 @@ __global__ void __launch_bounds__(256) mse_chunk_kernel(const T *prediction, con
                 const int c = CM::index(warp, r, lane, e);
                 const uint64_t i = chunk0 + c;
                 T q = T(0);
-                if (!stopped && i < n && !checked_square<T>(prediction[i], target[i], i, policy, status, q)) {
+                if (!stopped && i < n && !checked_square<T>(prediction[i], target[i], base + i, policy, status, q)) {
                     atomicMin(&s_fault, (unsigned)c);
                     stopped = true;
                 }
@@ -595,7 +595,8 @@ template <typename T>
 __global__ void __launch_bounds__(256) mse_walk_kernel(const T *prediction, const T *target, uint64_t n,
                                                        const MseHead *heads, const typename MseTraits<T>::D *deltas,
                                                        const MseHead *bheads, const typename MseTraits<T>::D *bdeltas,
-                                                       uint64_t chunks, uint64_t blocks, T denominator, int policy,
+                                                       uint64_t chunks, uint64_t blocks, uint64_t base, uint64_t total,
+                                                       T denominator, int policy, const T *carry_in, T *carry_out,
                                                        T *out, unsigned long long *status) {
     using Tr = MseTraits<T>;
     using F = Fmt<T>;
@@ -618,13 +619,18 @@ __global__ void __launch_bounds__(256) mse_walk_kernel(const T *prediction, cons
     __shared__ uint64_t s_xstop;
 
     // every Subtract/Multiply fault is already in the status word; the walk stops in front of
-    // the earliest one, so only earlier Adds can still report (their events are smaller)
+    // the earliest one, so only earlier Adds can still report (their events are smaller).  The
+    // segment holds global elements [base, base + n); a fault in front of it stops it at once.
     const unsigned long long st0 = read_status(status);
-    const uint64_t stop = st0 == kStatusOk ? n : ((st0 >> 3) / 3 < n ? (st0 >> 3) / 3 : n);
+    uint64_t stop = n;
+    if (st0 != kStatusOk) {
+        const uint64_t first = (st0 >> 3) / 3;
+        stop = first < base ? 0 : (first - base < n ? first - base : n);
+    }
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
     if (tid == 0) {
-        s_sum = T(0);
+        s_sum = carry_in ? *carry_in : T(0);
         s_done = 0;
     }
     __syncthreads();
@@ -781,7 +787,7 @@ __global__ void __launch_bounds__(256) mse_walk_kernel(const T *prediction, cons
                 if (cut < len) {
                     const T t = F::add(s, sq[cut]);
                     if (nonfinite_bits<T>(F::bits(t))) {
-                        record_fault(status, (i0 + cut) * 3 + 2, kOverflow);
+                        record_fault(status, (base + i0 + cut) * 3 + 2, kOverflow);
                         s_done = 2;
                         s_pos = len;
                     } else {
@@ -795,14 +801,15 @@ __global__ void __launch_bounds__(256) mse_walk_kernel(const T *prediction, cons
             }
             __syncthreads();
         }
-        if (s_done == 2) return;
+        if (s_done == 2) break;
     }
     if (tid == 0) {
-        if (stop < n || fault_precedes(status, n * 3)) return;
+        if (carry_out) *carry_out = s_sum;  // the running sum handed to the next segment
+        if (!out || s_done == 2 || stop < n || fault_precedes(status, total * 3)) return;
         T mean;
         const unsigned kind = checked_div<T>(s_sum, denominator, policy, mean);
         if (kind) {
-            record_fault(status, n * 3, kind);
+            record_fault(status, total * 3, kind);
             return;
         }
         out[0] = mean;
@@ -854,24 +861,41 @@ template <typename T> struct MseLayout {
     }
 };
 
+// Phases 1 and 2 of a segment (global elements [base, base + n)): chunk maps and block maps.
 template <typename T>
-int run_mse(int policy, const T *p, const T *t, T *out, uint64_t n, void *workspace, size_t workspace_bytes,
-            unsigned long long *status, cudaStream_t stream) {
+int prepare_mse(int policy, const T *p, const T *t, uint64_t n, uint64_t base, void *workspace, size_t workspace_bytes,
+                unsigned long long *status, cudaStream_t stream) {
     using D = typename MseTraits<T>::D;
     MseLayout<T> lay(n);
     if (!workspace || workspace_bytes < lay.bytes) return PCU_B200_ERROR_WORKSPACE;
     if (lay.chunks > 0x7fffffffull) return PCU_B200_ERROR_SIZE_OVERFLOW;
+    if (!n) return PCU_B200_OK;
     char *ws = reinterpret_cast<char *>(workspace);
     auto *heads = reinterpret_cast<MseHead *>(ws + lay.heads_off);
     auto *deltas = reinterpret_cast<D *>(ws + lay.deltas_off);
     auto *bheads = reinterpret_cast<MseHead *>(ws + lay.bheads_off);
     auto *bdeltas = reinterpret_cast<D *>(ws + lay.bdeltas_off);
-    mse_chunk_kernel<T><<<(unsigned)lay.chunks, 256, 0, stream>>>(p, t, n, policy, heads, deltas, status);
+    mse_chunk_kernel<T><<<(unsigned)lay.chunks, 256, 0, stream>>>(p, t, n, base, policy, heads, deltas, status);
     int rc = pcu_host::launch_status();
     if (rc) return rc;
     mse_block_kernel<T><<<(unsigned)lay.blocks, 64, 0, stream>>>(heads, deltas, lay.chunks, bheads, bdeltas);
-    rc = pcu_host::launch_status();
-    if (rc) return rc;
+    return pcu_host::launch_status();
+}
+
+// Phase 3 of a segment: the ordered walk from *carry_in (+0 if null); the running sum goes to
+// *carry_out (if not null) and, when out is not null, the checked mean over `total` elements.
+template <typename T>
+int walk_mse(int policy, const T *p, const T *t, uint64_t n, uint64_t base, uint64_t total, const T *carry_in,
+             T *carry_out, T *out, void *workspace, size_t workspace_bytes, unsigned long long *status,
+             cudaStream_t stream) {
+    using D = typename MseTraits<T>::D;
+    MseLayout<T> lay(n);
+    if (n && (!workspace || workspace_bytes < lay.bytes)) return PCU_B200_ERROR_WORKSPACE;
+    char *ws = reinterpret_cast<char *>(workspace);
+    auto *heads = reinterpret_cast<MseHead *>(ws + lay.heads_off);
+    auto *deltas = reinterpret_cast<D *>(ws + lay.deltas_off);
+    auto *bheads = reinterpret_cast<MseHead *>(ws + lay.bheads_off);
+    auto *bdeltas = reinterpret_cast<D *>(ws + lay.bdeltas_off);
     static bool configured[64] = {false};
     int device = 0;
     cudaGetDevice(&device);
@@ -882,9 +906,17 @@ int run_mse(int policy, const T *p, const T *t, T *out, uint64_t n, void *worksp
         configured[device] = true;
     }
     mse_walk_kernel<T><<<1, 256, WalkSmem<T>::BYTES, stream>>>(p, t, n, heads, deltas, bheads, bdeltas, lay.chunks,
-                                                               lay.blocks,
-                                                               count_value<T>(n), policy, out, status);
+                                                               lay.blocks, base, total, count_value<T>(total), policy,
+                                                               carry_in, carry_out, out, status);
     return pcu_host::launch_status();
+}
+
+template <typename T>
+int run_mse(int policy, const T *p, const T *t, T *out, uint64_t n, void *workspace, size_t workspace_bytes,
+            unsigned long long *status, cudaStream_t stream) {
+    int rc = prepare_mse<T>(policy, p, t, n, 0, workspace, workspace_bytes, status, stream);
+    if (rc) return rc;
+    return walk_mse<T>(policy, p, t, n, 0, n, nullptr, nullptr, out, workspace, workspace_bytes, status, stream);
 }
 
 }  // namespace pcu
@@ -908,4 +940,41 @@ extern "C" int pcu_b200_strict_mse(int dtype, int policy, const void *prediction
                                    workspace, workspace_bytes, st, s);
     return pcu::run_mse<double>(policy, (const double *)prediction, (const double *)target, (double *)out, count,
                                 workspace, workspace_bytes, st, s);
+}
+
+extern "C" int pcu_b200_strict_mse_segment_prepare(int dtype, int policy, const void *prediction, const void *target,
+                                                   uint64_t count, uint64_t first_index, void *workspace,
+                                                   size_t workspace_bytes, uint64_t *status, void *stream) {
+    if ((dtype != PCU_B200_F32 && dtype != PCU_B200_F64) || policy < 0 || policy > 2 || !status)
+        return PCU_B200_ERROR_INVALID_ARGUMENT;
+    if (count && (!prediction || !target)) return PCU_B200_ERROR_INVALID_ARGUMENT;
+    if (count > (1ull << 58) || first_index > (1ull << 58) - count) return PCU_B200_ERROR_SIZE_OVERFLOW;
+    auto *st = reinterpret_cast<unsigned long long *>(status);
+    cudaStream_t s = pcu_host::as_stream(stream);
+    if (dtype == PCU_B200_F32)
+        return pcu::prepare_mse<float>(policy, (const float *)prediction, (const float *)target, count, first_index,
+                                       workspace, workspace_bytes, st, s);
+    return pcu::prepare_mse<double>(policy, (const double *)prediction, (const double *)target, count, first_index,
+                                    workspace, workspace_bytes, st, s);
+}
+
+extern "C" int pcu_b200_strict_mse_segment_walk(int dtype, int policy, const void *prediction, const void *target,
+                                                uint64_t count, uint64_t first_index, uint64_t total_count,
+                                                const void *carry_in, void *carry_out, void *out, void *workspace,
+                                                size_t workspace_bytes, uint64_t *status, void *stream) {
+    if ((dtype != PCU_B200_F32 && dtype != PCU_B200_F64) || policy < 0 || policy > 2 || !status)
+        return PCU_B200_ERROR_INVALID_ARGUMENT;
+    if (count && (!prediction || !target)) return PCU_B200_ERROR_INVALID_ARGUMENT;
+    if (total_count > (1ull << 58) || first_index > total_count || count > total_count - first_index)
+        return PCU_B200_ERROR_SIZE_OVERFLOW;
+    if (out && (total_count == 0 || first_index + count != total_count)) return PCU_B200_ERROR_INVALID_ARGUMENT;
+    auto *st = reinterpret_cast<unsigned long long *>(status);
+    cudaStream_t s = pcu_host::as_stream(stream);
+    if (dtype == PCU_B200_F32)
+        return pcu::walk_mse<float>(policy, (const float *)prediction, (const float *)target, count, first_index,
+                                    total_count, (const float *)carry_in, (float *)carry_out, (float *)out, workspace,
+                                    workspace_bytes, st, s);
+    return pcu::walk_mse<double>(policy, (const double *)prediction, (const double *)target, count, first_index,
+                                 total_count, (const double *)carry_in, (double *)carry_out, (double *)out, workspace,
+                                 workspace_bytes, st, s);
 }

@@ -158,6 +158,28 @@ int pcu_b200_strict_mse(int dtype, int policy, const void *prediction, const voi
                         uint64_t count, void *workspace, size_t workspace_bytes, uint64_t *status,
                         void *stream);
 
+/* Segment form of pcu_b200_strict_mse for a reduction split across devices (one tensor's
+ * elements sharded over GPUs) with an ordered hand-off of the running sum.  It has no
+ * counterpart in the reference, whose strict MSE runs on one device; the results are those of
+ * the one-device reduction over the concatenated segments.
+ *
+ * The segment holds the global elements [first_index, first_index + count) of a reduction
+ * over total_count elements; its fault events are global (element i -> i*3 + step, Divide
+ * -> total_count*3).  Call prepare (all of the segment's bandwidth-bound work; it does not
+ * depend on the running sum, so every device runs it at once), then walk with the running
+ * sum that enters the segment (carry_in, a device scalar, NULL = +0).  Walk writes the running
+ * sum after the segment to *carry_out (if not NULL; it may equal carry_in) and, for the last
+ * segment (first_index + count == total_count) with out not NULL, the checked mean to out[0].
+ * A fault already recorded in `status` in front of the segment stops the walk at once.  Both
+ * take the workspace of pcu_b200_strict_mse_workspace_size(dtype, count); count may be 0. */
+int pcu_b200_strict_mse_segment_prepare(int dtype, int policy, const void *prediction, const void *target,
+                                        uint64_t count, uint64_t first_index, void *workspace,
+                                        size_t workspace_bytes, uint64_t *status, void *stream);
+int pcu_b200_strict_mse_segment_walk(int dtype, int policy, const void *prediction, const void *target,
+                                     uint64_t count, uint64_t first_index, uint64_t total_count,
+                                     const void *carry_in, void *carry_out, void *out, void *workspace,
+                                     size_t workspace_bytes, uint64_t *status, void *stream);
+
 /* ------------------------------------------------------------------ checked elementwise */
 
 /* out[i] = op(left[i], right[i]); a nonzero *_uniform flag broadcasts element 0 of that

@@ -69,6 +69,8 @@ def _declare(L):
     L.pcu_oracle_soft_matmul_threads.restype = u64
     L.pcu_oracle_mse.argtypes = [i32, vp, vp, u64, i32, vp]
     L.pcu_oracle_mse.restype = u64
+    L.pcu_oracle_mse_segment.argtypes = [i32, vp, vp, u64, u64, u64, i32, ctypes.POINTER(u64), vp]
+    L.pcu_oracle_mse_segment.restype = u64
     L.pcu_oracle_sgd.argtypes = [i32, vp, vp, u32, u64, i32, vp]
     L.pcu_oracle_sgd.restype = u64
     L.pcu_oracle_binary.argtypes = [i32, i32, vp, vp, u64, i32, i32, i32, vp]
@@ -179,6 +181,18 @@ def mse(prediction, target, policy=0):
     status = lib().pcu_oracle_mse(_elem(prediction), _ptr(prediction), _ptr(target), prediction.size, policy,
                                   _ptr(out))
     return status, out
+
+
+def mse_segment(prediction, target, first_index, total_count, carry_bits=0, policy=0, last=False):
+    """One segment of a split ordered MSE: returns (status, carry bits after it, mean or None)."""
+    prediction = np.ascontiguousarray(prediction)
+    target = np.ascontiguousarray(target)
+    carry = ctypes.c_uint64(carry_bits)
+    out = np.zeros(1, dtype=prediction.dtype) if last else None
+    status = lib().pcu_oracle_mse_segment(_elem(prediction), _ptr(prediction), _ptr(target), prediction.size,
+                                          first_index, total_count, policy, ctypes.byref(carry),
+                                          _ptr(out) if last else None)
+    return status, carry.value, out
 
 
 def sgd(weights, gradient, rate, policy=0):

@@ -67,6 +67,9 @@ uint64_t pcu_oracle_matmul_cells(int elem, const void *left, const void *right, 
                                  const uint64_t *cells, uint64_t cell_count);
 uint64_t pcu_oracle_mse(int elem, const void *prediction, const void *target, uint64_t count,
                         int policy, void *out);
+uint64_t pcu_oracle_mse_segment(int elem, const void *prediction, const void *target, uint64_t count,
+                                uint64_t first_index, uint64_t total_count, int policy, uint64_t *carry,
+                                void *out);
 uint64_t pcu_oracle_sgd(int elem, const void *weights, const void *gradient, uint32_t rate_bits_f32,
                         uint64_t count, int policy, void *out);
 uint64_t pcu_oracle_binary(int elem, int op, const void *left, const void *right, uint64_t count,

@@ -119,25 +119,41 @@ uint64_t pcu_oracle_matmul_cells(int elem, const void *left, const void *right, 
     return status;
 }
 
+/* One segment [first_index, first_index + count) of the ordered MSE reduction over
+ * total_count elements: the loop of pcu_oracle_mse started from the running sum *carry
+ * (bits) instead of +0, with global event ordinals.  *carry receives the running sum after
+ * the segment; the last segment (out != NULL) also divides by count(total_count).  Splitting
+ * the reduction this way is exactly the one-pass loop, since each step only reads the sum. */
+uint64_t pcu_oracle_mse_segment(int elem, const void *prediction, const void *target, uint64_t count,
+                                uint64_t first_index, uint64_t total_count, int policy, uint64_t *carry,
+                                void *out)
+{
+    uint64_t total = *carry;
+    for (uint64_t i = 0; i < count; ++i) {
+        const uint64_t g = first_index + i;
+        uint64_t difference = 0, square = 0;
+        int kind = binop(elem, load(elem, prediction, i), load(elem, target, i), 1, policy, &difference);
+        if (kind) return status_of(g * 3, kind);
+        kind = binop(elem, difference, difference, 2, policy, &square);
+        if (kind) return status_of(g * 3 + 1, kind);
+        kind = binop(elem, total, square, 0, policy, &total);
+        if (kind) return status_of(g * 3 + 2, kind);
+    }
+    *carry = total;
+    if (!out) return STATUS_OK;
+    uint64_t denominator = elem == 4 ? pcu_oracle_count_f32(total_count) : pcu_oracle_count_f64(total_count);
+    uint64_t mean = 0;
+    int kind = binop(elem, total, denominator, 3, policy, &mean);
+    if (kind) return status_of(total_count * 3, kind);
+    store(elem, out, 0, mean);
+    return STATUS_OK;
+}
+
 uint64_t pcu_oracle_mse(int elem, const void *prediction, const void *target, uint64_t count,
                         int policy, void *out)
 {
-    uint64_t total = 0;
-    for (uint64_t i = 0; i < count; ++i) {
-        uint64_t difference = 0, square = 0;
-        int kind = binop(elem, load(elem, prediction, i), load(elem, target, i), 1, policy, &difference);
-        if (kind) return status_of(i * 3, kind);
-        kind = binop(elem, difference, difference, 2, policy, &square);
-        if (kind) return status_of(i * 3 + 1, kind);
-        kind = binop(elem, total, square, 0, policy, &total);
-        if (kind) return status_of(i * 3 + 2, kind);
-    }
-    uint64_t denominator = elem == 4 ? pcu_oracle_count_f32(count) : pcu_oracle_count_f64(count);
-    uint64_t mean = 0;
-    int kind = binop(elem, total, denominator, 3, policy, &mean);
-    if (kind) return status_of(count * 3, kind);
-    store(elem, out, 0, mean);
-    return STATUS_OK;
+    uint64_t carry = 0;
+    return pcu_oracle_mse_segment(elem, prediction, target, count, 0, count, policy, &carry, out);
 }
 
 uint64_t pcu_oracle_sgd(int elem, const void *weights, const void *gradient, uint32_t rate_bits_f32,

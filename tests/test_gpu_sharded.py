@@ -1,0 +1,154 @@
+"""Split strict MSE (segment prepare + ordered walk) and the multi-GPU sharded path on B200s.
+
+* On one GPU: a reduction cut into segments and walked in order with the carried running sum
+  must give the bits and the first fault of the one-call strict MSE and of the oracle, for cuts
+  inside chunks, on chunk edges and of length zero.
+* On 2+ GPUs (skipped with fewer): MatMul rows, SGD elements and MSE segments sharded over NCCL
+  ranks must reproduce the one-device results and first faults exactly.
+"""
+import importlib
+import os
+import socket
+
+import numpy as np
+import pytest
+
+import oracle
+from gpu_util import bits, dyadic_uniform, status_word, to_device, to_host
+
+pytestmark = pytest.mark.gpu
+
+pcu = importlib.import_module("fusion-pcu_b200")
+
+
+def _segments(p, t, cuts, width):
+    import torch
+
+    n = p.numel()
+    edges = [0] + list(cuts) + [n]
+    status = pcu.new_status()
+    carry = torch.zeros((), dtype=p.dtype, device=p.device)
+    mean = torch.zeros((), dtype=p.dtype, device=p.device)
+    for a, b in zip(edges, edges[1:]):
+        ps, ts = p[a:b].contiguous(), t[a:b].contiguous()
+        _, ws = pcu.strict_mse_segment_prepare(ps, ts, a, status=status)
+        pcu.strict_mse_segment_walk(ps, ts, a, n, carry, ws, status, out=mean if b == n else None)
+    torch.cuda.synchronize()
+    return status_word(status), bits(to_host(mean).reshape(1))[0]
+
+
+@pytest.mark.parametrize("width", [32, 64])
+@pytest.mark.parametrize("case", ["clean", "nan_mid", "inf_late", "overflow_by_carry"])
+def test_segments_match_one_call_and_oracle(width, case):
+    import torch
+
+    rng = np.random.default_rng(31 + width)
+    n = 3 * 8192 + 777
+    p = dyadic_uniform(rng, n, width)
+    t = dyadic_uniform(rng, n, width)
+    if case == "nan_mid":
+        p[20000] = np.nan
+    elif case == "inf_late":
+        t[n - 3] = np.inf
+    elif case == "overflow_by_carry":
+        big = 1.5e19 if width == 32 else 1e154
+        p[9000:] = big
+        t[9000:] = 0
+    st_o, out_o = oracle.mse(p, t)
+    pd, td = to_device(p), to_device(t)
+    status = pcu.new_status()
+    whole = pcu.strict_mse(pd, td, status=status)
+    torch.cuda.synchronize()
+    assert status_word(status) == st_o
+    for cuts in ([8192], [100, 8192 * 2 + 5], [5000, 5000, 20001], [1, 2, 3, n - 1]):
+        word, got = _segments(pd, td, cuts, width)
+        assert word == st_o, (cuts, hex(word), hex(st_o))
+        if st_o == oracle.STATUS_OK:
+            assert got == bits(out_o)[0] == bits(to_host(whole).reshape(1))[0], cuts
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _nccl_worker(rank, world, port, queue):
+    import torch
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    import datetime
+
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        sharded = importlib.import_module("fusion-pcu_b200.sharded")
+        rng = np.random.default_rng(77)
+        m, k, n = 512, 384, 256
+        a = dyadic_uniform(rng, (m, k), 32)
+        b = dyadic_uniform(rng, (k, n), 32)
+        a[300, 17] = np.nan
+        rows = m // world
+        r0 = rank * rows
+        status = pcu.new_status()
+        local = torch.empty((rows, n), dtype=torch.float32, device="cuda")
+        full = torch.empty((m, n), dtype=torch.float32, device="cuda")
+        sharded.strict_matmul_rows(to_device(a[r0:r0 + rows]), to_device(b), r0, local, status, gathered=full)
+        sharded.all_reduce_min_status(status)
+        mm_word = status_word(status)
+        mm_bits = bits(to_host(full)) if mm_word == pcu.STATUS_OK else None
+
+        e = 5 * 8192 + 123
+        p = dyadic_uniform(rng, e, 32)
+        t = dyadic_uniform(rng, e, 32)
+        e0, e1 = sharded.shard_bounds(e, rank, world, align=4)
+        st2 = pcu.new_status()
+        sgd_out = sharded.strict_sgd_block(to_device(p[e0:e1]), to_device(t[e0:e1]), 0.25, e0, st2)
+        sharded.all_reduce_min_status(st2)
+        st3 = pcu.new_status()
+        mse = sharded.ShardedMse(to_device(p[e0:e1]), to_device(t[e0:e1]), e0, e)
+        mean = mse.run(st3)
+        torch.cuda.synchronize()
+        queue.put((rank, mm_word, mm_bits, status_word(st2), bits(to_host(sgd_out)), status_word(st3),
+                   bits(to_host(mean).reshape(1))[0]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_nccl_sharded_matches_one_device():
+    import torch
+
+    world = min(torch.cuda.device_count(), 4)
+    if world < 2:
+        pytest.skip("needs 2 or more GPUs")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_nccl_worker, args=(r, world, port, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict((r[0], r[1:]) for r in (queue.get(timeout=300) for _ in range(world)))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    rng = np.random.default_rng(77)
+    a = dyadic_uniform(rng, (512, 384), 32)
+    b = dyadic_uniform(rng, (384, 256), 32)
+    a[300, 17] = np.nan
+    mm_st, _ = oracle.matmul(a, b, fast=True)
+    e = 5 * 8192 + 123
+    p = dyadic_uniform(rng, e, 32)
+    t = dyadic_uniform(rng, e, 32)
+    sgd_st, sgd_out = oracle.sgd(p, t, 0.25)
+    mse_st, mse_out = oracle.mse(p, t)
+    for rank in range(world):
+        mm_word, _, sgd_word, sgd_bits, mse_word, mean_bits = got[rank]
+        assert mm_word == mm_st
+        assert sgd_word == sgd_st and mse_word == mse_st
+        assert mean_bits == bits(mse_out)[0]
+    sgd_all = np.concatenate([got[r][3] for r in range(world)])
+    assert np.array_equal(sgd_all, bits(sgd_out))
