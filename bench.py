@@ -4,8 +4,9 @@ Workload (the headline): strict checked F32 MatMul 819
 entries dyadic U[-1,1) from a seed, fault-free.  A "step" is one pcu_b200_strict_matmul call
 (exponent prescan + ordered-K kernel).  N GPUs: the output rows are sharded across ranks (K is
 never split, so the strict order is untouched) and the row blocks are all-gathered with NCCL
-(strong scaling: the 8192^3 product is fixed).  Secondary line items
-(strict MSE + SGD on 2^28 F32 elements, HBM GB/s) at N = 1.
+(strong scaling: the 8192^3 product is fixed), and the per-rank fault words are combined into
+the global first fault every step.  Secondary line item: BASELINE configs[4] (strict MSE + SGD
+on 2^28 F32 elements, HBM GB/s), element-sharded at N > 1.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
@@ -13,6 +14,7 @@ never split, so the strict order is untouched) and the row blocks are all-gather
 itself is Rust and cannot be built here) on all host cores over a bounded row sample.
 """
 import argparse
+import importlib
 import json
 import os
 import statistics
@@ -176,7 +178,6 @@ def main():
         return
     import torch
     import torch.distributed as dist
-    import importlib
 
     pcu = importlib.import_module("fusion-pcu_b200")
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -208,10 +209,15 @@ def main():
     ws_bytes = lib.pcu_b200_strict_matmul_workspace_size(rows_per, N, N)
     workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=device)
 
+    sharded = importlib.import_module("fusion-pcu_b200.sharded") if world > 1 else None
+
     def step():
-        pcu.strict_matmul(a, b, out=c_local, status=status, workspace=workspace, stream=stream)
         if world > 1:
-            dist.all_gather_into_tensor(c_full, c_local)
+            # rank-local rows with global fault events, all-gather of C, global first fault
+            sharded.strict_matmul_rows(a, b, r0, c_local, status, gathered=c_full, workspace=workspace, stream=stream)
+            sharded.all_reduce_min_status(status)
+        else:
+            pcu.strict_matmul(a, b, out=c_local, status=status, workspace=workspace, stream=stream)
 
     for _ in range(args.warmup):
         step()
@@ -275,8 +281,8 @@ def main():
     ms, kernel_ms, e2e_ms = times.tolist()
 
     secondary = None
-    if rank == 0 and world == 1 and not args.no_secondary:
-        secondary = mse_sgd(torch, pcu, device, stream, hbm_gbs, args)
+    if not args.no_secondary:
+        secondary = mse_sgd(torch, pcu, device, stream, hbm_gbs, args, rank, world)
 
     if world > 1:
         dist.barrier()
@@ -315,44 +321,70 @@ def main():
     print(json.dumps(line), flush=True)
 
 
-def mse_sgd(torch, pcu, device, stream, hbm_gbs, args):
-    """strict MSE + SGD on four 2^28-element F32 tensors."""
+def mse_sgd(torch, pcu, device, stream, hbm_gbs, args, rank, world):
+    """strict MSE + SGD on four 2^28-element F32 tensors.  With N ranks each
+    holds a contiguous element block (strong scaling); SGD needs no exchange, MSE hands its
+    running sum from rank to rank in order (fusion-pcu_b200/sharded.py)."""
+    import torch.distributed as dist
+
     n = MSE_SGD_ELEMS
-    w = dyadic(torch, (n,), 11, device)
-    g = dyadic(torch, (n,), 12, device)
-    p = dyadic(torch, (n,), 13, device)
-    t = dyadic(torch, (n,), 14, device)
+    sharded = importlib.import_module("fusion-pcu_b200.sharded") if world > 1 else None
+    e0, e1 = sharded.shard_bounds(n, rank, world, align=8192) if world > 1 else (0, n)
+    m = e1 - e0
+
+    def block(seed):  # this rank's block of the seeded full tensor
+        g = torch.Generator(device=device)
+        g.manual_seed(seed)
+        if e0:
+            torch.randint(-(1 << 23), 1 << 23, (e0,), generator=g, device=device, dtype=torch.int32)
+        k = torch.randint(-(1 << 23), 1 << 23, (m,), generator=g, device=device, dtype=torch.int32)
+        return k.to(torch.float32) * (2.0 ** -23)
+
+    w, g_, p, t = block(11), block(12), block(13), block(14)
     out_w = torch.empty_like(w)
     loss = torch.empty((), dtype=torch.float32, device=device)
     s1, s2 = pcu.new_status(device=device), pcu.new_status(device=device)
-    lib = pcu.library()
-    ws = torch.empty(lib.pcu_b200_strict_mse_workspace_size(0, n), dtype=torch.uint8, device=device)
+    if world > 1:
+        smse = sharded.ShardedMse(p, t, e0, n)
+        mse_call = lambda: smse.run(s1, stream=stream)  # noqa: E731
+        sgd_call = lambda: (sharded.strict_sgd_block(w, g_, 0.01, e0, s2, out=out_w, stream=stream),  # noqa: E731
+                            sharded.all_reduce_min_status(s2))
+    else:
+        ws = pcu.mse_workspace(p)
+        mse_call = lambda: pcu.strict_mse(p, t, out=loss, status=s1, workspace=ws, stream=stream)  # noqa: E731
+        sgd_call = lambda: pcu.strict_sgd(w, g_, 0.01, out=out_w, status=s2, stream=stream)  # noqa: E731
 
-    def step():
-        pcu.strict_mse(p, t, out=loss, status=s1, workspace=ws, stream=stream)
-        pcu.strict_sgd(w, g, 0.01, out=out_w, status=s2, stream=stream)
-
-    for _ in range(max(1, min(args.warmup, 2))):
-        step()
+    for _ in range(max(3, min(args.warmup, 3))):
+        mse_call()
+        sgd_call()
     torch.cuda.synchronize()
-    steps = max(1, min(args.steps, 3))
+    steps = max(1, min(args.steps, 5))
     times = {}
-    for name, fn in (("mse", lambda: pcu.strict_mse(p, t, out=loss, status=s1, workspace=ws, stream=stream)),
-                     ("sgd", lambda: pcu.strict_sgd(w, g, 0.01, out=out_w, status=s2, stream=stream))):
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
+    for name, fn in (("mse", mse_call), ("sgd", sgd_call)):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e_0, e_1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e_0.record(stream)
         for _ in range(steps):
             fn()
-        e1.record(stream)
+        e_1.record(stream)
         torch.cuda.synchronize()
-        times[name] = e0.elapsed_time(e1) / steps
+        times[name] = e_0.elapsed_time(e_1) / steps
+    tt = torch.tensor([times["mse"], times["sgd"]], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    times["mse"], times["sgd"] = tt.tolist()
     ok = all(int(s.cpu().numpy().view(np.uint64)[0]) == pcu.STATUS_OK for s in (s1, s2))
     mse_bytes, sgd_bytes = 2 * n * 4, 3 * n * 4
     total_ms = times["mse"] + times["sgd"]
     return {"value": (mse_bytes + sgd_bytes) / (total_ms * 1e-3) / 1e9, "unit": "GB/s", "elements": n,
+            "scaling": "strong", "parallelism": f"element blocks x{world}" + (
+                " + ordered MSE hand-off" if world > 1 else ""),
             "mse_ms": times["mse"], "sgd_ms": times["sgd"],
             "sgd_gbs": sgd_bytes / (times["sgd"] * 1e-3) / 1e9, "mse_gbs": mse_bytes / (times["mse"] * 1e-3) / 1e9,
-            "hbm_peak_gbs": hbm_gbs, "fault_free": ok}
+            "hbm_peak_gbs": hbm_gbs * world, "frac": (mse_bytes + sgd_bytes) / (total_ms * 1e-3) / 1e9 / (
+                hbm_gbs * world), "fault_free": ok}
 
 
 if __name__ == "__main__":

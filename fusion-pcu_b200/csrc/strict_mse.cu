@@ -213,7 +213,7 @@ __device__ __noinline__ bool checked_square(T p, T t, uint64_t i, int policy, un
 
 template <typename T>
 __global__ void __launch_bounds__(256) mse_chunk_kernel(const T *prediction, const T *target, uint64_t n,
-                                                        uint64_t base, int policy, MseHead *heads,
+                                                        uint64_t base, bool vec, int policy, MseHead *heads,
                                                         typename MseTraits<T>::D *deltas,
                                                         unsigned long long *status) {
     using Tr = MseTraits<T>;
@@ -255,7 +255,7 @@ __global__ void __launch_bounds__(256) mse_chunk_kernel(const T *prediction, con
     for (int r = 0; r < ROWS; ++r) {
         const uint64_t i0 = chunk0 + CM::index(warp, r, lane, 0);
         T pv[V], tv[V];
-        if (i0 + V <= n) {
+        if (vec && i0 + V <= n) {  // 16-byte loads only when both operands are 16-byte aligned
             const VT a = __ldcs(reinterpret_cast<const VT *>(prediction + i0));
             const VT b = __ldcs(reinterpret_cast<const VT *>(target + i0));
 #pragma unroll
@@ -875,7 +875,8 @@ int prepare_mse(int policy, const T *p, const T *t, uint64_t n, uint64_t base, v
     auto *deltas = reinterpret_cast<D *>(ws + lay.deltas_off);
     auto *bheads = reinterpret_cast<MseHead *>(ws + lay.bheads_off);
     auto *bdeltas = reinterpret_cast<D *>(ws + lay.bdeltas_off);
-    mse_chunk_kernel<T><<<(unsigned)lay.chunks, 256, 0, stream>>>(p, t, n, base, policy, heads, deltas, status);
+    const bool vec = pcu_host::aligned(p, 16) && pcu_host::aligned(t, 16);
+    mse_chunk_kernel<T><<<(unsigned)lay.chunks, 256, 0, stream>>>(p, t, n, base, vec, policy, heads, deltas, status);
     int rc = pcu_host::launch_status();
     if (rc) return rc;
     mse_block_kernel<T><<<(unsigned)lay.blocks, 64, 0, stream>>>(heads, deltas, lay.chunks, bheads, bdeltas);

@@ -113,8 +113,8 @@ class ShardedMse:
         self.p, self.t = prediction, target
         self.first, self.total, self.policy, self.group = first_index, total, policy, group
         self.workspace = pcu.mse_workspace(prediction)
-        self.carry = torch.zeros((), dtype=prediction.dtype, device=prediction.device)
-        self.mean = torch.zeros((), dtype=prediction.dtype, device=prediction.device)
+        self.carry = torch.zeros(1, dtype=prediction.dtype, device=prediction.device)
+        self.mean = torch.zeros(1, dtype=prediction.dtype, device=prediction.device)
         self.last = first_index + prediction.numel() == total
 
     def run(self, status, stream=None, reduce_status=True):
@@ -130,4 +130,4 @@ class ShardedMse:
         dist.broadcast(self.mean, src=_ranks(self.group)[-1], group=self.group)
         if reduce_status:
             all_reduce_min_status(status, self.group)
-        return self.mean
+        return self.mean.reshape(())

@@ -60,6 +60,14 @@ def test_segments_match_one_call_and_oracle(width, case):
     whole = pcu.strict_mse(pd, td, status=status)
     torch.cuda.synchronize()
     assert status_word(status) == st_o
+    # the one-call form on operands that are not 16-byte aligned (element offset 1)
+    st_u, out_u = oracle.mse(p[1:], t[1:])
+    status_u = pcu.new_status()
+    got_u = pcu.strict_mse(pd[1:], td[1:], status=status_u)
+    torch.cuda.synchronize()
+    assert status_word(status_u) == st_u
+    if st_u == oracle.STATUS_OK:
+        assert bits(to_host(got_u).reshape(1))[0] == bits(out_u)[0]
     for cuts in ([8192], [100, 8192 * 2 + 5], [5000, 5000, 20001], [1, 2, 3, n - 1]):
         word, got = _segments(pd, td, cuts, width)
         assert word == st_o, (cuts, hex(word), hex(st_o))
