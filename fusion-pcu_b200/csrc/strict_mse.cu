@@ -50,6 +50,10 @@
 #include "common.cuh"
 #include "pcu_b200.h"
 
+#ifndef PCU_MSE_MIN_BLOCKS_F32
+#define PCU_MSE_MIN_BLOCKS_F32 3
+#endif
+
 namespace pcu {
 
 template <typename T> struct MseTraits;
@@ -63,6 +67,7 @@ template <> struct MseTraits<float> {
     static constexpr int KMIN = -149;            // smallest ulp exponent
     static constexpr int PLANES = 6;             // vertical counter planes: counts up to 63
     static constexpr uint64_t SAT = 1ull << 40;  // no valid increment comes near this
+    static constexpr int MIN_BLOCKS = PCU_MSE_MIN_BLOCKS_F32;  // chunk kernel residency target per SM
 };
 template <> struct MseTraits<double> {
     using Fix = uint64_t;
@@ -74,6 +79,7 @@ template <> struct MseTraits<double> {
     static constexpr int KMIN = -1074;
     static constexpr int PLANES = 5;
     static constexpr uint64_t SAT = 1ull << 62;
+    static constexpr int MIN_BLOCKS = 2;
 };
 
 constexpr int kBlockChunks = 64;
@@ -211,27 +217,74 @@ __device__ __noinline__ bool checked_square(T p, T t, uint64_t i, int policy, un
     return true;
 }
 
+// carry-save adder on bit vectors: a + b + c = 2 * hi + lo in every bit position
+template <typename X> __device__ __forceinline__ void csa(X &hi, X &lo, X a, X b, X c) {
+    const X u = a ^ b;
+    hi = (a & b) | (u & c);
+    lo = u ^ c;
+}
+
+// Harley-Seal tree: adds the 2^L words q[BASE .. BASE + 2^L) into the vertical bit counters
+// acc[0 .. L-1] (acc[i] holds bit i of every column's count) and returns the carry word of
+// weight 2^L.  2^L - 1 carry-save adders in all.
+template <int L, int BASE> struct SealTree {
+    template <typename X, int N, int P>
+    __device__ static __forceinline__ X run(const X (&q)[N], X (&acc)[P]) {
+        const X a = SealTree<L - 1, BASE>::run(q, acc);
+        const X b = SealTree<L - 1, BASE + (1 << (L - 1))>::run(q, acc);
+        X h;
+        csa(h, acc[L - 1], acc[L - 1], a, b);
+        return h;
+    }
+};
+template <int BASE> struct SealTree<1, BASE> {
+    template <typename X, int N, int P>
+    __device__ static __forceinline__ X run(const X (&q)[N], X (&acc)[P]) {
+        X h;
+        csa(h, acc[0], acc[0], q[BASE], q[BASE + 1]);
+        return h;
+    }
+};
+
+// 32 x 32 bit-matrix transpose across a warp: on return lane b holds, in bit l, bit b of lane
+// l's input word (five butterfly stages, each swapping the off-diagonal blocks).
+__device__ __forceinline__ unsigned warp_transpose32(unsigned x, int lane) {
+#pragma unroll
+    for (int h = 16; h; h >>= 1) {
+        const unsigned m = h == 16 ? 0x0000ffffu : h == 8 ? 0x00ff00ffu : h == 4 ? 0x0f0f0f0fu
+                         : h == 2 ? 0x33333333u : 0x55555555u;  // bit positions with (index & h) == 0
+        const unsigned y = __shfl_xor_sync(0xffffffffu, x, h);
+        x = (lane & h) ? ((x & ~m) | ((y >> h) & m)) : ((x & m) | ((y << h) & ~m));
+    }
+    return x;
+}
+
 template <typename T>
-__global__ void __launch_bounds__(256) mse_chunk_kernel(const T *prediction, const T *target, uint64_t n,
-                                                        uint64_t base, bool vec, int policy, MseHead *heads,
-                                                        typename MseTraits<T>::D *deltas,
-                                                        unsigned long long *status) {
+__global__ void __launch_bounds__(256, MseTraits<T>::MIN_BLOCKS)
+mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base, bool vec, int policy,
+                 MseHead *heads, typename MseTraits<T>::D *deltas, unsigned long long *status) {
     using Tr = MseTraits<T>;
     using F = Fmt<T>;
     using B = typename F::Bits;
     using Fix = typename Tr::Fix;
     using CM = ChunkMap<T>;
     constexpr int EPT = Tr::EPT, W = Tr::W, V = CM::V, ROWS = CM::ROWS;
+    constexpr int LOG_EPT = EPT == 32 ? 5 : 4;
+    static_assert((1 << LOG_EPT) == EPT && LOG_EPT + 1 == Tr::PLANES, "counter planes");
     constexpr int FIXBITS = sizeof(Fix) * 8;
     constexpr Fix kSticky = (Fix)1 << (FIXBITS - 1);
+    // |d| below 2^-62 (binary32) / 2^-510 (binary64) may square to <= the smallest normal
+    constexpr B kTinyDiff = sizeof(T) == 4 ? (B)(127 - 62) << 23 : (B)(1023 - 510) << 52;
     using VT = typename std::conditional<sizeof(T) == 4, float4, double2>::type;
 
     __shared__ unsigned int s_fault;
     __shared__ unsigned long long s_qmax;
     __shared__ unsigned int s_cnt[W];
     __shared__ Fix s_warp_xor[8];
+    __shared__ Fix s_lane_ex[ROWS][256];
     __shared__ unsigned int s_tie_count;
     __shared__ int s_jmin;
+    __shared__ uint64_t s_W[W + 1];
     __shared__ Tie s_ties[kMaxTies];
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -244,18 +297,20 @@ __global__ void __launch_bounds__(256) mse_chunk_kernel(const T *prediction, con
     if (tid < W) s_cnt[tid] = 0;
     __syncthreads();
 
-    // ---- squares.  Fast test: a non-finite square means an invalid operand or an overflow in
-    // one of the two steps; a square at or below the smallest normal of a nonzero difference
-    // may hide an underflow decision (and under RejectSubnormalResult a subnormal difference
-    // always squares into that range).  Flagged threads redo their elements with the checked
-    // law, in order, and stop at their first fault (their later events cannot win).
+    // ---- squares.  A thread is suspect when one of its squares is non-finite (an invalid
+    // operand or an overflow in either step) or, unless the policy allows gradual underflow, one
+    // of its differences is nonzero and below 2^-62 / 2^-510 (only such a difference can square
+    // to <= the smallest normal, and a subnormal difference is one of them).  Suspect threads
+    // redo their elements with the checked law, in order, and stop at their first fault (their
+    // later events cannot win).
     Fix qf[EPT];  // q's bits first, its fixed-point form later; qf[row * V + e]
-    bool suspect = false;
+    B qmax_t = 0, dmin = ~(B)0;
+    const bool full = vec && chunk0 + Tr::CHUNK <= n;  // every row in range: no per-row guard
 #pragma unroll
     for (int r = 0; r < ROWS; ++r) {
         const uint64_t i0 = chunk0 + CM::index(warp, r, lane, 0);
         T pv[V], tv[V];
-        if (vec && i0 + V <= n) {  // 16-byte loads only when both operands are 16-byte aligned
+        if (full || (vec && i0 + V <= n)) {  // 16-byte loads only when both operands are 16-byte aligned
             const VT a = __ldcs(reinterpret_cast<const VT *>(prediction + i0));
             const VT b = __ldcs(reinterpret_cast<const VT *>(target + i0));
 #pragma unroll
@@ -274,12 +329,14 @@ __global__ void __launch_bounds__(256) mse_chunk_kernel(const T *prediction, con
         for (int e = 0; e < V; ++e) {
             const T d = F::sub(pv[e], tv[e]);
             const B qb = F::bits(F::mul(d, d));
-            suspect |= nonfinite_bits<T>(qb) ||
-                       (policy != kPolicyGradual && qb <= F::kMinNormalBits && (F::bits(d) << 1) != 0);
+            qmax_t = qb > qmax_t ? qb : qmax_t;
+            const B dd = F::bits(d) * 2 - 1;  // |d| doubled minus one: +-0 becomes all ones
+            dmin = dd < dmin ? dd : dmin;
             qf[r * V + e] = (Fix)qb;
         }
     }
-    if (suspect) {  // rare: reload and redo this thread's elements with the checked law
+    if (qmax_t >= F::kExpMask || (policy != kPolicyGradual && dmin < kTinyDiff * 2 - 1)) {
+        // rare: reload and redo this thread's elements with the checked law
         bool stopped = false;
 #pragma unroll 1
         for (int r = 0; r < ROWS; ++r)
@@ -294,12 +351,12 @@ __global__ void __launch_bounds__(256) mse_chunk_kernel(const T *prediction, con
                 }
                 if (i < n) set_at(qf, r * V + e, stopped ? (Fix)0 : (Fix)F::bits(q));
             }
-    }
-    B local_max = 0;
+        qmax_t = 0;
 #pragma unroll
-    for (int e = 0; e < EPT; ++e) local_max = (B)qf[e] > local_max ? (B)qf[e] : local_max;
-    local_max = warp_max_bits<T>(local_max);
-    if (lane == 0) atomicMax(&s_qmax, (unsigned long long)local_max);
+        for (int e = 0; e < EPT; ++e) qmax_t = (B)qf[e] > qmax_t ? (B)qf[e] : qmax_t;
+    }
+    qmax_t = warp_max_bits<T>(qmax_t);
+    if (lane == 0) atomicMax(&s_qmax, (unsigned long long)qmax_t);
     __syncthreads();
 
     MseHead head;
@@ -318,101 +375,128 @@ __global__ void __launch_bounds__(256) mse_chunk_kernel(const T *prediction, con
     const int k_hi = exponent_of<T>(qmax) + 1;
     const int k_lo = max(k_hi - (W - 1), Tr::KMIN);
     const int L0 = k_lo - 1;  // fixed-point unit 2^L0
+    // q = m * 2^(e1 - bias - frac) with e1 = max(field, 1) and m the significand (implicit bit
+    // included for normals); Q = floor(q / 2^L0) = (8 m) >> (C - e1), C - e1 >= 0 because
+    // q <= qmax < 2^(L0 + W + 1).
+    const int C = F::kBias + F::kFrac + 3 + L0;
 
-    // ---- fixed point (branch-free), vertical bit counters, per-row XOR of R = Q ^ (Q << 1)
-    Fix planes[Tr::PLANES];
-#pragma unroll
-    for (int pl = 0; pl < Tr::PLANES; ++pl) planes[pl] = 0;
-    Fix row_xor[ROWS];
+    // ---- fixed point with sticky bit, and per row the XOR of the fixed-point words
+    Fix X[ROWS];
 #pragma unroll
     for (int r = 0; r < ROWS; ++r) {
-        row_xor[r] = 0;
+        X[r] = 0;
 #pragma unroll
         for (int e = 0; e < V; ++e) {
-            const B qb = (B)qf[r * V + e];
-            const int field = (int)((qb & F::kExpMask) >> F::kFrac);
-            const Fix m = (Fix)(qb & F::kFracMask) | (field ? ((Fix)1 << F::kFrac) : (Fix)0);
-            // q = m * 2^(field' - bias - frac), field' = max(field, 1); Q = m * 2^sh, sh <= 3
-            const int sh = (field ? field : 1) - F::kBias - F::kFrac - L0;
-            const int up = sh > 0 ? sh : 0;
-            const int dn = sh < 0 ? min(-sh, FIXBITS - 1) : 0;
-            const Fix mm = m << up;
-            const Fix Q = mm >> dn;
-            const Fix sticky = (mm & (((Fix)1 << dn) - 1)) ? kSticky : (Fix)0;
-            qf[r * V + e] = Q | sticky;
-            Fix carry = Q;
-#pragma unroll
-            for (int pl = 0; pl < Tr::PLANES; ++pl) {
-                const Fix t = planes[pl] & carry;
-                planes[pl] ^= carry;
-                carry = t;
+            const Fix qb = qf[r * V + e];
+            const int e1 = max((int)(qb >> F::kFrac), 1);
+            const Fix mm = (qb << 3) - ((Fix)(e1 - 1) << (F::kFrac + 3));  // 8 m (exact modulo 2^FIXBITS)
+            const int dn = C - e1;
+            Fix Q, back;
+            if constexpr (sizeof(Fix) == 4) {
+                Q = __funnelshift_rc(mm, 0u, dn);    // mm >> dn, 0 once dn >= 32
+                back = __funnelshift_lc(0u, Q, dn);  // Q << dn, 0 once dn >= 32
+            } else {
+                Q = dn < 64 ? mm >> dn : 0;
+                back = dn < 64 ? Q << dn : 0;
             }
-            row_xor[r] ^= Q ^ (Q << 1);
+            const Fix qs = back != mm ? (Q | kSticky) : Q;
+            qf[r * V + e] = qs;
+            X[r] ^= qs;
         }
     }
-    // per-bit counts: planes -> counts, warp reduce, block accumulate
+    // ---- per-bit population counts: Harley-Seal vertical counters per thread, then one warp
+    // bit-transpose per counter plane puts bit b of every lane's plane into lane b
+    {
+        Fix acc[LOG_EPT + 1];
 #pragma unroll
-    for (int b = 0; b < W; ++b) {
-        unsigned c = 0;
+        for (int i = 0; i <= LOG_EPT; ++i) acc[i] = 0;
+        acc[LOG_EPT] = SealTree<LOG_EPT, 0>::run(qf, acc);
 #pragma unroll
-        for (int pl = 0; pl < Tr::PLANES; ++pl) c |= (unsigned)((planes[pl] >> b) & 1) << pl;
-        c = __reduce_add_sync(0xffffffffu, c);
-        if (lane == 0 && c) atomicAdd(&s_cnt[b], c);
+        for (int w = 0; w < (int)(sizeof(Fix) / 4); ++w) {
+            unsigned cnt = 0;
+#pragma unroll
+            for (int pl = 0; pl <= LOG_EPT; ++pl)
+                cnt += (unsigned)__popc(warp_transpose32((unsigned)(acc[pl] >> (32 * w)), lane)) << pl;
+            const int b = 32 * w + lane;
+            if (b < W && cnt) atomicAdd(&s_cnt[b], cnt);
+        }
     }
-    // exclusive prefix XOR in element order: row by row across lanes, then across warps
-    Fix lane_ex[ROWS];
+    // ---- exclusive prefix XOR of R = Q ^ (Q << 1) in element order: row by row across lanes,
+    // then across warps.  XOR is linear, so a row's R total is R of the row's XOR.
     Fix warp_total = 0;
 #pragma unroll
     for (int r = 0; r < ROWS; ++r) {
-        Fix incl = row_xor[r];
+        const Fix row = X[r] ^ (X[r] << 1);
+        Fix incl = row;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
             const Fix v = shfl_up_x(incl, o);
             if (lane >= o) incl ^= v;
         }
-        lane_ex[r] = warp_total ^ incl ^ row_xor[r];  // rows before r, then lanes before this one
+        s_lane_ex[r][tid] = warp_total ^ incl ^ row;  // rows before r, then lanes before this one
         warp_total ^= shfl_x(incl, 31);
     }
     if (lane == 0) s_warp_xor[warp] = warp_total;
     __syncthreads();
     Fix warp_prefix = 0;
     for (int w = 0; w < warp; ++w) warp_prefix ^= s_warp_xor[w];
-    // Lowest binade offset whose half-up sum could still fit inside one binade (< 2^(P+1)).
-    if (tid == 0) {
-        int jmin = W + 1;
-        uint64_t Wj = 0;
-        for (int j = W; j >= 1; --j) {
-            if (j < W) Wj = 2 * Wj + s_cnt[j];
-            if (Wj >= Tr::SAT || Wj + s_cnt[j - 1] >= (2ull << Tr::P)) break;  // sums only grow as j falls
-            jmin = j;
+    // Per binade offset j (binade k = k_lo + j - 1): W_j = sum over bits b >= j of cnt[b] 2^(b-j)
+    // (the chunk's sum of floor(Q / 2^j), saturated), one lane per j with independent terms.
+    // jmin: the lowest j from which on every half-up sum W_j + cnt[j-1] still fits inside one
+    // binade (< 2^(P+1)); the sums only grow as j falls, so the failing j form a prefix.
+    if (warp == 0) {
+        int fail_max = 0;
+#pragma unroll
+        for (int h = 0; h < (W + 31) / 32; ++h) {
+            const int j = 1 + lane + 32 * h;
+            uint64_t wj = 0;
+            if (j <= W) {
+#pragma unroll
+                for (int b = 1; b < W; ++b) {
+                    if (b < j) continue;
+                    const uint64_t c = s_cnt[b];
+                    const int sh = b - j;
+                    const uint64_t term = c >= ((uint64_t)Tr::SAT >> sh) ? (uint64_t)Tr::SAT : c << sh;  // sh < 62
+                    wj = min(wj + term, (uint64_t)Tr::SAT);
+                }
+                s_W[j] = wj;
+                if (wj >= Tr::SAT || wj + s_cnt[j - 1] >= (2ull << Tr::P)) fail_max = j;
+            }
         }
-        s_jmin = jmin;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) fail_max = max(fail_max, __shfl_xor_sync(0xffffffffu, fail_max, o));
+        if (lane == 0) s_jmin = fail_max + 1;
     }
     __syncthreads();
     const int jmin = s_jmin;
 
-    // ---- ties at the usable binades, with the parity of the half-up increments in front
-    const Fix qmask = (Fix)~kSticky;
+    // ---- ties at the usable binades: a word whose lowest set bit is at or above jmin - 1 and
+    // that has no sticky bit (rare), with the parity of the half-up increments in front of it
+    const Fix tiemask = (((Fix)1 << (jmin - 1)) - 1) | kSticky;
+    bool cand = false;
 #pragma unroll
-    for (int r = 0; r < ROWS; ++r) {
-        Fix prefix = warp_prefix ^ lane_ex[r];
+    for (int i = 0; i < EPT; ++i) cand |= qf[i] != 0 && (qf[i] & tiemask) == 0;
+    if (cand) {
 #pragma unroll
-        for (int e = 0; e < V; ++e) {
-            const Fix qs = qf[r * V + e];
-            const Fix Q = qs & qmask;
-            const int j = sizeof(Fix) == 4 ? __ffs((int)Q) : __ffsll((long long)Q);  // lowest bit + 1
-            if (Q && !(qs & kSticky) && j >= jmin && j <= W) {
-                const unsigned slot = atomicAdd(&s_tie_count, 1u);
-                if (slot < (unsigned)kMaxTies) {
-                    Tie t;
-                    t.index = (uint32_t)CM::index(warp, r, lane, e);
-                    t.j = (uint16_t)j;
-                    t.mpar = (uint8_t)((j < FIXBITS) ? ((Q >> j) & 1) : 0);
-                    t.pi = (uint8_t)((j < FIXBITS) ? ((prefix >> j) & 1) : 0);
-                    s_ties[slot] = t;
+        for (int r = 0; r < ROWS; ++r) {
+            Fix prefix = warp_prefix ^ s_lane_ex[r][tid];
+#pragma unroll
+            for (int e = 0; e < V; ++e) {
+                const Fix qs = qf[r * V + e];
+                if (qs != 0 && (qs & tiemask) == 0) {
+                    const int j = sizeof(Fix) == 4 ? __ffs((int)qs) : __ffsll((long long)qs);  // lowest bit + 1
+                    const unsigned slot = atomicAdd(&s_tie_count, 1u);
+                    if (slot < (unsigned)kMaxTies) {
+                        Tie t;
+                        t.index = (uint32_t)CM::index(warp, r, lane, e);
+                        t.j = (uint16_t)j;
+                        t.mpar = (uint8_t)((qs >> j) & 1);
+                        t.pi = (uint8_t)((prefix >> j) & 1);
+                        s_ties[slot] = t;
+                    }
                 }
+                prefix ^= qs ^ (qs << 1);
             }
-            prefix ^= Q ^ (Q << 1);
         }
     }
     __syncthreads();
@@ -426,11 +510,7 @@ __global__ void __launch_bounds__(256) mse_chunk_kernel(const T *prediction, con
     // ---- one thread per binade: half-up sum from the counts, then the tie corrections
     if (tid < W) {
         const int j = tid + 1;  // binade k = k_lo + tid
-        uint64_t Wj = 0;
-        for (int b = W - 1; b >= j; --b) {
-            Wj = 2 * Wj + s_cnt[b];
-            if (Wj >= Tr::SAT) { Wj = Tr::SAT; break; }
-        }
+        const uint64_t Wj = s_W[j];
         const bool usable = Wj < Tr::SAT && j >= jmin;
         const uint64_t half_up = usable ? Wj + s_cnt[j - 1] : Tr::SAT;
         int64_t corr[2] = {0, 0};
@@ -529,67 +609,72 @@ __global__ void __launch_bounds__(64) mse_block_kernel(const MseHead *heads, con
     out[1] = valid ? sat_d<T>(D[1]) : no_map<T>();
 }
 
-// Apply a map to s if the binade's window covers s and the result stays inside the binade.
+// One map (chunk or block) at the binade of the state: x -> x + D[x mod 2].  `ok` is false when
+// the map cannot be used there (its window does not reach down to k, the chunk must be resolved
+// element by element, or a Subtract/Multiply fault lies in it).
+struct MapStep {
+    uint64_t d0, d1;
+    bool ok;
+};
+
 template <typename T>
-__device__ __forceinline__ bool apply_map(const MseHead &h, const typename MseTraits<T>::D *deltas, T &s) {
+__device__ __forceinline__ MapStep map_at(const MseHead &h, const typename MseTraits<T>::D *row, int k) {
     using Tr = MseTraits<T>;
-    constexpr int W = Tr::W;
-    if (h.flags & (kHeadExact | kHeadFault)) return false;
-    if (h.flags & kHeadZero) return true;
+    MapStep m{0, 0, true};
+    if (h.flags & (kHeadExact | kHeadFault)) { m.ok = false; return m; }
+    if ((h.flags & kHeadZero) || k > h.k_lo + Tr::W - 1) return m;  // identity: every square < half an ulp
+    if (k < h.k_lo) { m.ok = false; return m; }
+    const typename Tr::D a = row[(size_t)(k - h.k_lo) * 2], b = row[(size_t)(k - h.k_lo) * 2 + 1];
+    if (a == no_map<T>() || b == no_map<T>()) { m.ok = false; return m; }
+    m.d0 = a;
+    m.d1 = b;
+    return m;
+}
+
+// Warp 0: apply as many of the `avail` (<= 32) consecutive maps starting at `first` as keep the
+// state inside its binade, all at once: lane i loads map first + i at the state's binade, an
+// inclusive scan composes the maps (first L, then R: D[p] = L[p] + R[(p + L[p]) mod 2]), and the
+// leading lanes whose state stays below 2^(P+1) are applied.  Returns how many were applied.
+template <typename T>
+__device__ __forceinline__ unsigned apply_maps(const MseHead *heads, const typename MseTraits<T>::D *deltas,
+                                               uint64_t first, unsigned avail, T &s, int lane) {
+    using Tr = MseTraits<T>;
     uint64_t x;
     int k;
     state_of<T>(s, x, k);
-    if (k > h.k_lo + W - 1) return true;  // identity: every square < half an ulp
-    if (k < h.k_lo) return false;
-    const typename Tr::D d = deltas[(size_t)(k - h.k_lo) * 2 + (x & 1)];
-    if (d == no_map<T>()) return false;
-    const uint64_t nx = x + d;
-    if (nx >= (2ull << Tr::P)) return false;  // would leave the binade (or overflow)
-    s = value_of<T>(nx, k);
-    return true;
-}
-
-// Summaries the walker stages in shared memory: one head and W increment pairs per map.
-template <typename T> struct WalkSmem {
-    using Tr = MseTraits<T>;
-    using D = typename Tr::D;
-    static constexpr int BATCH = 32;  // block maps staged per batch
-    static constexpr size_t MAP_BYTES = sizeof(MseHead) + (size_t)Tr::W * 2 * sizeof(D);
-    static constexpr size_t SQ_OFF = 0;
-    static constexpr size_t BLOCKS_OFF = SQ_OFF + (size_t)Tr::CHUNK * sizeof(T);
-    static constexpr size_t CHUNKS_OFF = BLOCKS_OFF + BATCH * MAP_BYTES;
-    static constexpr size_t BYTES = CHUNKS_OFF + (size_t)kBlockChunks * MAP_BYTES;
-};
-
-// Copy `count` maps (heads and increment rows) starting at `first` into shared memory.
-template <typename T>
-__device__ __forceinline__ void stage_maps(const MseHead *heads, const typename MseTraits<T>::D *deltas,
-                                           uint64_t first, unsigned count, unsigned char *dst) {
-    using Tr = MseTraits<T>;
-    using D = typename Tr::D;
-    auto *h = reinterpret_cast<MseHead *>(dst);
-    auto *d = reinterpret_cast<D *>(dst + count * sizeof(MseHead));  // rows follow the heads
-    for (unsigned i = threadIdx.x; i < count; i += blockDim.x) h[i] = heads[first + i];
-    // at most kBlockChunks rows: a fixed, unrolled trip count keeps every load in flight at once
-    const unsigned words = count * Tr::W * 2;
-    constexpr unsigned kMaxWords = (unsigned)kBlockChunks * Tr::W * 2;
-#pragma unroll
-    for (unsigned r = 0; r < (kMaxWords + 255) / 256; ++r) {
-        const unsigned i = threadIdx.x + r * 256;
-        if (i < words) d[i] = deltas[first * Tr::W * 2 + i];
+    MapStep m{0, 0, false};
+    if ((unsigned)lane < avail) {
+        const MseHead h = heads[first + lane];
+        m = map_at<T>(h, deltas + (first + lane) * (size_t)Tr::W * 2, k);
     }
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const unsigned long long l0 = __shfl_up_sync(0xffffffffu, (unsigned long long)m.d0, o);
+        const unsigned long long l1 = __shfl_up_sync(0xffffffffu, (unsigned long long)m.d1, o);
+        const bool lok = __shfl_up_sync(0xffffffffu, (int)m.ok, o) != 0;
+        if (lane >= o) {
+            const uint64_t n0 = l0 + (((0 + l0) & 1) ? m.d1 : m.d0);
+            const uint64_t n1 = l1 + (((1 + l1) & 1) ? m.d1 : m.d0);
+            m.d0 = n0;
+            m.d1 = n1;
+            m.ok = m.ok && lok;
+        }
+    }
+    const uint64_t nx = x + ((x & 1) ? m.d1 : m.d0);
+    const bool good = m.ok && nx < (2ull << Tr::P);  // the state only grows: the last one decides
+    const unsigned bad = __ballot_sync(0xffffffffu, !good);
+    const unsigned applied = bad ? (unsigned)(__ffs((int)bad) - 1) : 32u;
+    if (applied) s = value_of<T>(__shfl_sync(0xffffffffu, (unsigned long long)nx, (int)applied - 1), k);
+    return applied;
 }
 
-template <typename T>
-__device__ __forceinline__ bool apply_staged(const unsigned char *base, unsigned count, unsigned i, T &s) {
-    using Tr = MseTraits<T>;
-    using D = typename Tr::D;
-    const auto *h = reinterpret_cast<const MseHead *>(base);
-    const auto *d = reinterpret_cast<const D *>(base + count * sizeof(MseHead));
-    return apply_map<T>(h[i], d + (size_t)i * Tr::W * 2, s);
-}
-
-enum : int { kReqDone = 0, kReqBlocks = 1, kReqChunks = 2, kReqResolve = 3 };
+// Squares of a chunk being resolved, transposed so that thread t's PER consecutive elements sit
+// in one column: element c -> slot (c mod PER) * SQ_PITCH + c / PER.  The odd pitch keeps both
+// the coalesced fill (consecutive c) and the owners' reads (consecutive t) free of bank conflicts.
+template <typename T> struct ResolveLayout {
+    static constexpr int PER = MseTraits<T>::CHUNK / 256;
+    static constexpr int SQ_PITCH = 257;
+};
 
 template <typename T>
 __global__ void __launch_bounds__(256) mse_walk_kernel(const T *prediction, const T *target, uint64_t n,
@@ -600,25 +685,19 @@ __global__ void __launch_bounds__(256) mse_walk_kernel(const T *prediction, cons
                                                        T *out, unsigned long long *status) {
     using Tr = MseTraits<T>;
     using F = Fmt<T>;
-    using SM = WalkSmem<T>;
-    constexpr int PER = Tr::CHUNK / 256;
+    using RL = ResolveLayout<T>;
+    constexpr int PER = RL::PER, PITCH = RL::SQ_PITCH;
     constexpr uint64_t BLOCK_ELEMS = (uint64_t)kBlockChunks * Tr::CHUNK;
-    extern __shared__ __align__(16) unsigned char walk_smem[];
-    T *sq = reinterpret_cast<T *>(walk_smem + SM::SQ_OFF);
-    unsigned char *staged_blocks = walk_smem + SM::BLOCKS_OFF;
-    unsigned char *staged_chunks = walk_smem + SM::CHUNKS_OFF;
-    __shared__ int s_req;
-    __shared__ uint64_t s_arg;
-    __shared__ unsigned s_arg_count;
-    __shared__ int s_done;  // 2: overflow recorded
+    constexpr uint64_t TOP = 2ull << Tr::P;  // a state at or above this has left its binade
+    __shared__ T sq[PER * PITCH];
     __shared__ T s_sum;
-    __shared__ uint64_t s_x;
-    __shared__ int s_k;
-    __shared__ unsigned s_pos, s_stop;
+    __shared__ uint64_t s_g;       // elements [0, s_g) of the segment are summed into s_sum
+    __shared__ uint64_t s_arg;     // chunk to resolve, or ~0 when the walk is done
+    __shared__ int s_done;         // 2: overflow recorded
+    __shared__ unsigned s_pos, s_stop[2];
     __shared__ uint64_t s_warp_sum[8];
-    __shared__ uint64_t s_xstop;
 
-    // every Subtract/Multiply fault is already in the status word; the walk stops in front of
+    // Every Subtract/Multiply fault is already in the status word; the walk stops in front of
     // the earliest one, so only earlier Adds can still report (their events are smaller).  The
     // segment holds global elements [base, base + n); a fault in front of it stops it at once.
     const unsigned long long st0 = read_status(status);
@@ -627,113 +706,75 @@ __global__ void __launch_bounds__(256) mse_walk_kernel(const T *prediction, cons
         const uint64_t first = (st0 >> 3) / 3;
         stop = first < base ? 0 : (first - base < n ? first - base : n);
     }
+    // chunk / block maps cover whole chunks and blocks (the last ones end at n)
+    const uint64_t map_chunks = stop == n ? chunks : stop / Tr::CHUNK;
+    const uint64_t map_blocks = stop == n ? blocks : stop / BLOCK_ELEMS;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
     if (tid == 0) {
         s_sum = carry_in ? *carry_in : T(0);
+        s_g = 0;
         s_done = 0;
     }
     __syncthreads();
-    // thread 0's cursor
-    uint64_t blk = 0, chunk = 0, batch0 = 0;
-    unsigned batch_count = 0;
-    bool in_block = false, chunks_staged = false;
     for (;;) {
-        if (tid == 0) {
+        if (warp == 0) {  // maps as far as they reach; then the chunk to resolve, if any
             T s = s_sum;
-            int req = kReqDone;
-            for (;;) {
-                if (!in_block) {
-                    if (blk >= blocks || blk * BLOCK_ELEMS >= stop) break;  // done
-                    if (blk >= batch0 + batch_count) {  // stage the next batch of block maps
-                        batch0 = blk;
-                        batch_count = (unsigned)min((uint64_t)SM::BATCH, blocks - blk);
-                        req = kReqBlocks;
-                        s_arg = batch0;
-                        s_arg_count = batch_count;
-                        break;
-                    }
-                    if ((blk + 1) * BLOCK_ELEMS <= stop &&
-                        apply_staged<T>(staged_blocks, batch_count, (unsigned)(blk - batch0), s)) {
-                        ++blk;
-                        continue;
-                    }
-                    in_block = true;
-                    chunks_staged = false;
-                    chunk = blk * kBlockChunks;
+            uint64_t g = s_g, arg = ~0ull;
+            while (g < stop) {
+                if (g % BLOCK_ELEMS == 0 && g / BLOCK_ELEMS < map_blocks) {
+                    const uint64_t b = g / BLOCK_ELEMS;
+                    const unsigned avail = (unsigned)min((uint64_t)32, map_blocks - b);
+                    const unsigned m = apply_maps<T>(bheads, bdeltas, b, avail, s, lane);
+                    g = min(g + m * BLOCK_ELEMS, n);
+                    if (m == avail) continue;
                 }
-                const uint64_t cfirst = blk * kBlockChunks;
-                const uint64_t cend = cfirst + kBlockChunks < chunks ? cfirst + kBlockChunks : chunks;
-                if (!chunks_staged) {
-                    chunks_staged = true;
-                    req = kReqChunks;
-                    s_arg = cfirst;
-                    s_arg_count = (unsigned)(cend - cfirst);
-                    break;
+                const uint64_t c = g / Tr::CHUNK;
+                const uint64_t block_end = (c / kBlockChunks + 1) * kBlockChunks;
+                const uint64_t lim = min(block_end, map_chunks);
+                if (c < lim) {
+                    const unsigned avail = (unsigned)min((uint64_t)32, lim - c);
+                    const unsigned m = apply_maps<T>(heads, deltas, c, avail, s, lane);
+                    g = min(g + m * Tr::CHUNK, n);
+                    if (m) continue;
                 }
-                if (chunk >= cend) {
-                    in_block = false;
-                    ++blk;
-                    continue;
-                }
-                if (chunk * Tr::CHUNK >= stop) break;  // done
-                if ((chunk + 1) * Tr::CHUNK <= stop &&
-                    apply_staged<T>(staged_chunks, (unsigned)(cend - cfirst), (unsigned)(chunk - cfirst), s)) {
-                    ++chunk;
-                    continue;
-                }
-                req = kReqResolve;  // resolve this chunk element by element
-                s_arg = chunk;
-                ++chunk;
+                arg = c;  // this chunk needs the element-by-element resolution
                 break;
             }
-            s_sum = s;
-            s_req = req;
+            if (lane == 0) {
+                s_sum = s;
+                s_g = g;
+                s_arg = arg;
+            }
         }
         __syncthreads();
-        const int req = s_req;
-        if (req == kReqDone) break;
-        if (req == kReqBlocks) {
-            stage_maps<T>(bheads, bdeltas, s_arg, s_arg_count, staged_blocks);
-            __syncthreads();
-            continue;
-        }
-        if (req == kReqChunks) {
-            stage_maps<T>(heads, deltas, s_arg, s_arg_count, staged_chunks);
-            __syncthreads();
-            continue;
-        }
+        if (s_arg == ~0ull) break;
+
         // ---- resolve one chunk: recompute its squares (all fault-free in front of `stop`)
         const uint64_t i0 = s_arg * Tr::CHUNK;
         const unsigned len = (unsigned)((i0 + Tr::CHUNK < stop ? i0 + Tr::CHUNK : stop) - i0);
-        // fixed trip count, unrolled: all of a thread's loads are in flight together
 #pragma unroll
         for (int e = 0; e < PER; ++e) {
             const unsigned c = (unsigned)tid + (unsigned)e * 256;
             if (c < len) {
                 const T d = F::sub(prediction[i0 + c], target[i0 + c]);
-                sq[c] = F::mul(d, d);
+                sq[(c % PER) * PITCH + c / PER] = F::mul(d, d);
             }
         }
-        if (tid == 0) s_pos = 0;
+        if (tid == 0) {
+            s_pos = 0;
+            s_stop[0] = s_stop[1] = len;
+        }
         __syncthreads();
         // Apply every element in front of the first tie or binade crossing at once (prefix sums of
         // half-up increments), then add that element exactly; repeat.
-        for (;;) {
+        const unsigned c0 = (unsigned)tid * PER;  // this thread's elements [c0, c0 + PER)
+        for (int it = 0;; it ^= 1) {
             const unsigned pos = s_pos;
             if (pos >= len) break;
-            if (tid == 0) {
-                uint64_t x;
-                int k;
-                state_of<T>(s_sum, x, k);
-                s_x = x;
-                s_k = k;
-                s_stop = len;
-            }
-            __syncthreads();
-            const uint64_t x = s_x;
-            const int k = s_k;
-            const unsigned c0 = pos + (unsigned)tid * PER;
+            uint64_t x;
+            int k;
+            state_of<T>(s_sum, x, k);
             uint64_t inc[PER];
             uint64_t local = 0;
             unsigned first_tie = len;
@@ -741,8 +782,8 @@ __global__ void __launch_bounds__(256) mse_walk_kernel(const T *prediction, cons
             for (int e = 0; e < PER; ++e) {
                 const unsigned c = c0 + e;
                 bool tie = false;
-                inc[e] = c < len ? half_up_increment<T>(sq[c < len ? c : 0], k, tie) : 0;
-                if (tie && c < len && first_tie == len) first_tie = c;
+                inc[e] = (c >= pos && c < len) ? half_up_increment<T>(sq[e * PITCH + tid], k, tie) : 0;
+                if (tie && c >= pos && c < len && first_tie == len) first_tie = c;
                 local = min(local + inc[e], (uint64_t)Tr::SAT);
             }
             // exclusive prefix sum of thread totals (element order = thread order)
@@ -765,27 +806,22 @@ __global__ void __launch_bounds__(256) mse_walk_kernel(const T *prediction, cons
 #pragma unroll
             for (int e = 0; e < PER; ++e) {
                 const unsigned c = c0 + e;
-                if (c < len && c < mine && run + inc[e] >= (2ull << Tr::P)) mine = c;
+                if (c >= pos && c < len && c < mine && run + inc[e] >= TOP) mine = c;
                 run = min(run + inc[e], (uint64_t)Tr::SAT);
             }
-            if (mine < len) atomicMin(&s_stop, mine);
+            if (mine < len) atomicMin(&s_stop[it], mine);
             __syncthreads();
-            const unsigned cut = s_stop;
-            // the owner of `cut` (or the last thread) publishes the state in front of it
-            if (cut >= c0 && cut < c0 + PER) {
+            const unsigned cut = s_stop[it];
+            // the owner of `cut` (the last thread when nothing stops) publishes the state there,
+            // adds that element exactly, and moves the cursor
+            if ((cut < len && cut >= c0 && cut < c0 + PER) || (cut == len && tid == 255)) {
                 uint64_t r = x + before;
 #pragma unroll
                 for (int e = 0; e < PER; ++e)
                     if (c0 + e < cut) r += inc[e];
-                s_xstop = r;
-            } else if (cut == len && tid == 255) {
-                s_xstop = x + before + local;
-            }
-            __syncthreads();
-            if (tid == 0) {
-                T s = value_of<T>(s_xstop, k);
+                T s = value_of<T>(r, k);
                 if (cut < len) {
-                    const T t = F::add(s, sq[cut]);
+                    const T t = F::add(s, sq[(cut % PER) * PITCH + cut / PER]);
                     if (nonfinite_bits<T>(F::bits(t))) {
                         record_fault(status, (base + i0 + cut) * 3 + 2, kOverflow);
                         s_done = 2;
@@ -798,9 +834,12 @@ __global__ void __launch_bounds__(256) mse_walk_kernel(const T *prediction, cons
                     s_pos = len;
                 }
                 s_sum = s;
+                s_stop[it ^ 1] = len;  // armed for the next iteration
             }
             __syncthreads();
         }
+        if (tid == 0) s_g = s_done == 2 ? stop : i0 + len;
+        __syncthreads();
         if (s_done == 2) break;
     }
     if (tid == 0) {
@@ -897,16 +936,7 @@ int walk_mse(int policy, const T *p, const T *t, uint64_t n, uint64_t base, uint
     auto *deltas = reinterpret_cast<D *>(ws + lay.deltas_off);
     auto *bheads = reinterpret_cast<MseHead *>(ws + lay.bheads_off);
     auto *bdeltas = reinterpret_cast<D *>(ws + lay.bdeltas_off);
-    static bool configured[64] = {false};
-    int device = 0;
-    cudaGetDevice(&device);
-    if (device >= 0 && device < 64 && !configured[device]) {
-        cudaError_t e = cudaFuncSetAttribute(mse_walk_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)WalkSmem<T>::BYTES);
-        if (e != cudaSuccess) return pcu_host::set_cuda_error(e);
-        configured[device] = true;
-    }
-    mse_walk_kernel<T><<<1, 256, WalkSmem<T>::BYTES, stream>>>(p, t, n, heads, deltas, bheads, bdeltas, lay.chunks,
+    mse_walk_kernel<T><<<1, 256, 0, stream>>>(p, t, n, heads, deltas, bheads, bdeltas, lay.chunks,
                                                                lay.blocks, base, total, count_value<T>(total), policy,
                                                                carry_in, carry_out, out, status);
     return pcu_host::launch_status();

@@ -3,7 +3,7 @@
   python fusion-pcu_b200/profile_cases.py matmul --m 8192 --n 8192 --k 1024 [--dtype f32|f64]
          [--layout nn|tn|nt|tt] [--policy 0|1|2] [--repeat R]
   python fusion-pcu_b200/profile_cases.py sgd --count 67108864 [--repeat R]
-  python fusion-pcu_b200/profile_cases.py mse --count 67108864 [--repeat R]
+  python fusion-pcu_b200/profile_cases.py mse --count 67108864 [--repeat R] [--phases]
 
 Each run prints the CUDA-event time per call; it checks that the status word stayed clean.
 """
@@ -36,6 +36,7 @@ def main():
     ap.add_argument("--layout", default="nn", choices=["nn", "tn", "nt", "tt"])
     ap.add_argument("--policy", type=int, default=0)
     ap.add_argument("--repeat", type=int, default=2)
+    ap.add_argument("--phases", action="store_true", help="mse: also time the prepare and walk phases")
     args = ap.parse_args()
 
     import torch
@@ -83,6 +84,19 @@ def main():
     assert word == pcu.STATUS_OK, hex(word)
     scale = 1e12 if unit == "TFLOP/s" else 1e9
     print(f"{args.case} {args.dtype} {ms:.3f} ms/call  {work / (ms * 1e-3) / scale:.2f} {unit}")
+    if args.case == "mse" and args.phases:
+        # the two phases through the segment form: bandwidth-bound maps, then the ordered walk
+        carry = torch.zeros(1, dtype=dt, device="cuda")
+        for name, fn in (("prepare", lambda: pcu.strict_mse_segment_prepare(p, t, 0, args.policy, status=status,
+                                                                             workspace=ws)),
+                         ("walk", lambda: pcu.strict_mse_segment_walk(p, t, 0, args.count, carry.zero_(), ws,
+                                                                      status, args.policy, out=out))):
+            e0.record()
+            for _ in range(args.repeat):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            print(f"  {name} {e0.elapsed_time(e1) / args.repeat:.3f} ms/call")
 
 
 if __name__ == "__main__":
