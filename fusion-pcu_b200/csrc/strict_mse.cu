@@ -51,7 +51,7 @@
 #include "pcu_b200.h"
 
 #ifndef PCU_MSE_MIN_BLOCKS_F32
-#define PCU_MSE_MIN_BLOCKS_F32 3
+#define PCU_MSE_MIN_BLOCKS_F32 4
 #endif
 
 namespace pcu {
@@ -190,7 +190,7 @@ template <typename X> __device__ __forceinline__ X shfl_x(X v, int src) {
 // Element layout of a chunk: warp w owns a contiguous span of 32*V*ROWS elements; in row r
 // lane l owns V consecutive elements (one 16-byte load per row, coalesced across the warp).
 template <typename T> struct ChunkMap {
-    static constexpr int V = 16 / sizeof(T);
+    static constexpr int V = 32 / sizeof(T);
     static constexpr int ROWS = MseTraits<T>::EPT / V;
     static constexpr int WARP_SPAN = 32 * V * ROWS;
     __device__ static __forceinline__ int index(int warp, int row, int lane, int e) {
@@ -246,23 +246,51 @@ template <int BASE> struct SealTree<1, BASE> {
     }
 };
 
+// Ask the L2 to fetch [p, p + bytes) ahead of its use (a hint: no destination, no completion).
+__device__ __forceinline__ void prefetch_l2(const void *p, unsigned bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // 32 x 32 bit-matrix transpose across a warp: on return lane b holds, in bit l, bit b of lane
-// l's input word (five butterfly stages, each swapping the off-diagonal blocks).
+// l's input word.  Five butterfly stages swap the off-diagonal blocks: the 16- and 8-bit
+// stages are byte permutes, the 4-, 2- and 1-bit stages a rotation and a masked merge (the
+// rotated-in bits always land in positions the mask drops).
 __device__ __forceinline__ unsigned warp_transpose32(unsigned x, int lane) {
+    unsigned y = __shfl_xor_sync(0xffffffffu, x, 16);
+    x = __byte_perm(x, y, (lane & 16) ? 0x3276 : 0x5410);
+    y = __shfl_xor_sync(0xffffffffu, x, 8);
+    x = __byte_perm(x, y, (lane & 8) ? 0x3715 : 0x6240);
 #pragma unroll
-    for (int h = 16; h; h >>= 1) {
-        const unsigned m = h == 16 ? 0x0000ffffu : h == 8 ? 0x00ff00ffu : h == 4 ? 0x0f0f0f0fu
-                         : h == 2 ? 0x33333333u : 0x55555555u;  // bit positions with (index & h) == 0
-        const unsigned y = __shfl_xor_sync(0xffffffffu, x, h);
-        x = (lane & h) ? ((x & ~m) | ((y >> h) & m)) : ((x & m) | ((y << h) & ~m));
+    for (int h = 4; h; h >>= 1) {
+        const unsigned m = h == 4 ? 0x0f0f0f0fu : h == 2 ? 0x33333333u : 0x55555555u;  // (index & h) == 0
+        const bool hi = lane & h;
+        y = __shfl_xor_sync(0xffffffffu, x, h);
+        const unsigned t = __funnelshift_r(y, y, hi ? h : 32 - h);  // hi: y >> h, lo: y << h (rotations)
+        const unsigned keep = hi ? ~m : m;
+        x = (x & keep) | (t & ~keep);
     }
     return x;
+}
+
+// Fixed-point form of one square (bits qb, finite, >= +0): Q = floor(q / 2^L0) given
+// C = bias + frac + 3 + L0 and K = (1 - C) * 2^(frac + 3).  q = m * 2^(e1 - bias - frac) with
+// e1 = max(field, 1) and m its significand; Q = (8 m) >> (C - e1) (C - e1 >= 0 for q <= qmax).
+template <typename T>
+__device__ __forceinline__ typename MseTraits<T>::Fix fixed_point(typename MseTraits<T>::Fix qb, int C,
+                                                                  typename MseTraits<T>::Fix K) {
+    using F = Fmt<T>;
+    using Fix = typename MseTraits<T>::Fix;
+    const int field = (int)(qb >> F::kFrac);
+    const int dn = min(C - field, C - 1);                              // C - e1
+    const Fix mm = qb * (Fix)8 + K + (Fix)dn * ((Fix)1 << (F::kFrac + 3));  // 8 m, exact modulo 2^bits
+    if constexpr (sizeof(Fix) == 4) return __funnelshift_rc(mm, 0u, dn);   // 0 once dn >= 32
+    else return dn < 64 ? mm >> dn : 0;
 }
 
 template <typename T>
 __global__ void __launch_bounds__(256, MseTraits<T>::MIN_BLOCKS)
 mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base, bool vec, int policy,
-                 MseHead *heads, typename MseTraits<T>::D *deltas, unsigned long long *status) {
+                 uint64_t ahead, MseHead *heads, typename MseTraits<T>::D *deltas, unsigned long long *status) {
     using Tr = MseTraits<T>;
     using F = Fmt<T>;
     using B = typename F::Bits;
@@ -271,11 +299,10 @@ mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base
     constexpr int EPT = Tr::EPT, W = Tr::W, V = CM::V, ROWS = CM::ROWS;
     constexpr int LOG_EPT = EPT == 32 ? 5 : 4;
     static_assert((1 << LOG_EPT) == EPT && LOG_EPT + 1 == Tr::PLANES, "counter planes");
-    constexpr int FIXBITS = sizeof(Fix) * 8;
-    constexpr Fix kSticky = (Fix)1 << (FIXBITS - 1);
     // |d| below 2^-62 (binary32) / 2^-510 (binary64) may square to <= the smallest normal
     constexpr B kTinyDiff = sizeof(T) == 4 ? (B)(127 - 62) << 23 : (B)(1023 - 510) << 52;
     using VT = typename std::conditional<sizeof(T) == 4, float4, double2>::type;
+    constexpr int VW = 16 / sizeof(T);  // elements per 16-byte load
 
     __shared__ unsigned int s_fault;
     __shared__ unsigned long long s_qmax;
@@ -293,6 +320,16 @@ mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base
         s_fault = 0xffffffffu;
         s_qmax = 0;
         s_tie_count = 0;
+        // the chunk that will run `ahead` CTAs later (one wave of resident CTAs): its operands
+        // come from L2 instead of HBM when it starts
+        const uint64_t next = chunk0 + ahead * Tr::CHUNK;
+        if (vec && next < n) {
+            const unsigned bytes = (unsigned)(min((uint64_t)Tr::CHUNK, n - next) * sizeof(T)) & ~15u;
+            if (bytes) {
+                prefetch_l2(prediction + next, bytes);
+                prefetch_l2(target + next, bytes);
+            }
+        }
     }
     if (tid < W) s_cnt[tid] = 0;
     __syncthreads();
@@ -305,35 +342,39 @@ mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base
     // later events cannot win).
     Fix qf[EPT];  // q's bits first, its fixed-point form later; qf[row * V + e]
     B qmax_t = 0, dmin = ~(B)0;
-    const bool full = vec && chunk0 + Tr::CHUNK <= n;  // every row in range: no per-row guard
+    const uint64_t t0 = chunk0 + CM::index(warp, 0, lane, 0);  // this thread's first element
+    const T *pp = prediction + t0;
+    const T *tp = target + t0;
+    if (vec && chunk0 + Tr::CHUNK <= n) {  // whole chunk in range, 16-byte aligned operands
 #pragma unroll
-    for (int r = 0; r < ROWS; ++r) {
-        const uint64_t i0 = chunk0 + CM::index(warp, r, lane, 0);
-        T pv[V], tv[V];
-        if (full || (vec && i0 + V <= n)) {  // 16-byte loads only when both operands are 16-byte aligned
-            const VT a = __ldcs(reinterpret_cast<const VT *>(prediction + i0));
-            const VT b = __ldcs(reinterpret_cast<const VT *>(target + i0));
+        for (int r = 0; r < ROWS; ++r)
+#pragma unroll
+            for (int v = 0; v < V / VW; ++v) {
+                const VT a = __ldcs(reinterpret_cast<const VT *>(pp + r * 32 * V + v * VW));
+                const VT b = __ldcs(reinterpret_cast<const VT *>(tp + r * 32 * V + v * VW));
+#pragma unroll
+                for (int e = 0; e < VW; ++e) {
+                    const T d = F::sub(reinterpret_cast<const T *>(&a)[e], reinterpret_cast<const T *>(&b)[e]);
+                    const B qb = F::bits(F::mul(d, d));
+                    qmax_t = qb > qmax_t ? qb : qmax_t;
+                    const B dd = F::bits(d) * 2 - 1;  // |d| doubled minus one: +-0 becomes all ones
+                    dmin = dd < dmin ? dd : dmin;
+                    qf[r * V + v * VW + e] = (Fix)qb;
+                }
+            }
+    } else {
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r)
 #pragma unroll
             for (int e = 0; e < V; ++e) {
-                pv[e] = reinterpret_cast<const T *>(&a)[e];
-                tv[e] = reinterpret_cast<const T *>(&b)[e];
+                const uint64_t i = t0 + r * 32 * V + e;
+                const T d = i < n ? F::sub(prediction[i], target[i]) : T(0);
+                const B qb = F::bits(F::mul(d, d));
+                qmax_t = qb > qmax_t ? qb : qmax_t;
+                const B dd = F::bits(d) * 2 - 1;
+                dmin = dd < dmin ? dd : dmin;
+                qf[r * V + e] = (Fix)qb;
             }
-        } else {
-#pragma unroll
-            for (int e = 0; e < V; ++e) {
-                pv[e] = i0 + e < n ? prediction[i0 + e] : T(0);
-                tv[e] = i0 + e < n ? target[i0 + e] : T(0);
-            }
-        }
-#pragma unroll
-        for (int e = 0; e < V; ++e) {
-            const T d = F::sub(pv[e], tv[e]);
-            const B qb = F::bits(F::mul(d, d));
-            qmax_t = qb > qmax_t ? qb : qmax_t;
-            const B dd = F::bits(d) * 2 - 1;  // |d| doubled minus one: +-0 becomes all ones
-            dmin = dd < dmin ? dd : dmin;
-            qf[r * V + e] = (Fix)qb;
-        }
     }
     if (qmax_t >= F::kExpMask || (policy != kPolicyGradual && dmin < kTinyDiff * 2 - 1)) {
         // rare: reload and redo this thread's elements with the checked law
@@ -375,33 +416,23 @@ mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base
     const int k_hi = exponent_of<T>(qmax) + 1;
     const int k_lo = max(k_hi - (W - 1), Tr::KMIN);
     const int L0 = k_lo - 1;  // fixed-point unit 2^L0
-    // q = m * 2^(e1 - bias - frac) with e1 = max(field, 1) and m the significand (implicit bit
-    // included for normals); Q = floor(q / 2^L0) = (8 m) >> (C - e1), C - e1 >= 0 because
-    // q <= qmax < 2^(L0 + W + 1).
     const int C = F::kBias + F::kFrac + 3 + L0;
+    const Fix K = (Fix)(1 - C) * ((Fix)1 << (F::kFrac + 3));
 
-    // ---- fixed point with sticky bit, and per row the XOR of the fixed-point words
+    // ---- fixed point Q = floor(q / 2^L0); per row the XOR of the Q; the largest lowest set bit
+    // (a tie at binade offset j is a Q whose lowest set bit is j - 1 with nothing below 2^L0)
     Fix X[ROWS];
+    Fix maxlow = 0;
 #pragma unroll
     for (int r = 0; r < ROWS; ++r) {
         X[r] = 0;
 #pragma unroll
         for (int e = 0; e < V; ++e) {
-            const Fix qb = qf[r * V + e];
-            const int e1 = max((int)(qb >> F::kFrac), 1);
-            const Fix mm = (qb << 3) - ((Fix)(e1 - 1) << (F::kFrac + 3));  // 8 m (exact modulo 2^FIXBITS)
-            const int dn = C - e1;
-            Fix Q, back;
-            if constexpr (sizeof(Fix) == 4) {
-                Q = __funnelshift_rc(mm, 0u, dn);    // mm >> dn, 0 once dn >= 32
-                back = __funnelshift_lc(0u, Q, dn);  // Q << dn, 0 once dn >= 32
-            } else {
-                Q = dn < 64 ? mm >> dn : 0;
-                back = dn < 64 ? Q << dn : 0;
-            }
-            const Fix qs = back != mm ? (Q | kSticky) : Q;
-            qf[r * V + e] = qs;
-            X[r] ^= qs;
+            const Fix Q = fixed_point<T>(qf[r * V + e], C, K);
+            qf[r * V + e] = Q;
+            X[r] ^= Q;
+            const Fix low = Q & ((Fix)0 - Q);
+            maxlow = low > maxlow ? low : maxlow;
         }
     }
     // ---- per-bit population counts: Harley-Seal vertical counters per thread, then one warp
@@ -438,8 +469,6 @@ mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base
     }
     if (lane == 0) s_warp_xor[warp] = warp_total;
     __syncthreads();
-    Fix warp_prefix = 0;
-    for (int w = 0; w < warp; ++w) warp_prefix ^= s_warp_xor[w];
     // Per binade offset j (binade k = k_lo + j - 1): W_j = sum over bits b >= j of cnt[b] 2^(b-j)
     // (the chunk's sum of floor(Q / 2^j), saturated), one lane per j with independent terms.
     // jmin: the lowest j from which on every half-up sum W_j + cnt[j-1] still fits inside one
@@ -470,32 +499,49 @@ mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base
     __syncthreads();
     const int jmin = s_jmin;
 
-    // ---- ties at the usable binades: a word whose lowest set bit is at or above jmin - 1 and
-    // that has no sticky bit (rare), with the parity of the half-up increments in front of it
-    const Fix tiemask = (((Fix)1 << (jmin - 1)) - 1) | kSticky;
-    bool cand = false;
-#pragma unroll
-    for (int i = 0; i < EPT; ++i) cand |= qf[i] != 0 && (qf[i] & tiemask) == 0;
-    if (cand) {
-#pragma unroll
+    // ---- ties at the usable binades (rare): recompute this thread's squares exactly and list
+    // the Q whose lowest set bit is at or above jmin - 1 with nothing below 2^L0, with the parity
+    // of the half-up increments in front of each
+    // (a chunk with a Subtract/Multiply fault is never mapped, only resolved up to the fault)
+    if (!(head.flags & kHeadFault) && jmin <= W && maxlow >= ((Fix)1 << (jmin - 1))) {
+        Fix warp_prefix = 0;
+        for (int w = 0; w < warp; ++w) warp_prefix ^= s_warp_xor[w];
+        const Fix lowmask = ((Fix)1 << (jmin - 1)) - 1;
+#pragma unroll 1
         for (int r = 0; r < ROWS; ++r) {
             Fix prefix = warp_prefix ^ s_lane_ex[r][tid];
-#pragma unroll
+#pragma unroll 1
             for (int e = 0; e < V; ++e) {
-                const Fix qs = qf[r * V + e];
-                if (qs != 0 && (qs & tiemask) == 0) {
-                    const int j = sizeof(Fix) == 4 ? __ffs((int)qs) : __ffsll((long long)qs);  // lowest bit + 1
-                    const unsigned slot = atomicAdd(&s_tie_count, 1u);
-                    if (slot < (unsigned)kMaxTies) {
-                        Tie t;
-                        t.index = (uint32_t)CM::index(warp, r, lane, e);
-                        t.j = (uint16_t)j;
-                        t.mpar = (uint8_t)((qs >> j) & 1);
-                        t.pi = (uint8_t)((prefix >> j) & 1);
-                        s_ties[slot] = t;
+                const int c = CM::index(warp, r, lane, e);
+                const uint64_t i = chunk0 + c;
+                // recompute the square (the register copy is not indexed here, so that it stays
+                // in registers; the chunk is fault-free, so the IEEE square is the law's)
+                Fix qb = 0;
+                if (i < n) {
+                    const T d = F::sub(prediction[i], target[i]);
+                    qb = (Fix)F::bits(F::mul(d, d));
+                }
+                const int field = (int)(qb >> F::kFrac);
+                const int dn = min(C - field, C - 1);
+                const Fix mm = qb * (Fix)8 + K + (Fix)dn * ((Fix)1 << (F::kFrac + 3));
+                const Fix Q = fixed_point<T>(qb, C, K);
+                if (Q != 0 && (Q & lowmask) == 0) {
+                    // a tie needs nothing of q below 2^L0
+                    const bool sticky = dn >= (int)(sizeof(Fix) * 8) ? mm != 0 : (mm & (((Fix)1 << dn) - 1)) != 0;
+                    if (!sticky) {
+                        const int j = sizeof(Fix) == 4 ? __ffs((int)Q) : __ffsll((long long)Q);  // lowest bit + 1
+                        const unsigned slot = atomicAdd(&s_tie_count, 1u);
+                        if (slot < (unsigned)kMaxTies) {
+                            Tie t;
+                            t.index = (uint32_t)c;
+                            t.j = (uint16_t)j;
+                            t.mpar = (uint8_t)((Q >> j) & 1);
+                            t.pi = (uint8_t)((prefix >> j) & 1);
+                            s_ties[slot] = t;
+                        }
                     }
                 }
-                prefix ^= qs ^ (qs << 1);
+                prefix ^= Q ^ (Q << 1);
             }
         }
     }
@@ -547,26 +593,35 @@ mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base
     }
 }
 
-// Compose the maps of kBlockChunks consecutive chunks into one block map per binade.
+// Compose the maps of kBlockChunks consecutive chunks into one block map per binade.  The
+// chunks' heads and increment rows are staged in shared memory, kStageChunks at a time, with
+// coalesced loads; then one thread per binade folds them in chunk order.
+constexpr int kStageChunks = 16;
 template <typename T>
-__global__ void __launch_bounds__(64) mse_block_kernel(const MseHead *heads, const typename MseTraits<T>::D *deltas,
-                                                       uint64_t chunks, MseHead *bheads,
-                                                       typename MseTraits<T>::D *bdeltas) {
+__global__ void __launch_bounds__(256) mse_block_kernel(const MseHead *heads, const typename MseTraits<T>::D *deltas,
+                                                        uint64_t chunks, MseHead *bheads,
+                                                        typename MseTraits<T>::D *bdeltas) {
     using Tr = MseTraits<T>;
+    using D = typename Tr::D;
     constexpr int W = Tr::W;
+    constexpr int ROW = W * 2;  // increment words per chunk
     const uint64_t c0 = (uint64_t)blockIdx.x * kBlockChunks;
-    const uint64_t c1 = c0 + kBlockChunks < chunks ? c0 + kBlockChunks : chunks;
-    __shared__ int s_khi;
-    __shared__ int s_flags;
+    const int count = (int)(c0 + kBlockChunks < chunks ? kBlockChunks : chunks - c0);
+    __shared__ MseHead s_heads[kBlockChunks];
+    __shared__ D s_rows[kStageChunks * ROW];
+    __shared__ int s_khi, s_flags;
     __shared__ unsigned s_fault;
-    if (threadIdx.x == 0) {
+    const int tid = threadIdx.x, lane = tid & 31;
+    if (tid < count) s_heads[tid] = heads[c0 + tid];
+    __syncthreads();
+    if (tid < 32) {  // block head: union of the flags, highest window top, earliest fault
         int khi = INT_MIN, flags = kHeadZero;
         unsigned fault = 0xffffffffu;
-        for (uint64_t c = c0; c < c1; ++c) {
-            const MseHead h = heads[c];
+        for (int c = lane; c < count; c += 32) {
+            const MseHead h = s_heads[c];
             if (h.flags & kHeadFault) {
                 flags |= kHeadFault;
-                fault = min(fault, (unsigned)((c - c0) * Tr::CHUNK + h.fault));
+                fault = min(fault, (unsigned)(c * Tr::CHUNK + h.fault));
             }
             if (h.flags & kHeadExact) flags |= kHeadExact;
             if (!(h.flags & kHeadZero)) {
@@ -574,9 +629,18 @@ __global__ void __launch_bounds__(64) mse_block_kernel(const MseHead *heads, con
                 khi = max(khi, h.k_lo + W - 1);
             }
         }
-        s_khi = khi;
-        s_flags = flags;
-        s_fault = fault;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            khi = max(khi, __shfl_xor_sync(0xffffffffu, khi, o));
+            fault = min(fault, __shfl_xor_sync(0xffffffffu, fault, o));
+            const int f = __shfl_xor_sync(0xffffffffu, flags, o);
+            flags = ((flags | f) & ~kHeadZero) | (flags & f & kHeadZero);
+        }
+        if (lane == 0) {
+            s_khi = khi;
+            s_flags = flags;
+            s_fault = fault;
+        }
     }
     __syncthreads();
     const int flags = s_flags;
@@ -585,28 +649,37 @@ __global__ void __launch_bounds__(64) mse_block_kernel(const MseHead *heads, con
     bh.flags = flags;
     bh.fault = s_fault;
     bh.k_lo = (flags & kHeadZero) ? 0 : max(s_khi - (W - 1), Tr::KMIN);
-    if (threadIdx.x == 0) bheads[blockIdx.x] = bh;
-    if ((flags & kHeadZero) || threadIdx.x >= W) return;
-    const int k = bh.k_lo + threadIdx.x;
-    uint64_t D[2] = {0, 0};
+    if (tid == 0) bheads[blockIdx.x] = bh;
+    if (flags & kHeadZero) return;  // uniform across the CTA
+    const int k = bh.k_lo + tid;
+    uint64_t acc[2] = {0, 0};
     bool valid = !(flags & (kHeadExact | kHeadFault));
-    for (uint64_t c = c0; c < c1 && valid; ++c) {
-        const MseHead h = heads[c];
-        if (h.flags & kHeadZero) continue;
-        if (k > h.k_lo + W - 1) continue;  // every square of the chunk is below half an ulp
-        if (k < h.k_lo) { valid = false; break; }
-        const typename Tr::D *d = deltas + ((size_t)c * W + (k - h.k_lo)) * 2;
-        const typename Tr::D d0 = d[0], d1 = d[1];
-        if (d0 == no_map<T>() || d1 == no_map<T>()) { valid = false; break; }
-        const uint64_t n0 = D[0] + ((D[0] & 1) ? d1 : d0);
-        const uint64_t n1 = D[1] + (((1 + D[1]) & 1) ? d1 : d0);
-        D[0] = n0;
-        D[1] = n1;
-        if (D[0] >= (2ull << Tr::P) || D[1] >= (2ull << Tr::P)) valid = false;  // cannot fit a binade
+    for (int g = 0; g < count; g += kStageChunks) {
+        const int in_stage = min(kStageChunks, count - g);
+        __syncthreads();  // the previous stage has been consumed
+        for (int i = tid; i < in_stage * ROW; i += 256) s_rows[i] = deltas[(c0 + g) * ROW + i];
+        __syncthreads();
+        if (tid < W && valid) {
+            for (int c = 0; c < in_stage; ++c) {
+                const MseHead h = s_heads[g + c];
+                if (h.flags & kHeadZero) continue;
+                if (k > h.k_lo + W - 1) continue;  // every square of the chunk is below half an ulp
+                if (k < h.k_lo) { valid = false; break; }
+                const D d0 = s_rows[c * ROW + (k - h.k_lo) * 2], d1 = s_rows[c * ROW + (k - h.k_lo) * 2 + 1];
+                if (d0 == no_map<T>() || d1 == no_map<T>()) { valid = false; break; }
+                const uint64_t n0 = acc[0] + ((acc[0] & 1) ? d1 : d0);
+                const uint64_t n1 = acc[1] + (((1 + acc[1]) & 1) ? d1 : d0);
+                acc[0] = n0;
+                acc[1] = n1;
+                if (acc[0] >= (2ull << Tr::P) || acc[1] >= (2ull << Tr::P)) { valid = false; break; }  // cannot fit a binade
+            }
+        }
     }
-    typename Tr::D *out = bdeltas + ((size_t)blockIdx.x * W + threadIdx.x) * 2;
-    out[0] = valid ? sat_d<T>(D[0]) : no_map<T>();
-    out[1] = valid ? sat_d<T>(D[1]) : no_map<T>();
+    if (tid < W) {
+        D *out = bdeltas + ((size_t)blockIdx.x * W + tid) * 2;
+        out[0] = valid ? sat_d<T>(acc[0]) : no_map<T>();
+        out[1] = valid ? sat_d<T>(acc[1]) : no_map<T>();
+    }
 }
 
 // One map (chunk or block) at the binade of the state: x -> x + D[x mod 2].  `ok` is false when
@@ -668,34 +741,77 @@ __device__ __forceinline__ unsigned apply_maps(const MseHead *heads, const typen
     return applied;
 }
 
-// Squares of a chunk being resolved, transposed so that thread t's PER consecutive elements sit
-// in one column: element c -> slot (c mod PER) * SQ_PITCH + c / PER.  The odd pitch keeps both
-// the coalesced fill (consecutive c) and the owners' reads (consecutive t) free of bank conflicts.
+// The walker's resolution of one chunk runs on all kWalkThreads threads; thread t owns the PER
+// consecutive elements [t * PER, t * PER + PER) of the chunk.  Their squares sit in column t of
+// `sq` (element t * PER + e at e * PITCH + t): the owners' reads at a fixed e are consecutive.
+constexpr int kWalkThreads = 1024;
 template <typename T> struct ResolveLayout {
-    static constexpr int PER = MseTraits<T>::CHUNK / 256;
-    static constexpr int SQ_PITCH = 257;
+    static constexpr int PER = MseTraits<T>::CHUNK / kWalkThreads;
+    static constexpr int PITCH = kWalkThreads + 1;
 };
 
+// Prefix sums of half-up increments inside one binade: 32-bit for binary32 (a state is below
+// 2^24 and everything is clamped at 2^30), 64-bit for binary64.
+template <typename T> struct WalkAcc;
+template <> struct WalkAcc<float> {
+    using U = uint32_t;
+    static constexpr U SAT = 1u << 30;
+};
+template <> struct WalkAcc<double> {
+    using U = uint64_t;
+    static constexpr U SAT = 1ull << 62;
+};
+
+template <typename U> __device__ __forceinline__ U sat_add(U a, U b, U sat) {
+    const U s = a + b;  // a, b <= sat, so no wrap-around
+    return s < sat ? s : sat;
+}
+
+// Half-up increment of a square (bits qb) at ulp 2^k, clamped at WalkAcc<T>::SAT, and whether
+// it is a tie there (q / 2^k an exact half-integer).
 template <typename T>
-__global__ void __launch_bounds__(256) mse_walk_kernel(const T *prediction, const T *target, uint64_t n,
-                                                       const MseHead *heads, const typename MseTraits<T>::D *deltas,
-                                                       const MseHead *bheads, const typename MseTraits<T>::D *bdeltas,
-                                                       uint64_t chunks, uint64_t blocks, uint64_t base, uint64_t total,
-                                                       T denominator, int policy, const T *carry_in, T *carry_out,
-                                                       T *out, unsigned long long *status) {
+__device__ __forceinline__ typename WalkAcc<T>::U walk_increment(typename Fmt<T>::Bits qb, int k, bool &tie) {
+    using F = Fmt<T>;
+    using U = typename WalkAcc<T>::U;
+    constexpr U SAT = WalkAcc<T>::SAT;
+    constexpr int UB = sizeof(U) * 8;
+    const int field = (int)(qb >> F::kFrac);
+    const int e1 = field > 1 ? field : 1;
+    const U m = (U)(qb - ((typename F::Bits)(e1 - 1) << F::kFrac));  // significand, implicit bit included
+    const int sh = e1 - F::kBias - F::kFrac - k;                      // q = m * 2^(k + sh)
+    tie = false;
+    if (sh >= 0) return (sh >= UB - F::kFrac - 2 || m >= (SAT >> sh)) ? (m ? SAT : (U)0) : m << sh;
+    const int d = -sh;
+    if (d > F::kFrac + 2) return 0;  // q < 2^(k-1): below half an ulp
+    const U half = (U)1 << (d - 1);
+    tie = (m & ((half << 1) - 1)) == half;
+    return (m + half) >> d;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kWalkThreads) mse_walk_kernel(
+    const T *prediction, const T *target, uint64_t n, bool vec, const MseHead *heads,
+    const typename MseTraits<T>::D *deltas, const MseHead *bheads, const typename MseTraits<T>::D *bdeltas,
+    uint64_t chunks, uint64_t blocks, uint64_t base, uint64_t total, T denominator, int policy, const T *carry_in,
+    T *carry_out, T *out, unsigned long long *status) {
     using Tr = MseTraits<T>;
     using F = Fmt<T>;
     using RL = ResolveLayout<T>;
-    constexpr int PER = RL::PER, PITCH = RL::SQ_PITCH;
+    using U = typename WalkAcc<T>::U;
+    constexpr U SAT = WalkAcc<T>::SAT;
+    constexpr int PER = RL::PER, PITCH = RL::PITCH, WARPS = kWalkThreads / 32;
     constexpr uint64_t BLOCK_ELEMS = (uint64_t)kBlockChunks * Tr::CHUNK;
-    constexpr uint64_t TOP = 2ull << Tr::P;  // a state at or above this has left its binade
-    __shared__ T sq[PER * PITCH];
+    constexpr U TOP = (U)2 << Tr::P;  // a state at or above this has left its binade
+    using VT = typename std::conditional<sizeof(T) == 4, float4, double2>::type;
+    constexpr int VW = 16 / sizeof(T);
+    static_assert(PER % VW == 0, "owner spans are whole 16-byte vectors");
+    __shared__ typename F::Bits sq[PER * PITCH];
     __shared__ T s_sum;
-    __shared__ uint64_t s_g;       // elements [0, s_g) of the segment are summed into s_sum
-    __shared__ uint64_t s_arg;     // chunk to resolve, or ~0 when the walk is done
-    __shared__ int s_done;         // 2: overflow recorded
+    __shared__ uint64_t s_g;    // elements [0, s_g) of the segment are summed into s_sum
+    __shared__ uint64_t s_arg;  // chunk to resolve, or ~0 when the walk is done
+    __shared__ int s_done;      // 2: overflow recorded
     __shared__ unsigned s_pos, s_stop[2];
-    __shared__ uint64_t s_warp_sum[8];
+    __shared__ U s_warp_sum[WARPS];
 
     // Every Subtract/Multiply fault is already in the status word; the walk stops in front of
     // the earliest one, so only earlier Adds can still report (their events are smaller).  The
@@ -753,12 +869,25 @@ __global__ void __launch_bounds__(256) mse_walk_kernel(const T *prediction, cons
         // ---- resolve one chunk: recompute its squares (all fault-free in front of `stop`)
         const uint64_t i0 = s_arg * Tr::CHUNK;
         const unsigned len = (unsigned)((i0 + Tr::CHUNK < stop ? i0 + Tr::CHUNK : stop) - i0);
+        const unsigned c0 = (unsigned)tid * PER;  // this thread's elements [c0, c0 + PER)
+        if (vec && c0 + PER <= len) {
 #pragma unroll
-        for (int e = 0; e < PER; ++e) {
-            const unsigned c = (unsigned)tid + (unsigned)e * 256;
-            if (c < len) {
-                const T d = F::sub(prediction[i0 + c], target[i0 + c]);
-                sq[(c % PER) * PITCH + c / PER] = F::mul(d, d);
+            for (int v = 0; v < PER / VW; ++v) {
+                const VT a = *reinterpret_cast<const VT *>(prediction + i0 + c0 + v * VW);
+                const VT b = *reinterpret_cast<const VT *>(target + i0 + c0 + v * VW);
+#pragma unroll
+                for (int e = 0; e < VW; ++e) {
+                    const T d = F::sub(reinterpret_cast<const T *>(&a)[e], reinterpret_cast<const T *>(&b)[e]);
+                    sq[(v * VW + e) * PITCH + tid] = F::bits(F::mul(d, d));
+                }
+            }
+        } else {
+#pragma unroll
+            for (int e = 0; e < PER; ++e) {
+                if (c0 + e < len) {
+                    const T d = F::sub(prediction[i0 + c0 + e], target[i0 + c0 + e]);
+                    sq[e * PITCH + tid] = F::bits(F::mul(d, d));
+                }
             }
         }
         if (tid == 0) {
@@ -768,60 +897,72 @@ __global__ void __launch_bounds__(256) mse_walk_kernel(const T *prediction, cons
         __syncthreads();
         // Apply every element in front of the first tie or binade crossing at once (prefix sums of
         // half-up increments), then add that element exactly; repeat.
-        const unsigned c0 = (unsigned)tid * PER;  // this thread's elements [c0, c0 + PER)
         for (int it = 0;; it ^= 1) {
             const unsigned pos = s_pos;
             if (pos >= len) break;
-            uint64_t x;
+            uint64_t x64;
             int k;
-            state_of<T>(s_sum, x, k);
-            uint64_t inc[PER];
-            uint64_t local = 0;
+            state_of<T>(s_sum, x64, k);
+            const U x = (U)x64;  // below 2^(P+1)
+            U inc[PER];
+            U local = 0;
             unsigned first_tie = len;
 #pragma unroll
             for (int e = 0; e < PER; ++e) {
                 const unsigned c = c0 + e;
                 bool tie = false;
-                inc[e] = (c >= pos && c < len) ? half_up_increment<T>(sq[e * PITCH + tid], k, tie) : 0;
-                if (tie && c >= pos && c < len && first_tie == len) first_tie = c;
-                local = min(local + inc[e], (uint64_t)Tr::SAT);
+                inc[e] = 0;
+                if (c >= pos && c < len) {
+                    inc[e] = walk_increment<T>(sq[e * PITCH + tid], k, tie);
+                    if (tie && first_tie == len) first_tie = c;
+                }
+                local = sat_add<U>(local, inc[e], SAT);
             }
-            // exclusive prefix sum of thread totals (element order = thread order)
-            uint64_t incl = local;
+            // exclusive prefix of thread totals in element (= thread) order
+            U incl = local;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
-                const uint64_t v = __shfl_up_sync(0xffffffffu, (unsigned long long)incl, o);
-                if (lane >= o) incl = min(incl + v, (uint64_t)Tr::SAT);
+                const U v = shfl_up_x(incl, o);
+                if (lane >= o) incl = sat_add<U>(incl, v, SAT);
             }
             if (lane == 31) s_warp_sum[warp] = incl;
             __syncthreads();
-            // exclusive prefix from the previous lane (not incl - local: both may be saturated
-            // when this thread's own range holds the element that saturates)
-            uint64_t before = __shfl_up_sync(0xffffffffu, (unsigned long long)incl, 1);
+            // warps in front: every warp scans the warp totals itself (no extra barrier)
+            U wsum = s_warp_sum[lane];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const U v = shfl_up_x(wsum, o);
+                if (lane >= o) wsum = sat_add<U>(wsum, v, SAT);
+            }
+            const U warp_before = warp ? shfl_x(wsum, warp - 1) : (U)0;
+            // exclusive prefix from the previous lane (not incl - local: both may be clamped when
+            // this thread's own range holds the element that saturates)
+            U before = shfl_up_x(incl, 1);
             if (lane == 0) before = 0;
-            for (int w = 0; w < warp; ++w) before = min(before + s_warp_sum[w], (uint64_t)Tr::SAT);
+            before = sat_add<U>(before, warp_before, SAT);
             // first element whose half-up result may leave the binade, or the first tie
-            uint64_t run = x + before;
+            U run = sat_add<U>(x, before, SAT);
             unsigned mine = first_tie;
 #pragma unroll
             for (int e = 0; e < PER; ++e) {
                 const unsigned c = c0 + e;
-                if (c >= pos && c < len && c < mine && run + inc[e] >= TOP) mine = c;
-                run = min(run + inc[e], (uint64_t)Tr::SAT);
+                const U next = sat_add<U>(run, inc[e], SAT);
+                if (c >= pos && c < len && c < mine && next >= TOP) mine = c;
+                run = next;
             }
             if (mine < len) atomicMin(&s_stop[it], mine);
             __syncthreads();
             const unsigned cut = s_stop[it];
             // the owner of `cut` (the last thread when nothing stops) publishes the state there,
             // adds that element exactly, and moves the cursor
-            if ((cut < len && cut >= c0 && cut < c0 + PER) || (cut == len && tid == 255)) {
-                uint64_t r = x + before;
+            if ((cut < len && cut >= c0 && cut < c0 + PER) || (cut == len && tid == kWalkThreads - 1)) {
+                U r = x + before;  // below TOP: nothing in front of `cut` left the binade
 #pragma unroll
                 for (int e = 0; e < PER; ++e)
                     if (c0 + e < cut) r += inc[e];
-                T s = value_of<T>(r, k);
+                T s = value_of<T>((uint64_t)r, k);
                 if (cut < len) {
-                    const T t = F::add(s, sq[(cut % PER) * PITCH + cut / PER]);
+                    const T t = F::add(s, F::value(sq[(cut % PER) * PITCH + cut / PER]));
                     if (nonfinite_bits<T>(F::bits(t))) {
                         record_fault(status, (base + i0 + cut) * 3 + 2, kOverflow);
                         s_done = 2;
@@ -915,10 +1056,22 @@ int prepare_mse(int policy, const T *p, const T *t, uint64_t n, uint64_t base, v
     auto *bheads = reinterpret_cast<MseHead *>(ws + lay.bheads_off);
     auto *bdeltas = reinterpret_cast<D *>(ws + lay.bdeltas_off);
     const bool vec = pcu_host::aligned(p, 16) && pcu_host::aligned(t, 16);
-    mse_chunk_kernel<T><<<(unsigned)lay.chunks, 256, 0, stream>>>(p, t, n, base, vec, policy, heads, deltas, status);
+    static int resident[64] = {0};  // chunk-kernel CTAs resident at once, per device
+    int device = 0;
+    cudaGetDevice(&device);
+    int ahead = device >= 0 && device < 64 ? resident[device] : 0;
+    if (!ahead) {
+        int per_sm = 0;
+        cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mse_chunk_kernel<T>, 256, 0);
+        if (e != cudaSuccess) return pcu_host::set_cuda_error(e);
+        ahead = per_sm * pcu_host::sm_count();
+        if (device >= 0 && device < 64) resident[device] = ahead;
+    }
+    mse_chunk_kernel<T><<<(unsigned)lay.chunks, 256, 0, stream>>>(p, t, n, base, vec, policy, (uint64_t)ahead, heads,
+                                                                  deltas, status);
     int rc = pcu_host::launch_status();
     if (rc) return rc;
-    mse_block_kernel<T><<<(unsigned)lay.blocks, 64, 0, stream>>>(heads, deltas, lay.chunks, bheads, bdeltas);
+    mse_block_kernel<T><<<(unsigned)lay.blocks, 256, 0, stream>>>(heads, deltas, lay.chunks, bheads, bdeltas);
     return pcu_host::launch_status();
 }
 
@@ -936,7 +1089,8 @@ int walk_mse(int policy, const T *p, const T *t, uint64_t n, uint64_t base, uint
     auto *deltas = reinterpret_cast<D *>(ws + lay.deltas_off);
     auto *bheads = reinterpret_cast<MseHead *>(ws + lay.bheads_off);
     auto *bdeltas = reinterpret_cast<D *>(ws + lay.bdeltas_off);
-    mse_walk_kernel<T><<<1, 256, 0, stream>>>(p, t, n, heads, deltas, bheads, bdeltas, lay.chunks,
+    const bool vec = pcu_host::aligned(p, 16) && pcu_host::aligned(t, 16);
+    mse_walk_kernel<T><<<1, kWalkThreads, 0, stream>>>(p, t, n, vec, heads, deltas, bheads, bdeltas, lay.chunks,
                                                                lay.blocks, base, total, count_value<T>(total), policy,
                                                                carry_in, carry_out, out, status);
     return pcu_host::launch_status();
