@@ -19,31 +19,35 @@
 // D12[p] = D1[p] + D2[(p + D1[p]) mod 2].  Squares are >= 0, so s is monotone and only ever
 // moves up through the binades.
 //
-//   phase 1 (mse_chunk_kernel, all SMs, HBM bound): per CHUNK elements, the subtract and the
-//     square (a cheap test of the square selects the exact checked path for the rare suspects),
-//     then D for every binade k in the window [k_hi - W + 1, k_hi], k_hi = exponent(max q) + 1
+//   phase 1 (mse_chunk_kernel, all SMs, HBM bound): one warp per CHUNK elements computes the
+//     subtract and the square (a cheap test selects the exact checked path for rare suspects),
+//     then D for every binade k of the window [k_hi - W + 1, k_hi], k_hi = exponent(max q) + 1
 //     (above it every y < 1/2: identity):
-//       * q in fixed point Q = floor(q / 2^(k_lo - 1)) plus a sticky bit; the half-up
-//         increment at binade k is (Q + 2^(j-1)) >> j, j = k - k_lo + 1, so its chunk sum is
-//         W_j + cnt[j-1] with W_j = 2 W_(j+1) + cnt[j] from per-bit population counts cnt[b]
-//         (vertical bit-plane counters, then warp reductions);
+//       * q in fixed point Q = floor(q / 2^(k_lo - 1)); the half-up increment at binade k is
+//         (Q + 2^(j-1)) >> j, j = k - k_lo + 1, so its chunk sum is W_j + cnt[j-1] with
+//         W_j = sum over b >= j of cnt[b] 2^(b-j), from the per-bit population counts cnt[b]
+//         (Harley-Seal vertical counters per lane, a warp bit-transpose per counter plane);
 //       * the parity of a half-up increment is bit j of R = Q ^ (Q << 1), so one exclusive
 //         prefix-XOR of R gives, for every binade at once, the parity of the half-up running
 //         increment in front of each element;
-//       * a tie at binade k is an element whose lowest set bit (and no sticky) is bit j-1.  Only
-//         binades where the chunk's sum can fit in one binade are kept (below them the map is
-//         never applied, and every square is a tie at the binade of its own lowest bit); those
-//         ties are rare and give the exact corrections for an even and an odd start.
-//   phase 2 (mse_block_kernel): compose the chunk maps of each BLOCK of 64 chunks.
-//   phase 3 (mse_walk_kernel, one CTA): from s = +0, apply block maps in order, descending to
-//     chunk maps when a block map cannot be applied.  A chunk whose map cannot be applied (the
-//     state crosses a binade inside it, a Subtract/Multiply fault lies in it, or it had too
-//     many ties) is resolved in parallel: its squares are recomputed, the half-up increments
-//     at the current binade are prefix-summed, every element before the first tie or binade
-//     crossing is applied at once, and that one element is added exactly with the IEEE add.
-//     The only fault an Add of nonnegative finite squares can raise is overflow
-//     (fault_domain.rs:207-214); a map is never applied when its result would leave the
-//     binade, so overflow is always met by the exact add.  Then the checked divide.
+//       * a tie at binade k is a square whose lowest set bit of Q is bit j-1, with nothing of q
+//         below 2^(k_lo - 1).  Only binades where the chunk's sum can fit in one binade are kept
+//         (below them the map is never applied); their ties (rare for rounded squares, common
+//         for exact ones) are found from the largest lowest set bit, confirmed exactly, listed
+//         in element order and give the corrections for an even and an odd start.
+//   phase 2 (mse_compose_kernel, twice): compose the maps of kFanout chunks into block maps,
+//     and of kFanout blocks into superblock maps.
+//   phase 3 (mse_walk_kernel, one CTA): from the carried running sum, warp 0 applies up to 32
+//     superblock, block or chunk maps at a time (a prefix scan of the map composition over the
+//     lanes; the leading maps whose state stays inside the binade are taken), descending a
+//     level where a map cannot be applied.  A chunk whose map cannot be applied (the state
+//     crosses a binade inside it, or a Subtract/Multiply fault lies in it) is resolved with one
+//     thread per element: the half-up increments at the current
+//     binade are prefix-summed, every element before the first tie or binade crossing is
+//     applied at once, and that one element is added exactly with the IEEE add.  The only
+//     fault an Add of nonnegative finite squares can raise is overflow (fault_domain.rs:207-214);
+//     a map is never applied when its result would leave the binade, so overflow is always met
+//     by the exact add.  Then the checked divide.
 #include <cstring>
 #include <type_traits>
 
@@ -58,10 +62,10 @@ namespace pcu {
 
 template <typename T> struct MseTraits;
 template <> struct MseTraits<float> {
-    using Fix = uint32_t;     // fixed-point square (W bits) + sticky in the top bit
+    using Fix = uint32_t;     // fixed-point square (W bits)
     using D = uint32_t;       // map increment: a valid one is below 2^24
-    static constexpr int EPT = 32;               // elements per thread
-    static constexpr int CHUNK = 256 * EPT;      // 8192
+    static constexpr int EPT = 32;               // elements per lane
+    static constexpr int CHUNK = 32 * EPT;       // 1024: one warp
     static constexpr int W = 27;                 // binades per window
     static constexpr int P = 23;                 // fraction bits
     static constexpr int KMIN = -149;            // smallest ulp exponent
@@ -73,7 +77,7 @@ template <> struct MseTraits<double> {
     using Fix = uint64_t;
     using D = uint64_t;       // a valid increment is below 2^53
     static constexpr int EPT = 16;
-    static constexpr int CHUNK = 256 * EPT;      // 4096
+    static constexpr int CHUNK = 32 * EPT;       // 512
     static constexpr int W = 56;
     static constexpr int P = 52;
     static constexpr int KMIN = -1074;
@@ -82,15 +86,16 @@ template <> struct MseTraits<double> {
     static constexpr int MIN_BLOCKS = 2;
 };
 
-constexpr int kBlockChunks = 64;
-constexpr int kMaxTies = 256;
+constexpr int kFanout = 64;      // child maps per parent map: chunk -> block -> superblock
+constexpr int kLevels = 3;       // chunk, block, superblock
+constexpr int kChunkWarps = 8;   // chunks (warps) per CTA of the chunk kernel
 
-enum : int { kHeadZero = 1, kHeadExact = 2, kHeadFault = 4 };
+enum : int { kHeadZero = 1, kHeadFault = 4 };
 
 struct MseHead {
     int32_t k_lo;      // window [k_lo, k_lo + W - 1]
-    int32_t flags;     // kHeadZero: every square is +0; kHeadExact: resolve element by element
-    uint32_t fault;    // first Subtract/Multiply fault (chunk- or block-relative) if kHeadFault
+    int32_t flags;     // kHeadZero: every square is +0; kHeadFault: a Subtract/Multiply fault
+    uint32_t fault;    // first Subtract/Multiply fault (relative to the map's first element)
     uint32_t pad;
 };
 
@@ -137,31 +142,10 @@ __device__ __forceinline__ T value_of(uint64_t x, int k) {
                     ((typename F::Bits)x & F::kFracMask));
 }
 
-// Half-up increment of a square at ulp 2^k (saturating) and whether it is a tie there.
-template <typename T>
-__device__ __forceinline__ uint64_t half_up_increment(T q, int k, bool &tie) {
-    using F = Fmt<T>;
-    using Tr = MseTraits<T>;
-    const typename F::Bits b = F::bits(q);
-    tie = false;
-    if (!b) return 0;
-    const int field = (int)((b & F::kExpMask) >> F::kFrac);
-    const uint64_t m = (uint64_t)(b & F::kFracMask) | (field ? (1ull << F::kFrac) : 0);
-    const int e = (field ? field : 1) - F::kBias - F::kFrac;  // q = m * 2^e
-    const int sh = e - k;
-    if (sh >= 0) return sh + Tr::P + 1 >= 62 ? Tr::SAT : min((uint64_t)Tr::SAT, m << sh);
-    const int d = -sh;
-    if (d > Tr::P + 2) return 0;  // y < 1/2
-    const uint64_t half = 1ull << (d - 1);
-    tie = (m & ((half << 1) - 1)) == half;
-    return (m + half) >> d;
-}
-
 struct Tie {
-    uint32_t index;   // chunk-relative element
-    uint16_t j;       // binade offset: k = k_lo + j - 1
-    uint8_t mpar;     // parity of floor(q / 2^k)
-    uint8_t pi;       // parity of the half-up increments in front of it
+    uint16_t index;   // chunk-relative element
+    uint8_t j;        // binade offset: k = k_lo + j - 1
+    uint8_t bits;     // bit 0: parity of floor(q / 2^k); bit 1: parity of the half-up increments in front
 };
 
 template <typename T> __device__ __forceinline__ typename Fmt<T>::Bits warp_max_bits(typename Fmt<T>::Bits v) {
@@ -182,21 +166,32 @@ template <typename X> __device__ __forceinline__ X shfl_up_x(X v, int o) {
     else return __shfl_up_sync(0xffffffffu, (unsigned long long)v, o);
 }
 
+template <typename X> __device__ __forceinline__ X shfl_down_x(X v, int o) {
+    if constexpr (sizeof(X) == 4) return __shfl_down_sync(0xffffffffu, (unsigned)v, o);
+    else return __shfl_down_sync(0xffffffffu, (unsigned long long)v, o);
+}
+
 template <typename X> __device__ __forceinline__ X shfl_x(X v, int src) {
     if constexpr (sizeof(X) == 4) return __shfl_sync(0xffffffffu, (unsigned)v, src);
     else return __shfl_sync(0xffffffffu, (unsigned long long)v, src);
 }
 
-// Element layout of a chunk: warp w owns a contiguous span of 32*V*ROWS elements; in row r
-// lane l owns V consecutive elements (one 16-byte load per row, coalesced across the warp).
+// Element layout of a chunk (one warp): in row r lane l owns the V consecutive elements from
+// r * 32 * V + l * V (32 bytes per lane and row, coalesced across the warp).
 template <typename T> struct ChunkMap {
     static constexpr int V = 32 / sizeof(T);
     static constexpr int ROWS = MseTraits<T>::EPT / V;
-    static constexpr int WARP_SPAN = 32 * V * ROWS;
-    __device__ static __forceinline__ int index(int warp, int row, int lane, int e) {
-        return warp * WARP_SPAN + row * 32 * V + lane * V + e;
-    }
+    __device__ static __forceinline__ int index(int row, int lane, int e) { return row * 32 * V + lane * V + e; }
 };
+
+// a[idx] for a register array and a run-time index, without demoting the array to memory
+template <typename X, int N> __device__ __forceinline__ X get_at(const X (&a)[N], int idx) {
+    X v = a[0];
+#pragma unroll
+    for (int i = 1; i < N; ++i)
+        if (i == idx) v = a[i];
+    return v;
+}
 
 // a[idx] = v for a register array and a run-time index, without demoting the array to memory
 template <typename X, int N> __device__ __forceinline__ void set_at(X (&a)[N], int idx, X v) {
@@ -246,11 +241,6 @@ template <int BASE> struct SealTree<1, BASE> {
     }
 };
 
-// Ask the L2 to fetch [p, p + bytes) ahead of its use (a hint: no destination, no completion).
-__device__ __forceinline__ void prefetch_l2(const void *p, unsigned bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
-
 // 32 x 32 bit-matrix transpose across a warp: on return lane b holds, in bit l, bit b of lane
 // l's input word.  Five butterfly stages swap the off-diagonal blocks: the 16- and 8-bit
 // stages are byte permutes, the 4-, 2- and 1-bit stages a rotation and a masked merge (the
@@ -275,22 +265,37 @@ __device__ __forceinline__ unsigned warp_transpose32(unsigned x, int lane) {
 // Fixed-point form of one square (bits qb, finite, >= +0): Q = floor(q / 2^L0) given
 // C = bias + frac + 3 + L0 and K = (1 - C) * 2^(frac + 3).  q = m * 2^(e1 - bias - frac) with
 // e1 = max(field, 1) and m its significand; Q = (8 m) >> (C - e1) (C - e1 >= 0 for q <= qmax).
+// `mm` receives 8 m and `dn` the shift (for the exact remainder test of the rare tie path).
 template <typename T>
 __device__ __forceinline__ typename MseTraits<T>::Fix fixed_point(typename MseTraits<T>::Fix qb, int C,
-                                                                  typename MseTraits<T>::Fix K) {
+                                                                  typename MseTraits<T>::Fix K, int &dn,
+                                                                  typename MseTraits<T>::Fix &mm) {
     using F = Fmt<T>;
     using Fix = typename MseTraits<T>::Fix;
     const int field = (int)(qb >> F::kFrac);
-    const int dn = min(C - field, C - 1);                              // C - e1
-    const Fix mm = qb * (Fix)8 + K + (Fix)dn * ((Fix)1 << (F::kFrac + 3));  // 8 m, exact modulo 2^bits
-    if constexpr (sizeof(Fix) == 4) return __funnelshift_rc(mm, 0u, dn);   // 0 once dn >= 32
+    dn = min(C - field, C - 1);                                        // C - e1
+    mm = qb * (Fix)8 + K + (Fix)dn * ((Fix)1 << (F::kFrac + 3));       // 8 m, exact modulo 2^bits
+    if constexpr (sizeof(Fix) == 4) return __funnelshift_rc(mm, 0u, dn);  // 0 once dn >= 32
     else return dn < 64 ? mm >> dn : 0;
 }
 
+// Ask the L2 to fetch [p, p + bytes) ahead of its use (a hint: no destination, no completion).
+__device__ __forceinline__ void prefetch_l2(const void *p, unsigned bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// x << s clamped at `sat` (x <= sat), for 0 <= s
+__device__ __forceinline__ uint64_t sat_shl(uint64_t x, int s, uint64_t sat) {
+    if (!x) return 0;
+    if (s >= 63) return sat;
+    return x >= (sat >> s) ? sat : x << s;
+}
+
 template <typename T>
-__global__ void __launch_bounds__(256, MseTraits<T>::MIN_BLOCKS)
+__global__ void __launch_bounds__(32 * kChunkWarps, MseTraits<T>::MIN_BLOCKS)
 mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base, bool vec, int policy,
-                 uint64_t ahead, MseHead *heads, typename MseTraits<T>::D *deltas, unsigned long long *status) {
+                 uint64_t chunks, uint64_t ahead, MseHead *heads, typename MseTraits<T>::D *deltas,
+                 unsigned long long *status) {
     using Tr = MseTraits<T>;
     using F = Fmt<T>;
     using B = typename F::Bits;
@@ -298,29 +303,22 @@ mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base
     using CM = ChunkMap<T>;
     constexpr int EPT = Tr::EPT, W = Tr::W, V = CM::V, ROWS = CM::ROWS;
     constexpr int LOG_EPT = EPT == 32 ? 5 : 4;
+    constexpr int NW = (W + 31) / 32;  // 32-bit words of a fixed-point square
     static_assert((1 << LOG_EPT) == EPT && LOG_EPT + 1 == Tr::PLANES, "counter planes");
     // |d| below 2^-62 (binary32) / 2^-510 (binary64) may square to <= the smallest normal
     constexpr B kTinyDiff = sizeof(T) == 4 ? (B)(127 - 62) << 23 : (B)(1023 - 510) << 52;
     using VT = typename std::conditional<sizeof(T) == 4, float4, double2>::type;
     constexpr int VW = 16 / sizeof(T);  // elements per 16-byte load
+    constexpr unsigned FULL = 0xffffffffu;
 
-    __shared__ unsigned int s_fault;
-    __shared__ unsigned long long s_qmax;
-    __shared__ unsigned int s_cnt[W];
-    __shared__ Fix s_warp_xor[8];
-    __shared__ Fix s_lane_ex[ROWS][256];
-    __shared__ unsigned int s_tie_count;
-    __shared__ int s_jmin;
-    __shared__ uint64_t s_W[W + 1];
-    __shared__ Tie s_ties[kMaxTies];
+    __shared__ Tie s_ties[kChunkWarps][Tr::CHUNK];  // a chunk's ties in element order
 
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const uint64_t chunk0 = (uint64_t)blockIdx.x * Tr::CHUNK;
-    if (tid == 0) {
-        s_fault = 0xffffffffu;
-        s_qmax = 0;
-        s_tie_count = 0;
-        // the chunk that will run `ahead` CTAs later (one wave of resident CTAs): its operands
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint64_t chunk = (uint64_t)blockIdx.x * kChunkWarps + warp;
+    if (chunk >= chunks) return;  // the whole warp: nothing below synchronises beyond it
+    const uint64_t chunk0 = chunk * Tr::CHUNK;
+    if (lane == 0) {
+        // the chunk that will run `ahead` chunks later (one wave of resident warps): its operands
         // come from L2 instead of HBM when it starts
         const uint64_t next = chunk0 + ahead * Tr::CHUNK;
         if (vec && next < n) {
@@ -331,21 +329,19 @@ mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base
             }
         }
     }
-    if (tid < W) s_cnt[tid] = 0;
-    __syncthreads();
 
-    // ---- squares.  A thread is suspect when one of its squares is non-finite (an invalid
-    // operand or an overflow in either step) or, unless the policy allows gradual underflow, one
-    // of its differences is nonzero and below 2^-62 / 2^-510 (only such a difference can square
-    // to <= the smallest normal, and a subnormal difference is one of them).  Suspect threads
-    // redo their elements with the checked law, in order, and stop at their first fault (their
-    // later events cannot win).
+    // ---- squares.  A lane is suspect when one of its squares is non-finite (an invalid operand
+    // or an overflow in either step) or, unless the policy allows gradual underflow, one of its
+    // differences is nonzero and below 2^-62 / 2^-510 (only such a difference can square to <=
+    // the smallest normal, and a subnormal difference is one of them).  Suspect lanes redo their
+    // elements with the checked law, in order, and stop at their first fault (their later events
+    // cannot win).
     Fix qf[EPT];  // q's bits first, its fixed-point form later; qf[row * V + e]
     B qmax_t = 0, dmin = ~(B)0;
-    const uint64_t t0 = chunk0 + CM::index(warp, 0, lane, 0);  // this thread's first element
-    const T *pp = prediction + t0;
-    const T *tp = target + t0;
+    const uint64_t t0 = chunk0 + CM::index(0, lane, 0);  // this lane's first element
     if (vec && chunk0 + Tr::CHUNK <= n) {  // whole chunk in range, 16-byte aligned operands
+        const T *pp = prediction + t0;
+        const T *tp = target + t0;
 #pragma unroll
         for (int r = 0; r < ROWS; ++r)
 #pragma unroll
@@ -376,18 +372,19 @@ mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base
                 qf[r * V + e] = (Fix)qb;
             }
     }
+    unsigned my_fault = 0xffffffffu;
     if (qmax_t >= F::kExpMask || (policy != kPolicyGradual && dmin < kTinyDiff * 2 - 1)) {
-        // rare: reload and redo this thread's elements with the checked law
+        // rare: reload and redo this lane's elements with the checked law
         bool stopped = false;
 #pragma unroll 1
         for (int r = 0; r < ROWS; ++r)
 #pragma unroll 1
             for (int e = 0; e < V; ++e) {
-                const int c = CM::index(warp, r, lane, e);
+                const int c = CM::index(r, lane, e);
                 const uint64_t i = chunk0 + c;
                 T q = T(0);
                 if (!stopped && i < n && !checked_square<T>(prediction[i], target[i], base + i, policy, status, q)) {
-                    atomicMin(&s_fault, (unsigned)c);
+                    my_fault = (unsigned)c;
                     stopped = true;
                 }
                 if (i < n) set_at(qf, r * V + e, stopped ? (Fix)0 : (Fix)F::bits(q));
@@ -396,20 +393,18 @@ mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base
 #pragma unroll
         for (int e = 0; e < EPT; ++e) qmax_t = (B)qf[e] > qmax_t ? (B)qf[e] : qmax_t;
     }
-    qmax_t = warp_max_bits<T>(qmax_t);
-    if (lane == 0) atomicMax(&s_qmax, (unsigned long long)qmax_t);
-    __syncthreads();
+    const unsigned chunk_fault = __reduce_min_sync(FULL, my_fault);
+    const B qmax = warp_max_bits<T>(qmax_t);
 
     MseHead head;
     head.pad = 0;
-    head.fault = s_fault;
-    head.flags = s_fault != 0xffffffffu ? kHeadFault : 0;
-    const B qmax = (B)s_qmax;
+    head.fault = chunk_fault;
+    head.flags = chunk_fault != 0xffffffffu ? kHeadFault : 0;
+    head.k_lo = 0;
     if (qmax == 0) {  // every square is +0 (or faulted): the identity at every binade
-        if (tid == 0) {
-            head.k_lo = 0;
+        if (lane == 0) {
             head.flags |= kHeadZero;
-            heads[blockIdx.x] = head;
+            heads[chunk] = head;
         }
         return;
     }
@@ -418,6 +413,7 @@ mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base
     const int L0 = k_lo - 1;  // fixed-point unit 2^L0
     const int C = F::kBias + F::kFrac + 3 + L0;
     const Fix K = (Fix)(1 - C) * ((Fix)1 << (F::kFrac + 3));
+    head.k_lo = k_lo;
 
     // ---- fixed point Q = floor(q / 2^L0); per row the XOR of the Q; the largest lowest set bit
     // (a tie at binade offset j is a Q whose lowest set bit is j - 1 with nothing below 2^L0)
@@ -428,202 +424,205 @@ mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base
         X[r] = 0;
 #pragma unroll
         for (int e = 0; e < V; ++e) {
-            const Fix Q = fixed_point<T>(qf[r * V + e], C, K);
+            int dn;
+            Fix mm;
+            const Fix Q = fixed_point<T>(qf[r * V + e], C, K, dn, mm);
             qf[r * V + e] = Q;
             X[r] ^= Q;
             const Fix low = Q & ((Fix)0 - Q);
             maxlow = low > maxlow ? low : maxlow;
         }
     }
-    // ---- per-bit population counts: Harley-Seal vertical counters per thread, then one warp
-    // bit-transpose per counter plane puts bit b of every lane's plane into lane b
+    // ---- per-bit population counts of the chunk: Harley-Seal vertical counters per lane, then
+    // a warp bit-transpose per counter plane leaves the count of bit 32 w + b in lane b, word w
+    uint64_t cnt[NW];
     {
         Fix acc[LOG_EPT + 1];
 #pragma unroll
         for (int i = 0; i <= LOG_EPT; ++i) acc[i] = 0;
         acc[LOG_EPT] = SealTree<LOG_EPT, 0>::run(qf, acc);
 #pragma unroll
-        for (int w = 0; w < (int)(sizeof(Fix) / 4); ++w) {
-            unsigned cnt = 0;
+        for (int w = 0; w < NW; ++w) {
+            unsigned c = 0;
 #pragma unroll
             for (int pl = 0; pl <= LOG_EPT; ++pl)
-                cnt += (unsigned)__popc(warp_transpose32((unsigned)(acc[pl] >> (32 * w)), lane)) << pl;
-            const int b = 32 * w + lane;
-            if (b < W && cnt) atomicAdd(&s_cnt[b], cnt);
+                c += (unsigned)__popc(warp_transpose32((unsigned)(acc[pl] >> (32 * w)), lane)) << pl;
+            cnt[w] = 32 * w + lane < W ? c : 0;
         }
     }
-    // ---- exclusive prefix XOR of R = Q ^ (Q << 1) in element order: row by row across lanes,
-    // then across warps.  XOR is linear, so a row's R total is R of the row's XOR.
-    Fix warp_total = 0;
+    // ---- exclusive prefix XOR of R = Q ^ (Q << 1) in element order, per row across the lanes
+    // (XOR is linear: a row's R total is R of the row's XOR)
+    Fix lane_ex[ROWS];
+    {
+        Fix total = 0;
 #pragma unroll
-    for (int r = 0; r < ROWS; ++r) {
-        const Fix row = X[r] ^ (X[r] << 1);
-        Fix incl = row;
+        for (int r = 0; r < ROWS; ++r) {
+            const Fix row = X[r] ^ (X[r] << 1);
+            Fix incl = row;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const Fix v = shfl_up_x(incl, o);
+                if (lane >= o) incl ^= v;
+            }
+            lane_ex[r] = total ^ incl ^ row;  // rows before r, then lanes before this one
+            total ^= shfl_x(incl, 31);
+        }
+    }
+    // ---- S_b = sum over bits b' >= b of cnt[b'] 2^(b'-b) (saturated) for b = 32 w + lane: a
+    // suffix scan over the lanes per word, the upper word's total carried into the lower one.
+    // W_j = S_j.  jmin: the lowest j from which on every half-up sum W_j + cnt[j-1] fits inside
+    // one binade (< 2^(P+1)); the sums only grow as j falls, so the failing j form a prefix.
+    uint64_t S[NW];
+#pragma unroll
+    for (int w = NW - 1; w >= 0; --w) {
+        uint64_t s = cnt[w];
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
-            const Fix v = shfl_up_x(incl, o);
-            if (lane >= o) incl ^= v;
+            const uint64_t v = shfl_down_x(s, o);
+            if (lane + o < 32) s = min(s + sat_shl(v, o, Tr::SAT), (uint64_t)Tr::SAT);
         }
-        s_lane_ex[r][tid] = warp_total ^ incl ^ row;  // rows before r, then lanes before this one
-        warp_total ^= shfl_x(incl, 31);
+        if (w + 1 < NW) s = min(s + sat_shl(shfl_x(S[w + 1 < NW ? w + 1 : w], 0), 32 - lane, Tr::SAT), (uint64_t)Tr::SAT);
+        S[w] = s;
     }
-    if (lane == 0) s_warp_xor[warp] = warp_total;
-    __syncthreads();
-    // Per binade offset j (binade k = k_lo + j - 1): W_j = sum over bits b >= j of cnt[b] 2^(b-j)
-    // (the chunk's sum of floor(Q / 2^j), saturated), one lane per j with independent terms.
-    // jmin: the lowest j from which on every half-up sum W_j + cnt[j-1] still fits inside one
-    // binade (< 2^(P+1)); the sums only grow as j falls, so the failing j form a prefix.
-    if (warp == 0) {
-        int fail_max = 0;
+    uint64_t cprev[NW];  // cnt[b - 1] for b = 32 w + lane
+    int fail_max = 0;
 #pragma unroll
-        for (int h = 0; h < (W + 31) / 32; ++h) {
-            const int j = 1 + lane + 32 * h;
-            uint64_t wj = 0;
-            if (j <= W) {
-#pragma unroll
-                for (int b = 1; b < W; ++b) {
-                    if (b < j) continue;
-                    const uint64_t c = s_cnt[b];
-                    const int sh = b - j;
-                    const uint64_t term = c >= ((uint64_t)Tr::SAT >> sh) ? (uint64_t)Tr::SAT : c << sh;  // sh < 62
-                    wj = min(wj + term, (uint64_t)Tr::SAT);
-                }
-                s_W[j] = wj;
-                if (wj >= Tr::SAT || wj + s_cnt[j - 1] >= (2ull << Tr::P)) fail_max = j;
-            }
-        }
-#pragma unroll
-        for (int o = 16; o; o >>= 1) fail_max = max(fail_max, __shfl_xor_sync(0xffffffffu, fail_max, o));
-        if (lane == 0) s_jmin = fail_max + 1;
+    for (int w = 0; w < NW; ++w) {
+        const uint64_t below = shfl_up_x(cnt[w], 1);
+        const uint64_t carry = shfl_x(cnt[w > 0 ? w - 1 : 0], 31);
+        cprev[w] = lane > 0 ? below : (w > 0 ? carry : 0);
+        const int j = 32 * w + lane;
+        if (j >= 1 && j <= W && (S[w] >= Tr::SAT || S[w] + cprev[w] >= (2ull << Tr::P))) fail_max = j;
     }
-    __syncthreads();
-    const int jmin = s_jmin;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) fail_max = max(fail_max, __shfl_xor_sync(FULL, fail_max, o));
+    const int jmin = fail_max + 1;
 
-    // ---- ties at the usable binades (rare): recompute this thread's squares exactly and list
-    // the Q whose lowest set bit is at or above jmin - 1 with nothing below 2^L0, with the parity
-    // of the half-up increments in front of each
-    // (a chunk with a Subtract/Multiply fault is never mapped, only resolved up to the fault)
-    if (!(head.flags & kHeadFault) && jmin <= W && maxlow >= ((Fix)1 << (jmin - 1))) {
-        Fix warp_prefix = 0;
-        for (int w = 0; w < warp; ++w) warp_prefix ^= s_warp_xor[w];
+    // ---- ties at the usable binades: a Q whose lowest set bit is at or above jmin - 1 with
+    // nothing of q below 2^L0.  Rare for rounded squares (a warp enters only when some lane's
+    // largest lowest set bit reaches jmin - 1), common for exactly representable ones.  The
+    // lanes recompute their squares exactly (the register copy is not indexed here, so that it
+    // stays in registers; the chunk is fault-free, so the IEEE square is the law's) and the
+    // ties are listed in element order with the parity of the half-up increments in front of
+    // each.  (A chunk with a Subtract/Multiply fault is never mapped, only resolved up to it.)
+    unsigned ties = 0;
+    const bool probe = !(head.flags & kHeadFault) && jmin <= W && maxlow >= ((Fix)1 << (jmin - 1));
+    if (__any_sync(FULL, probe)) {
         const Fix lowmask = ((Fix)1 << (jmin - 1)) - 1;
 #pragma unroll 1
         for (int r = 0; r < ROWS; ++r) {
-            Fix prefix = warp_prefix ^ s_lane_ex[r][tid];
-#pragma unroll 1
+            Fix prefix = get_at(lane_ex, r);
+            unsigned mask = 0;   // bit e: element (r, lane, e) is a tie
+            uint64_t code = 0;   // byte e: its j (6 bits) and parities (2 bits)
+#pragma unroll
             for (int e = 0; e < V; ++e) {
-                const int c = CM::index(warp, r, lane, e);
+                const int c = CM::index(r, lane, e);
                 const uint64_t i = chunk0 + c;
-                // recompute the square (the register copy is not indexed here, so that it stays
-                // in registers; the chunk is fault-free, so the IEEE square is the law's)
                 Fix qb = 0;
-                if (i < n) {
+                if (probe && i < n) {
                     const T d = F::sub(prediction[i], target[i]);
                     qb = (Fix)F::bits(F::mul(d, d));
                 }
-                const int field = (int)(qb >> F::kFrac);
-                const int dn = min(C - field, C - 1);
-                const Fix mm = qb * (Fix)8 + K + (Fix)dn * ((Fix)1 << (F::kFrac + 3));
-                const Fix Q = fixed_point<T>(qb, C, K);
+                int dn;
+                Fix mm;
+                const Fix Q = fixed_point<T>(qb, C, K, dn, mm);
                 if (Q != 0 && (Q & lowmask) == 0) {
-                    // a tie needs nothing of q below 2^L0
                     const bool sticky = dn >= (int)(sizeof(Fix) * 8) ? mm != 0 : (mm & (((Fix)1 << dn) - 1)) != 0;
                     if (!sticky) {
                         const int j = sizeof(Fix) == 4 ? __ffs((int)Q) : __ffsll((long long)Q);  // lowest bit + 1
-                        const unsigned slot = atomicAdd(&s_tie_count, 1u);
-                        if (slot < (unsigned)kMaxTies) {
-                            Tie t;
-                            t.index = (uint32_t)c;
-                            t.j = (uint16_t)j;
-                            t.mpar = (uint8_t)((Q >> j) & 1);
-                            t.pi = (uint8_t)((prefix >> j) & 1);
-                            s_ties[slot] = t;
-                        }
+                        mask |= 1u << e;
+                        code |= (uint64_t)(j | (int)((Q >> j) & 1) << 6 | (int)((prefix >> j) & 1) << 7) << (8 * e);
                     }
                 }
                 prefix ^= Q ^ (Q << 1);
             }
-        }
-    }
-    __syncthreads();
-
-    const unsigned ties = s_tie_count;
-    if (tid == 0) {
-        head.k_lo = k_lo;
-        if (ties > (unsigned)kMaxTies) head.flags |= kHeadExact;
-        heads[blockIdx.x] = head;
-    }
-    // ---- one thread per binade: half-up sum from the counts, then the tie corrections
-    if (tid < W) {
-        const int j = tid + 1;  // binade k = k_lo + tid
-        const uint64_t Wj = s_W[j];
-        const bool usable = Wj < Tr::SAT && j >= jmin;
-        const uint64_t half_up = usable ? Wj + s_cnt[j - 1] : Tr::SAT;
-        int64_t corr[2] = {0, 0};
-        if (usable && ties <= (unsigned)kMaxTies) {
-            // this binade's ties in element order (few): repeated minimum selection
-            uint32_t last = 0;
-            bool first_pick = true;
-            for (;;) {
-                uint32_t best = 0xffffffffu;
-                int bi = -1;
-                for (unsigned t = 0; t < ties; ++t) {
-                    const Tie c = s_ties[t];
-                    if (c.j == j && (first_pick || c.index > last) && c.index < best) {
-                        best = c.index;
-                        bi = (int)t;
-                    }
+            // lanes in order, each lane's elements in order: an exclusive prefix of the counts
+            const unsigned cnt_here = __popc(mask);
+            unsigned before = cnt_here;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const unsigned v = __shfl_up_sync(FULL, before, o);
+                if (lane >= o) before += v;
+            }
+            const unsigned row_total = __shfl_sync(FULL, before, 31);
+            before -= cnt_here;
+            unsigned slot = ties + before;
+#pragma unroll
+            for (int e = 0; e < V; ++e) {
+                if (mask >> e & 1) {
+                    const unsigned b = (unsigned)(code >> (8 * e)) & 0xffu;
+                    Tie t;
+                    t.index = (uint16_t)CM::index(r, lane, e);
+                    t.j = (uint8_t)(b & 63);
+                    t.bits = (uint8_t)(b >> 6);
+                    s_ties[warp][slot++] = t;
                 }
-                if (bi < 0) break;
-                last = best;
-                first_pick = false;
-                const Tie t = s_ties[bi];
+            }
+            ties += row_total;
+        }
+        __syncwarp();
+    }
+    if (lane == 0) heads[chunk] = head;
+    // ---- one lane per binade offset j (binade k = k_lo + j - 1): the half-up sum
+    // W_j + cnt[j-1] = S_j + cnt[j-1] (both held by lane j - 32 w of word w), then the ties of
+    // that binade in element order
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+        const int j = 32 * w + lane;
+        if (j < 1 || j > W) continue;
+        const bool usable = j >= jmin;
+        const uint64_t half_up = usable ? S[w] + cprev[w] : Tr::SAT;
+        int64_t corr[2] = {0, 0};
+        if (usable) {
+            for (unsigned i = 0; i < ties; ++i) {
+                const Tie t = s_ties[warp][i];
+                if (t.j != j) continue;
 #pragma unroll
                 for (int p0 = 0; p0 < 2; ++p0) {
                     // state parity in front of the tie: start + half-up prefix + corrections so far
-                    const int parity = (p0 + t.pi + (int)(corr[p0] & 1)) & 1;
+                    const int parity = (p0 + ((t.bits >> 1) & 1) + (int)(corr[p0] & 1)) & 1;
                     // round to even: up iff (state + floor(q/u)) is odd; half-up assumed up
-                    if (((parity + t.mpar) & 1) == 0) corr[p0] -= 1;
+                    if (((parity + (t.bits & 1)) & 1) == 0) corr[p0] -= 1;
                 }
             }
         }
-        typename Tr::D *d = deltas + ((size_t)blockIdx.x * W + tid) * 2;
+        typename Tr::D *d = deltas + ((size_t)chunk * W + (j - 1)) * 2;
         d[0] = usable ? sat_d<T>((uint64_t)((int64_t)half_up + corr[0])) : no_map<T>();
         d[1] = usable ? sat_d<T>((uint64_t)((int64_t)half_up + corr[1])) : no_map<T>();
     }
 }
 
-// Compose the maps of kBlockChunks consecutive chunks into one block map per binade.  The
-// chunks' heads and increment rows are staged in shared memory, kStageChunks at a time, with
-// coalesced loads; then one thread per binade folds them in chunk order.
-constexpr int kStageChunks = 16;
+// Compose the maps of kFanout consecutive children (chunks or blocks, each spanning `span`
+// elements) into one parent map per binade.  The children's heads and increment rows are
+// staged in shared memory, kStageMaps at a time, with coalesced loads; then one thread per
+// binade folds them in order.
+constexpr int kStageMaps = 16;
 template <typename T>
-__global__ void __launch_bounds__(256) mse_block_kernel(const MseHead *heads, const typename MseTraits<T>::D *deltas,
-                                                        uint64_t chunks, MseHead *bheads,
-                                                        typename MseTraits<T>::D *bdeltas) {
+__global__ void __launch_bounds__(256) mse_compose_kernel(const MseHead *heads, const typename MseTraits<T>::D *deltas,
+                                                          uint64_t children, uint64_t span, MseHead *pheads,
+                                                          typename MseTraits<T>::D *pdeltas) {
     using Tr = MseTraits<T>;
     using D = typename Tr::D;
     constexpr int W = Tr::W;
-    constexpr int ROW = W * 2;  // increment words per chunk
-    const uint64_t c0 = (uint64_t)blockIdx.x * kBlockChunks;
-    const int count = (int)(c0 + kBlockChunks < chunks ? kBlockChunks : chunks - c0);
-    __shared__ MseHead s_heads[kBlockChunks];
-    __shared__ D s_rows[kStageChunks * ROW];
+    constexpr int ROW = W * 2;  // increment words per map
+    const uint64_t c0 = (uint64_t)blockIdx.x * kFanout;
+    const int count = (int)(c0 + kFanout < children ? kFanout : children - c0);
+    __shared__ MseHead s_heads[kFanout];
+    __shared__ D s_rows[kStageMaps * ROW];
     __shared__ int s_khi, s_flags;
     __shared__ unsigned s_fault;
     const int tid = threadIdx.x, lane = tid & 31;
     if (tid < count) s_heads[tid] = heads[c0 + tid];
     __syncthreads();
-    if (tid < 32) {  // block head: union of the flags, highest window top, earliest fault
+    if (tid < 32) {  // parent head: union of the flags, highest window top, earliest fault
         int khi = INT_MIN, flags = kHeadZero;
         unsigned fault = 0xffffffffu;
         for (int c = lane; c < count; c += 32) {
             const MseHead h = s_heads[c];
             if (h.flags & kHeadFault) {
                 flags |= kHeadFault;
-                fault = min(fault, (unsigned)(c * Tr::CHUNK + h.fault));
+                fault = min(fault, (unsigned)((uint64_t)c * span + h.fault));
             }
-            if (h.flags & kHeadExact) flags |= kHeadExact;
             if (!(h.flags & kHeadZero)) {
                 flags &= ~kHeadZero;
                 khi = max(khi, h.k_lo + W - 1);
@@ -649,13 +648,13 @@ __global__ void __launch_bounds__(256) mse_block_kernel(const MseHead *heads, co
     bh.flags = flags;
     bh.fault = s_fault;
     bh.k_lo = (flags & kHeadZero) ? 0 : max(s_khi - (W - 1), Tr::KMIN);
-    if (tid == 0) bheads[blockIdx.x] = bh;
+    if (tid == 0) pheads[blockIdx.x] = bh;
     if (flags & kHeadZero) return;  // uniform across the CTA
     const int k = bh.k_lo + tid;
     uint64_t acc[2] = {0, 0};
-    bool valid = !(flags & (kHeadExact | kHeadFault));
-    for (int g = 0; g < count; g += kStageChunks) {
-        const int in_stage = min(kStageChunks, count - g);
+    bool valid = !(flags & kHeadFault);
+    for (int g = 0; g < count; g += kStageMaps) {
+        const int in_stage = min(kStageMaps, count - g);
         __syncthreads();  // the previous stage has been consumed
         for (int i = tid; i < in_stage * ROW; i += 256) s_rows[i] = deltas[(c0 + g) * ROW + i];
         __syncthreads();
@@ -663,7 +662,7 @@ __global__ void __launch_bounds__(256) mse_block_kernel(const MseHead *heads, co
             for (int c = 0; c < in_stage; ++c) {
                 const MseHead h = s_heads[g + c];
                 if (h.flags & kHeadZero) continue;
-                if (k > h.k_lo + W - 1) continue;  // every square of the chunk is below half an ulp
+                if (k > h.k_lo + W - 1) continue;  // every square of the child is below half an ulp
                 if (k < h.k_lo) { valid = false; break; }
                 const D d0 = s_rows[c * ROW + (k - h.k_lo) * 2], d1 = s_rows[c * ROW + (k - h.k_lo) * 2 + 1];
                 if (d0 == no_map<T>() || d1 == no_map<T>()) { valid = false; break; }
@@ -676,15 +675,15 @@ __global__ void __launch_bounds__(256) mse_block_kernel(const MseHead *heads, co
         }
     }
     if (tid < W) {
-        D *out = bdeltas + ((size_t)blockIdx.x * W + tid) * 2;
+        D *out = pdeltas + ((size_t)blockIdx.x * W + tid) * 2;
         out[0] = valid ? sat_d<T>(acc[0]) : no_map<T>();
         out[1] = valid ? sat_d<T>(acc[1]) : no_map<T>();
     }
 }
 
-// One map (chunk or block) at the binade of the state: x -> x + D[x mod 2].  `ok` is false when
-// the map cannot be used there (its window does not reach down to k, the chunk must be resolved
-// element by element, or a Subtract/Multiply fault lies in it).
+// One map at the binade of the state: x -> x + D[x mod 2].  `ok` is false when the map cannot
+// be used there (its window does not reach down to k, its sum does not fit a binade there, or a
+// Subtract/Multiply fault lies in it).
 struct MapStep {
     uint64_t d0, d1;
     bool ok;
@@ -694,7 +693,7 @@ template <typename T>
 __device__ __forceinline__ MapStep map_at(const MseHead &h, const typename MseTraits<T>::D *row, int k) {
     using Tr = MseTraits<T>;
     MapStep m{0, 0, true};
-    if (h.flags & (kHeadExact | kHeadFault)) { m.ok = false; return m; }
+    if (h.flags & kHeadFault) { m.ok = false; return m; }
     if ((h.flags & kHeadZero) || k > h.k_lo + Tr::W - 1) return m;  // identity: every square < half an ulp
     if (k < h.k_lo) { m.ok = false; return m; }
     const typename Tr::D a = row[(size_t)(k - h.k_lo) * 2], b = row[(size_t)(k - h.k_lo) * 2 + 1];
@@ -741,15 +740,6 @@ __device__ __forceinline__ unsigned apply_maps(const MseHead *heads, const typen
     return applied;
 }
 
-// The walker's resolution of one chunk runs on all kWalkThreads threads; thread t owns the PER
-// consecutive elements [t * PER, t * PER + PER) of the chunk.  Their squares sit in column t of
-// `sq` (element t * PER + e at e * PITCH + t): the owners' reads at a fixed e are consecutive.
-constexpr int kWalkThreads = 1024;
-template <typename T> struct ResolveLayout {
-    static constexpr int PER = MseTraits<T>::CHUNK / kWalkThreads;
-    static constexpr int PITCH = kWalkThreads + 1;
-};
-
 // Prefix sums of half-up increments inside one binade: 32-bit for binary32 (a state is below
 // 2^24 and everything is clamped at 2^30), 64-bit for binary64.
 template <typename T> struct WalkAcc;
@@ -788,30 +778,26 @@ __device__ __forceinline__ typename WalkAcc<T>::U walk_increment(typename Fmt<T>
     return (m + half) >> d;
 }
 
+// The walker runs with one thread per chunk element (CHUNK threads).
 template <typename T>
-__global__ void __launch_bounds__(kWalkThreads) mse_walk_kernel(
-    const T *prediction, const T *target, uint64_t n, bool vec, const MseHead *heads,
-    const typename MseTraits<T>::D *deltas, const MseHead *bheads, const typename MseTraits<T>::D *bdeltas,
-    uint64_t chunks, uint64_t blocks, uint64_t base, uint64_t total, T denominator, int policy, const T *carry_in,
-    T *carry_out, T *out, unsigned long long *status) {
+__global__ void __launch_bounds__(1024) mse_walk_kernel(
+    const T *prediction, const T *target, uint64_t n, const MseHead *heads0, const typename MseTraits<T>::D *deltas0,
+    const MseHead *heads1, const typename MseTraits<T>::D *deltas1, const MseHead *heads2,
+    const typename MseTraits<T>::D *deltas2, uint64_t chunks, uint64_t blocks, uint64_t supers, uint64_t base,
+    uint64_t total, T denominator, int policy, const T *carry_in, T *carry_out, T *out, unsigned long long *status) {
     using Tr = MseTraits<T>;
     using F = Fmt<T>;
-    using RL = ResolveLayout<T>;
     using U = typename WalkAcc<T>::U;
     constexpr U SAT = WalkAcc<T>::SAT;
-    constexpr int PER = RL::PER, PITCH = RL::PITCH, WARPS = kWalkThreads / 32;
-    constexpr uint64_t BLOCK_ELEMS = (uint64_t)kBlockChunks * Tr::CHUNK;
+    constexpr int THREADS = Tr::CHUNK, WARPS = THREADS / 32;
     constexpr U TOP = (U)2 << Tr::P;  // a state at or above this has left its binade
-    using VT = typename std::conditional<sizeof(T) == 4, float4, double2>::type;
-    constexpr int VW = 16 / sizeof(T);
-    static_assert(PER % VW == 0, "owner spans are whole 16-byte vectors");
-    __shared__ typename F::Bits sq[PER * PITCH];
+    __shared__ typename F::Bits sq[THREADS];
     __shared__ T s_sum;
     __shared__ uint64_t s_g;    // elements [0, s_g) of the segment are summed into s_sum
     __shared__ uint64_t s_arg;  // chunk to resolve, or ~0 when the walk is done
     __shared__ int s_done;      // 2: overflow recorded
     __shared__ unsigned s_pos, s_stop[2];
-    __shared__ U s_warp_sum[WARPS];
+    __shared__ U s_warp_sum[32];
 
     // Every Subtract/Multiply fault is already in the status word; the walk stops in front of
     // the earliest one, so only earlier Adds can still report (their events are smaller).  The
@@ -822,9 +808,6 @@ __global__ void __launch_bounds__(kWalkThreads) mse_walk_kernel(
         const uint64_t first = (st0 >> 3) / 3;
         stop = first < base ? 0 : (first - base < n ? first - base : n);
     }
-    // chunk / block maps cover whole chunks and blocks (the last ones end at n)
-    const uint64_t map_chunks = stop == n ? chunks : stop / Tr::CHUNK;
-    const uint64_t map_blocks = stop == n ? blocks : stop / BLOCK_ELEMS;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
     if (tid == 0) {
@@ -832,30 +815,40 @@ __global__ void __launch_bounds__(kWalkThreads) mse_walk_kernel(
         s_g = 0;
         s_done = 0;
     }
+    if (tid < 32) s_warp_sum[tid] = 0;
     __syncthreads();
     for (;;) {
         if (warp == 0) {  // maps as far as they reach; then the chunk to resolve, if any
+            const MseHead *lh[kLevels] = {heads0, heads1, heads2};
+            const typename Tr::D *ld[kLevels] = {deltas0, deltas1, deltas2};
+            const uint64_t count[kLevels] = {chunks, blocks, supers};
             T s = s_sum;
             uint64_t g = s_g, arg = ~0ull;
+            uint64_t fail_g = ~0ull;  // a scan at level fail_level stopped at element fail_g
+            int fail_level = kLevels;
             while (g < stop) {
-                if (g % BLOCK_ELEMS == 0 && g / BLOCK_ELEMS < map_blocks) {
-                    const uint64_t b = g / BLOCK_ELEMS;
-                    const unsigned avail = (unsigned)min((uint64_t)32, map_blocks - b);
-                    const unsigned m = apply_maps<T>(bheads, bdeltas, b, avail, s, lane);
-                    g = min(g + m * BLOCK_ELEMS, n);
-                    if (m == avail) continue;
+                bool advanced = false;
+                for (int l = kLevels - 1; l >= 0 && !advanced; --l) {
+                    const uint64_t span = (uint64_t)Tr::CHUNK << (6 * l);  // kFanout = 2^6
+                    if (g % span || (g == fail_g && l >= fail_level)) continue;
+                    const uint64_t i = g / span;
+                    // maps lie wholly in front of `stop` (the last one of a level ends at n)
+                    uint64_t lim = stop == n ? count[l] : stop / span;
+                    if (l + 1 < kLevels) lim = min(lim, (i / kFanout + 1) * kFanout);  // inside the parent
+                    if (i >= lim) continue;
+                    const unsigned avail = (unsigned)min((uint64_t)32, lim - i);
+                    const unsigned m = apply_maps<T>(lh[l], ld[l], i, avail, s, lane);
+                    g = min(g + m * span, n);
+                    if (m < avail) {
+                        fail_g = g;
+                        fail_level = l;
+                    }
+                    advanced = m > 0;
                 }
-                const uint64_t c = g / Tr::CHUNK;
-                const uint64_t block_end = (c / kBlockChunks + 1) * kBlockChunks;
-                const uint64_t lim = min(block_end, map_chunks);
-                if (c < lim) {
-                    const unsigned avail = (unsigned)min((uint64_t)32, lim - c);
-                    const unsigned m = apply_maps<T>(heads, deltas, c, avail, s, lane);
-                    g = min(g + m * Tr::CHUNK, n);
-                    if (m) continue;
+                if (!advanced) {
+                    arg = g / Tr::CHUNK;  // this chunk needs the element-by-element resolution
+                    break;
                 }
-                arg = c;  // this chunk needs the element-by-element resolution
-                break;
             }
             if (lane == 0) {
                 s_sum = s;
@@ -866,37 +859,20 @@ __global__ void __launch_bounds__(kWalkThreads) mse_walk_kernel(
         __syncthreads();
         if (s_arg == ~0ull) break;
 
-        // ---- resolve one chunk: recompute its squares (all fault-free in front of `stop`)
+        // ---- resolve one chunk: thread t owns element t (all fault-free in front of `stop`)
         const uint64_t i0 = s_arg * Tr::CHUNK;
         const unsigned len = (unsigned)((i0 + Tr::CHUNK < stop ? i0 + Tr::CHUNK : stop) - i0);
-        const unsigned c0 = (unsigned)tid * PER;  // this thread's elements [c0, c0 + PER)
-        if (vec && c0 + PER <= len) {
-#pragma unroll
-            for (int v = 0; v < PER / VW; ++v) {
-                const VT a = *reinterpret_cast<const VT *>(prediction + i0 + c0 + v * VW);
-                const VT b = *reinterpret_cast<const VT *>(target + i0 + c0 + v * VW);
-#pragma unroll
-                for (int e = 0; e < VW; ++e) {
-                    const T d = F::sub(reinterpret_cast<const T *>(&a)[e], reinterpret_cast<const T *>(&b)[e]);
-                    sq[(v * VW + e) * PITCH + tid] = F::bits(F::mul(d, d));
-                }
-            }
-        } else {
-#pragma unroll
-            for (int e = 0; e < PER; ++e) {
-                if (c0 + e < len) {
-                    const T d = F::sub(prediction[i0 + c0 + e], target[i0 + c0 + e]);
-                    sq[e * PITCH + tid] = F::bits(F::mul(d, d));
-                }
-            }
+        if ((unsigned)tid < len) {
+            const T d = F::sub(prediction[i0 + tid], target[i0 + tid]);
+            sq[tid] = F::bits(F::mul(d, d));
         }
         if (tid == 0) {
             s_pos = 0;
             s_stop[0] = s_stop[1] = len;
         }
         __syncthreads();
-        // Apply every element in front of the first tie or binade crossing at once (prefix sums of
-        // half-up increments), then add that element exactly; repeat.
+        // Apply every element in front of the first tie or binade crossing at once (a prefix sum
+        // of half-up increments), then add that element exactly; repeat.
         for (int it = 0;; it ^= 1) {
             const unsigned pos = s_pos;
             if (pos >= len) break;
@@ -904,22 +880,11 @@ __global__ void __launch_bounds__(kWalkThreads) mse_walk_kernel(
             int k;
             state_of<T>(s_sum, x64, k);
             const U x = (U)x64;  // below 2^(P+1)
-            U inc[PER];
-            U local = 0;
-            unsigned first_tie = len;
-#pragma unroll
-            for (int e = 0; e < PER; ++e) {
-                const unsigned c = c0 + e;
-                bool tie = false;
-                inc[e] = 0;
-                if (c >= pos && c < len) {
-                    inc[e] = walk_increment<T>(sq[e * PITCH + tid], k, tie);
-                    if (tie && first_tie == len) first_tie = c;
-                }
-                local = sat_add<U>(local, inc[e], SAT);
-            }
-            // exclusive prefix of thread totals in element (= thread) order
-            U incl = local;
+            const bool active = (unsigned)tid >= pos && (unsigned)tid < len;
+            bool tie = false;
+            const U inc = active ? walk_increment<T>(sq[tid], k, tie) : (U)0;
+            // inclusive prefix over the threads (element order)
+            U incl = inc;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
                 const U v = shfl_up_x(incl, o);
@@ -928,41 +893,30 @@ __global__ void __launch_bounds__(kWalkThreads) mse_walk_kernel(
             if (lane == 31) s_warp_sum[warp] = incl;
             __syncthreads();
             // warps in front: every warp scans the warp totals itself (no extra barrier)
-            U wsum = s_warp_sum[lane];
+            U wsum = lane < WARPS ? s_warp_sum[lane] : (U)0;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
                 const U v = shfl_up_x(wsum, o);
                 if (lane >= o) wsum = sat_add<U>(wsum, v, SAT);
             }
             const U warp_before = warp ? shfl_x(wsum, warp - 1) : (U)0;
-            // exclusive prefix from the previous lane (not incl - local: both may be clamped when
-            // this thread's own range holds the element that saturates)
             U before = shfl_up_x(incl, 1);
             if (lane == 0) before = 0;
             before = sat_add<U>(before, warp_before, SAT);
-            // first element whose half-up result may leave the binade, or the first tie
-            U run = sat_add<U>(x, before, SAT);
-            unsigned mine = first_tie;
-#pragma unroll
-            for (int e = 0; e < PER; ++e) {
-                const unsigned c = c0 + e;
-                const U next = sat_add<U>(run, inc[e], SAT);
-                if (c >= pos && c < len && c < mine && next >= TOP) mine = c;
-                run = next;
-            }
-            if (mine < len) atomicMin(&s_stop[it], mine);
+            // the state after this element (clamped): the first element that reaches TOP, or the
+            // first tie, stops the run
+            const U after = sat_add<U>(sat_add<U>(x, before, SAT), inc, SAT);
+            if (active && (tie || after >= TOP)) atomicMin(&s_stop[it], (unsigned)tid);
             __syncthreads();
             const unsigned cut = s_stop[it];
             // the owner of `cut` (the last thread when nothing stops) publishes the state there,
             // adds that element exactly, and moves the cursor
-            if ((cut < len && cut >= c0 && cut < c0 + PER) || (cut == len && tid == kWalkThreads - 1)) {
-                U r = x + before;  // below TOP: nothing in front of `cut` left the binade
-#pragma unroll
-                for (int e = 0; e < PER; ++e)
-                    if (c0 + e < cut) r += inc[e];
+            if ((cut < len && (unsigned)tid == cut) || (cut == len && tid == THREADS - 1)) {
+                // below TOP: nothing in front of `cut` left the binade
+                const U r = cut < len ? x + before : after;
                 T s = value_of<T>((uint64_t)r, k);
                 if (cut < len) {
-                    const T t = F::add(s, F::value(sq[(cut % PER) * PITCH + cut / PER]));
+                    const T t = F::add(s, F::value(sq[cut]));
                     if (nonfinite_bits<T>(F::bits(t))) {
                         record_fault(status, (base + i0 + cut) * 3 + 2, kOverflow);
                         s_done = 2;
@@ -1024,55 +978,64 @@ template <typename T> T count_value(uint64_t n) {
     return v;
 }
 
+// Workspace: per level (chunk, block, superblock) the map heads, then the increment rows.
 template <typename T> struct MseLayout {
-    uint64_t chunks, blocks;
-    size_t heads_off, deltas_off, bheads_off, bdeltas_off, bytes;
+    uint64_t count[kLevels];
+    size_t heads_off[kLevels], deltas_off[kLevels], bytes;
     explicit MseLayout(uint64_t n) {
         using Tr = MseTraits<T>;
         auto up = [](size_t v) { return (v + 255) / 256 * 256; };
-        const size_t dsz = Tr::W * 2 * sizeof(typename Tr::D);
-        chunks = (n + Tr::CHUNK - 1) / Tr::CHUNK;
-        blocks = (chunks + kBlockChunks - 1) / kBlockChunks;
-        heads_off = 0;
-        deltas_off = up(chunks * sizeof(MseHead));
-        bheads_off = deltas_off + up(chunks * dsz);
-        bdeltas_off = bheads_off + up(blocks * sizeof(MseHead));
-        bytes = bdeltas_off + up(blocks * dsz);
+        const size_t row = Tr::W * 2 * sizeof(typename Tr::D);
+        count[0] = (n + Tr::CHUNK - 1) / Tr::CHUNK;
+        for (int l = 1; l < kLevels; ++l) count[l] = (count[l - 1] + kFanout - 1) / kFanout;
+        size_t off = 0;
+        for (int l = 0; l < kLevels; ++l) {
+            heads_off[l] = off;
+            off += up(count[l] * sizeof(MseHead));
+            deltas_off[l] = off;
+            off += up(count[l] * row);
+        }
+        bytes = off;
     }
 };
 
-// Phases 1 and 2 of a segment (global elements [base, base + n)): chunk maps and block maps.
+// Phases 1 and 2 of a segment (global elements [base, base + n)): chunk maps, then block and
+// superblock maps.
 template <typename T>
 int prepare_mse(int policy, const T *p, const T *t, uint64_t n, uint64_t base, void *workspace, size_t workspace_bytes,
                 unsigned long long *status, cudaStream_t stream) {
     using D = typename MseTraits<T>::D;
     MseLayout<T> lay(n);
     if (!workspace || workspace_bytes < lay.bytes) return PCU_B200_ERROR_WORKSPACE;
-    if (lay.chunks > 0x7fffffffull) return PCU_B200_ERROR_SIZE_OVERFLOW;
+    if (lay.count[0] > 0x7fffffffull * kChunkWarps) return PCU_B200_ERROR_SIZE_OVERFLOW;
     if (!n) return PCU_B200_OK;
     char *ws = reinterpret_cast<char *>(workspace);
-    auto *heads = reinterpret_cast<MseHead *>(ws + lay.heads_off);
-    auto *deltas = reinterpret_cast<D *>(ws + lay.deltas_off);
-    auto *bheads = reinterpret_cast<MseHead *>(ws + lay.bheads_off);
-    auto *bdeltas = reinterpret_cast<D *>(ws + lay.bdeltas_off);
     const bool vec = pcu_host::aligned(p, 16) && pcu_host::aligned(t, 16);
-    static int resident[64] = {0};  // chunk-kernel CTAs resident at once, per device
+    static int resident[64] = {0};  // chunk-kernel warps resident at once, per device
     int device = 0;
     cudaGetDevice(&device);
     int ahead = device >= 0 && device < 64 ? resident[device] : 0;
     if (!ahead) {
         int per_sm = 0;
-        cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mse_chunk_kernel<T>, 256, 0);
+        cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mse_chunk_kernel<T>, 32 * kChunkWarps, 0);
         if (e != cudaSuccess) return pcu_host::set_cuda_error(e);
-        ahead = per_sm * pcu_host::sm_count();
+        ahead = per_sm * kChunkWarps * pcu_host::sm_count();
         if (device >= 0 && device < 64) resident[device] = ahead;
     }
-    mse_chunk_kernel<T><<<(unsigned)lay.chunks, 256, 0, stream>>>(p, t, n, base, vec, policy, (uint64_t)ahead, heads,
-                                                                  deltas, status);
+    const unsigned grid = (unsigned)((lay.count[0] + kChunkWarps - 1) / kChunkWarps);
+    mse_chunk_kernel<T><<<grid, 32 * kChunkWarps, 0, stream>>>(
+        p, t, n, base, vec, policy, lay.count[0], (uint64_t)ahead, reinterpret_cast<MseHead *>(ws + lay.heads_off[0]),
+        reinterpret_cast<D *>(ws + lay.deltas_off[0]), status);
     int rc = pcu_host::launch_status();
-    if (rc) return rc;
-    mse_block_kernel<T><<<(unsigned)lay.blocks, 256, 0, stream>>>(heads, deltas, lay.chunks, bheads, bdeltas);
-    return pcu_host::launch_status();
+    for (int l = 1; l < kLevels && !rc; ++l) {
+        mse_compose_kernel<T><<<(unsigned)lay.count[l], 256, 0, stream>>>(
+            reinterpret_cast<const MseHead *>(ws + lay.heads_off[l - 1]),
+            reinterpret_cast<const D *>(ws + lay.deltas_off[l - 1]), lay.count[l - 1],
+            (uint64_t)MseTraits<T>::CHUNK << (6 * (l - 1)), reinterpret_cast<MseHead *>(ws + lay.heads_off[l]),
+            reinterpret_cast<D *>(ws + lay.deltas_off[l]));
+        rc = pcu_host::launch_status();
+    }
+    return rc;
 }
 
 // Phase 3 of a segment: the ordered walk from *carry_in (+0 if null); the running sum goes to
@@ -1085,14 +1048,12 @@ int walk_mse(int policy, const T *p, const T *t, uint64_t n, uint64_t base, uint
     MseLayout<T> lay(n);
     if (n && (!workspace || workspace_bytes < lay.bytes)) return PCU_B200_ERROR_WORKSPACE;
     char *ws = reinterpret_cast<char *>(workspace);
-    auto *heads = reinterpret_cast<MseHead *>(ws + lay.heads_off);
-    auto *deltas = reinterpret_cast<D *>(ws + lay.deltas_off);
-    auto *bheads = reinterpret_cast<MseHead *>(ws + lay.bheads_off);
-    auto *bdeltas = reinterpret_cast<D *>(ws + lay.bdeltas_off);
-    const bool vec = pcu_host::aligned(p, 16) && pcu_host::aligned(t, 16);
-    mse_walk_kernel<T><<<1, kWalkThreads, 0, stream>>>(p, t, n, vec, heads, deltas, bheads, bdeltas, lay.chunks,
-                                                               lay.blocks, base, total, count_value<T>(total), policy,
-                                                               carry_in, carry_out, out, status);
+    auto H = [&](int l) { return reinterpret_cast<const MseHead *>(ws + lay.heads_off[l]); };
+    auto R = [&](int l) { return reinterpret_cast<const D *>(ws + lay.deltas_off[l]); };
+    mse_walk_kernel<T><<<1, MseTraits<T>::CHUNK, 0, stream>>>(p, t, n, H(0), R(0), H(1), R(1), H(2), R(2),
+                                                              lay.count[0], lay.count[1], lay.count[2], base, total,
+                                                              count_value<T>(total), policy, carry_in, carry_out, out,
+                                                              status);
     return pcu_host::launch_status();
 }
 
