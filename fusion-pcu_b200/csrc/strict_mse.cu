@@ -31,8 +31,8 @@
 //         prefix-XOR of R gives, for every binade at once, the parity of the half-up running
 //         increment in front of each element;
 //       * a tie at binade k is a square whose lowest set bit of Q is bit j-1, with nothing of q
-//         below 2^(k_lo - 1).  Only binades where the chunk's sum can fit in one binade are kept
-//         (below them the map is never applied); their ties (rare for rounded squares, common
+//         below 2^(k_lo - 1).  Only binades where the chunk's half-up sum stays below 2^P are
+//         kept (below them the map could never be applied); their ties (rare for rounded squares, common
 //         for exact ones) are found from the largest lowest set bit, confirmed exactly, listed
 //         in element order and give the corrections for an even and an odd start.
 //   phase 2 (mse_compose_kernel, twice): compose the maps of kFanout chunks into block maps,
@@ -62,11 +62,11 @@ namespace pcu {
 
 template <typename T> struct MseTraits;
 template <> struct MseTraits<float> {
-    using Fix = uint32_t;     // fixed-point square (W bits)
+    using Fix = uint32_t;     // fixed-point square (W bits) under the bits of 2^P
     using D = uint32_t;       // map increment: a valid one is below 2^24
     static constexpr int EPT = 32;               // elements per lane
     static constexpr int CHUNK = 32 * EPT;       // 1024: one warp
-    static constexpr int W = 27;                 // binades per window
+    static constexpr int W = 23;                 // binades per window: Q < 2^W fits a significand
     static constexpr int P = 23;                 // fraction bits
     static constexpr int KMIN = -149;            // smallest ulp exponent
     static constexpr int PLANES = 6;             // vertical counter planes: counts up to 63
@@ -78,7 +78,7 @@ template <> struct MseTraits<double> {
     using D = uint64_t;       // a valid increment is below 2^53
     static constexpr int EPT = 16;
     static constexpr int CHUNK = 32 * EPT;       // 512
-    static constexpr int W = 56;
+    static constexpr int W = 52;
     static constexpr int P = 52;
     static constexpr int KMIN = -1074;
     static constexpr int PLANES = 5;
@@ -279,6 +279,10 @@ __device__ __forceinline__ typename MseTraits<T>::Fix fixed_point(typename MseTr
     else return dn < 64 ? mm >> dn : 0;
 }
 
+// a + b rounded toward zero (for a >= 0 and b = 2^P: 2^P + floor(a) while a < 2^P)
+__device__ __forceinline__ float add_rz(float a, float b) { return __fadd_rz(a, b); }
+__device__ __forceinline__ double add_rz(double a, double b) { return __dadd_rz(a, b); }
+
 // Ask the L2 to fetch [p, p + bytes) ahead of its use (a hint: no destination, no completion).
 __device__ __forceinline__ void prefetch_l2(const void *p, unsigned bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
@@ -311,7 +315,9 @@ mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base
     constexpr int VW = 16 / sizeof(T);  // elements per 16-byte load
     constexpr unsigned FULL = 0xffffffffu;
 
-    __shared__ Tie s_ties[kChunkWarps][Tr::CHUNK];  // a chunk's ties in element order
+    // per warp: the chunk's fixed-point squares, then (in place) its ties in element order
+    __shared__ __align__(16) unsigned char s_slot[kChunkWarps][Tr::CHUNK * sizeof(Fix)];
+    __shared__ Fix s_lane_ex[kChunkWarps][ROWS][32];  // exclusive prefix XOR in front of (row, lane)
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint64_t chunk = (uint64_t)blockIdx.x * kChunkWarps + warp;
@@ -337,7 +343,7 @@ mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base
     // elements with the checked law, in order, and stop at their first fault (their later events
     // cannot win).
     Fix qf[EPT];  // q's bits first, its fixed-point form later; qf[row * V + e]
-    B qmax_t = 0, dmin = ~(B)0;
+    B qmax_t = 0, dmin = ~(B)0;  // the lane's largest square (bits), smallest nonzero |d| (below)
     const uint64_t t0 = chunk0 + CM::index(0, lane, 0);  // this lane's first element
     if (vec && chunk0 + Tr::CHUNK <= n) {  // whole chunk in range, 16-byte aligned operands
         const T *pp = prediction + t0;
@@ -408,31 +414,67 @@ mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base
         }
         return;
     }
-    const int k_hi = exponent_of<T>(qmax) + 1;
+    const int k_hi = exponent_of<T>(qmax) + 1;  // every square is below 2^k_hi
     const int k_lo = max(k_hi - (W - 1), Tr::KMIN);
     const int L0 = k_lo - 1;  // fixed-point unit 2^L0
     const int C = F::kBias + F::kFrac + 3 + L0;
     const Fix K = (Fix)(1 - C) * ((Fix)1 << (F::kFrac + 3));
     head.k_lo = k_lo;
 
-    // ---- fixed point Q = floor(q / 2^L0); per row the XOR of the Q; the largest lowest set bit
-    // (a tie at binade offset j is a Q whose lowest set bit is j - 1 with nothing below 2^L0)
-    Fix X[ROWS];
-    Fix maxlow = 0;
+    // ---- fixed point Q = floor(q / 2^L0) < 2^W, carried as the bits of 2^P + Q (MARK | Q), with a
+    // sticky flag in the (otherwise clear) sign bit when q has bits below 2^L0.  While
+    // 2^-L0 is a normal number, q * 2^-L0 is exact and the round-toward-zero add of 2^P floors it,
+    // both on the FP pipe; otherwise the integer form.  Per row: the XOR of the words, and the OR
+    // of the trailing-zero masks of the nonzero Q with nothing below 2^L0 (bit b set: such a Q
+    // has its lowest set bit above b), which flags the rows that hold ties.  The words also go to this warp's
+    // shared-memory slot, where the tie pass reads them.
+    constexpr Fix MARK = sizeof(T) == 4 ? (Fix)0x4b000000u : (Fix)0x4330000000000000ull;  // bits of 2^P
+    constexpr Fix LOW = ((Fix)1 << W) - 1;
+    constexpr Fix STICKY = (Fix)1 << (sizeof(Fix) * 8 - 1);  // the sign bit: set when q has bits below 2^L0
+    Fix X[ROWS], tz[ROWS];
+    Fix *qs = reinterpret_cast<Fix *>(s_slot[warp]);
+    if (L0 >= -F::kBias) {
+        const T scale = F::value((B)(F::kBias - L0) << F::kFrac);  // 2^-L0
+        const T magic = F::value((B)MARK);                         // 2^P
 #pragma unroll
-    for (int r = 0; r < ROWS; ++r) {
-        X[r] = 0;
+        for (int r = 0; r < ROWS; ++r) {
+            X[r] = 0;
+            tz[r] = 0;
 #pragma unroll
-        for (int e = 0; e < V; ++e) {
-            int dn;
-            Fix mm;
-            const Fix Q = fixed_point<T>(qf[r * V + e], C, K, dn, mm);
-            qf[r * V + e] = Q;
-            X[r] ^= Q;
-            const Fix low = Q & ((Fix)0 - Q);
-            maxlow = low > maxlow ? low : maxlow;
+            for (int e = 0; e < V; ++e) {
+                const T qs_ = F::mul(F::value((B)qf[r * V + e]), scale);  // q / 2^L0, exact
+                const T t = add_rz(qs_, magic);                          // 2^P + floor(q / 2^L0)
+                const bool exact = F::sub(t, magic) == qs_;  // nothing of q below 2^L0
+                const Fix tb = (Fix)F::bits(t) | (exact ? (Fix)0 : STICKY);
+                qf[r * V + e] = tb;
+                X[r] ^= tb;
+                // only a nonzero Q with nothing below 2^L0 can be a tie
+                if (exact && tb != MARK) tz[r] |= (tb - 1) & ~tb;
+            }
+        }
+    } else {
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r) {
+            X[r] = 0;
+            tz[r] = 0;
+#pragma unroll
+            for (int e = 0; e < V; ++e) {
+                int dn;
+                Fix mm;
+                const Fix Q = fixed_point<T>(qf[r * V + e], C, K, dn, mm);
+                const bool exact = dn >= (int)(sizeof(Fix) * 8) ? mm == 0 : (mm & (((Fix)1 << dn) - 1)) == 0;
+                const Fix tb = Q | MARK | (exact ? (Fix)0 : STICKY);
+                qf[r * V + e] = tb;
+                X[r] ^= tb;
+                if (Q != 0 && exact) tz[r] |= (tb - 1) & ~tb;
+            }
         }
     }
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r)
+#pragma unroll
+        for (int v = 0; v < (int)(V * sizeof(Fix) / 16); ++v)
+            reinterpret_cast<uint4 *>(qs + CM::index(r, lane, 0))[v] = reinterpret_cast<const uint4 *>(&qf[r * V])[v];
     // ---- per-bit population counts of the chunk: Harley-Seal vertical counters per lane, then
     // a warp bit-transpose per counter plane leaves the count of bit 32 w + b in lane b, word w
     uint64_t cnt[NW];
@@ -452,26 +494,27 @@ mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base
     }
     // ---- exclusive prefix XOR of R = Q ^ (Q << 1) in element order, per row across the lanes
     // (XOR is linear: a row's R total is R of the row's XOR)
-    Fix lane_ex[ROWS];
     {
         Fix total = 0;
 #pragma unroll
         for (int r = 0; r < ROWS; ++r) {
-            const Fix row = X[r] ^ (X[r] << 1);
+            const Fix xr = X[r] & LOW;
+            const Fix row = xr ^ (xr << 1);
             Fix incl = row;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
                 const Fix v = shfl_up_x(incl, o);
                 if (lane >= o) incl ^= v;
             }
-            lane_ex[r] = total ^ incl ^ row;  // rows before r, then lanes before this one
+            s_lane_ex[warp][r][lane] = total ^ incl ^ row;  // rows before r, then lanes before this one
             total ^= shfl_x(incl, 31);
         }
     }
     // ---- S_b = sum over bits b' >= b of cnt[b'] 2^(b'-b) (saturated) for b = 32 w + lane: a
     // suffix scan over the lanes per word, the upper word's total carried into the lower one.
-    // W_j = S_j.  jmin: the lowest j from which on every half-up sum W_j + cnt[j-1] fits inside
-    // one binade (< 2^(P+1)); the sums only grow as j falls, so the failing j form a prefix.
+    // W_j = S_j.  jmin: the lowest j from which on every half-up sum W_j + cnt[j-1] is below 2^P
+    // (a state in a normal binade is at least 2^P ulps, so a larger sum always leaves it); the
+    // sums only grow as j falls, so the failing j form a prefix.
     uint64_t S[NW];
 #pragma unroll
     for (int w = NW - 1; w >= 0; --w) {
@@ -492,61 +535,55 @@ mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base
         const uint64_t carry = shfl_x(cnt[w > 0 ? w - 1 : 0], 31);
         cprev[w] = lane > 0 ? below : (w > 0 ? carry : 0);
         const int j = 32 * w + lane;
-        if (j >= 1 && j <= W && (S[w] >= Tr::SAT || S[w] + cprev[w] >= (2ull << Tr::P))) fail_max = j;
+        if (j >= 1 && j <= W && (S[w] >= Tr::SAT || S[w] + cprev[w] >= (1ull << Tr::P))) fail_max = j;
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) fail_max = max(fail_max, __shfl_xor_sync(FULL, fail_max, o));
     const int jmin = fail_max + 1;
 
     // ---- ties at the usable binades: a Q whose lowest set bit is at or above jmin - 1 with
-    // nothing of q below 2^L0.  Rare for rounded squares (a warp enters only when some lane's
-    // largest lowest set bit reaches jmin - 1), common for exactly representable ones.  The
-    // lanes recompute their squares exactly (the register copy is not indexed here, so that it
-    // stays in registers; the chunk is fault-free, so the IEEE square is the law's) and the
-    // ties are listed in element order with the parity of the half-up increments in front of
-    // each.  (A chunk with a Subtract/Multiply fault is never mapped, only resolved up to it.)
+    // nothing of q below 2^L0.  Rare for rounded squares, common for exactly representable
+    // ones.  Only rows flagged by the trailing-zero masks are visited.  The ties are listed
+    // in element order, with the parity of the half-up increments in front of each, in place of
+    // the Q already read (a row's ties never outnumber its elements).  (A chunk with a
+    // Subtract/Multiply fault is never mapped, only resolved up to the fault.)
     unsigned ties = 0;
-    const bool probe = !(head.flags & kHeadFault) && jmin <= W && maxlow >= ((Fix)1 << (jmin - 1));
-    if (__any_sync(FULL, probe)) {
-        const Fix lowmask = ((Fix)1 << (jmin - 1)) - 1;
-#pragma unroll 1
+    Tie *tl = reinterpret_cast<Tie *>(s_slot[warp]);
+    if (!(head.flags & kHeadFault) && jmin <= W) {
+        const Fix threshold = (Fix)1 << (jmin - 1), lowmask = threshold - 1;
+#pragma unroll
         for (int r = 0; r < ROWS; ++r) {
-            Fix prefix = get_at(lane_ex, r);
+            const bool row_may = jmin < 2 || ((tz[r] >> (jmin - 2)) & 1);
+            if (!__any_sync(FULL, row_may)) continue;
+            Fix Q[V];
+#pragma unroll
+            for (int v = 0; v < (int)(V * sizeof(Fix) / 16); ++v)
+                reinterpret_cast<uint4 *>(Q)[v] = reinterpret_cast<const uint4 *>(qs + CM::index(r, lane, 0))[v];
             unsigned mask = 0;   // bit e: element (r, lane, e) is a tie
             uint64_t code = 0;   // byte e: its j (6 bits) and parities (2 bits)
+            if (row_may) {
+                Fix prefix = s_lane_ex[warp][r][lane];
 #pragma unroll
-            for (int e = 0; e < V; ++e) {
-                const int c = CM::index(r, lane, e);
-                const uint64_t i = chunk0 + c;
-                Fix qb = 0;
-                if (probe && i < n) {
-                    const T d = F::sub(prediction[i], target[i]);
-                    qb = (Fix)F::bits(F::mul(d, d));
-                }
-                int dn;
-                Fix mm;
-                const Fix Q = fixed_point<T>(qb, C, K, dn, mm);
-                if (Q != 0 && (Q & lowmask) == 0) {
-                    const bool sticky = dn >= (int)(sizeof(Fix) * 8) ? mm != 0 : (mm & (((Fix)1 << dn) - 1)) != 0;
-                    if (!sticky) {
-                        const int j = sizeof(Fix) == 4 ? __ffs((int)Q) : __ffsll((long long)Q);  // lowest bit + 1
+                for (int e = 0; e < V; ++e) {
+                    const Fix q = Q[e] & LOW;
+                    if (q != 0 && (q & lowmask) == 0 && !(Q[e] & STICKY)) {
+                        const int j = sizeof(Fix) == 4 ? __ffs((int)q) : __ffsll((long long)q);  // lowest bit + 1
                         mask |= 1u << e;
-                        code |= (uint64_t)(j | (int)((Q >> j) & 1) << 6 | (int)((prefix >> j) & 1) << 7) << (8 * e);
+                        code |= (uint64_t)(j | (int)((q >> j) & 1) << 6 | (int)((prefix >> j) & 1) << 7) << (8 * e);
                     }
+                    prefix ^= q ^ (q << 1);
                 }
-                prefix ^= Q ^ (Q << 1);
             }
             // lanes in order, each lane's elements in order: an exclusive prefix of the counts
-            const unsigned cnt_here = __popc(mask);
-            unsigned before = cnt_here;
+            const unsigned here = __popc(mask);
+            unsigned before = here;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
                 const unsigned v = __shfl_up_sync(FULL, before, o);
                 if (lane >= o) before += v;
             }
             const unsigned row_total = __shfl_sync(FULL, before, 31);
-            before -= cnt_here;
-            unsigned slot = ties + before;
+            unsigned slot = ties + before - here;  // <= this row's first element: already read
 #pragma unroll
             for (int e = 0; e < V; ++e) {
                 if (mask >> e & 1) {
@@ -555,12 +592,12 @@ mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base
                     t.index = (uint16_t)CM::index(r, lane, e);
                     t.j = (uint8_t)(b & 63);
                     t.bits = (uint8_t)(b >> 6);
-                    s_ties[warp][slot++] = t;
+                    tl[slot++] = t;
                 }
             }
             ties += row_total;
+            __syncwarp();
         }
-        __syncwarp();
     }
     if (lane == 0) heads[chunk] = head;
     // ---- one lane per binade offset j (binade k = k_lo + j - 1): the half-up sum
@@ -575,7 +612,7 @@ mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base
         int64_t corr[2] = {0, 0};
         if (usable) {
             for (unsigned i = 0; i < ties; ++i) {
-                const Tie t = s_ties[warp][i];
+                const Tie t = tl[i];
                 if (t.j != j) continue;
 #pragma unroll
                 for (int p0 = 0; p0 < 2; ++p0) {
