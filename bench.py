@@ -69,10 +69,13 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200", "-i",
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100", "-i",
                  str(self.device_index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.reader = threading.Thread(target=self._read, daemon=True)
             self.reader.start()
+            deadline = time.time() + 5.0  # the timed region starts once sampling has begun
+            while not self.lines and time.time() < deadline and self.proc.poll() is None:
+                time.sleep(0.02)
         except (OSError, ValueError):
             self.proc = None
         return self
