@@ -94,7 +94,11 @@ template <typename T> struct ReluBackwardOp {
 };
 
 // a and b are element streams; a uniform stream (or a missing b) reads element 0 only.
-template <typename T, int V, class Op>
+#ifndef PCU_STREAM_UNROLL
+#define PCU_STREAM_UNROLL 2
+#endif
+
+template <typename T, int V, class Op, int U = (V > 1 ? PCU_STREAM_UNROLL : 1)>
 __global__ void __launch_bounds__(256) streaming_kernel(const T *a, const T *b,
                                                          T *out, uint64_t n, int a_uniform, int b_uniform,
                                                          Op op, unsigned long long *status) {
@@ -103,31 +107,44 @@ __global__ void __launch_bounds__(256) streaming_kernel(const T *a, const T *b,
     const uint64_t nvec = n / V;
     const T a0 = a_uniform ? a[0] : T(0);
     const T b0 = (b_uniform && b) ? b[0] : T(0);
-    for (uint64_t v = tid; v < nvec; v += stride) {
-        const uint64_t base = v * V;
-        T av[V], bv[V], ov[V];
-        if (a_uniform) {
+    // U vectors per trip (the thread's vectors v, v + stride, ...: still in increasing order), all
+    // loads issued before any is used, so every thread keeps U * 32 bytes in flight
+    for (uint64_t v0 = tid; v0 < nvec; v0 += stride * U) {
+        T av[U][V], bv[U][V];
 #pragma unroll
-            for (int i = 0; i < V; ++i) av[i] = a0;
-        } else {
-            load_vec<T, V>(a + base, av);
-        }
-        if (b_uniform || !b) {
+        for (int u = 0; u < U; ++u) {
+            const uint64_t v = v0 + (uint64_t)u * stride;
+            if (v >= nvec) break;
+            if (a_uniform) {
 #pragma unroll
-            for (int i = 0; i < V; ++i) bv[i] = b0;
-        } else {
-            load_vec<T, V>(b + base, bv);
-        }
+                for (int i = 0; i < V; ++i) av[u][i] = a0;
+            } else {
+                load_vec<T, V>(a + v * V, av[u]);
+            }
+            if (b_uniform || !b) {
 #pragma unroll
-        for (int i = 0; i < V; ++i) {
-            unsigned step;
-            unsigned kind = op(av[i], bv[i], ov[i], step);
-            if (kind) {
-                record_fault(status, (unsigned long long)(base + i) * Op::kSteps + step, kind);
-                return;
+                for (int i = 0; i < V; ++i) bv[u][i] = b0;
+            } else {
+                load_vec<T, V>(b + v * V, bv[u]);
             }
         }
-        store_vec<T, V>(out + base, ov);
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const uint64_t v = v0 + (uint64_t)u * stride;
+            if (v >= nvec) break;
+            const uint64_t base = v * V;
+            T ov[V];
+#pragma unroll
+            for (int i = 0; i < V; ++i) {
+                unsigned step;
+                unsigned kind = op(av[u][i], bv[u][i], ov[i], step);
+                if (kind) {
+                    record_fault(status, (unsigned long long)(base + i) * Op::kSteps + step, kind);
+                    return;
+                }
+            }
+            store_vec<T, V>(out + base, ov);
+        }
     }
     for (uint64_t i = nvec * V + tid; i < n; i += stride) {
         T x = a_uniform ? a0 : a[i];
@@ -153,7 +170,10 @@ int launch_streaming(const T *a, const T *b, T *out, uint64_t n, int a_uniform, 
     const int threads = 256;
     uint64_t units = vec ? (n + V - 1) / V : n;
     uint64_t want = (units + threads - 1) / threads;
-    uint64_t cap = (uint64_t)pcu_host::sm_count() * 8;
+#ifndef PCU_STREAM_CTAS_PER_SM
+#define PCU_STREAM_CTAS_PER_SM 8
+#endif
+    uint64_t cap = (uint64_t)pcu_host::sm_count() * PCU_STREAM_CTAS_PER_SM;
     unsigned blocks = (unsigned)(want < cap ? (want ? want : 1) : cap);
     if (vec)
         streaming_kernel<T, V, Op><<<blocks, threads, 0, stream>>>(a, b, out, n, a_uniform, b_uniform, op, status);
