@@ -32,6 +32,7 @@ METRIC = "strict F32 MatMul TFLOP/s @8192^3 at 1/2/4/8 B200; MSE+SGD HBM GB/s"
 N = 8192
 FLOPS = 2.0 * N * N * N
 MSE_SGD_ELEMS = 1 << 28
+MATMUL_TRAFFIC_BYTES = 3378593536 + 266733056  # measured DRAM bytes of one 8192^3 strict MatMul launch
 
 
 def parse():
@@ -313,7 +314,10 @@ def main():
                                     "non-FMA: 1 FMUL + 1 FADD per (cell,k); tensor cores are excluded by the "
                                     "strict contract",
                      "frac_at_run_clock": (kernel_tflops / run_peak) if run_peak else None,
-                     "traffic": None},
+                     # dram__bytes_read.sum + dram__bytes_write.sum of one 8192^3 launch (ncu,
+                     # profiles/strict_matmul_f32_8192cubed_traffic.md); per rank at N > 1 the
+                     # launch is the rank's row block
+                     "traffic": MATMUL_TRAFFIC_BYTES / world, "traffic_unit": "bytes per launch"},
         "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"]},
         "gpu_launches": 3 * args.steps,
     }

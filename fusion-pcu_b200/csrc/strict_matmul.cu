@@ -221,6 +221,7 @@ template <typename T> struct TileShape {
 // sub-partition and cap every thread at 168 registers.  Thread 0 issues the TMA copies instead.
 constexpr int kConsumerWarps = 8;
 constexpr int kThreads = kConsumerWarps * 32;
+constexpr unsigned kGroupRows = 8;  // tile rows per group of the CTA order
 // Stages in flight beyond the one being folded.  Thread 0 refills the slot of stage kt-2 while
 // folding stage kt, so it practically never waits for a slower warp to release a slot.
 constexpr int kLookahead = PCU_MM_LOOKAHEAD;
@@ -245,7 +246,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     __shared__ int abort_flag;
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const uint64_t m0 = (uint64_t)blockIdx.y * BM, n0 = (uint64_t)blockIdx.x * BN;
+    // Tiles in groups of kGroupRows tile rows, column by column inside a group: the CTAs resident
+    // at once share a few A row panels and B column panels, which stay in L2 while they are read.
+    uint64_t m0, n0;
+    {
+        const unsigned tiles_n = gridDim.x, tiles_m = gridDim.y;
+        const unsigned id = blockIdx.y * tiles_n + blockIdx.x;  // launch order
+        const unsigned first_m = id / (kGroupRows * tiles_n) * kGroupRows;
+        const unsigned rows_here = min((unsigned)kGroupRows, tiles_m - first_m);
+        const unsigned in_group = id - first_m * tiles_n;
+        m0 = (uint64_t)(first_m + in_group % rows_here) * BM;
+        n0 = (uint64_t)(in_group / rows_here) * BN;
+    }
     const int KT = (int)((p.inner + BK - 1) / BK);
 
     if (threadIdx.x == 0) {
