@@ -315,9 +315,9 @@ def main():
                                     "strict contract",
                      "frac_at_run_clock": (kernel_tflops / run_peak) if run_peak else None,
                      # dram__bytes_read.sum + dram__bytes_write.sum of one 8192^3 launch (ncu,
-                     # profiles/strict_matmul_f32_8192cubed_traffic.md); per rank at N > 1 the
-                     # launch is the rank's row block
-                     "traffic": MATMUL_TRAFFIC_BYTES / world, "traffic_unit": "bytes per launch"},
+                     # profiles/strict_matmul_f32_8192cubed_traffic.md); not captured for the
+                     # row blocks of N > 1
+                     "traffic": MATMUL_TRAFFIC_BYTES if world == 1 else None, "traffic_unit": "bytes per launch"},
         "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"]},
         "gpu_launches": 3 * args.steps,
     }
