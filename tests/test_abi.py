@@ -70,9 +70,10 @@ def test_workspace_sizes(provider, rows, inner, columns):
     lib = provider.library()
     need = lib.pcu_b200_strict_matmul_workspace_size(rows, inner, columns)
     assert need >= 4 * (rows + columns) and need % 256 == 0
-    # strict MSE keeps one ordered-sum map per chunk (F32: 8192 elements -> a 16-byte head and
-    # 2 x 27 u32 deltas; F64: 4096 elements -> a head and 2 x 56 u64 deltas), plus one per block
-    for dtype, chunk, per_chunk in ((0, 8192, 16 + 2 * 27 * 4), (1, 4096, 16 + 2 * 56 * 8)):
+    # strict MSE keeps one ordered-sum map per chunk (F32: 1024 elements -> a 16-byte head and
+    # 2 x 23 u32 increments; F64: 512 elements -> a head and 2 x 52 u64 increments), plus one per
+    # block of 64 chunks and one per superblock of 64 blocks
+    for dtype, chunk, per_chunk in ((0, 1024, 16 + 2 * 23 * 4), (1, 512, 16 + 2 * 52 * 8)):
         got = lib.pcu_b200_strict_mse_workspace_size(dtype, 1 << 28)
         assert got >= ((1 << 28) // chunk) * per_chunk and got % 256 == 0
         assert got < ((1 << 28) // chunk) * per_chunk * 1.1
