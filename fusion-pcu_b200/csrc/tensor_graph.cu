@@ -293,7 +293,6 @@ struct pcu_b200_graph {
 
 // ============================================================================ execution
 struct pcu_b200_prepared {
-    const pcu_b200_graph *graph_snapshot = nullptr;
     pcu_b200_graph graph;           // frozen copy of the captured graph
     std::vector<int32_t> plan;      // node ids in graph order
     std::vector<int32_t> inputs;    // planned Input node ids in capture order
@@ -302,7 +301,12 @@ struct pcu_b200_prepared {
     void *workspace = nullptr;
     size_t workspace_bytes = 0;
     size_t elem = 4;
+    cudaGraphExec_t replay = nullptr;  // the node launches recorded as one CUDA graph
+    cudaStream_t replay_stream = nullptr;  // the stream it was recorded on
+    cudaStream_t own_stream = nullptr;     // used for replay when the caller passes the legacy stream
     ~pcu_b200_prepared() {
+        if (replay) cudaGraphExecDestroy(replay);
+        if (own_stream) cudaStreamDestroy(own_stream);
         for (void *b : buffers)
             if (b) cudaFree(b);
         if (status) cudaFree(status);
@@ -627,11 +631,74 @@ extern "C" void *pcu_b200_prepared_buffer(const pcu_b200_prepared *p, int32_t v)
     return (p && v >= 0 && (size_t)v < p->buffers.size()) ? p->buffers[v] : nullptr;
 }
 
-extern "C" int pcu_b200_prepared_execute(pcu_b200_prepared *p, const void *const *host_inputs, int wait_each_node,
+namespace {
+
+// The status reset and every planned node, launched back to back on `s`.
+int launch_plan(pcu_b200_prepared &p, cudaStream_t s, int32_t &failed) {
+    failed = -1;
+    int rc = pcu_b200_status_reset(p.status, p.graph.nodes.size(), s);
+    if (rc) return rc;
+    for (int32_t id : p.plan) {
+        rc = launch(p, id, s);
+        if (rc) {
+            failed = id;
+            return rc;
+        }
+    }
+    return PCU_B200_OK;
+}
+
+// One read of every status word; the lowest faulting node in graph order wins.
+int read_and_decode(pcu_b200_prepared &p, cudaStream_t s, pcu_b200_tensor_error *e) {
+    std::vector<uint64_t> words(p.graph.nodes.size());
+    cudaError_t err = cudaMemcpyAsync(words.data(), p.status, words.size() * 8, cudaMemcpyDeviceToHost, s);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(s);
+    if (err != cudaSuccess) return backend_error(e, -1, (int)err);
+    for (int32_t id : p.plan)
+        if (int code = decode(p, id, words[id], e)) return code;
+    return PCU_B200_TENSOR_OK;
+}
+
+// Record the launch sequence of the plan as a CUDA graph on `s` (after one ordinary run, so that
+// every kernel's one-time host set-up has happened outside the capture).
+int record_replay(pcu_b200_prepared &p, cudaStream_t s, pcu_b200_tensor_error *e) {
+    cudaError_t err = cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal);
+    if (err != cudaSuccess) return backend_error(e, -1, (int)err);
+    int32_t failed = -1;
+    const int rc = launch_plan(p, s, failed);
+    cudaGraph_t g = nullptr;
+    err = cudaStreamEndCapture(s, &g);
+    if (rc) {
+        if (g) cudaGraphDestroy(g);
+        return backend_error(e, failed, rc);
+    }
+    if (err != cudaSuccess) return backend_error(e, -1, (int)err);
+    err = cudaGraphInstantiate(&p.replay, g, 0);
+    cudaGraphDestroy(g);
+    if (err != cudaSuccess) {
+        p.replay = nullptr;
+        return backend_error(e, -1, (int)err);
+    }
+    p.replay_stream = s;
+    return PCU_B200_TENSOR_OK;
+}
+
+}  // namespace
+
+extern "C" int pcu_b200_prepared_execute(pcu_b200_prepared *p, const void *const *host_inputs, int mode,
                                          void *stream, pcu_b200_tensor_error *e) {
     clear(e);
     if (!p) return fail(e, PCU_B200_TENSOR_UNKNOWN_VALUE), PCU_B200_TENSOR_UNKNOWN_VALUE;
+    if (mode < PCU_B200_EXEC_CHAINED || mode > PCU_B200_EXEC_GRAPH)
+        return fail(e, PCU_B200_TENSOR_UNKNOWN_VALUE), PCU_B200_TENSOR_UNKNOWN_VALUE;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (mode == PCU_B200_EXEC_GRAPH && !s) {  // a CUDA graph cannot be recorded on the legacy stream
+        if (!p->own_stream) {
+            cudaError_t err = cudaStreamCreateWithFlags(&p->own_stream, cudaStreamNonBlocking);
+            if (err != cudaSuccess) return backend_error(e, -1, (int)err);
+        }
+        s = p->own_stream;
+    }
     for (size_t i = 0; i < p->inputs.size(); ++i) {
         if (!host_inputs || !host_inputs[i]) continue;
         const int32_t v = p->inputs[i];
@@ -639,13 +706,36 @@ extern "C" int pcu_b200_prepared_execute(pcu_b200_prepared *p, const void *const
                                           cudaMemcpyHostToDevice, s);
         if (err != cudaSuccess) return backend_error(e, v, (int)err);
     }
+    if (mode == PCU_B200_EXEC_GRAPH) {
+        if (p->replay && p->replay_stream == s) {
+            cudaError_t err = cudaGraphLaunch(p->replay, s);
+            if (err != cudaSuccess) return backend_error(e, -1, (int)err);
+            return read_and_decode(*p, s, e);
+        }
+        // first run on this stream: an ordinary run gives the answer, then the plan is recorded
+        int32_t failed = -1;
+        const int rc = launch_plan(*p, s, failed);
+        if (rc) return backend_error(e, failed, rc);
+        const int code = read_and_decode(*p, s, e);
+        if (p->replay) {
+            cudaGraphExecDestroy(p->replay);
+            p->replay = nullptr;
+        }
+        pcu_b200_tensor_error scratch;
+        const int rec = record_replay(*p, s, &scratch);
+        if (rec && !code) {
+            if (e) *e = scratch;
+            return rec;
+        }
+        return code;
+    }
     int rc = pcu_b200_status_reset(p->status, p->graph.nodes.size(), stream);
     if (rc) return backend_error(e, -1, rc);
     uint64_t word = 0;
     for (int32_t id : p->plan) {
         rc = launch(*p, id, stream);
         if (rc) return backend_error(e, id, rc);
-        if (wait_each_node && p->graph.nodes[id].op != PCU_B200_NODE_INPUT &&
+        if (mode == PCU_B200_EXEC_EACH_NODE && p->graph.nodes[id].op != PCU_B200_NODE_INPUT &&
             p->graph.nodes[id].op != PCU_B200_NODE_UNIFORM) {
             // the reference's per-node completion wait and status decode (strict_matmul.rs:317-331)
             cudaError_t err = cudaMemcpyAsync(&word, p->status + id, 8, cudaMemcpyDeviceToHost, s);
@@ -654,14 +744,7 @@ extern "C" int pcu_b200_prepared_execute(pcu_b200_prepared *p, const void *const
             if (int code = decode(*p, id, word, e)) return code;
         }
     }
-    if (!wait_each_node) {
-        std::vector<uint64_t> words(p->graph.nodes.size());
-        cudaError_t err = cudaMemcpyAsync(words.data(), p->status, words.size() * 8, cudaMemcpyDeviceToHost, s);
-        if (err == cudaSuccess) err = cudaStreamSynchronize(s);
-        if (err != cudaSuccess) return backend_error(e, -1, (int)err);
-        for (int32_t id : p->plan)  // the lowest faulting node in graph order wins
-            if (int code = decode(*p, id, words[id], e)) return code;
-    }
+    if (mode == PCU_B200_EXEC_CHAINED) return read_and_decode(*p, s, e);
     return PCU_B200_TENSOR_OK;
 }
 

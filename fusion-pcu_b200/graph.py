@@ -19,6 +19,7 @@ from . import (KIND_NAMES, POLICY, ArithmeticFault, CompoundArithmeticFault, Pro
 NODE_OPS = ["input", "uniform", "add", "sub", "mul", "div", "relu", "relu_backward", "matmul", "mean_squared_error",
             "sgd_update"]
 STEPS = ["Multiply", "Add", "Subtract", "Divide"]
+EXEC_MODES = {"chained": 0, "each_node": 1, "graph": 2}
 CODES = {1: "ArithmeticFault", 2: "CompoundArithmeticFault", 3: "ShapeMismatch", 4: "MatMulShape", 5: "UnknownValue",
          6: "InvalidLearningRate", 7: "GradientRootNotMse", 8: "UnsupportedGradient", 9: "EmptyOutputs",
          10: "DataLength", 11: "Backend"}
@@ -241,8 +242,11 @@ class PreparedGraph:
         """Device address of a planned value's buffer (0 if the value is not planned)."""
         return self._L.pcu_b200_prepared_buffer(self._h, value) or 0
 
-    def execute(self, inputs=None, wait_each_node=True, stream=None):
-        """Copy the host `inputs` ({input value: array}) in, run the plan and raise the first fault."""
+    def execute(self, inputs=None, wait_each_node=True, stream=None, mode=None):
+        """Copy the host `inputs` ({input value: array}) in, run the plan and raise the first fault.
+
+        mode: "chained" (one status read at the end), "each_node" (the reference's per-node wait)
+        or "graph" (CUDA-graph replay); by default wait_each_node picks the first two."""
         inputs = inputs or {}
         held = []
         ptrs = (ctypes.c_void_p * max(len(self.inputs), 1))()
@@ -256,7 +260,8 @@ class PreparedGraph:
                 ptrs[i] = arr.ctypes.data
         e = TensorErrorStruct()
         s = ctypes.c_void_p(stream.cuda_stream) if stream is not None else None
-        rc = self._L.pcu_b200_prepared_execute(self._h, ptrs, int(wait_each_node), s, ctypes.byref(e))
+        code = EXEC_MODES[mode] if mode is not None else (1 if wait_each_node else 0)
+        rc = self._L.pcu_b200_prepared_execute(self._h, ptrs, code, s, ctypes.byref(e))
         del held
         if rc:
             _raise(e)
@@ -270,8 +275,8 @@ class PreparedGraph:
             raise GraphError(rc, value)
         return out
 
-    def run(self, inputs, outputs, wait_each_node=True):
-        self.execute(inputs, wait_each_node)
+    def run(self, inputs, outputs, wait_each_node=True, mode=None):
+        self.execute(inputs, wait_each_node, mode=mode)
         return {o: self.read(o) for o in outputs}
 
 

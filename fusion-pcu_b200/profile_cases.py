@@ -27,7 +27,7 @@ def dyadic(torch, shape, seed, dtype):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["matmul", "sgd", "mse", "binary"])
+    ap.add_argument("case", choices=["matmul", "sgd", "mse", "binary", "train1"])
     ap.add_argument("--m", type=int, default=8192)
     ap.add_argument("--n", type=int, default=8192)
     ap.add_argument("--k", type=int, default=1024)
@@ -43,6 +43,9 @@ def main():
 
     pcu = importlib.import_module("fusion-pcu_b200")
     dt = torch.float32 if args.dtype == "f32" else torch.float64
+    if args.case == "train1":
+        train_step(args)
+        return
     status = pcu.new_status()
     if args.case == "matmul":
         tl, tr = args.layout[0] == "t", args.layout[1] == "t"
@@ -97,6 +100,38 @@ def main():
             e1.record()
             torch.cuda.synchronize()
             print(f"  {name} {e0.elapsed_time(e1) / args.repeat:.3f} ms/call")
+
+
+def train_step(args):
+    """The single-layer strict train step of BASELINE configs[0] (X 256x512, W 512x256, bias and
+    target 256x256, lr 0.5) through the graph layer: milliseconds per step in each execution mode,
+    the weights fed back from the device buffer between steps."""
+    import numpy as np
+    import torch
+
+    graph = importlib.import_module("fusion-pcu_b200.graph")
+    rng = np.random.default_rng(1)
+    g = graph.Graph(32, 0)
+    x, w, b, t = g.input((256, 512)), g.input((512, 256)), g.input((256, 256)), g.input((256, 256))
+    y = g.relu(g.add(g.matmul(x, w), b))
+    loss = g.mean_squared_error(y, t)
+    upd = g.sgd_update(w, g.backward_mse_for(loss, w), 0.5)
+    prepared = g.prepare([upd, loss])
+    feed = {x: (rng.integers(-2**23, 2**23, (256, 512)) * 2.0**-23).astype(np.float32),
+            w: (rng.integers(-2**23, 2**23, (512, 256)) * 2.0**-23).astype(np.float32),
+            b: (rng.integers(-2**23, 2**23, (256, 256)) * 2.0**-23).astype(np.float32),
+            t: (rng.integers(0, 2**24, (256, 256)) * 2.0**-24).astype(np.float32)}
+    stream = torch.cuda.Stream()
+    for mode in ("each_node", "chained", "graph"):
+        with torch.cuda.stream(stream):
+            prepared.execute(feed, mode=mode, stream=stream)
+            torch.cuda.synchronize()
+            import time
+            t0 = time.perf_counter()
+            for _ in range(args.repeat):
+                prepared.execute({}, mode=mode, stream=stream)  # inputs stay on the device
+            dt = (time.perf_counter() - t0) / args.repeat
+        print(f"train1 {mode} {dt * 1e3:.3f} ms/step (host-observed, status read included)")
 
 
 if __name__ == "__main__":

@@ -117,13 +117,19 @@ int32_t pcu_b200_prepared_input_value(const pcu_b200_prepared *prepared, int32_t
 /* Device buffer of a planned value (inputs can be written there directly). */
 void *pcu_b200_prepared_buffer(const pcu_b200_prepared *prepared, int32_t value);
 
+/* Execution modes of pcu_b200_prepared_execute */
+#define PCU_B200_EXEC_CHAINED 0   /* every node launched back to back; one status read at the end */
+#define PCU_B200_EXEC_EACH_NODE 1 /* the reference's protocol: one host wait and status read per node */
+#define PCU_B200_EXEC_GRAPH 2     /* the launches replayed as one CUDA graph; one status read at the end */
+
 /* Execute: copies `host_inputs` (one host pointer per planned input, NULL = already on the
  * device buffer) to the device, runs every planned node in graph order on `stream`, and
- * reports the first faulting node exactly as the reference does.
- *   wait_each_node != 0: the reference's protocol, one host wait and status read per node.
- *   wait_each_node == 0: every node is launched back to back; one status read at the end.
- * Returns 0 on success or a PCU_B200_TENSOR_* code (details in *error). */
-int pcu_b200_prepared_execute(pcu_b200_prepared *prepared, const void *const *host_inputs, int wait_each_node,
+ * reports the first faulting node exactly as the reference does (every mode gives the same
+ * answer: the lowest faulting node, and in it the lowest event).  PCU_B200_EXEC_GRAPH records
+ * the plan's launches as a CUDA graph on the first call on a stream (that call runs the plan
+ * normally) and replays it afterwards; with the legacy stream (NULL) the prepared graph uses a
+ * stream of its own.  Returns 0 on success or a PCU_B200_TENSOR_* code (details in *error). */
+int pcu_b200_prepared_execute(pcu_b200_prepared *prepared, const void *const *host_inputs, int mode,
                               void *stream, pcu_b200_tensor_error *error);
 /* Copy a planned value back to host memory (bytes must cover the value). */
 int pcu_b200_prepared_read(const pcu_b200_prepared *prepared, int32_t value, void *host, size_t bytes, void *stream);

@@ -71,8 +71,8 @@ def _single_layer(width, policy=0):
     return n, o, names, loss, upd
 
 
-@pytest.mark.parametrize("wait_each_node", [True, False])
-def test_single_layer_train_ten_steps_bit_exact(wait_each_node):
+@pytest.mark.parametrize("mode", ["each_node", "chained", "graph"])
+def test_single_layer_train_ten_steps_bit_exact(mode):
     rng = np.random.default_rng(20260101)
     x = dyadic_uniform(rng, (256, 512), 32)
     w = dyadic_uniform(rng, (512, 256), 32)
@@ -83,7 +83,7 @@ def test_single_layer_train_ten_steps_bit_exact(wait_each_node):
     w_dev, w_ref = w.copy(), w.copy()
     for step in range(10):
         got = prepared.run({ids["x"]: x, ids["w"]: w_dev, ids["bias"]: bias, ids["target"]: target}, [upd, loss],
-                           wait_each_node)
+                           mode=mode)
         want, fault = o.evaluate({"x": x, "w": w_ref, "bias": bias, "target": target}, ["updated", "loss"], 0,
                                  fast=True)
         assert fault is None
@@ -131,8 +131,8 @@ def test_mlp_step_shared_backward(width):
             assert np.array_equal(_bits(got[a]), _bits(want[b])), (a, b)
 
 
-@pytest.mark.parametrize("wait_each_node", [True, False])
-def test_first_faulting_node_wins(wait_each_node):
+@pytest.mark.parametrize("mode", ["each_node", "chained", "graph"])
+def test_first_faulting_node_wins(mode):
     """A later node that faults at a smaller element must not hide the earlier node's fault."""
     g = graph_mod.Graph(32, 0)
     a = g.input((64,))
@@ -147,14 +147,18 @@ def test_first_faulting_node_wins(wait_each_node):
     cv = np.ones(64, np.float32)
     cv[0] = 3e38
     with pytest.raises(pcu.ArithmeticFault) as info:
-        prepared.execute({a: av, b: bv, c: cv}, wait_each_node)
+        prepared.execute({a: av, b: bv, c: cv}, mode=mode)
     assert (info.value.value, info.value.element_index, info.value.kind) == (q, 40, "DivideByZero")
     bv[40] = 1.0
     with pytest.raises(pcu.ArithmeticFault) as info:
-        prepared.execute({a: av, b: bv, c: cv}, wait_each_node)
+        prepared.execute({a: av, b: bv, c: cv}, mode=mode)
     assert (info.value.value, info.value.element_index, info.value.kind) == (m, 0, "ArithmeticOverflow")
     cv[0] = 1.0
-    prepared.execute({a: av, b: bv, c: cv}, wait_each_node)
+    prepared.execute({a: av, b: bv, c: cv}, mode=mode)
+    bv[40] = 0.0  # a replay after a clean run reports the fault again
+    with pytest.raises(pcu.ArithmeticFault) as info:
+        prepared.execute({a: av, b: bv, c: cv}, mode=mode)
+    assert (info.value.value, info.value.element_index, info.value.kind) == (q, 40, "DivideByZero")
 
 
 @pytest.mark.parametrize("width", [32, 64])
