@@ -19,6 +19,7 @@ without GPUs; the arithmetic itself is always the CUDA provider's.
 """
 import importlib
 
+import numpy as np
 import torch
 import torch.distributed as dist
 
@@ -131,3 +132,101 @@ class ShardedMse:
         if reduce_status:
             all_reduce_min_status(status, self.group)
         return self.mean.reshape(())
+
+
+# ------------------------------------------------------------------------------- MLP
+def gather_columns(shard, full, group=None):
+    """All-gather the column blocks of a row-major (rows x n_r) tensor into `full` (rows x
+    world * n_r): NCCL gathers whole blocks, a strided copy interleaves them."""
+    world = dist.get_world_size(group)
+    rows, n_r = shard.shape
+    blocks = torch.empty((world, rows, n_r), dtype=shard.dtype, device=shard.device)
+    dist.all_gather_into_tensor(blocks, shard.contiguous(), group=group)
+    full.view(rows, world, n_r).copy_(blocks.permute(1, 0, 2))
+    return full
+
+
+class ColumnShardedMlp:
+    """A strict MLP training step with every weight's output columns split over the ranks.
+
+    Layers dims[0] -> ... -> dims[-1], ReLU after all but the last, strict MSE against the
+    target, the reverse mode of the strict graph layer (MSE gradient (p - t) * 2/n, ReLU
+    backward, dW = H^T G, dH = G W^T) and strict SGD.  Rank r owns columns [c0, c1) of every
+    weight and computes those columns of every activation and gradient; each cell still runs
+    its whole ordered reduction on one GPU, so the results are bit for bit those of one device.
+    Exchanges: the activations (forward), the output gradients and the weights (backward, for
+    dH = G W^T) are all-gathered.  Every dims[k >= 1] must be a multiple of the world size.
+    Status words (one per kernel call, rank-local event ordinals) stay in `self.status`.
+    """
+
+    def __init__(self, dims, batch, rate, dtype=None, policy=0, group=None, device=None):
+        self.dims, self.batch, self.rate, self.policy, self.group = list(dims), batch, rate, policy, group
+        self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        self.dtype = dtype or torch.float32
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        for d in self.dims[1:]:
+            if d % self.world:
+                raise ValueError(f"layer width {d} is not a multiple of {self.world} ranks")
+        self.cols = [(self.rank * d // self.world, (self.rank + 1) * d // self.world) for d in self.dims]
+        self.status = pcu.new_status(8 * len(dims) + 4, device=self.device)
+        self._next = 0
+
+    def _st(self):
+        s = self.status[self._next:self._next + 1]
+        self._next += 1
+        return s
+
+    def load(self, x, weights, target):
+        """Full host or device tensors; each rank keeps its column blocks of the weights."""
+        to = lambda a: torch.as_tensor(a).to(device=self.device, dtype=self.dtype)  # noqa: E731
+        self.x = to(x).contiguous()
+        self.t_full = to(target).contiguous()
+        c0, c1 = self.cols[-1]
+        self.t = self.t_full[:, c0:c1].contiguous()
+        self.w = []
+        for k, w in enumerate(weights):
+            c0, c1 = self.cols[k + 1]
+            self.w.append(to(w)[:, c0:c1].contiguous())
+
+    def full_weights(self):
+        out = []
+        for k, w in enumerate(self.w):
+            full = torch.empty((self.dims[k], self.dims[k + 1]), dtype=self.dtype, device=self.device)
+            out.append(gather_columns(w, full, self.group))
+        return out
+
+    def step(self, stream=None):
+        """One training step; returns the loss (a device scalar, the same on every rank)."""
+        self._next = 0
+        self.status.fill_(-1)
+        L, P, st, g = len(self.w), self.policy, self._st, self.group
+        dev, dt = self.device, self.dtype
+        zs, hs = [], [self.x]
+        for k in range(L):  # forward: column blocks of every layer, all-gathered
+            z = pcu.strict_matmul(hs[-1], self.w[k], False, False, P, status=st(), stream=stream)
+            zs.append(z)
+            a = pcu.checked_relu(z, P, status=st(), stream=stream) if k + 1 < L else z
+            full = torch.empty((self.batch, self.dims[k + 1]), dtype=dt, device=dev)
+            hs.append(gather_columns(a, full, g))
+        y = hs[-1]
+        loss = pcu.strict_mse(y, self.t_full, P, status=st(), stream=stream)
+        # d loss / d y = (y - t) * 2/n on this rank's columns
+        c0, c1 = self.cols[-1]
+        diff = pcu.checked_binary("sub", zs[-1], self.t, P, status=st(), stream=stream)
+        # 2 / n correctly rounded in the element type (n itself is exact: below 2^24 elements)
+        n = self.batch * self.dims[-1]
+        two_over_n = float(np.float32(2.0) / np.float32(n)) if dt == torch.float32 else 2.0 / float(n)
+        scale = torch.full((1,), two_over_n, dtype=dt, device=dev)
+        grad = pcu.checked_binary("mul", diff, scale, P, right_uniform=True, status=st(), stream=stream)
+        weights_full = self.full_weights()
+        for k in range(L - 1, -1, -1):
+            dw = pcu.strict_matmul(hs[k], grad, True, False, P, status=st(), stream=stream)
+            if k > 0:
+                gfull = torch.empty((self.batch, self.dims[k + 1]), dtype=dt, device=dev)
+                gather_columns(grad, gfull, g)
+                i0, i1 = self.cols[k]
+                rows = weights_full[k][i0:i1].contiguous()  # this rank's rows of W_k
+                dh = pcu.strict_matmul(gfull, rows, False, True, P, status=st(), stream=stream)
+                grad = pcu.checked_relu_backward(zs[k - 1], dh, P, status=st(), stream=stream)
+            self.w[k] = pcu.strict_sgd(self.w[k], dw, self.rate, P, status=st(), stream=stream)
+        return loss
