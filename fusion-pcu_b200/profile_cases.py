@@ -27,7 +27,7 @@ def dyadic(torch, shape, seed, dtype):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["matmul", "sgd", "mse", "binary", "train1"])
+    ap.add_argument("case", choices=["matmul", "sgd", "mse", "binary", "train1", "mlp"])
     ap.add_argument("--m", type=int, default=8192)
     ap.add_argument("--n", type=int, default=8192)
     ap.add_argument("--k", type=int, default=1024)
@@ -45,6 +45,9 @@ def main():
     dt = torch.float32 if args.dtype == "f32" else torch.float64
     if args.case == "train1":
         train_step(args)
+        return
+    if args.case == "mlp":
+        mlp_step(args)
         return
     status = pcu.new_status()
     if args.case == "matmul":
@@ -132,6 +135,77 @@ def train_step(args):
                 prepared.execute({}, mode=mode, stream=stream)  # inputs stay on the device
             dt = (time.perf_counter() - t0) / args.repeat
         print(f"train1 {mode} {dt * 1e3:.3f} ms/step (host-observed, status read included)")
+
+
+def mlp_step(args):
+    """the 4-layer strict MLP step (1024 -> 4096 x 3 -> 256, batch 8192,
+    lr binary32(1e-3)), He-uniform weights.  One GPU: the graph layer in CUDA-graph mode.  Under
+    torchrun: the column-sharded step of fusion-pcu_b200/sharded.py.  Prints TFLOP/s of checked
+    flops (forward, dW and dH MatMuls: 1.838e12 per step)."""
+    import os
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    dims, batch, rate = [1024, 4096, 4096, 4096, 256], 8192, 1e-3
+    flops = sum(2.0 * batch * dims[k] * dims[k + 1] for k in range(4)) * 2 + \
+        sum(2.0 * batch * dims[k] * dims[k + 1] for k in range(1, 4))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    rng = np.random.default_rng(5)
+    dy = lambda shape, lo=-1: ((rng.integers(lo * 2**23, 2**23, shape)) * 2.0**-23).astype(np.float32)  # noqa: E731
+    x, t = dy((batch, dims[0])), dy((batch, dims[-1]), 0)
+    ws = [(dy((dims[k], dims[k + 1])) * np.float32(np.sqrt(6.0 / dims[k]))).astype(np.float32) for k in range(4)]
+    if world == 1:
+        graph = importlib.import_module("fusion-pcu_b200.graph")
+        g = graph.Graph(32, 0)
+        gx, gt = g.input(x.shape), g.input(t.shape)
+        gws = [g.input(w.shape) for w in ws]
+        h = gx
+        for k, w in enumerate(gws):
+            h = g.matmul(h, w)
+            if k < 3:
+                h = g.relu(h)
+        loss = g.mean_squared_error(h, gt)
+        ups = [g.sgd_update(w, d, rate) for w, d in zip(gws, g.backward_mse_for_targets(loss, gws))]
+        prepared = g.prepare(ups + [loss])
+        stream = torch.cuda.Stream()
+        prepared.execute({gx: x, gt: t, **dict(zip(gws, ws))}, mode="graph", stream=stream)
+        prepared.execute({}, mode="graph", stream=stream)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.repeat):
+            prepared.execute({}, mode="graph", stream=stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.repeat
+    else:
+        import datetime
+
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+        sharded = importlib.import_module("fusion-pcu_b200.sharded")
+        mlp = sharded.ColumnShardedMlp(dims, batch, rate)
+        mlp.load(x, ws, t)
+        mlp.step()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.repeat):
+            mlp.step()
+        e1.record()
+        torch.cuda.synchronize()
+        tt = torch.tensor([e0.elapsed_time(e1) / args.repeat], device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+        dist.destroy_process_group()
+    if rank == 0:
+        print(f"mlp {world} GPU(s) {ms:.2f} ms/step  {flops / (ms * 1e-3) / 1e12:.2f} TFLOP/s")
 
 
 if __name__ == "__main__":
