@@ -18,7 +18,8 @@ import numpy as np
 __all__ = [
     "ProviderUnavailable", "TensorError", "ArithmeticFault", "CompoundArithmeticFault", "ProviderFailure",
     "library", "POLICY", "OPS", "STATUS_OK", "new_status", "decode_status", "strict_matmul", "strict_sgd",
-    "strict_mse", "mse_workspace", "strict_mse_segment_prepare", "strict_mse_segment_walk", "checked_binary", "checked_relu", "checked_relu_backward", "matmul_fault", "sgd_fault",
+    "strict_mse", "mse_workspace", "strict_mse_segment_prepare", "strict_mse_segment_walk", "strict_mse_sgd",
+    "strict_mse_sgd_segment_prepare", "checked_binary", "checked_relu", "checked_relu_backward", "matmul_fault", "sgd_fault",
     "mse_fault", "element_fault",
 ]
 
@@ -93,6 +94,9 @@ def _declare(L):
     L.pcu_b200_strict_mse.argtypes = [i32, i32, vp, vp, vp, u64, vp, sz, vp, vp]
     L.pcu_b200_strict_mse_segment_prepare.argtypes = [i32, i32, vp, vp, u64, u64, vp, sz, vp, vp]
     L.pcu_b200_strict_mse_segment_walk.argtypes = [i32, i32, vp, vp, u64, u64, u64, vp, vp, vp, vp, sz, vp, vp]
+    L.pcu_b200_strict_mse_sgd.argtypes = [i32, i32, vp, vp, vp, u64, vp, sz, vp, vp, vp, vp, u64, u32, vp, vp]
+    L.pcu_b200_strict_mse_sgd_segment_prepare.argtypes = [i32, i32, vp, vp, u64, u64, vp, sz, vp, vp, vp, vp, u64,
+                                                          u64, u32, vp, vp]
     L.pcu_b200_checked_binary.argtypes = [i32, i32, i32, vp, vp, vp, u64, i32, i32, vp, vp]
     L.pcu_b200_checked_relu.argtypes = [i32, i32, vp, vp, u64, vp, vp]
     L.pcu_b200_checked_relu_backward.argtypes = [i32, i32, vp, vp, vp, u64, vp, vp]
@@ -284,6 +288,58 @@ def strict_mse_segment_walk(prediction, target, first_index, total_count, carry,
         total_count, _ptr(carry), _ptr(carry), _ptr(out), _ptr(workspace), workspace.numel(), _ptr(status),
         _stream(stream)))
     return out
+
+
+def _rate_bits(rate):
+    return int(np.array([rate], dtype=np.float32).view(np.uint32)[0])
+
+
+def strict_mse_sgd(prediction, target, weights, gradient, rate, policy=0, loss=None, updated=None, mse_status=None,
+                   sgd_status=None, workspace=None, stream=None):
+    """The strict MSE of (prediction, target) and the strict SGD update of `weights` in one pass
+    (two independent nodes, each with its own status word).  Returns (loss, updated)."""
+    torch = _torch()
+    for t in (prediction, target, weights, gradient):
+        assert t.is_contiguous() and t.dtype == prediction.dtype
+    assert prediction.numel() == target.numel() and weights.numel() == gradient.numel()
+    if loss is None:
+        loss = torch.empty((), dtype=prediction.dtype, device=prediction.device)
+    if updated is None:
+        updated = torch.empty_like(weights)
+    if mse_status is None:
+        mse_status = new_status(device=prediction.device)
+    if sgd_status is None:
+        sgd_status = new_status(device=prediction.device)
+    if workspace is None:
+        workspace = mse_workspace(prediction)
+    _check(library().pcu_b200_strict_mse_sgd(
+        _dtype_code(prediction), policy, _ptr(prediction), _ptr(target), _ptr(loss), prediction.numel(),
+        _ptr(workspace), workspace.numel(), _ptr(mse_status), _ptr(weights), _ptr(gradient), _ptr(updated),
+        weights.numel(), _rate_bits(rate), _ptr(sgd_status), _stream(stream)))
+    return loss, updated
+
+
+def strict_mse_sgd_segment_prepare(prediction, target, first_index, weights, gradient, rate, sgd_first_index,
+                                   policy=0, updated=None, mse_status=None, sgd_status=None, workspace=None,
+                                   stream=None):
+    """strict_mse_segment_prepare carrying an SGD share (global SGD elements
+    [sgd_first_index, sgd_first_index + weights.numel())).  Returns (mse_status, workspace, updated)."""
+    torch = _torch()
+    assert prediction.is_contiguous() and target.is_contiguous() and prediction.numel() == target.numel()
+    assert weights.is_contiguous() and gradient.is_contiguous() and weights.numel() == gradient.numel()
+    if updated is None:
+        updated = torch.empty_like(weights)
+    if mse_status is None:
+        mse_status = new_status(device=prediction.device)
+    if sgd_status is None:
+        sgd_status = new_status(device=prediction.device)
+    if workspace is None:
+        workspace = mse_workspace(prediction)
+    _check(library().pcu_b200_strict_mse_sgd_segment_prepare(
+        _dtype_code(prediction), policy, _ptr(prediction), _ptr(target), prediction.numel(), first_index,
+        _ptr(workspace), workspace.numel(), _ptr(mse_status), _ptr(weights), _ptr(gradient), _ptr(updated),
+        weights.numel(), sgd_first_index, _rate_bits(rate), _ptr(sgd_status), _stream(stream)))
+    return mse_status, workspace, updated
 
 
 def checked_binary(op, left, right, policy=0, left_uniform=False, right_uniform=False, out=None, status=None,

@@ -74,6 +74,7 @@ template <> struct Fmt<float> {
     __device__ static __forceinline__ float add(float a, float b) { return __fadd_rn(a, b); }
     __device__ static __forceinline__ float sub(float a, float b) { return __fsub_rn(a, b); }
     __device__ static __forceinline__ float div(float a, float b) { return __fdiv_rn(a, b); }
+    __device__ static __forceinline__ float abs(float x) { return fabsf(x); }
 };
 
 template <> struct Fmt<double> {
@@ -92,6 +93,7 @@ template <> struct Fmt<double> {
     __device__ static __forceinline__ double add(double a, double b) { return __dadd_rn(a, b); }
     __device__ static __forceinline__ double sub(double a, double b) { return __dsub_rn(a, b); }
     __device__ static __forceinline__ double div(double a, double b) { return __ddiv_rn(a, b); }
+    __device__ static __forceinline__ double abs(double x) { return fabs(x); }
 };
 
 template <typename T>
@@ -397,6 +399,46 @@ __device__ __forceinline__ unsigned checked_binary(int op, T a, T b, int policy,
     case kOpMul: return checked_mul<T>(a, b, policy, out);
     default: return checked_div<T>(a, b, policy, out);
     }
+}
+
+// Strict SGD of one element (Crates/core/dialect/tensor/reference/strict_sgd/strict_sgd.rs:20-46):
+// p = rate * g, then w - p, each step checked; `step` is 0 for the multiply and 1 for the
+// subtract (event = index * 2 + step, tensor/strict_sgd/strict_sgd.rs:184-196).
+template <typename T>
+__device__ __forceinline__ unsigned checked_sgd(T w, T g, T rate, int policy, T &out, unsigned &step) {
+    T p;
+    const unsigned k = checked_mul<T>(rate, g, policy, p);
+    if (k) {
+        step = 0;
+        return k;
+    }
+    step = 1;
+    return checked_sub<T>(w, p, policy, out);
+}
+
+// The strict SGD law on V elements at once, for the common case.  Suppose every product
+// rate * g is finite and either above the smallest normal or the product of a zero gradient, and
+// every difference w - p is finite (and, under RejectSubnormalResult, zero or at least the
+// smallest normal).  Then no step of any element faults and the hardware results are the
+// law's: `out` holds them and the call returns true.  Otherwise it returns false, `out` is
+// meaningless, and the caller runs checked_sgd element by element.  A non-finite w or g always
+// shows as a non-finite product or difference, because the rate is finite.  A few compares
+// per element and one branch per vector replace the per-step branches of checked_sgd.
+template <typename T, int V>
+__device__ __forceinline__ bool sgd_fast(const T *w, const T *g, T rate, int policy, T *out) {
+    using F = Fmt<T>;
+    const T inf = F::value(F::kExpMask), tiny = F::value(F::kMinNormalBits);
+    const bool lax = policy != kPolicyRejectSubnormal;
+    bool ok = true;
+#pragma unroll
+    for (int e = 0; e < V; ++e) {
+        const T p = F::mul(rate, g[e]);
+        const T r = F::sub(w[e], p);
+        const T ap = F::abs(p), ar = F::abs(r);
+        ok = ok & (ap < inf) & ((ap > tiny) | (g[e] == T(0))) & (ar < inf) & (lax | (ar >= tiny) | (r == T(0)));
+        out[e] = r;
+    }
+    return ok;
 }
 
 // ReLU selection (scalar_checked_float.rs:273-309): non-finite -> Invalid; negative or either

@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <cstring>
 
 #include "checked_law.cuh"
 
@@ -48,5 +49,31 @@ int sm_count(void);                   // SMs of the current device (cached per d
 inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
 
 inline bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// the SGD learning rate: a binary32 pattern, used as is (binary32) or widened (binary64)
+inline float rate_f32(uint32_t bits) {
+    float r;
+    memcpy(&r, &bits, 4);
+    return r;
+}
+
+// exact binary32 -> binary64 widening of a finite pattern (Crates/core/scalar_widen.rs:9-33)
+inline double rate_f64(uint32_t bits) {
+    uint64_t sign = (uint64_t)(bits >> 31) << 63;
+    uint32_t field = (bits >> 23) & 0xffu, frac = bits & 0x7fffffu;
+    uint64_t out;
+    if (field != 0) {
+        out = sign | ((uint64_t)(field + 1023 - 127) << 52) | ((uint64_t)frac << 29);
+    } else if (frac == 0) {
+        out = sign;
+    } else {
+        int lead = 31 - __builtin_clz(frac);
+        uint64_t sig = (uint64_t)frac << (52 - lead);
+        out = sign | ((uint64_t)(lead + 874) << 52) | (sig & 0x000fffffffffffffull);
+    }
+    double r;
+    memcpy(&r, &out, 8);
+    return r;
+}
 
 }  // namespace pcu_host

@@ -14,7 +14,9 @@
 // grid-stride loop (coalesced LDG.128/STG.128 with streaming cache hints), evaluates each
 // element with the hardware-exact checked ops of checked_law.cuh and, at its first fault,
 // records (event << 3) | kind with atomicMin and stops: later events of the same thread
-// cannot be the minimum.  Unaligned or uniform operands use the same loop with V = 1.
+// cannot be the minimum.  Every element in front of the first fault is still written, as in
+// the reference's element-by-element loop.  Unaligned or uniform operands use the same loop
+// with V = 1.
 #include <cstring>
 
 #include "common.cuh"
@@ -52,22 +54,24 @@ __device__ __forceinline__ void store_vec(T *p, const T (&v)[V]) {
 }
 
 // ---- per-element operations: return kOk or a kind, set `step` (event = index * kSteps + step)
+// kFast: fast(a, b, out) evaluates a whole vector when no element can fault (false: run the
+// elements one at a time)
 template <typename T> struct SgdOp {
     static constexpr unsigned kSteps = 2;
+    static constexpr bool kFast = true;
     T rate;
     int policy;
     __device__ __forceinline__ unsigned operator()(T w, T g, T &out, unsigned &step) const {
-        T p;
-        unsigned k = checked_mul<T>(rate, g, policy, p);
-        if (k) { step = 0; return k; }
-        k = checked_sub<T>(w, p, policy, out);
-        step = 1;
-        return k;
+        return checked_sgd<T>(w, g, rate, policy, out, step);
+    }
+    template <int V> __device__ __forceinline__ bool fast(const T *w, const T *g, T *out) const {
+        return sgd_fast<T, V>(w, g, rate, policy, out);
     }
 };
 
 template <typename T> struct BinaryOp {
     static constexpr unsigned kSteps = 1;
+    static constexpr bool kFast = false;
     int op, policy;
     __device__ __forceinline__ unsigned operator()(T a, T b, T &out, unsigned &step) const {
         step = 0;
@@ -77,6 +81,7 @@ template <typename T> struct BinaryOp {
 
 template <typename T> struct ReluOp {
     static constexpr unsigned kSteps = 1;
+    static constexpr bool kFast = false;
     int policy;
     __device__ __forceinline__ unsigned operator()(T a, T, T &out, unsigned &step) const {
         step = 0;
@@ -86,6 +91,7 @@ template <typename T> struct ReluOp {
 
 template <typename T> struct ReluBackwardOp {
     static constexpr unsigned kSteps = 1;
+    static constexpr bool kFast = false;
     int policy;
     __device__ __forceinline__ unsigned operator()(T x, T dy, T &out, unsigned &step) const {
         step = 0;
@@ -134,11 +140,15 @@ __global__ void __launch_bounds__(256) streaming_kernel(const T *a, const T *b,
             if (v >= nvec) break;
             const uint64_t base = v * V;
             T ov[V];
+            bool done = false;
+            if constexpr (Op::kFast && V > 1) done = op.template fast<V>(av[u], bv[u], ov);
 #pragma unroll
-            for (int i = 0; i < V; ++i) {
+            for (int i = 0; i < V && !done; ++i) {
                 unsigned step;
                 unsigned kind = op(av[u][i], bv[u][i], ov[i], step);
-                if (kind) {
+                if (kind) {  // the elements in front of it are still written, as one at a time would
+#pragma unroll
+                    for (int q = 0; q < i; ++q) out[base + q] = ov[q];
                     record_fault(status, (unsigned long long)(base + i) * Op::kSteps + step, kind);
                     return;
                 }
@@ -182,31 +192,6 @@ int launch_streaming(const T *a, const T *b, T *out, uint64_t n, int a_uniform, 
     return pcu_host::launch_status();
 }
 
-static inline float rate_f32(uint32_t bits) {
-    float r;
-    memcpy(&r, &bits, 4);
-    return r;
-}
-
-// exact binary32 -> binary64 widening of a finite pattern (Crates/core/scalar_widen.rs:9-33)
-static inline double rate_f64(uint32_t bits) {
-    uint64_t sign = (uint64_t)(bits >> 31) << 63;
-    uint32_t field = (bits >> 23) & 0xffu, frac = bits & 0x7fffffu;
-    uint64_t out;
-    if (field != 0) {
-        out = sign | ((uint64_t)(field + 1023 - 127) << 52) | ((uint64_t)frac << 29);
-    } else if (frac == 0) {
-        out = sign;
-    } else {
-        int lead = 31 - __builtin_clz(frac);
-        uint64_t sig = (uint64_t)frac << (52 - lead);
-        out = sign | ((uint64_t)(lead + 874) << 52) | (sig & 0x000fffffffffffffull);
-    }
-    double r;
-    memcpy(&r, &out, 8);
-    return r;
-}
-
 }  // namespace pcu
 
 using namespace pcu;
@@ -224,11 +209,11 @@ extern "C" int pcu_b200_strict_sgd(int dtype, int policy, const void *weights, c
     auto *st = reinterpret_cast<unsigned long long *>(status);
     cudaStream_t s = pcu_host::as_stream(stream);
     if (dtype == PCU_B200_F32) {
-        SgdOp<float> op{rate_f32(rate_bits_f32), policy};
+        SgdOp<float> op{pcu_host::rate_f32(rate_bits_f32), policy};
         return launch_streaming<float>((const float *)weights, (const float *)gradient, (float *)out, count, 0, 0,
                                        op, st, s);
     }
-    SgdOp<double> op{rate_f64(rate_bits_f32), policy};
+    SgdOp<double> op{pcu_host::rate_f64(rate_bits_f32), policy};
     return launch_streaming<double>((const double *)weights, (const double *)gradient, (double *)out, count, 0, 0,
                                     op, st, s);
 }

@@ -295,11 +295,91 @@ __device__ __forceinline__ uint64_t sat_shl(uint64_t x, int s, uint64_t sat) {
     return x >= (sat >> s) ? sat : x << s;
 }
 
+// ---- an independent strict SGD node riding along (pcu_b200_strict_mse_sgd).  Its HBM traffic
+// overlaps the chunk kernel's integer work (and, for an SGD node far larger than the MSE, the
+// single-CTA walker); its elements, events and status word are its own, so the result is that
+// of the SGD node run alone.
+template <typename T> struct SgdRider {
+    const T *weights, *gradient;
+    T *out;
+    uint64_t n;         // elements [0, n) of this launch's share
+    uint64_t base;      // global index of element 0: events (base + i) * 2 + step
+    uint64_t per_unit;  // chunk kernel: elements per SGD CTA (a multiple of sgd_unit<T>())
+    T rate;
+    int policy;
+    bool vec;  // weights, gradient and out 16-byte aligned
+    unsigned long long *status;
+};
+
+// The chunk kernel carries its SGD share in dedicated CTAs: every kSgdPeriod-th CTA of the launch
+// streams a block of SGD elements, the others are chunk CTAs.  The chunk warps are bound by
+// integer issue and the SGD CTAs by HBM, so an SM holding both keeps both busy (an SGD slice
+// inside every chunk warp instead stalls that warp's integer work on memory).
+constexpr int kSgdPeriod = 4;
+constexpr int kSgdTrip = 2;  // 16-byte vectors per thread in flight
+// elements of one SGD CTA trip: the per-CTA share is a multiple of it
+template <typename T> constexpr uint64_t sgd_unit() { return 32ull * kChunkWarps * (16 / sizeof(T)) * kSgdTrip; }
+
+// Elements [s0, s1) of a rider over `lanes` threads (this one is `lane`), s0 a multiple of the
+// vector width.  Every thread takes its elements in increasing order and stops at its first
+// fault: its later events cannot be the minimum.
 template <typename T>
+__device__ __forceinline__ void sgd_range(const SgdRider<T> &r, uint64_t s0, uint64_t s1, uint64_t lane,
+                                          uint64_t lanes) {
+    using VT = typename std::conditional<sizeof(T) == 4, float4, double2>::type;
+    constexpr int VW = 16 / sizeof(T);
+    const uint64_t vend = r.vec ? s0 + (s1 - s0) / VW * VW : s0;
+    const uint64_t nv = (vend - s0) / VW;
+    for (uint64_t j0 = lane; j0 < nv; j0 += lanes * kSgdTrip) {
+        VT a[kSgdTrip], b[kSgdTrip];
+#pragma unroll
+        for (int u = 0; u < kSgdTrip; ++u) {
+            const uint64_t j = j0 + u * lanes;
+            if (j < nv) {
+                a[u] = __ldcs(reinterpret_cast<const VT *>(r.weights + s0) + j);
+                b[u] = __ldcs(reinterpret_cast<const VT *>(r.gradient + s0) + j);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kSgdTrip; ++u) {
+            const uint64_t j = j0 + u * lanes;
+            if (j >= nv) break;
+            VT o;
+            const bool done = sgd_fast<T, VW>(reinterpret_cast<const T *>(&a[u]), reinterpret_cast<const T *>(&b[u]),
+                                              r.rate, r.policy, reinterpret_cast<T *>(&o));
+#pragma unroll
+            for (int e = 0; e < VW && !done; ++e) {
+                unsigned step;
+                const unsigned kind = checked_sgd<T>(reinterpret_cast<const T *>(&a[u])[e],
+                                                     reinterpret_cast<const T *>(&b[u])[e], r.rate, r.policy,
+                                                     reinterpret_cast<T *>(&o)[e], step);
+                if (kind) {  // the elements in front of it are still written, as one at a time would
+#pragma unroll
+                    for (int q = 0; q < e; ++q) r.out[s0 + j * VW + q] = reinterpret_cast<const T *>(&o)[q];
+                    record_fault(r.status, (r.base + s0 + j * VW + e) * 2 + step, kind);
+                    return;
+                }
+            }
+            __stcs(reinterpret_cast<VT *>(r.out + s0) + j, o);
+        }
+    }
+    for (uint64_t i = vend + lane; i < s1; i += lanes) {
+        T o;
+        unsigned step;
+        const unsigned kind = checked_sgd<T>(r.weights[i], r.gradient[i], r.rate, r.policy, o, step);
+        if (kind) {
+            record_fault(r.status, (r.base + i) * 2 + step, kind);
+            return;
+        }
+        r.out[i] = o;
+    }
+}
+
+template <typename T, bool RIDE>
 __global__ void __launch_bounds__(32 * kChunkWarps, MseTraits<T>::MIN_BLOCKS)
 mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base, bool vec, int policy,
                  uint64_t chunks, uint64_t ahead, MseHead *heads, typename MseTraits<T>::D *deltas,
-                 unsigned long long *status) {
+                 unsigned long long *status, SgdRider<T> rider) {
     using Tr = MseTraits<T>;
     using F = Fmt<T>;
     using B = typename F::Bits;
@@ -320,7 +400,16 @@ mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base
     __shared__ Fix s_lane_ex[kChunkWarps][ROWS][32];  // exclusive prefix XOR in front of (row, lane)
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const uint64_t chunk = (uint64_t)blockIdx.x * kChunkWarps + warp;
+    uint64_t cta = blockIdx.x;
+    if constexpr (RIDE) {
+        if (blockIdx.x % kSgdPeriod == kSgdPeriod - 1) {  // an SGD CTA (its own status word)
+            const uint64_t s0 = (uint64_t)(blockIdx.x / kSgdPeriod) * rider.per_unit;
+            if (s0 < rider.n) sgd_range<T>(rider, s0, min(s0 + rider.per_unit, rider.n), threadIdx.x, blockDim.x);
+            return;
+        }
+        cta = blockIdx.x - blockIdx.x / kSgdPeriod;
+    }
+    const uint64_t chunk = cta * kChunkWarps + warp;
     if (chunk >= chunks) return;  // the whole warp: nothing below synchronises beyond it
     const uint64_t chunk0 = chunk * Tr::CHUNK;
     if (lane == 0) {
@@ -815,9 +904,9 @@ __device__ __forceinline__ typename WalkAcc<T>::U walk_increment(typename Fmt<T>
     return (m + half) >> d;
 }
 
-// The walker runs with one thread per chunk element (CHUNK threads).
+// The walker runs with one thread per chunk element (one CTA of CHUNK threads).
 template <typename T>
-__global__ void __launch_bounds__(1024) mse_walk_kernel(
+__device__ __forceinline__ void mse_walk(
     const T *prediction, const T *target, uint64_t n, const MseHead *heads0, const typename MseTraits<T>::D *deltas0,
     const MseHead *heads1, const typename MseTraits<T>::D *deltas1, const MseHead *heads2,
     const typename MseTraits<T>::D *deltas2, uint64_t chunks, uint64_t blocks, uint64_t supers, uint64_t base,
@@ -987,6 +1076,37 @@ __global__ void __launch_bounds__(1024) mse_walk_kernel(
     }
 }
 
+#define PCU_MSE_WALK_PARAMS                                                                                        \
+    const T *prediction, const T *target, uint64_t n, const MseHead *heads0, const typename MseTraits<T>::D *deltas0, \
+        const MseHead *heads1, const typename MseTraits<T>::D *deltas1, const MseHead *heads2,                   \
+        const typename MseTraits<T>::D *deltas2, uint64_t chunks, uint64_t blocks, uint64_t supers, uint64_t base, \
+        uint64_t total, T denominator, int policy, const T *carry_in, T *carry_out, T *out,                       \
+        unsigned long long *status
+#define PCU_MSE_WALK_ARGS                                                                                     \
+    prediction, target, n, heads0, deltas0, heads1, deltas1, heads2, deltas2, chunks, blocks, supers, base, total, \
+        denominator, policy, carry_in, carry_out, out, status
+
+template <typename T> __global__ void __launch_bounds__(1024) mse_walk_kernel(PCU_MSE_WALK_PARAMS) {
+    mse_walk<T>(PCU_MSE_WALK_ARGS);
+}
+
+// CTA 0 walks; the other CTAs stream an SGD node's elements meanwhile (the walker is latency
+// bound and holds one SM).
+template <typename T>
+__global__ void __launch_bounds__(1024) mse_walk_sgd_kernel(PCU_MSE_WALK_PARAMS, SgdRider<T> rider) {
+    if (blockIdx.x == 0) {
+        mse_walk<T>(PCU_MSE_WALK_ARGS);
+        return;
+    }
+    sgd_range<T>(rider, 0, rider.n, (uint64_t)(blockIdx.x - 1) * blockDim.x + threadIdx.x,
+                 (uint64_t)(gridDim.x - 1) * blockDim.x);
+}
+
+// An SGD share on its own (the part a segment's chunk warps do not carry).
+template <typename T> __global__ void __launch_bounds__(256) sgd_share_kernel(SgdRider<T> rider) {
+    sgd_range<T>(rider, 0, rider.n, (uint64_t)blockIdx.x * blockDim.x + threadIdx.x, (uint64_t)gridDim.x * blockDim.x);
+}
+
 // binary32/binary64 encoding of an element count, nearest-even (constants/constants.rs:18-27)
 template <typename T> T count_value(uint64_t n) {
     const int frac = sizeof(T) == 4 ? 23 : 52;
@@ -1036,33 +1156,53 @@ template <typename T> struct MseLayout {
     }
 };
 
+// The chunk kernel's grid when it carries SGD, and how many units (chunk warps or SGD CTAs)
+// carry it.
+inline uint64_t chunk_grid(uint64_t chunks, bool ride) {
+    const uint64_t ctas = (chunks + kChunkWarps - 1) / kChunkWarps;
+    return ride ? ctas + (ctas + kSgdPeriod - 2) / (kSgdPeriod - 1) + kSgdPeriod : ctas;
+}
+inline uint64_t sgd_units(uint64_t chunks) { return chunk_grid(chunks, true) / kSgdPeriod; }
+
 // Phases 1 and 2 of a segment (global elements [base, base + n)): chunk maps, then block and
-// superblock maps.
+// superblock maps.  `sgd` (if not null and not empty) rides on the chunk kernel, per_unit
+// elements per SGD CTA.
 template <typename T>
 int prepare_mse(int policy, const T *p, const T *t, uint64_t n, uint64_t base, void *workspace, size_t workspace_bytes,
-                unsigned long long *status, cudaStream_t stream) {
+                unsigned long long *status, cudaStream_t stream, const SgdRider<T> *sgd = nullptr) {
     using D = typename MseTraits<T>::D;
     MseLayout<T> lay(n);
     if (!workspace || workspace_bytes < lay.bytes) return PCU_B200_ERROR_WORKSPACE;
     if (lay.count[0] > 0x7fffffffull * kChunkWarps) return PCU_B200_ERROR_SIZE_OVERFLOW;
     if (!n) return PCU_B200_OK;
+    const bool ride = sgd && sgd->n;
     char *ws = reinterpret_cast<char *>(workspace);
     const bool vec = pcu_host::aligned(p, 16) && pcu_host::aligned(t, 16);
-    static int resident[64] = {0};  // chunk-kernel warps resident at once, per device
+    static int resident[2][64] = {};  // chunk-kernel warps resident at once, per variant and device
     int device = 0;
     cudaGetDevice(&device);
-    int ahead = device >= 0 && device < 64 ? resident[device] : 0;
+    const bool cached = device >= 0 && device < 64;
+    int ahead = cached ? resident[ride][device] : 0;
     if (!ahead) {
         int per_sm = 0;
-        cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mse_chunk_kernel<T>, 32 * kChunkWarps, 0);
+        cudaError_t e = ride ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mse_chunk_kernel<T, true>,
+                                                                           32 * kChunkWarps, 0)
+                             : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mse_chunk_kernel<T, false>,
+                                                                           32 * kChunkWarps, 0);
         if (e != cudaSuccess) return pcu_host::set_cuda_error(e);
         ahead = per_sm * kChunkWarps * pcu_host::sm_count();
-        if (device >= 0 && device < 64) resident[device] = ahead;
+        if (cached) resident[ride][device] = ahead;
     }
-    const unsigned grid = (unsigned)((lay.count[0] + kChunkWarps - 1) / kChunkWarps);
-    mse_chunk_kernel<T><<<grid, 32 * kChunkWarps, 0, stream>>>(
-        p, t, n, base, vec, policy, lay.count[0], (uint64_t)ahead, reinterpret_cast<MseHead *>(ws + lay.heads_off[0]),
-        reinterpret_cast<D *>(ws + lay.deltas_off[0]), status);
+    const unsigned grid = (unsigned)chunk_grid(lay.count[0], ride);
+    MseHead *h0 = reinterpret_cast<MseHead *>(ws + lay.heads_off[0]);
+    D *d0 = reinterpret_cast<D *>(ws + lay.deltas_off[0]);
+    if (ride)
+        mse_chunk_kernel<T, true><<<grid, 32 * kChunkWarps, 0, stream>>>(p, t, n, base, vec, policy, lay.count[0],
+                                                                         (uint64_t)ahead, h0, d0, status, *sgd);
+    else
+        mse_chunk_kernel<T, false><<<grid, 32 * kChunkWarps, 0, stream>>>(p, t, n, base, vec, policy, lay.count[0],
+                                                                          (uint64_t)ahead, h0, d0, status,
+                                                                          SgdRider<T>{});
     int rc = pcu_host::launch_status();
     for (int l = 1; l < kLevels && !rc; ++l) {
         mse_compose_kernel<T><<<(unsigned)lay.count[l], 256, 0, stream>>>(
@@ -1077,20 +1217,31 @@ int prepare_mse(int policy, const T *p, const T *t, uint64_t n, uint64_t base, v
 
 // Phase 3 of a segment: the ordered walk from *carry_in (+0 if null); the running sum goes to
 // *carry_out (if not null) and, when out is not null, the checked mean over `total` elements.
+// `sgd` (if not null and not empty) is streamed by extra CTAs of the same launch.
 template <typename T>
 int walk_mse(int policy, const T *p, const T *t, uint64_t n, uint64_t base, uint64_t total, const T *carry_in,
              T *carry_out, T *out, void *workspace, size_t workspace_bytes, unsigned long long *status,
-             cudaStream_t stream) {
+             cudaStream_t stream, const SgdRider<T> *sgd = nullptr) {
     using D = typename MseTraits<T>::D;
+    constexpr unsigned THREADS = MseTraits<T>::CHUNK;
     MseLayout<T> lay(n);
     if (n && (!workspace || workspace_bytes < lay.bytes)) return PCU_B200_ERROR_WORKSPACE;
     char *ws = reinterpret_cast<char *>(workspace);
     auto H = [&](int l) { return reinterpret_cast<const MseHead *>(ws + lay.heads_off[l]); };
     auto R = [&](int l) { return reinterpret_cast<const D *>(ws + lay.deltas_off[l]); };
-    mse_walk_kernel<T><<<1, MseTraits<T>::CHUNK, 0, stream>>>(p, t, n, H(0), R(0), H(1), R(1), H(2), R(2),
-                                                              lay.count[0], lay.count[1], lay.count[2], base, total,
-                                                              count_value<T>(total), policy, carry_in, carry_out, out,
-                                                              status);
+    if (sgd && sgd->n) {
+        const uint64_t per_cta = (uint64_t)THREADS * (16 / sizeof(T)) * kSgdTrip;
+        const uint64_t cap = (uint64_t)(2048 / THREADS) * pcu_host::sm_count() - 1;
+        const uint64_t want = (sgd->n + per_cta - 1) / per_cta;
+        const unsigned extra = (unsigned)(want < cap ? want : cap);
+        mse_walk_sgd_kernel<T><<<1 + extra, THREADS, 0, stream>>>(
+            p, t, n, H(0), R(0), H(1), R(1), H(2), R(2), lay.count[0], lay.count[1], lay.count[2], base, total,
+            count_value<T>(total), policy, carry_in, carry_out, out, status, *sgd);
+    } else {
+        mse_walk_kernel<T><<<1, THREADS, 0, stream>>>(p, t, n, H(0), R(0), H(1), R(1), H(2), R(2), lay.count[0],
+                                                      lay.count[1], lay.count[2], base, total, count_value<T>(total),
+                                                      policy, carry_in, carry_out, out, status);
+    }
     return pcu_host::launch_status();
 }
 
@@ -1100,6 +1251,80 @@ int run_mse(int policy, const T *p, const T *t, T *out, uint64_t n, void *worksp
     int rc = prepare_mse<T>(policy, p, t, n, 0, workspace, workspace_bytes, status, stream);
     if (rc) return rc;
     return walk_mse<T>(policy, p, t, n, 0, n, nullptr, nullptr, out, workspace, workspace_bytes, status, stream);
+}
+
+// ---- MSE + SGD in one pass.  The SGD node's elements go to the chunk kernel's SGD CTAs, up to
+// kMaxSgdPerCta each; what is left (an SGD node far larger than the MSE) is streamed by extra
+// CTAs of the walker's launch.
+constexpr uint64_t kMaxSgdPerCta = 131072;
+
+template <typename T>
+SgdRider<T> make_rider(int policy, const void *weights, const void *gradient, void *out, uint64_t n, uint64_t base,
+                       uint32_t rate_bits, unsigned long long *status) {
+    SgdRider<T> r{};
+    r.weights = reinterpret_cast<const T *>(weights);
+    r.gradient = reinterpret_cast<const T *>(gradient);
+    r.out = reinterpret_cast<T *>(out);
+    r.n = n;
+    r.base = base;
+    r.per_unit = 0;
+    if constexpr (sizeof(T) == 4)
+        r.rate = pcu_host::rate_f32(rate_bits);
+    else
+        r.rate = pcu_host::rate_f64(rate_bits);
+    r.policy = policy;
+    r.vec = pcu_host::aligned(weights, 16) && pcu_host::aligned(gradient, 16) && pcu_host::aligned(out, 16);
+    r.status = status;
+    return r;
+}
+
+// head: elements [0, h) carried by `units` SGD CTAs of the chunk kernel; tail: the rest
+template <typename T>
+void split_sgd(const SgdRider<T> &all, uint64_t units, SgdRider<T> &head, SgdRider<T> &tail) {
+    uint64_t per = units ? (all.n + units - 1) / units : 0;
+    per = (per + sgd_unit<T>() - 1) / sgd_unit<T>() * sgd_unit<T>();
+    if (per > kMaxSgdPerCta) per = kMaxSgdPerCta;
+    const uint64_t h = per * units < all.n ? per * units : all.n;
+    head = all;
+    head.n = h;
+    head.per_unit = per;
+    tail = all;
+    tail.weights += h;
+    tail.gradient += h;
+    tail.out += h;
+    tail.n = all.n - h;
+    tail.base = all.base + h;
+}
+
+template <typename T>
+int run_mse_sgd(int policy, const T *p, const T *t, T *loss, uint64_t n, void *workspace, size_t workspace_bytes,
+                unsigned long long *mse_status, const SgdRider<T> &sgd, cudaStream_t stream) {
+    MseLayout<T> lay(n);
+    SgdRider<T> head, tail;
+    split_sgd<T>(sgd, sgd_units(lay.count[0]), head, tail);
+    int rc = prepare_mse<T>(policy, p, t, n, 0, workspace, workspace_bytes, mse_status, stream, &head);
+    if (rc) return rc;
+    return walk_mse<T>(policy, p, t, n, 0, n, nullptr, nullptr, loss, workspace, workspace_bytes, mse_status, stream,
+                       &tail);
+}
+
+// A segment's phases 1 and 2 with an SGD share on the chunk warps; what they cannot carry runs
+// in a launch of its own.
+template <typename T>
+int prepare_mse_sgd(int policy, const T *p, const T *t, uint64_t n, uint64_t base, void *workspace,
+                    size_t workspace_bytes, unsigned long long *mse_status, const SgdRider<T> &sgd,
+                    cudaStream_t stream) {
+    MseLayout<T> lay(n);
+    if (!workspace || workspace_bytes < lay.bytes) return PCU_B200_ERROR_WORKSPACE;
+    SgdRider<T> head, tail;
+    split_sgd<T>(sgd, n ? sgd_units(lay.count[0]) : 0, head, tail);
+    int rc = prepare_mse<T>(policy, p, t, n, base, workspace, workspace_bytes, mse_status, stream, &head);
+    if (rc || !tail.n) return rc;
+    const uint64_t per_cta = 256ull * (16 / sizeof(T)) * kSgdTrip;
+    const uint64_t cap = 8ull * pcu_host::sm_count();
+    const uint64_t want = (tail.n + per_cta - 1) / per_cta;
+    sgd_share_kernel<T><<<(unsigned)(want < cap ? want : cap), 256, 0, stream>>>(tail);
+    return pcu_host::launch_status();
 }
 
 }  // namespace pcu
@@ -1160,4 +1385,68 @@ extern "C" int pcu_b200_strict_mse_segment_walk(int dtype, int policy, const voi
     return pcu::walk_mse<double>(policy, (const double *)prediction, (const double *)target, count, first_index,
                                  total_count, (const double *)carry_in, (double *)carry_out, (double *)out, workspace,
                                  workspace_bytes, st, s);
+}
+
+static bool valid_sgd_args(int dtype, uint64_t count, const void *weights, const void *gradient, const void *updated,
+                           uint32_t rate_bits_f32, const uint64_t *status) {
+    if (!status || (rate_bits_f32 & 0x7f800000u) == 0x7f800000u) return false;  // capture rejects
+    (void)dtype;
+    return !count || (weights && gradient && updated);
+}
+
+extern "C" int pcu_b200_strict_mse_sgd(int dtype, int policy, const void *prediction, const void *target, void *loss,
+                                       uint64_t mse_count, void *workspace, size_t workspace_bytes,
+                                       uint64_t *mse_status, const void *weights, const void *gradient,
+                                       void *updated, uint64_t sgd_count, uint32_t rate_bits_f32,
+                                       uint64_t *sgd_status, void *stream) {
+    if ((dtype != PCU_B200_F32 && dtype != PCU_B200_F64) || policy < 0 || policy > 2 || !mse_status)
+        return PCU_B200_ERROR_INVALID_ARGUMENT;
+    if (mse_count == 0 || !prediction || !target || !loss) return PCU_B200_ERROR_INVALID_ARGUMENT;
+    if (!valid_sgd_args(dtype, sgd_count, weights, gradient, updated, rate_bits_f32, sgd_status))
+        return PCU_B200_ERROR_INVALID_ARGUMENT;
+    if (mse_count > (1ull << 58) || sgd_count > (1ull << 59)) return PCU_B200_ERROR_SIZE_OVERFLOW;
+    auto *ms = reinterpret_cast<unsigned long long *>(mse_status);
+    auto *ss = reinterpret_cast<unsigned long long *>(sgd_status);
+    cudaStream_t s = pcu_host::as_stream(stream);
+    if (dtype == PCU_B200_F32)
+        return pcu::run_mse_sgd<float>(policy, (const float *)prediction, (const float *)target, (float *)loss,
+                                       mse_count, workspace, workspace_bytes, ms,
+                                       pcu::make_rider<float>(policy, weights, gradient, updated, sgd_count, 0,
+                                                              rate_bits_f32, ss),
+                                       s);
+    return pcu::run_mse_sgd<double>(policy, (const double *)prediction, (const double *)target, (double *)loss,
+                                    mse_count, workspace, workspace_bytes, ms,
+                                    pcu::make_rider<double>(policy, weights, gradient, updated, sgd_count, 0,
+                                                            rate_bits_f32, ss),
+                                    s);
+}
+
+extern "C" int pcu_b200_strict_mse_sgd_segment_prepare(int dtype, int policy, const void *prediction,
+                                                       const void *target, uint64_t mse_count,
+                                                       uint64_t mse_first_index, void *workspace,
+                                                       size_t workspace_bytes, uint64_t *mse_status,
+                                                       const void *weights, const void *gradient, void *updated,
+                                                       uint64_t sgd_count, uint64_t sgd_first_index,
+                                                       uint32_t rate_bits_f32, uint64_t *sgd_status, void *stream) {
+    if ((dtype != PCU_B200_F32 && dtype != PCU_B200_F64) || policy < 0 || policy > 2 || !mse_status)
+        return PCU_B200_ERROR_INVALID_ARGUMENT;
+    if (mse_count && (!prediction || !target)) return PCU_B200_ERROR_INVALID_ARGUMENT;
+    if (!valid_sgd_args(dtype, sgd_count, weights, gradient, updated, rate_bits_f32, sgd_status))
+        return PCU_B200_ERROR_INVALID_ARGUMENT;
+    if (mse_count > (1ull << 58) || mse_first_index > (1ull << 58) - mse_count) return PCU_B200_ERROR_SIZE_OVERFLOW;
+    if (sgd_count > (1ull << 59) || sgd_first_index > (1ull << 59) - sgd_count) return PCU_B200_ERROR_SIZE_OVERFLOW;
+    auto *ms = reinterpret_cast<unsigned long long *>(mse_status);
+    auto *ss = reinterpret_cast<unsigned long long *>(sgd_status);
+    cudaStream_t s = pcu_host::as_stream(stream);
+    if (dtype == PCU_B200_F32)
+        return pcu::prepare_mse_sgd<float>(policy, (const float *)prediction, (const float *)target, mse_count,
+                                           mse_first_index, workspace, workspace_bytes, ms,
+                                           pcu::make_rider<float>(policy, weights, gradient, updated, sgd_count,
+                                                                  sgd_first_index, rate_bits_f32, ss),
+                                           s);
+    return pcu::prepare_mse_sgd<double>(policy, (const double *)prediction, (const double *)target, mse_count,
+                                        mse_first_index, workspace, workspace_bytes, ms,
+                                        pcu::make_rider<double>(policy, weights, gradient, updated, sgd_count,
+                                                                sgd_first_index, rate_bits_f32, ss),
+                                        s);
 }

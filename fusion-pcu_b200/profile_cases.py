@@ -27,7 +27,7 @@ def dyadic(torch, shape, seed, dtype):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["matmul", "sgd", "mse", "binary", "train1", "mlp"])
+    ap.add_argument("case", choices=["matmul", "sgd", "mse", "msesgd", "binary", "train1", "mlp"])
     ap.add_argument("--m", type=int, default=8192)
     ap.add_argument("--n", type=int, default=8192)
     ap.add_argument("--k", type=int, default=1024)
@@ -69,6 +69,16 @@ def main():
         out = torch.empty_like(x)
         call = lambda: pcu.checked_binary("add", x, y, args.policy, out=out, status=status)  # noqa
         work, unit = 3.0 * args.count * x.element_size(), "GB/s"
+    elif args.case == "msesgd":
+        # MSE over (p, t) and SGD over (w, g), fused in one pass
+        p, t = dyadic(torch, (args.count,), 1, dt), dyadic(torch, (args.count,), 2, dt)
+        w, g = dyadic(torch, (args.count,), 3, dt), dyadic(torch, (args.count,), 4, dt)
+        out, upd = torch.empty((), dtype=dt, device="cuda"), torch.empty_like(w)
+        ws = pcu.mse_workspace(p)
+        status2 = pcu.new_status()
+        call = lambda: pcu.strict_mse_sgd(p, t, w, g, 0.01, args.policy, loss=out, updated=upd,  # noqa
+                                          mse_status=status, sgd_status=status2, workspace=ws)
+        work, unit = 5.0 * args.count * p.element_size(), "GB/s"
     else:
         p, t = dyadic(torch, (args.count,), 1, dt), dyadic(torch, (args.count,), 2, dt)
         out = torch.empty((), dtype=dt, device="cuda")
@@ -90,6 +100,18 @@ def main():
     assert word == pcu.STATUS_OK, hex(word)
     scale = 1e12 if unit == "TFLOP/s" else 1e9
     print(f"{args.case} {args.dtype} {ms:.3f} ms/call  {work / (ms * 1e-3) / scale:.2f} {unit}")
+    if args.case == "msesgd":
+        assert int(status2.cpu().item()) & ((1 << 64) - 1) == pcu.STATUS_OK
+        for name, fn in (("separate", lambda: (pcu.strict_mse(p, t, args.policy, out=out, status=status, workspace=ws),
+                                               pcu.strict_sgd(w, g, 0.01, args.policy, out=upd, status=status2))),):
+            fn()
+            e0.record()
+            for _ in range(args.repeat):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            sep = e0.elapsed_time(e1) / args.repeat
+            print(f"  {name} {sep:.3f} ms/call  {work / (sep * 1e-3) / 1e9:.2f} GB/s")
     if args.case == "mse" and args.phases:
         # the two phases through the segment form: bandwidth-bound maps, then the ordered walk
         carry = torch.zeros(1, dtype=dt, device="cuda")

@@ -118,9 +118,18 @@ class ShardedMse:
         self.mean = torch.zeros(1, dtype=prediction.dtype, device=prediction.device)
         self.last = first_index + prediction.numel() == total
 
-    def run(self, status, stream=None, reduce_status=True):
-        pcu.strict_mse_segment_prepare(self.p, self.t, self.first, self.policy, status=status,
-                                       workspace=self.workspace, stream=stream)
+    def run(self, status, stream=None, reduce_status=True, sgd=None):
+        """`sgd`: optionally an independent strict SGD block carried by the bandwidth-bound phase,
+        a dict with weights, gradient, rate, first_index (its global first element), out and
+        status (its own word, global events; not all-reduced here)."""
+        if sgd is None:
+            pcu.strict_mse_segment_prepare(self.p, self.t, self.first, self.policy, status=status,
+                                           workspace=self.workspace, stream=stream)
+        else:
+            pcu.strict_mse_sgd_segment_prepare(self.p, self.t, self.first, sgd["weights"], sgd["gradient"],
+                                               sgd["rate"], sgd["first_index"], self.policy, updated=sgd["out"],
+                                               mse_status=status, sgd_status=sgd["status"],
+                                               workspace=self.workspace, stream=stream)
         self.carry.zero_()
 
         def walk(carry):

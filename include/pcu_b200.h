@@ -180,6 +180,35 @@ int pcu_b200_strict_mse_segment_walk(int dtype, int policy, const void *predicti
                                      const void *carry_in, void *carry_out, void *out, void *workspace,
                                      size_t workspace_bytes, uint64_t *status, void *stream);
 
+/* ------------------------------------------------------------------ MSE and SGD in one pass */
+
+/* One strict MSE node and one strict SGD node that do not depend on each other, as the loss and
+ * a weight update of a training step are (the MSE gradient reads prediction and target, never
+ * the loss), run in one pass.  The MSE's chunk pass is bound by integer work and its final walk
+ * by latency, so the SGD's HBM traffic is streamed inside those launches instead of after them.
+ * There is no single counterpart in the reference; the call replaces its two executor calls
+ * (execute_strict_mse and execute_strict_sgd, tensor/tensor.rs:5144-5166 and 5077-5103).
+ * Results, events and status words are exactly those of pcu_b200_strict_mse (prediction,
+ * target, loss, mse_count, mse_status) and pcu_b200_strict_sgd (weights, gradient, updated,
+ * sgd_count, rate, sgd_status) run one after the other; each node keeps its own status word.
+ * The workspace is pcu_b200_strict_mse_workspace_size(dtype, mse_count).  updated may alias
+ * weights; no other buffer may overlap updated.  sgd_count may be 0. */
+int pcu_b200_strict_mse_sgd(int dtype, int policy, const void *prediction, const void *target, void *loss,
+                            uint64_t mse_count, void *workspace, size_t workspace_bytes, uint64_t *mse_status,
+                            const void *weights, const void *gradient, void *updated, uint64_t sgd_count,
+                            uint32_t rate_bits_f32, uint64_t *sgd_status, void *stream);
+
+/* pcu_b200_strict_mse_segment_prepare with an SGD share carried by the same launch: the SGD
+ * elements [0, sgd_count) given are the global elements [sgd_first_index, sgd_first_index +
+ * sgd_count) of their node (events (sgd_first_index + i) * 2 + step).  No counterpart in the
+ * reference (see pcu_b200_strict_mse_segment_prepare). */
+int pcu_b200_strict_mse_sgd_segment_prepare(int dtype, int policy, const void *prediction, const void *target,
+                                            uint64_t mse_count, uint64_t mse_first_index, void *workspace,
+                                            size_t workspace_bytes, uint64_t *mse_status, const void *weights,
+                                            const void *gradient, void *updated, uint64_t sgd_count,
+                                            uint64_t sgd_first_index, uint32_t rate_bits_f32,
+                                            uint64_t *sgd_status, void *stream);
+
 /* ------------------------------------------------------------------ checked elementwise */
 
 /* out[i] = op(left[i], right[i]); a nonzero *_uniform flag broadcasts element 0 of that
