@@ -16,7 +16,7 @@ CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(ROOT, "_build", "provider")
 LIBRARY = os.path.join(HERE, "libpcu_b200.so")
 SOURCES = ["abi.cu", "streaming.cu", "strict_matmul.cu", "strict_mse.cu", "tensor_graph.cu"]
-HEADERS = ["checked_law.cuh", "common.cuh"]
+HEADERS = ["checked_law.cuh", "common.cuh", "provider.h"]
 
 NVCC = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -4,6 +4,7 @@
 
 #include "common.cuh"
 #include "pcu_b200.h"
+#include "provider.h"
 
 namespace {
 
@@ -15,7 +16,19 @@ __global__ void fill_status_kernel(unsigned long long *status, uint64_t count) {
     for (; i < count; i += stride) status[i] = pcu::kStatusOk;
 }
 
+__global__ void chain_decide_kernel(pcu::ChainGuard guard) { (void)pcu::chain_admits(guard); }
+
 }  // namespace
+
+namespace pcu {
+
+int chain_decide_only(const ChainGuard &guard, cudaStream_t stream) {
+    if (!guard.disp || !guard.decide) return PCU_B200_OK;
+    chain_decide_kernel<<<1, 1, 0, stream>>>(guard);
+    return pcu_host::launch_status();
+}
+
+}  // namespace pcu
 
 namespace pcu_host {
 

@@ -27,6 +27,43 @@ __device__ __forceinline__ bool fault_precedes(const unsigned long long *status,
     return s != kStatusOk && (s >> 3) < event;
 }
 
+// ---- guarded stage chain (Crates/backends/cuda/owned_dispatch/guarded/guarded.rs:15-38,
+// Crates/core/runtime/execution/guarded/guarded.rs:30-55).  Every stage has a fault word and a
+// disposition (pending 0, executed 1, skipped 2).  A stage is admitted when it has no
+// predecessor, or when its predecessor executed and its fault word is still clear; otherwise
+// it is skipped and touches no user data (no loads, no arithmetic, no output writes).  The
+// stage's first kernel decides and records the disposition; its later kernels run only when
+// it recorded "executed".  Kernels on one stream run in order, so the predecessor's record is
+// final when a stage's first kernel reads it.
+enum : unsigned long long { kDispPending = 0, kDispExecuted = 1, kDispSkipped = 2 };
+
+struct ChainGuard {
+    const unsigned long long *prev_status;  // predecessor's fault word (null: first stage)
+    const unsigned long long *prev_disp;    // predecessor's disposition
+    unsigned long long *disp;               // this stage's disposition (null: not guarded)
+    int decide;                             // this launch is the stage's first kernel
+};
+
+// Out of line, so that unguarded launches (the common case) pay one compare and no registers.
+static __device__ __noinline__ bool chain_decide(const unsigned long long *prev_status, const unsigned long long *prev_disp,
+                                          unsigned long long *disp, int decide) {
+    if (!decide) return read_status(disp) == kDispExecuted;
+    const bool ok = !prev_disp || (read_status(prev_disp) == kDispExecuted && read_status(prev_status) == kStatusOk);
+    if ((blockIdx.x | blockIdx.y | blockIdx.z | threadIdx.x | threadIdx.y | threadIdx.z) == 0)
+        *disp = ok ? kDispExecuted : kDispSkipped;
+    return ok;
+}
+
+__device__ __forceinline__ bool chain_admits(const ChainGuard &g) {
+    return !g.disp || chain_decide(g.prev_status, g.prev_disp, g.disp, g.decide);
+}
+
+// The guard for a stage's later kernels.
+inline ChainGuard chain_follow(ChainGuard g) {
+    g.decide = 0;
+    return g;
+}
+
 __device__ __forceinline__ unsigned long long global_ns() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

@@ -21,6 +21,7 @@
 
 #include "common.cuh"
 #include "pcu_b200.h"
+#include "provider.h"
 
 namespace pcu {
 
@@ -107,7 +108,8 @@ template <typename T> struct ReluBackwardOp {
 template <typename T, int V, class Op, int U = (V > 1 ? PCU_STREAM_UNROLL : 1)>
 __global__ void __launch_bounds__(256) streaming_kernel(const T *a, const T *b,
                                                          T *out, uint64_t n, int a_uniform, int b_uniform,
-                                                         Op op, unsigned long long *status) {
+                                                         Op op, unsigned long long *status, ChainGuard guard) {
+    if (!chain_admits(guard)) return;  // a skipped stage of a guarded chain touches nothing
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     const uint64_t tid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const uint64_t nvec = n / V;
@@ -172,8 +174,8 @@ __global__ void __launch_bounds__(256) streaming_kernel(const T *a, const T *b,
 
 template <typename T, class Op>
 int launch_streaming(const T *a, const T *b, T *out, uint64_t n, int a_uniform, int b_uniform, Op op,
-                     unsigned long long *status, cudaStream_t stream) {
-    if (n == 0) return PCU_B200_OK;
+                     unsigned long long *status, cudaStream_t stream, const ChainGuard &guard) {
+    if (n == 0) return chain_decide_only(guard, stream);
     constexpr int V = 16 / sizeof(T);
     bool vec = pcu_host::aligned(out, 16) && (a_uniform || pcu_host::aligned(a, 16)) &&
                (b_uniform || !b || pcu_host::aligned(b, 16));
@@ -186,9 +188,11 @@ int launch_streaming(const T *a, const T *b, T *out, uint64_t n, int a_uniform, 
     uint64_t cap = (uint64_t)pcu_host::sm_count() * PCU_STREAM_CTAS_PER_SM;
     unsigned blocks = (unsigned)(want < cap ? (want ? want : 1) : cap);
     if (vec)
-        streaming_kernel<T, V, Op><<<blocks, threads, 0, stream>>>(a, b, out, n, a_uniform, b_uniform, op, status);
+        streaming_kernel<T, V, Op><<<blocks, threads, 0, stream>>>(a, b, out, n, a_uniform, b_uniform, op, status,
+                                                                    guard);
     else
-        streaming_kernel<T, 1, Op><<<blocks, threads, 0, stream>>>(a, b, out, n, a_uniform, b_uniform, op, status);
+        streaming_kernel<T, 1, Op><<<blocks, threads, 0, stream>>>(a, b, out, n, a_uniform, b_uniform, op, status,
+                                                                    guard);
     return pcu_host::launch_status();
 }
 
@@ -200,8 +204,8 @@ static bool valid_common(int dtype, int policy, const uint64_t *status) {
     return (dtype == PCU_B200_F32 || dtype == PCU_B200_F64) && policy >= 0 && policy <= 2 && status != nullptr;
 }
 
-extern "C" int pcu_b200_strict_sgd(int dtype, int policy, const void *weights, const void *gradient, void *out,
-                                   uint64_t count, uint32_t rate_bits_f32, uint64_t *status, void *stream) {
+int pcu::strict_sgd(int dtype, int policy, const void *weights, const void *gradient, void *out, uint64_t count,
+                    uint32_t rate_bits_f32, uint64_t *status, void *stream, const ChainGuard &guard) {
     if (!valid_common(dtype, policy, status)) return PCU_B200_ERROR_INVALID_ARGUMENT;
     if ((rate_bits_f32 & 0x7f800000u) == 0x7f800000u) return PCU_B200_ERROR_INVALID_ARGUMENT;  // capture rejects
     if (count && (!weights || !gradient || !out)) return PCU_B200_ERROR_INVALID_ARGUMENT;
@@ -211,16 +215,16 @@ extern "C" int pcu_b200_strict_sgd(int dtype, int policy, const void *weights, c
     if (dtype == PCU_B200_F32) {
         SgdOp<float> op{pcu_host::rate_f32(rate_bits_f32), policy};
         return launch_streaming<float>((const float *)weights, (const float *)gradient, (float *)out, count, 0, 0,
-                                       op, st, s);
+                                       op, st, s, guard);
     }
     SgdOp<double> op{pcu_host::rate_f64(rate_bits_f32), policy};
     return launch_streaming<double>((const double *)weights, (const double *)gradient, (double *)out, count, 0, 0,
-                                    op, st, s);
+                                    op, st, s, guard);
 }
 
-extern "C" int pcu_b200_checked_binary(int dtype, int policy, int op, const void *left, const void *right,
-                                       void *out, uint64_t count, int left_uniform, int right_uniform,
-                                       uint64_t *status, void *stream) {
+int pcu::checked_binary(int dtype, int policy, int op, const void *left, const void *right, void *out,
+                        uint64_t count, int left_uniform, int right_uniform, uint64_t *status, void *stream,
+                        const ChainGuard &guard) {
     if (!valid_common(dtype, policy, status) || op < 0 || op > 3) return PCU_B200_ERROR_INVALID_ARGUMENT;
     if (count && (!left || !right || !out)) return PCU_B200_ERROR_INVALID_ARGUMENT;
     if (count > (1ull << 60)) return PCU_B200_ERROR_SIZE_OVERFLOW;
@@ -228,13 +232,13 @@ extern "C" int pcu_b200_checked_binary(int dtype, int policy, int op, const void
     cudaStream_t s = pcu_host::as_stream(stream);
     if (dtype == PCU_B200_F32)
         return launch_streaming<float>((const float *)left, (const float *)right, (float *)out, count,
-                                       left_uniform != 0, right_uniform != 0, BinaryOp<float>{op, policy}, st, s);
+                                       left_uniform != 0, right_uniform != 0, BinaryOp<float>{op, policy}, st, s, guard);
     return launch_streaming<double>((const double *)left, (const double *)right, (double *)out, count,
-                                    left_uniform != 0, right_uniform != 0, BinaryOp<double>{op, policy}, st, s);
+                                    left_uniform != 0, right_uniform != 0, BinaryOp<double>{op, policy}, st, s, guard);
 }
 
-extern "C" int pcu_b200_checked_relu(int dtype, int policy, const void *input, void *out, uint64_t count,
-                                     uint64_t *status, void *stream) {
+int pcu::checked_relu(int dtype, int policy, const void *input, void *out, uint64_t count, uint64_t *status,
+                      void *stream, const ChainGuard &guard) {
     if (!valid_common(dtype, policy, status)) return PCU_B200_ERROR_INVALID_ARGUMENT;
     if (count && (!input || !out)) return PCU_B200_ERROR_INVALID_ARGUMENT;
     if (count > (1ull << 60)) return PCU_B200_ERROR_SIZE_OVERFLOW;
@@ -242,13 +246,13 @@ extern "C" int pcu_b200_checked_relu(int dtype, int policy, const void *input, v
     cudaStream_t s = pcu_host::as_stream(stream);
     if (dtype == PCU_B200_F32)
         return launch_streaming<float>((const float *)input, nullptr, (float *)out, count, 0, 0,
-                                       ReluOp<float>{policy}, st, s);
+                                       ReluOp<float>{policy}, st, s, guard);
     return launch_streaming<double>((const double *)input, nullptr, (double *)out, count, 0, 0,
-                                    ReluOp<double>{policy}, st, s);
+                                    ReluOp<double>{policy}, st, s, guard);
 }
 
-extern "C" int pcu_b200_checked_relu_backward(int dtype, int policy, const void *input, const void *upstream,
-                                              void *out, uint64_t count, uint64_t *status, void *stream) {
+int pcu::checked_relu_backward(int dtype, int policy, const void *input, const void *upstream, void *out,
+                               uint64_t count, uint64_t *status, void *stream, const ChainGuard &guard) {
     if (!valid_common(dtype, policy, status)) return PCU_B200_ERROR_INVALID_ARGUMENT;
     if (count && (!input || !upstream || !out)) return PCU_B200_ERROR_INVALID_ARGUMENT;
     if (count > (1ull << 60)) return PCU_B200_ERROR_SIZE_OVERFLOW;
@@ -256,7 +260,29 @@ extern "C" int pcu_b200_checked_relu_backward(int dtype, int policy, const void 
     cudaStream_t s = pcu_host::as_stream(stream);
     if (dtype == PCU_B200_F32)
         return launch_streaming<float>((const float *)input, (const float *)upstream, (float *)out, count, 0, 0,
-                                       ReluBackwardOp<float>{policy}, st, s);
+                                       ReluBackwardOp<float>{policy}, st, s, guard);
     return launch_streaming<double>((const double *)input, (const double *)upstream, (double *)out, count, 0, 0,
-                                    ReluBackwardOp<double>{policy}, st, s);
+                                    ReluBackwardOp<double>{policy}, st, s, guard);
+}
+
+extern "C" int pcu_b200_strict_sgd(int dtype, int policy, const void *weights, const void *gradient, void *out,
+                                   uint64_t count, uint32_t rate_bits_f32, uint64_t *status, void *stream) {
+    return pcu::strict_sgd(dtype, policy, weights, gradient, out, count, rate_bits_f32, status, stream, ChainGuard{});
+}
+
+extern "C" int pcu_b200_checked_binary(int dtype, int policy, int op, const void *left, const void *right,
+                                       void *out, uint64_t count, int left_uniform, int right_uniform,
+                                       uint64_t *status, void *stream) {
+    return pcu::checked_binary(dtype, policy, op, left, right, out, count, left_uniform, right_uniform, status, stream,
+                               ChainGuard{});
+}
+
+extern "C" int pcu_b200_checked_relu(int dtype, int policy, const void *input, void *out, uint64_t count,
+                                     uint64_t *status, void *stream) {
+    return pcu::checked_relu(dtype, policy, input, out, count, status, stream, ChainGuard{});
+}
+
+extern "C" int pcu_b200_checked_relu_backward(int dtype, int policy, const void *input, const void *upstream,
+                                              void *out, uint64_t count, uint64_t *status, void *stream) {
+    return pcu::checked_relu_backward(dtype, policy, input, upstream, out, count, status, stream, ChainGuard{});
 }

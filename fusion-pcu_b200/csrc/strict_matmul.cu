@@ -33,6 +33,7 @@
 
 #include "common.cuh"
 #include "pcu_b200.h"
+#include "provider.h"
 
 // Tuning knobs (defaults are the measured best; override with -D for sweeps).
 #ifndef PCU_MM_UNROLL_F32
@@ -57,6 +58,7 @@ template <typename T> struct MatmulParams {
     const int *col_minexp;
     unsigned long long *status;
     int vector_out;  // out is 16-byte aligned and columns is a multiple of the 16-byte vector
+    ChainGuard guard;  // the node's stage of a guarded chain (empty when not guarded)
 };
 
 // "no nonzero finite element" marker of the exponent prescan (also the memset byte pattern)
@@ -83,7 +85,8 @@ template <> __device__ __forceinline__ int min_exponent_of<double>(double x) {
 // min exponent along each row of a rows x cols row-major matrix (one warp per row)
 template <typename T>
 __global__ void __launch_bounds__(256) minexp_rows_kernel(const T *x, uint64_t rows, uint64_t cols, uint64_t ld,
-                                                          int *out) {
+                                                          int *out, ChainGuard guard) {
+    if (!chain_admits(guard)) return;
     const uint64_t warps = (uint64_t)gridDim.x * (blockDim.x / 32);
     const uint64_t warp = (uint64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
@@ -100,7 +103,8 @@ __global__ void __launch_bounds__(256) minexp_rows_kernel(const T *x, uint64_t r
 // min exponent down each column; blockIdx.y takes a slab of rows, atomicMin merges slabs
 template <typename T>
 __global__ void __launch_bounds__(256) minexp_cols_kernel(const T *x, uint64_t rows, uint64_t cols, uint64_t ld,
-                                                          uint64_t rows_per_slab, int *out) {
+                                                          uint64_t rows_per_slab, int *out, ChainGuard guard) {
+    if (!chain_admits(guard)) return;
     const uint64_t c = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= cols) return;
     const uint64_t r0 = (uint64_t)blockIdx.y * rows_per_slab;
@@ -238,6 +242,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     using VT = typename SVec<T, V>::type;
     using F = Fmt<T>;
 
+    if (!chain_admits(p.guard)) return;  // the whole CTA, before any barrier or copy
     extern __shared__ unsigned char smem_raw[];
     const uintptr_t base = (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023);
     T *const tiles = reinterpret_cast<T *>(base);
@@ -452,6 +457,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // threads, one cell each, 16-deep K slabs through shared memory, same epilogue.
 template <typename T>
 __global__ void __launch_bounds__(256) strict_matmul_generic_kernel(const __grid_constant__ MatmulParams<T> p) {
+    if (!chain_admits(p.guard)) return;  // the whole CTA
     using F = Fmt<T>;
     __shared__ T sa[16][17];
     __shared__ T sb[16][17];
@@ -540,10 +546,19 @@ int launch_tma(const CUtensorMap &ma, const CUtensorMap &mb, const MatmulParams<
 template <typename T>
 int run_matmul(int policy, const T *left, const T *right, T *out, uint64_t rows, uint64_t inner, uint64_t columns,
                uint64_t lda, uint64_t ldb, int tl, int tr, void *workspace, size_t workspace_bytes,
-               unsigned long long *status, cudaStream_t stream) {
-    MatmulParams<T> p{left, right, out,     rows,    inner,   columns, lda,
-                      ldb,  tl,    tr,      policy, 0,       nullptr, nullptr, status,
-                      pcu_host::aligned(out, 16) && columns % (16 / sizeof(T)) == 0};
+               unsigned long long *status, cudaStream_t stream, const ChainGuard &guard) {
+    MatmulParams<T> p{left,    right,   out,    rows,
+                      inner,   columns, lda,    ldb,
+                      tl,      tr,      policy, 0,
+                      nullptr, nullptr, status, pcu_host::aligned(out, 16) && columns % (16 / sizeof(T)) == 0,
+                      guard};
+    // the first kernel launched decides the stage's admission, the later ones follow it
+    ChainGuard next = guard;
+    auto take = [&]() {
+        const ChainGuard g = next;
+        next = chain_follow(next);
+        return g;
+    };
     if (policy != kPolicyGradual && inner > 0) {
         size_t need = pcu_b200_strict_matmul_workspace_size(rows, inner, columns);
         if (!workspace || workspace_bytes < need) return PCU_B200_ERROR_WORKSPACE;
@@ -555,7 +570,7 @@ int run_matmul(int policy, const T *left, const T *right, T *out, uint64_t rows,
         auto rows_pass = [&](const T *x, uint64_t r, uint64_t c, uint64_t ld, int *dst) {
             uint64_t blocks = (r + 7) / 8;
             if (blocks > (uint64_t)sms * 16) blocks = (uint64_t)sms * 16;
-            minexp_rows_kernel<T><<<(unsigned)blocks, 256, 0, stream>>>(x, r, c, ld, dst);
+            minexp_rows_kernel<T><<<(unsigned)blocks, 256, 0, stream>>>(x, r, c, ld, dst, take());
         };
         auto cols_pass = [&](const T *x, uint64_t r, uint64_t c, uint64_t ld, int *dst) {
             uint64_t col_blocks = (c + 255) / 256;
@@ -565,7 +580,7 @@ int run_matmul(int policy, const T *left, const T *right, T *out, uint64_t rows,
             uint64_t per = (r + slabs - 1) / slabs;
             slabs = (r + per - 1) / per;
             minexp_cols_kernel<T><<<dim3((unsigned)col_blocks, (unsigned)slabs), 256, 0, stream>>>(x, r, c, ld, per,
-                                                                                                 dst);
+                                                                                                 dst, take());
         };
         if (!tl) rows_pass(left, rows, inner, lda, row_min);
         else cols_pass(left, inner, rows, lda, row_min);
@@ -581,6 +596,7 @@ int run_matmul(int policy, const T *left, const T *right, T *out, uint64_t rows,
         const int emin = sizeof(T) == 4 ? -126 : -1022;
         p.threshold = policy == kPolicyIeee ? emin : emin + 2 * frac;
     }
+    p.guard = take();
     using S = TileShape<T>;
     CUtensorMap ma, mb;
     bool tma = inner > 0;
@@ -611,13 +627,13 @@ extern "C" size_t pcu_b200_strict_matmul_workspace_size(uint64_t rows, uint64_t 
     return ((rows * 4 + 255) / 256) * 256 + ((columns * 4 + 255) / 256) * 256;
 }
 
-extern "C" int pcu_b200_strict_matmul(int dtype, int policy, const void *left, const void *right, void *out,
-                                      uint64_t rows, uint64_t inner, uint64_t columns, uint64_t left_stride,
-                                      uint64_t right_stride, int transpose_left, int transpose_right,
-                                      void *workspace, size_t workspace_bytes, uint64_t *status, void *stream) {
+int pcu::strict_matmul(int dtype, int policy, const void *left, const void *right, void *out, uint64_t rows,
+                       uint64_t inner, uint64_t columns, uint64_t left_stride, uint64_t right_stride,
+                       int transpose_left, int transpose_right, void *workspace, size_t workspace_bytes,
+                       uint64_t *status, void *stream, const ChainGuard &guard) {
     if ((dtype != PCU_B200_F32 && dtype != PCU_B200_F64) || policy < 0 || policy > 2 || !status)
         return PCU_B200_ERROR_INVALID_ARGUMENT;
-    if (rows == 0 || columns == 0) return PCU_B200_OK;
+    if (rows == 0 || columns == 0) return chain_decide_only(guard, pcu_host::as_stream(stream));
     if (!out || (inner > 0 && (!left || !right))) return PCU_B200_ERROR_INVALID_ARGUMENT;
     // left is rows x inner (or inner x rows); right is inner x columns (or columns x inner)
     const uint64_t left_row_len = transpose_left ? rows : inner;
@@ -634,10 +650,19 @@ extern "C" int pcu_b200_strict_matmul(int dtype, int policy, const void *left, c
     if (dtype == PCU_B200_F32)
         return run_matmul<float>(policy, (const float *)left, (const float *)right, (float *)out, rows, inner, columns,
                                  left_stride, right_stride, transpose_left != 0, transpose_right != 0, workspace,
-                                 workspace_bytes, st, s);
+                                 workspace_bytes, st, s, guard);
     return run_matmul<double>(policy, (const double *)left, (const double *)right, (double *)out, rows, inner,
                               columns, left_stride, right_stride, transpose_left != 0, transpose_right != 0,
-                              workspace, workspace_bytes, st, s);
+                              workspace, workspace_bytes, st, s, guard);
+}
+
+extern "C" int pcu_b200_strict_matmul(int dtype, int policy, const void *left, const void *right, void *out,
+                                      uint64_t rows, uint64_t inner, uint64_t columns, uint64_t left_stride,
+                                      uint64_t right_stride, int transpose_left, int transpose_right,
+                                      void *workspace, size_t workspace_bytes, uint64_t *status, void *stream) {
+    return pcu::strict_matmul(dtype, policy, left, right, out, rows, inner, columns, left_stride, right_stride,
+                              transpose_left, transpose_right, workspace, workspace_bytes, status, stream,
+                              ChainGuard{});
 }
 
 // ============================================================================

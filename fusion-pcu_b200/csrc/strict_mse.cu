@@ -53,6 +53,7 @@
 
 #include "common.cuh"
 #include "pcu_b200.h"
+#include "provider.h"
 
 #ifndef PCU_MSE_MIN_BLOCKS_F32
 #define PCU_MSE_MIN_BLOCKS_F32 4
@@ -379,7 +380,7 @@ template <typename T, bool RIDE>
 __global__ void __launch_bounds__(32 * kChunkWarps, MseTraits<T>::MIN_BLOCKS)
 mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base, bool vec, int policy,
                  uint64_t chunks, uint64_t ahead, MseHead *heads, typename MseTraits<T>::D *deltas,
-                 unsigned long long *status, SgdRider<T> rider) {
+                 unsigned long long *status, SgdRider<T> rider, ChainGuard guard) {
     using Tr = MseTraits<T>;
     using F = Fmt<T>;
     using B = typename F::Bits;
@@ -399,6 +400,9 @@ mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base
     __shared__ __align__(16) unsigned char s_slot[kChunkWarps][Tr::CHUNK * sizeof(Fix)];
     __shared__ Fix s_lane_ex[kChunkWarps][ROWS][32];  // exclusive prefix XOR in front of (row, lane)
 
+    // a skipped stage of a guarded chain touches nothing (the SGD-carrying form is never guarded)
+    if constexpr (!RIDE)
+        if (!chain_admits(guard)) return;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     uint64_t cta = blockIdx.x;
     if constexpr (RIDE) {
@@ -726,7 +730,8 @@ constexpr int kStageMaps = 16;
 template <typename T>
 __global__ void __launch_bounds__(256) mse_compose_kernel(const MseHead *heads, const typename MseTraits<T>::D *deltas,
                                                           uint64_t children, uint64_t span, MseHead *pheads,
-                                                          typename MseTraits<T>::D *pdeltas) {
+                                                          typename MseTraits<T>::D *pdeltas, ChainGuard guard) {
+    if (!chain_admits(guard)) return;
     using Tr = MseTraits<T>;
     using D = typename Tr::D;
     constexpr int W = Tr::W;
@@ -1086,8 +1091,8 @@ __device__ __forceinline__ void mse_walk(
     prediction, target, n, heads0, deltas0, heads1, deltas1, heads2, deltas2, chunks, blocks, supers, base, total, \
         denominator, policy, carry_in, carry_out, out, status
 
-template <typename T> __global__ void __launch_bounds__(1024) mse_walk_kernel(PCU_MSE_WALK_PARAMS) {
-    mse_walk<T>(PCU_MSE_WALK_ARGS);
+template <typename T> __global__ void __launch_bounds__(1024) mse_walk_kernel(PCU_MSE_WALK_PARAMS, ChainGuard guard) {
+    if (chain_admits(guard)) mse_walk<T>(PCU_MSE_WALK_ARGS);
 }
 
 // CTA 0 walks; the other CTAs stream an SGD node's elements meanwhile (the walker is latency
@@ -1169,7 +1174,8 @@ inline uint64_t sgd_units(uint64_t chunks) { return chunk_grid(chunks, true) / k
 // elements per SGD CTA.
 template <typename T>
 int prepare_mse(int policy, const T *p, const T *t, uint64_t n, uint64_t base, void *workspace, size_t workspace_bytes,
-                unsigned long long *status, cudaStream_t stream, const SgdRider<T> *sgd = nullptr) {
+                unsigned long long *status, cudaStream_t stream, const SgdRider<T> *sgd = nullptr,
+                const ChainGuard &guard = ChainGuard{}) {
     using D = typename MseTraits<T>::D;
     MseLayout<T> lay(n);
     if (!workspace || workspace_bytes < lay.bytes) return PCU_B200_ERROR_WORKSPACE;
@@ -1198,18 +1204,18 @@ int prepare_mse(int policy, const T *p, const T *t, uint64_t n, uint64_t base, v
     D *d0 = reinterpret_cast<D *>(ws + lay.deltas_off[0]);
     if (ride)
         mse_chunk_kernel<T, true><<<grid, 32 * kChunkWarps, 0, stream>>>(p, t, n, base, vec, policy, lay.count[0],
-                                                                         (uint64_t)ahead, h0, d0, status, *sgd);
+                                                                         (uint64_t)ahead, h0, d0, status, *sgd, guard);
     else
         mse_chunk_kernel<T, false><<<grid, 32 * kChunkWarps, 0, stream>>>(p, t, n, base, vec, policy, lay.count[0],
                                                                           (uint64_t)ahead, h0, d0, status,
-                                                                          SgdRider<T>{});
+                                                                          SgdRider<T>{}, guard);
     int rc = pcu_host::launch_status();
     for (int l = 1; l < kLevels && !rc; ++l) {
         mse_compose_kernel<T><<<(unsigned)lay.count[l], 256, 0, stream>>>(
             reinterpret_cast<const MseHead *>(ws + lay.heads_off[l - 1]),
             reinterpret_cast<const D *>(ws + lay.deltas_off[l - 1]), lay.count[l - 1],
             (uint64_t)MseTraits<T>::CHUNK << (6 * (l - 1)), reinterpret_cast<MseHead *>(ws + lay.heads_off[l]),
-            reinterpret_cast<D *>(ws + lay.deltas_off[l]));
+            reinterpret_cast<D *>(ws + lay.deltas_off[l]), chain_follow(guard));
         rc = pcu_host::launch_status();
     }
     return rc;
@@ -1221,7 +1227,7 @@ int prepare_mse(int policy, const T *p, const T *t, uint64_t n, uint64_t base, v
 template <typename T>
 int walk_mse(int policy, const T *p, const T *t, uint64_t n, uint64_t base, uint64_t total, const T *carry_in,
              T *carry_out, T *out, void *workspace, size_t workspace_bytes, unsigned long long *status,
-             cudaStream_t stream, const SgdRider<T> *sgd = nullptr) {
+             cudaStream_t stream, const SgdRider<T> *sgd = nullptr, const ChainGuard &guard = ChainGuard{}) {
     using D = typename MseTraits<T>::D;
     constexpr unsigned THREADS = MseTraits<T>::CHUNK;
     MseLayout<T> lay(n);
@@ -1240,17 +1246,18 @@ int walk_mse(int policy, const T *p, const T *t, uint64_t n, uint64_t base, uint
     } else {
         mse_walk_kernel<T><<<1, THREADS, 0, stream>>>(p, t, n, H(0), R(0), H(1), R(1), H(2), R(2), lay.count[0],
                                                       lay.count[1], lay.count[2], base, total, count_value<T>(total),
-                                                      policy, carry_in, carry_out, out, status);
+                                                      policy, carry_in, carry_out, out, status, guard);
     }
     return pcu_host::launch_status();
 }
 
 template <typename T>
 int run_mse(int policy, const T *p, const T *t, T *out, uint64_t n, void *workspace, size_t workspace_bytes,
-            unsigned long long *status, cudaStream_t stream) {
-    int rc = prepare_mse<T>(policy, p, t, n, 0, workspace, workspace_bytes, status, stream);
+            unsigned long long *status, cudaStream_t stream, const ChainGuard &guard) {
+    int rc = prepare_mse<T>(policy, p, t, n, 0, workspace, workspace_bytes, status, stream, nullptr, guard);
     if (rc) return rc;
-    return walk_mse<T>(policy, p, t, n, 0, n, nullptr, nullptr, out, workspace, workspace_bytes, status, stream);
+    return walk_mse<T>(policy, p, t, n, 0, n, nullptr, nullptr, out, workspace, workspace_bytes, status, stream,
+                       nullptr, chain_follow(guard));
 }
 
 // ---- MSE + SGD in one pass.  The SGD node's elements go to the chunk kernel's SGD CTAs, up to
@@ -1337,6 +1344,12 @@ extern "C" size_t pcu_b200_strict_mse_workspace_size(int dtype, uint64_t count) 
 extern "C" int pcu_b200_strict_mse(int dtype, int policy, const void *prediction, const void *target, void *out,
                                    uint64_t count, void *workspace, size_t workspace_bytes, uint64_t *status,
                                    void *stream) {
+    return pcu::strict_mse(dtype, policy, prediction, target, out, count, workspace, workspace_bytes, status, stream,
+                           pcu::ChainGuard{});
+}
+
+int pcu::strict_mse(int dtype, int policy, const void *prediction, const void *target, void *out, uint64_t count,
+                    void *workspace, size_t workspace_bytes, uint64_t *status, void *stream, const ChainGuard &guard) {
     if ((dtype != PCU_B200_F32 && dtype != PCU_B200_F64) || policy < 0 || policy > 2 || !status)
         return PCU_B200_ERROR_INVALID_ARGUMENT;
     if (count == 0 || !prediction || !target || !out) return PCU_B200_ERROR_INVALID_ARGUMENT;
@@ -1345,9 +1358,9 @@ extern "C" int pcu_b200_strict_mse(int dtype, int policy, const void *prediction
     cudaStream_t s = pcu_host::as_stream(stream);
     if (dtype == PCU_B200_F32)
         return pcu::run_mse<float>(policy, (const float *)prediction, (const float *)target, (float *)out, count,
-                                   workspace, workspace_bytes, st, s);
+                                   workspace, workspace_bytes, st, s, guard);
     return pcu::run_mse<double>(policy, (const double *)prediction, (const double *)target, (double *)out, count,
-                                workspace, workspace_bytes, st, s);
+                                workspace, workspace_bytes, st, s, guard);
 }
 
 extern "C" int pcu_b200_strict_mse_segment_prepare(int dtype, int policy, const void *prediction, const void *target,

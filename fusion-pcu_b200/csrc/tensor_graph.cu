@@ -11,6 +11,7 @@
 
 #include "pcu_b200.h"
 #include "pcu_b200_graph.h"
+#include "provider.h"
 
 namespace {
 
@@ -298,6 +299,8 @@ struct pcu_b200_prepared {
     std::vector<int32_t> inputs;    // planned Input node ids in capture order
     std::vector<void *> buffers;    // per node id (nullptr if not planned)
     uint64_t *status = nullptr;     // per node id
+    uint64_t *disp = nullptr;       // per node id: guarded-chain disposition (pending 0, executed 1, skipped 2)
+    std::vector<int32_t> stages;    // the planned nodes that launch work, in plan order
     void *workspace = nullptr;
     size_t workspace_bytes = 0;
     size_t elem = 4;
@@ -310,6 +313,7 @@ struct pcu_b200_prepared {
         for (void *b : buffers)
             if (b) cudaFree(b);
         if (status) cudaFree(status);
+        if (disp) cudaFree(disp);
         if (workspace) cudaFree(workspace);
     }
 };
@@ -372,7 +376,7 @@ int decode(const pcu_b200_prepared &p, int32_t id, uint64_t word, pcu_b200_tenso
     return e->code;
 }
 
-int launch(pcu_b200_prepared &p, int32_t id, void *stream) {
+int launch(pcu_b200_prepared &p, int32_t id, void *stream, const pcu::ChainGuard &guard) {
     const Node &n = p.graph.nodes[id];
     const int dt = p.graph.dtype, pol = p.graph.policy;
     uint64_t *st = p.status + id;
@@ -387,23 +391,23 @@ int launch(pcu_b200_prepared &p, int32_t id, void *stream) {
     case PCU_B200_NODE_SUB:
     case PCU_B200_NODE_MUL:
     case PCU_B200_NODE_DIV:
-        return pcu_b200_checked_binary(dt, pol, n.op - PCU_B200_NODE_ADD, buf(n.left), buf(n.right), out, n.count(),
-                                       uni(n.left), uni(n.right), st, stream);
+        return pcu::checked_binary(dt, pol, n.op - PCU_B200_NODE_ADD, buf(n.left), buf(n.right), out, n.count(),
+                                   uni(n.left), uni(n.right), st, stream, guard);
     case PCU_B200_NODE_RELU:
-        return pcu_b200_checked_relu(dt, pol, buf(n.left), out, n.count(), st, stream);
+        return pcu::checked_relu(dt, pol, buf(n.left), out, n.count(), st, stream, guard);
     case PCU_B200_NODE_RELU_BACKWARD:
-        return pcu_b200_checked_relu_backward(dt, pol, buf(n.left), buf(n.right), out, n.count(), st, stream);
+        return pcu::checked_relu_backward(dt, pol, buf(n.left), buf(n.right), out, n.count(), st, stream, guard);
     case PCU_B200_NODE_MATMUL: {
         const auto &sa = p.graph.nodes[n.left].shape, &sb = p.graph.nodes[n.right].shape;
         const uint64_t inner = n.tl ? sa[0] : sa[1];
-        return pcu_b200_strict_matmul(dt, pol, buf(n.left), buf(n.right), out, n.shape[0], inner, n.shape[1], sa[1],
-                                      sb[1], n.tl, n.tr, p.workspace, p.workspace_bytes, st, stream);
+        return pcu::strict_matmul(dt, pol, buf(n.left), buf(n.right), out, n.shape[0], inner, n.shape[1], sa[1], sb[1],
+                                  n.tl, n.tr, p.workspace, p.workspace_bytes, st, stream, guard);
     }
     case PCU_B200_NODE_MEAN_SQUARED_ERROR:
-        return pcu_b200_strict_mse(dt, pol, buf(n.left), buf(n.right), out, p.graph.nodes[n.left].count(),
-                                   p.workspace, p.workspace_bytes, st, stream);
+        return pcu::strict_mse(dt, pol, buf(n.left), buf(n.right), out, p.graph.nodes[n.left].count(), p.workspace,
+                               p.workspace_bytes, st, stream, guard);
     case PCU_B200_NODE_SGD_UPDATE:
-        return pcu_b200_strict_sgd(dt, pol, buf(n.left), buf(n.right), out, n.count(), n.rate_bits, st, stream);
+        return pcu::strict_sgd(dt, pol, buf(n.left), buf(n.right), out, n.count(), n.rate_bits, st, stream, guard);
     default:
         return PCU_B200_ERROR_INVALID_ARGUMENT;
     }
@@ -608,7 +612,10 @@ extern "C" pcu_b200_prepared *pcu_b200_graph_prepare(const pcu_b200_graph *g, co
         if (n.op == PCU_B200_NODE_MEAN_SQUARED_ERROR)
             ws = std::max(ws, pcu_b200_strict_mse_workspace_size(g->dtype, g->nodes[n.left].count()));
     }
+    for (int32_t id : p->plan)
+        if (g->nodes[id].op != PCU_B200_NODE_INPUT && g->nodes[id].op != PCU_B200_NODE_UNIFORM) p->stages.push_back(id);
     cudaError_t err = cudaMalloc((void **)&p->status, std::max<size_t>(N, 1) * sizeof(uint64_t));
+    if (err == cudaSuccess) err = cudaMalloc((void **)&p->disp, std::max<size_t>(N, 1) * sizeof(uint64_t));
     if (err == cudaSuccess && ws) err = cudaMalloc(&p->workspace, ws);
     if (err != cudaSuccess) {
         backend_error(e, -1, (int)err);
@@ -633,27 +640,64 @@ extern "C" void *pcu_b200_prepared_buffer(const pcu_b200_prepared *p, int32_t v)
 
 namespace {
 
-// The status reset and every planned node, launched back to back on `s`.
-int launch_plan(pcu_b200_prepared &p, cudaStream_t s, int32_t &failed) {
+// The guard of stage i: its predecessor's fault word and disposition, and its own disposition.
+pcu::ChainGuard stage_guard(const pcu_b200_prepared &p, size_t i) {
+    pcu::ChainGuard g{};
+    const int32_t id = p.stages[i];
+    g.disp = reinterpret_cast<unsigned long long *>(p.disp + id);
+    g.decide = 1;
+    if (i > 0) {
+        g.prev_status = reinterpret_cast<const unsigned long long *>(p.status + p.stages[i - 1]);
+        g.prev_disp = reinterpret_cast<const unsigned long long *>(p.disp + p.stages[i - 1]);
+    }
+    return g;
+}
+
+// The status reset and every planned node, launched back to back on `s`; `guarded`: as a
+// guarded chain (dispositions reset to pending, each stage admitted by its predecessor).
+int launch_plan(pcu_b200_prepared &p, cudaStream_t s, int32_t &failed, bool guarded) {
     failed = -1;
     int rc = pcu_b200_status_reset(p.status, p.graph.nodes.size(), s);
     if (rc) return rc;
-    for (int32_t id : p.plan) {
-        rc = launch(p, id, s);
+    if (guarded) {
+        cudaError_t err = cudaMemsetAsync(p.disp, 0, p.graph.nodes.size() * sizeof(uint64_t), s);
+        if (err != cudaSuccess) return pcu_host::set_cuda_error(err);
+    }
+    for (size_t i = 0; i < p.stages.size(); ++i) {
+        rc = launch(p, p.stages[i], s, guarded ? stage_guard(p, i) : pcu::ChainGuard{});
         if (rc) {
-            failed = id;
+            failed = p.stages[i];
             return rc;
         }
     }
     return PCU_B200_OK;
 }
 
-// One read of every status word; the lowest faulting node in graph order wins.
-int read_and_decode(pcu_b200_prepared &p, cudaStream_t s, pcu_b200_tensor_error *e) {
-    std::vector<uint64_t> words(p.graph.nodes.size());
-    cudaError_t err = cudaMemcpyAsync(words.data(), p.status, words.size() * 8, cudaMemcpyDeviceToHost, s);
+// One read of every status word; the lowest faulting node in graph order wins.  A guarded
+// chain's records are also validated as the reference does (guarded.rs:109-147): every stage in
+// front of the first fault executed without a fault, every stage after it was skipped with a
+// clear fault word, and none is pending.  A violation blocks the result (FailedCompletion).
+int read_and_decode(pcu_b200_prepared &p, cudaStream_t s, pcu_b200_tensor_error *e, bool guarded) {
+    const size_t N = p.graph.nodes.size();
+    std::vector<uint64_t> words(N), disp(guarded ? N : 0);
+    cudaError_t err = cudaMemcpyAsync(words.data(), p.status, N * 8, cudaMemcpyDeviceToHost, s);
+    if (err == cudaSuccess && guarded) err = cudaMemcpyAsync(disp.data(), p.disp, N * 8, cudaMemcpyDeviceToHost, s);
     if (err == cudaSuccess) err = cudaStreamSynchronize(s);
     if (err != cudaSuccess) return backend_error(e, -1, (int)err);
+    if (guarded) {
+        int32_t first = -1;
+        for (int32_t id : p.stages) {
+            const bool executed = disp[id] == pcu::kDispExecuted, skipped = disp[id] == pcu::kDispSkipped;
+            const bool ok = first < 0 ? executed : (skipped && words[id] == PCU_B200_STATUS_OK);
+            if (!ok) {
+                fail(e, PCU_B200_TENSOR_FAILED_COMPLETION, id);
+                return PCU_B200_TENSOR_FAILED_COMPLETION;
+            }
+            if (first < 0 && words[id] != PCU_B200_STATUS_OK) first = id;
+        }
+        if (first >= 0) return decode(p, first, words[first], e);
+        return PCU_B200_TENSOR_OK;
+    }
     for (int32_t id : p.plan)
         if (int code = decode(p, id, words[id], e)) return code;
     return PCU_B200_TENSOR_OK;
@@ -665,7 +709,7 @@ int record_replay(pcu_b200_prepared &p, cudaStream_t s, pcu_b200_tensor_error *e
     cudaError_t err = cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal);
     if (err != cudaSuccess) return backend_error(e, -1, (int)err);
     int32_t failed = -1;
-    const int rc = launch_plan(p, s, failed);
+    const int rc = launch_plan(p, s, failed, true);
     cudaGraph_t g = nullptr;
     err = cudaStreamEndCapture(s, &g);
     if (rc) {
@@ -689,7 +733,7 @@ extern "C" int pcu_b200_prepared_execute(pcu_b200_prepared *p, const void *const
                                          void *stream, pcu_b200_tensor_error *e) {
     clear(e);
     if (!p) return fail(e, PCU_B200_TENSOR_UNKNOWN_VALUE), PCU_B200_TENSOR_UNKNOWN_VALUE;
-    if (mode < PCU_B200_EXEC_CHAINED || mode > PCU_B200_EXEC_GRAPH)
+    if (mode < PCU_B200_EXEC_CHAINED || mode > PCU_B200_EXEC_GUARDED)
         return fail(e, PCU_B200_TENSOR_UNKNOWN_VALUE), PCU_B200_TENSOR_UNKNOWN_VALUE;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     if (mode == PCU_B200_EXEC_GRAPH && !s) {  // a CUDA graph cannot be recorded on the legacy stream
@@ -706,17 +750,17 @@ extern "C" int pcu_b200_prepared_execute(pcu_b200_prepared *p, const void *const
                                           cudaMemcpyHostToDevice, s);
         if (err != cudaSuccess) return backend_error(e, v, (int)err);
     }
-    if (mode == PCU_B200_EXEC_GRAPH) {
+    if (mode == PCU_B200_EXEC_GRAPH) {  // the guarded chain, replayed as one CUDA graph
         if (p->replay && p->replay_stream == s) {
             cudaError_t err = cudaGraphLaunch(p->replay, s);
             if (err != cudaSuccess) return backend_error(e, -1, (int)err);
-            return read_and_decode(*p, s, e);
+            return read_and_decode(*p, s, e, true);
         }
         // first run on this stream: an ordinary run gives the answer, then the plan is recorded
         int32_t failed = -1;
-        const int rc = launch_plan(*p, s, failed);
+        const int rc = launch_plan(*p, s, failed, true);
         if (rc) return backend_error(e, failed, rc);
-        const int code = read_and_decode(*p, s, e);
+        const int code = read_and_decode(*p, s, e, true);
         if (p->replay) {
             cudaGraphExecDestroy(p->replay);
             p->replay = nullptr;
@@ -729,23 +773,39 @@ extern "C" int pcu_b200_prepared_execute(pcu_b200_prepared *p, const void *const
         }
         return code;
     }
+    if (mode != PCU_B200_EXEC_EACH_NODE) {  // chained or guarded: one observation at the end
+        const bool guarded = mode == PCU_B200_EXEC_GUARDED;
+        int32_t failed = -1;
+        const int rc = launch_plan(*p, s, failed, guarded);
+        if (rc) return backend_error(e, failed, rc);
+        return read_and_decode(*p, s, e, guarded);
+    }
     int rc = pcu_b200_status_reset(p->status, p->graph.nodes.size(), stream);
     if (rc) return backend_error(e, -1, rc);
     uint64_t word = 0;
-    for (int32_t id : p->plan) {
-        rc = launch(*p, id, stream);
+    for (int32_t id : p->stages) {
+        rc = launch(*p, id, stream, pcu::ChainGuard{});
         if (rc) return backend_error(e, id, rc);
-        if (mode == PCU_B200_EXEC_EACH_NODE && p->graph.nodes[id].op != PCU_B200_NODE_INPUT &&
-            p->graph.nodes[id].op != PCU_B200_NODE_UNIFORM) {
-            // the reference's per-node completion wait and status decode (strict_matmul.rs:317-331)
-            cudaError_t err = cudaMemcpyAsync(&word, p->status + id, 8, cudaMemcpyDeviceToHost, s);
-            if (err == cudaSuccess) err = cudaStreamSynchronize(s);
-            if (err != cudaSuccess) return backend_error(e, id, (int)err);
-            if (int code = decode(*p, id, word, e)) return code;
-        }
+        // the reference's per-node completion wait and status decode (strict_matmul.rs:317-331)
+        cudaError_t err = cudaMemcpyAsync(&word, p->status + id, 8, cudaMemcpyDeviceToHost, s);
+        if (err == cudaSuccess) err = cudaStreamSynchronize(s);
+        if (err != cudaSuccess) return backend_error(e, id, (int)err);
+        if (int code = decode(*p, id, word, e)) return code;
     }
-    if (mode == PCU_B200_EXEC_CHAINED) return read_and_decode(*p, s, e);
     return PCU_B200_TENSOR_OK;
+}
+
+extern "C" int pcu_b200_prepared_stage(const pcu_b200_prepared *p, int32_t value, uint64_t *fault_word,
+                                       uint64_t *disposition, void *stream) {
+    if (!p || value < 0 || (size_t)value >= p->buffers.size() || !p->buffers[value])
+        return PCU_B200_TENSOR_UNKNOWN_VALUE;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    cudaError_t err = cudaSuccess;
+    if (fault_word) err = cudaMemcpyAsync(fault_word, p->status + value, 8, cudaMemcpyDeviceToHost, s);
+    if (err == cudaSuccess && disposition)
+        err = cudaMemcpyAsync(disposition, p->disp + value, 8, cudaMemcpyDeviceToHost, s);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(s);
+    return err == cudaSuccess ? PCU_B200_TENSOR_OK : PCU_B200_TENSOR_BACKEND;
 }
 
 extern "C" int pcu_b200_prepared_read(const pcu_b200_prepared *p, int32_t v, void *host, size_t bytes, void *stream) {

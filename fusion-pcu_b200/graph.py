@@ -19,10 +19,11 @@ from . import (KIND_NAMES, POLICY, ArithmeticFault, CompoundArithmeticFault, Pro
 NODE_OPS = ["input", "uniform", "add", "sub", "mul", "div", "relu", "relu_backward", "matmul", "mean_squared_error",
             "sgd_update"]
 STEPS = ["Multiply", "Add", "Subtract", "Divide"]
-EXEC_MODES = {"chained": 0, "each_node": 1, "graph": 2}
+EXEC_MODES = {"chained": 0, "each_node": 1, "graph": 2, "guarded": 3}
+DISPOSITIONS = {0: "pending", 1: "executed", 2: "skipped"}
 CODES = {1: "ArithmeticFault", 2: "CompoundArithmeticFault", 3: "ShapeMismatch", 4: "MatMulShape", 5: "UnknownValue",
          6: "InvalidLearningRate", 7: "GradientRootNotMse", 8: "UnsupportedGradient", 9: "EmptyOutputs",
-         10: "DataLength", 11: "Backend"}
+         10: "DataLength", 11: "Backend", 12: "FailedCompletion"}
 
 
 class TensorErrorStruct(ctypes.Structure):
@@ -84,6 +85,9 @@ def _lib():
         L.pcu_b200_prepared_execute.restype = ctypes.c_int
         L.pcu_b200_prepared_read.argtypes = [vp, i32, vp, sz, vp]
         L.pcu_b200_prepared_read.restype = ctypes.c_int
+        L.pcu_b200_prepared_stage.argtypes = [vp, i32, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64),
+                                              vp]
+        L.pcu_b200_prepared_stage.restype = ctypes.c_int
         _declared = True
     return L
 
@@ -245,8 +249,10 @@ class PreparedGraph:
     def execute(self, inputs=None, wait_each_node=True, stream=None, mode=None):
         """Copy the host `inputs` ({input value: array}) in, run the plan and raise the first fault.
 
-        mode: "chained" (one status read at the end), "each_node" (the reference's per-node wait)
-        or "graph" (CUDA-graph replay); by default wait_each_node picks the first two."""
+        mode: "chained" (one status read at the end), "each_node" (the reference's per-node wait),
+        "guarded" (the guarded stage chain: nothing runs after the first fault; one read at the
+        end) or "graph" (the guarded chain as a CUDA-graph replay); by default wait_each_node
+        picks the first two."""
         inputs = inputs or {}
         held = []
         ptrs = (ctypes.c_void_p * max(len(self.inputs), 1))()
@@ -274,6 +280,15 @@ class PreparedGraph:
         if rc:
             raise GraphError(rc, value)
         return out
+
+    def stage(self, value, stream=None):
+        """The last execution's record of a planned node: (fault word, disposition name)."""
+        word, disp = ctypes.c_uint64(), ctypes.c_uint64()
+        s = ctypes.c_void_p(stream.cuda_stream) if stream is not None else None
+        rc = self._L.pcu_b200_prepared_stage(self._h, value, ctypes.byref(word), ctypes.byref(disp), s)
+        if rc:
+            raise GraphError(rc, value)
+        return word.value, DISPOSITIONS.get(disp.value, disp.value)
 
     def run(self, inputs, outputs, wait_each_node=True, mode=None):
         self.execute(inputs, wait_each_node, mode=mode)

@@ -39,6 +39,8 @@ extern "C" {
 #define PCU_B200_TENSOR_EMPTY_OUTPUTS 9
 #define PCU_B200_TENSOR_DATA_LENGTH 10
 #define PCU_B200_TENSOR_BACKEND 11                  /* CUDA failure or malformed/watchdog status */
+#define PCU_B200_TENSOR_FAILED_COMPLETION 12        /* guarded-chain records violate the protocol
+                                                       (CudaTensorExecutionError::FailedCompletion) */
 
 /* TensorArithmeticStep (Crates/core/dialect/tensor.rs:425-430) */
 #define PCU_B200_STEP_MULTIPLY 0
@@ -120,7 +122,20 @@ void *pcu_b200_prepared_buffer(const pcu_b200_prepared *prepared, int32_t value)
 /* Execution modes of pcu_b200_prepared_execute */
 #define PCU_B200_EXEC_CHAINED 0   /* every node launched back to back; one status read at the end */
 #define PCU_B200_EXEC_EACH_NODE 1 /* the reference's protocol: one host wait and status read per node */
-#define PCU_B200_EXEC_GRAPH 2     /* the launches replayed as one CUDA graph; one status read at the end */
+#define PCU_B200_EXEC_GRAPH 2     /* the guarded chain replayed as one CUDA graph; one read at the end */
+#define PCU_B200_EXEC_GUARDED 3   /* the guarded chain launched back to back; one read at the end */
+
+/* Guarded stage chain (Crates/backends/cuda/owned_dispatch/guarded/guarded.rs:15-38,
+ * Crates/core/runtime/execution/guarded/guarded.rs:30-147).  Every planned node that launches
+ * work is a stage with a fault word and a disposition.  A stage runs only when its predecessor
+ * executed with a clear fault word; otherwise it is skipped and touches no user data: no loads,
+ * no arithmetic and no output writes after the first fault.  The single observation at the
+ * end reads every record and validates the chain as the reference does.  The stages in front of
+ * the first fault must have executed cleanly, and the stages after it must be skipped with a
+ * clear word.  A violation returns PCU_B200_TENSOR_FAILED_COMPLETION. */
+#define PCU_B200_DISPOSITION_PENDING 0
+#define PCU_B200_DISPOSITION_EXECUTED 1
+#define PCU_B200_DISPOSITION_SKIPPED 2
 
 /* Execute: copies `host_inputs` (one host pointer per planned input, NULL = already on the
  * device buffer) to the device, runs every planned node in graph order on `stream`, and
@@ -131,6 +146,10 @@ void *pcu_b200_prepared_buffer(const pcu_b200_prepared *prepared, int32_t value)
  * stream of its own.  Returns 0 on success or a PCU_B200_TENSOR_* code (details in *error). */
 int pcu_b200_prepared_execute(pcu_b200_prepared *prepared, const void *const *host_inputs, int mode,
                               void *stream, pcu_b200_tensor_error *error);
+/* The last execution's record of a planned node: its fault word and, for the guarded modes,
+ * its disposition (PCU_B200_DISPOSITION_*). */
+int pcu_b200_prepared_stage(const pcu_b200_prepared *prepared, int32_t value, uint64_t *fault_word,
+                            uint64_t *disposition, void *stream);
 /* Copy a planned value back to host memory (bytes must cover the value). */
 int pcu_b200_prepared_read(const pcu_b200_prepared *prepared, int32_t value, void *host, size_t bytes, void *stream);
 

@@ -30,8 +30,8 @@ def _expect_runs(expect):
     return [b for b, n in expect["runs"] for _ in range(n)]
 
 
-@pytest.mark.parametrize("wait_each_node", [True, False])
-def test_reference_programs(kats, wait_each_node):
+@pytest.mark.parametrize("mode", ["each_node", "chained", "guarded", "graph"])
+def test_reference_programs(kats, mode):
     for program in kats["programs"]:
         g, ids = graph_mod.from_program(program)
         _, inputs = ograph.from_program(program)
@@ -39,11 +39,11 @@ def test_reference_programs(kats, wait_each_node):
         feed = {ids[name]: arr for name, arr in inputs.items()}
         expect = program["expect"]
         if "runs" in expect:
-            out = prepared.run(feed, [ids[program["output"]]], wait_each_node)[ids[program["output"]]]
+            out = prepared.run(feed, [ids[program["output"]]], mode=mode)[ids[program["output"]]]
             assert [hex(v) for v in _bits(out).ravel()] == _expect_runs(expect), program["cite"]
             continue
         with pytest.raises(pcu.TensorError) as info:
-            prepared.execute(feed, wait_each_node)
+            prepared.execute(feed, mode=mode)
         err = info.value
         if "fault" in expect:
             f = expect["fault"]
@@ -71,7 +71,7 @@ def _single_layer(width, policy=0):
     return n, o, names, loss, upd
 
 
-@pytest.mark.parametrize("mode", ["each_node", "chained", "graph"])
+@pytest.mark.parametrize("mode", ["each_node", "chained", "guarded", "graph"])
 def test_single_layer_train_ten_steps_bit_exact(mode):
     rng = np.random.default_rng(20260101)
     x = dyadic_uniform(rng, (256, 512), 32)
@@ -131,7 +131,7 @@ def test_mlp_step_shared_backward(width):
             assert np.array_equal(_bits(got[a]), _bits(want[b])), (a, b)
 
 
-@pytest.mark.parametrize("mode", ["each_node", "chained", "graph"])
+@pytest.mark.parametrize("mode", ["each_node", "chained", "guarded", "graph"])
 def test_first_faulting_node_wins(mode):
     """A later node that faults at a smaller element must not hide the earlier node's fault."""
     g = graph_mod.Graph(32, 0)
@@ -197,3 +197,49 @@ def test_train_step_fault_location_matches_oracle(width, case):
         assert err.kind == fault["kind"] and err.element_index == fault["element_index"], (err, fault)
         if "step" in fault:
             assert (err.reduction_index, err.step) == (fault["reduction_index"], fault["step"]), (err, fault)
+
+
+@pytest.mark.parametrize("mode", ["guarded", "graph"])
+def test_guarded_chain_skips_every_stage_after_the_first_fault(mode):
+    """Guarded chain (owned_dispatch/guarded/guarded.rs:15-38): after a faulting stage, every
+    later stage is skipped and touches nothing, so the outputs of a clean run stay in place even
+    though the inputs changed; the records validate as the reference requires (stages in front
+    executed, the faulting stage executed with its fault word, later stages skipped and clear)."""
+    rng = np.random.default_rng(11)
+    g = graph_mod.Graph(32, 0)
+    a, b, c, t = g.input((16, 16)), g.input((16, 16)), g.input((16, 16)), g.input((16, 16))
+    e = g.add(a, c)          # stage 0: clean
+    q = g.div(e, b)          # stage 1: DivideByZero in the second run
+    m = g.matmul(q, c)       # stage 2: depends on the fault
+    r = g.relu(m)            # stage 3
+    loss = g.mean_squared_error(r, t)  # stage 4
+    z = g.mul(c, c)          # stage 5: independent of the fault, but later in the chain
+    prepared = g.prepare([loss, z])
+    feed = {v: dyadic_uniform(rng, (16, 16), 32) for v in (a, b, c, t)}
+    feed[b] = np.abs(feed[b]) + np.float32(0.5)
+    prepared.execute(feed, mode=mode)
+    clean = {v: prepared.read(v) for v in (m, r, loss, z)}
+    for v in (e, q, m, r, loss, z):
+        assert prepared.stage(v) == (pcu.STATUS_OK, "executed")
+    feed2 = dict(feed)
+    feed2[c] = dyadic_uniform(rng, (16, 16), 32)
+    feed2[b] = feed[b].copy()
+    feed2[b][3, 5] = 0.0
+    with pytest.raises(pcu.ArithmeticFault) as info:
+        prepared.execute(feed2, mode=mode)
+    assert (info.value.value, info.value.element_index, info.value.kind) == (q, 3 * 16 + 5, "DivideByZero")
+    assert prepared.stage(e) == (pcu.STATUS_OK, "executed")
+    word, disp = prepared.stage(q)
+    assert disp == "executed" and word == ((3 * 16 + 5) << 3 | 1)
+    for v in (m, r, loss, z):
+        assert prepared.stage(v) == (pcu.STATUS_OK, "skipped"), v
+        assert np.array_equal(_bits(prepared.read(v)), _bits(clean[v])), v
+    # the chained mode runs every node: the later outputs move with the new inputs
+    with pytest.raises(pcu.ArithmeticFault):
+        prepared.execute(feed2, mode="chained")
+    assert not np.array_equal(_bits(prepared.read(z)), _bits(clean[z]))
+    # and a clean guarded run afterwards executes every stage again
+    prepared.execute(feed, mode=mode)
+    assert np.array_equal(_bits(prepared.read(z)), _bits(clean[z]))
+    for v in (e, q, m, r, loss, z):
+        assert prepared.stage(v) == (pcu.STATUS_OK, "executed")
