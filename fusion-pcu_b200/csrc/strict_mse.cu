@@ -517,14 +517,13 @@ mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base
     // ---- fixed point Q = floor(q / 2^L0) < 2^W, carried as the bits of 2^P + Q (MARK | Q), with a
     // sticky flag in the (otherwise clear) sign bit when q has bits below 2^L0.  While
     // 2^-L0 is a normal number, q * 2^-L0 is exact and the round-toward-zero add of 2^P floors it,
-    // both on the FP pipe; otherwise the integer form.  Per row: the XOR of the words, and the OR
-    // of the trailing-zero masks of the nonzero Q with nothing below 2^L0 (bit b set: such a Q
-    // has its lowest set bit above b), which flags the rows that hold ties.  The words also go to this warp's
-    // shared-memory slot, where the tie pass reads them.
+    // both on the FP pipe; otherwise the integer form (rare; rolled, through the shared-memory
+    // slot, to keep the kernel's code small).  Per row: the XOR of the words.  The words also go
+    // to this warp's shared-memory slot, where the tie pass reads them.
     constexpr Fix MARK = sizeof(T) == 4 ? (Fix)0x4b000000u : (Fix)0x4330000000000000ull;  // bits of 2^P
     constexpr Fix LOW = ((Fix)1 << W) - 1;
     constexpr Fix STICKY = (Fix)1 << (sizeof(Fix) * 8 - 1);  // the sign bit: set when q has bits below 2^L0
-    Fix X[ROWS], tz[ROWS];
+    Fix X[ROWS];
     Fix *qs = reinterpret_cast<Fix *>(s_slot[warp]);
     if (L0 >= -F::kBias) {
         const T scale = F::value((B)(F::kBias - L0) << F::kFrac);  // 2^-L0
@@ -532,7 +531,6 @@ mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base
 #pragma unroll
         for (int r = 0; r < ROWS; ++r) {
             X[r] = 0;
-            tz[r] = 0;
 #pragma unroll
             for (int e = 0; e < V; ++e) {
                 const T qs_ = F::mul(F::value((B)qf[r * V + e]), scale);  // q / 2^L0, exact
@@ -541,50 +539,41 @@ mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base
                 const Fix tb = (Fix)F::bits(t) | (exact ? (Fix)0 : STICKY);
                 qf[r * V + e] = tb;
                 X[r] ^= tb;
-                // only a nonzero Q with nothing below 2^L0 can be a tie
-                if (exact && tb != MARK) tz[r] |= (tb - 1) & ~tb;
             }
         }
-    } else {
+    } else {  // rare (squares far below 1): the integer form, one element at a time through the slot
 #pragma unroll
+        for (int r = 0; r < ROWS; ++r)
+#pragma unroll
+            for (int v = 0; v < (int)(V * sizeof(Fix) / 16); ++v)
+                reinterpret_cast<uint4 *>(qs + CM::index(r, lane, 0))[v] = reinterpret_cast<const uint4 *>(&qf[r * V])[v];
+#pragma unroll 1
         for (int r = 0; r < ROWS; ++r) {
-            X[r] = 0;
-            tz[r] = 0;
-#pragma unroll
+            Fix x = 0;
+#pragma unroll 1
             for (int e = 0; e < V; ++e) {
+                Fix *slot = qs + CM::index(r, lane, 0) + e;
                 int dn;
                 Fix mm;
-                const Fix Q = fixed_point<T>(qf[r * V + e], C, K, dn, mm);
+                const Fix Q = fixed_point<T>(*slot, C, K, dn, mm);
                 const bool exact = dn >= (int)(sizeof(Fix) * 8) ? mm == 0 : (mm & (((Fix)1 << dn) - 1)) == 0;
                 const Fix tb = Q | MARK | (exact ? (Fix)0 : STICKY);
-                qf[r * V + e] = tb;
-                X[r] ^= tb;
-                if (Q != 0 && exact) tz[r] |= (tb - 1) & ~tb;
+                *slot = tb;
+                x ^= tb;
             }
+            set_at(X, r, x);
         }
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r)
+#pragma unroll
+            for (int v = 0; v < (int)(V * sizeof(Fix) / 16); ++v)
+                reinterpret_cast<uint4 *>(&qf[r * V])[v] = reinterpret_cast<const uint4 *>(qs + CM::index(r, lane, 0))[v];
     }
 #pragma unroll
     for (int r = 0; r < ROWS; ++r)
 #pragma unroll
         for (int v = 0; v < (int)(V * sizeof(Fix) / 16); ++v)
             reinterpret_cast<uint4 *>(qs + CM::index(r, lane, 0))[v] = reinterpret_cast<const uint4 *>(&qf[r * V])[v];
-    // ---- per-bit population counts of the chunk: Harley-Seal vertical counters per lane, then
-    // a warp bit-transpose per counter plane leaves the count of bit 32 w + b in lane b, word w
-    uint64_t cnt[NW];
-    {
-        Fix acc[LOG_EPT + 1];
-#pragma unroll
-        for (int i = 0; i <= LOG_EPT; ++i) acc[i] = 0;
-        acc[LOG_EPT] = SealTree<LOG_EPT, 0>::run(qf, acc);
-#pragma unroll
-        for (int w = 0; w < NW; ++w) {
-            unsigned c = 0;
-#pragma unroll
-            for (int pl = 0; pl <= LOG_EPT; ++pl)
-                c += (unsigned)__popc(warp_transpose32((unsigned)(acc[pl] >> (32 * w)), lane)) << pl;
-            cnt[w] = 32 * w + lane < W ? c : 0;
-        }
-    }
     // ---- exclusive prefix XOR of R = Q ^ (Q << 1) in element order, per row across the lanes
     // (XOR is linear: a row's R total is R of the row's XOR)
     {
@@ -601,6 +590,23 @@ mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base
             }
             s_lane_ex[warp][r][lane] = total ^ incl ^ row;  // rows before r, then lanes before this one
             total ^= shfl_x(incl, 31);
+        }
+    }
+    // ---- per-bit population counts of the chunk: Harley-Seal vertical counters per lane, then
+    // a warp bit-transpose per counter plane leaves the count of bit 32 w + b in lane b, word w
+    uint64_t cnt[NW];
+    {
+        Fix acc[LOG_EPT + 1];
+#pragma unroll
+        for (int i = 0; i <= LOG_EPT; ++i) acc[i] = 0;
+        acc[LOG_EPT] = SealTree<LOG_EPT, 0>::run(qf, acc);
+#pragma unroll
+        for (int w = 0; w < NW; ++w) {
+            unsigned c = 0;
+#pragma unroll
+            for (int pl = 0; pl <= LOG_EPT; ++pl)
+                c += (unsigned)__popc(warp_transpose32((unsigned)(acc[pl] >> (32 * w)), lane)) << pl;
+            cnt[w] = 32 * w + lane < W ? c : 0;
         }
     }
     // ---- S_b = sum over bits b' >= b of cnt[b'] 2^(b'-b) (saturated) for b = 32 w + lane: a
@@ -636,7 +642,9 @@ mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base
 
     // ---- ties at the usable binades: a Q whose lowest set bit is at or above jmin - 1 with
     // nothing of q below 2^L0.  Rare for rounded squares, common for exactly representable
-    // ones.  Only rows flagged by the trailing-zero masks are visited.  The ties are listed
+    // ones.  The rows are read back from the slot one at a time (a rolled loop: the kernel is
+    // issue bound and its unrolled code no longer fit the instruction cache), and only rows
+    // holding a candidate go on to the listing.  The ties are listed
     // in element order, with the parity of the half-up increments in front of each, in place of
     // the Q already read (a row's ties never outnumber its elements).  (A chunk with a
     // Subtract/Multiply fault is never mapped, only resolved up to the fault.)
@@ -644,14 +652,19 @@ mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base
     Tie *tl = reinterpret_cast<Tie *>(s_slot[warp]);
     if (!(head.flags & kHeadFault) && jmin <= W) {
         const Fix threshold = (Fix)1 << (jmin - 1), lowmask = threshold - 1;
-#pragma unroll
+#pragma unroll 1
         for (int r = 0; r < ROWS; ++r) {
-            const bool row_may = jmin < 2 || ((tz[r] >> (jmin - 2)) & 1);
-            if (!__any_sync(FULL, row_may)) continue;
             Fix Q[V];
 #pragma unroll
             for (int v = 0; v < (int)(V * sizeof(Fix) / 16); ++v)
                 reinterpret_cast<uint4 *>(Q)[v] = reinterpret_cast<const uint4 *>(qs + CM::index(r, lane, 0))[v];
+            bool row_may = false;  // a nonzero Q, nothing of q below 2^L0, lowest set bit >= jmin - 1
+#pragma unroll
+            for (int e = 0; e < V; ++e) {
+                const Fix q = Q[e] & LOW;
+                row_may |= q != 0 && (q & lowmask) == 0 && !(Q[e] & STICKY);
+            }
+            if (!__any_sync(FULL, row_may)) continue;
             unsigned mask = 0;   // bit e: element (r, lane, e) is a tie
             uint64_t code = 0;   // byte e: its j (6 bits) and parities (2 bits)
             if (row_may) {
