@@ -376,11 +376,15 @@ __device__ __forceinline__ void sgd_range(const SgdRider<T> &r, uint64_t s0, uin
     }
 }
 
-template <typename T, bool RIDE>
-__global__ void __launch_bounds__(32 * kChunkWarps, MseTraits<T>::MIN_BLOCKS)
-mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base, bool vec, int policy,
-                 uint64_t chunks, uint64_t ahead, MseHead *heads, typename MseTraits<T>::D *deltas,
-                 unsigned long long *status, SgdRider<T> rider, ChainGuard guard) {
+// A chunk warp's shared-memory slot: its fixed-point squares, later its ties.
+template <typename T> constexpr size_t kSlotBytes = (size_t)MseTraits<T>::CHUNK * sizeof(typename MseTraits<T>::Fix);
+
+// The maps of one chunk, one warp (chunk `cta * kChunkWarps + warp`); returns early per warp.
+template <typename T>
+__device__ __forceinline__ void chunk_maps(uint64_t cta, const T *prediction, const T *target, uint64_t n,
+                                           uint64_t base, bool vec, int policy, uint64_t chunks, uint64_t ahead,
+                                           MseHead *heads, typename MseTraits<T>::D *deltas,
+                                           unsigned long long *status, unsigned char *slots) {
     using Tr = MseTraits<T>;
     using F = Fmt<T>;
     using B = typename F::Bits;
@@ -396,23 +400,11 @@ mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base
     constexpr int VW = 16 / sizeof(T);  // elements per 16-byte load
     constexpr unsigned FULL = 0xffffffffu;
 
-    // per warp: the chunk's fixed-point squares, then (in place) its ties in element order
-    __shared__ __align__(16) unsigned char s_slot[kChunkWarps][Tr::CHUNK * sizeof(Fix)];
+    // per warp, in `slots` (kChunkWarps x kSlotBytes<T> bytes of shared memory): the chunk's
+    // fixed-point squares, then (in place) its ties in element order
     __shared__ Fix s_lane_ex[kChunkWarps][ROWS][32];  // exclusive prefix XOR in front of (row, lane)
 
-    // a skipped stage of a guarded chain touches nothing (the SGD-carrying form is never guarded)
-    if constexpr (!RIDE)
-        if (!chain_admits(guard)) return;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    uint64_t cta = blockIdx.x;
-    if constexpr (RIDE) {
-        if (blockIdx.x % kSgdPeriod == kSgdPeriod - 1) {  // an SGD CTA (its own status word)
-            const uint64_t s0 = (uint64_t)(blockIdx.x / kSgdPeriod) * rider.per_unit;
-            if (s0 < rider.n) sgd_range<T>(rider, s0, min(s0 + rider.per_unit, rider.n), threadIdx.x, blockDim.x);
-            return;
-        }
-        cta = blockIdx.x - blockIdx.x / kSgdPeriod;
-    }
     const uint64_t chunk = cta * kChunkWarps + warp;
     if (chunk >= chunks) return;  // the whole warp: nothing below synchronises beyond it
     const uint64_t chunk0 = chunk * Tr::CHUNK;
@@ -420,7 +412,7 @@ mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base
         // the chunk that will run `ahead` chunks later (one wave of resident warps): its operands
         // come from L2 instead of HBM when it starts
         const uint64_t next = chunk0 + ahead * Tr::CHUNK;
-        if (vec && next < n) {
+        if (vec && ahead && next < n) {
             const unsigned bytes = (unsigned)(min((uint64_t)Tr::CHUNK, n - next) * sizeof(T)) & ~15u;
             if (bytes) {
                 prefetch_l2(prediction + next, bytes);
@@ -524,7 +516,7 @@ mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base
     constexpr Fix LOW = ((Fix)1 << W) - 1;
     constexpr Fix STICKY = (Fix)1 << (sizeof(Fix) * 8 - 1);  // the sign bit: set when q has bits below 2^L0
     Fix X[ROWS];
-    Fix *qs = reinterpret_cast<Fix *>(s_slot[warp]);
+    Fix *qs = reinterpret_cast<Fix *>(slots + (size_t)warp * kSlotBytes<T>);
     if (L0 >= -F::kBias) {
         const T scale = F::value((B)(F::kBias - L0) << F::kFrac);  // 2^-L0
         const T magic = F::value((B)MARK);                         // 2^P
@@ -649,7 +641,7 @@ mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base
     // the Q already read (a row's ties never outnumber its elements).  (A chunk with a
     // Subtract/Multiply fault is never mapped, only resolved up to the fault.)
     unsigned ties = 0;
-    Tie *tl = reinterpret_cast<Tie *>(s_slot[warp]);
+    Tie *tl = reinterpret_cast<Tie *>(slots + (size_t)warp * kSlotBytes<T>);
     if (!(head.flags & kHeadFault) && jmin <= W) {
         const Fix threshold = (Fix)1 << (jmin - 1), lowmask = threshold - 1;
 #pragma unroll 1
@@ -735,28 +727,63 @@ mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base
     }
 }
 
+// Which CTAs of a chunk launch carry the SGD node (every kSgdPeriod-th when it rides along), and
+// the chunk-CTA number of the others.
+template <bool RIDE> __device__ __forceinline__ bool sgd_cta(uint64_t b) {
+    return RIDE && b % kSgdPeriod == kSgdPeriod - 1;
+}
+template <bool RIDE> __device__ __forceinline__ uint64_t chunk_cta(uint64_t b) { return RIDE ? b - b / kSgdPeriod : b; }
+
+template <typename T>
+__device__ __forceinline__ void sgd_cta_work(uint64_t b, const SgdRider<T> &rider) {
+    const uint64_t s0 = (b / kSgdPeriod) * rider.per_unit;
+    if (s0 < rider.n) sgd_range<T>(rider, s0, min(s0 + rider.per_unit, rider.n), threadIdx.x, blockDim.x);
+}
+
+// Phase 1 of the three-launch form: chunk maps (and the riding SGD CTAs).
+template <typename T, bool RIDE>
+__global__ void __launch_bounds__(32 * kChunkWarps, MseTraits<T>::MIN_BLOCKS)
+mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base, bool vec, int policy,
+                 uint64_t chunks, uint64_t ahead, MseHead *heads, typename MseTraits<T>::D *deltas,
+                 unsigned long long *status, SgdRider<T> rider, ChainGuard guard) {
+    // a skipped stage of a guarded chain touches nothing (the SGD-carrying form is never guarded)
+    if constexpr (!RIDE)
+        if (!chain_admits(guard)) return;
+    __shared__ __align__(16) unsigned char s_slots[kChunkWarps * kSlotBytes<T>];
+    if (sgd_cta<RIDE>(blockIdx.x)) {  // an SGD CTA (its own status word)
+        sgd_cta_work<T>(blockIdx.x, rider);
+        return;
+    }
+    chunk_maps<T>(chunk_cta<RIDE>(blockIdx.x), prediction, target, n, base, vec, policy, chunks, ahead, heads, deltas,
+                  status, s_slots);
+}
+
 // Compose the maps of kFanout consecutive children (chunks or blocks, each spanning `span`
 // elements) into one parent map per binade.  The children's heads and increment rows are
 // staged in shared memory, kStageMaps at a time, with coalesced loads; then one thread per
 // binade folds them in order.
 constexpr int kStageMaps = 16;
-template <typename T>
-__global__ void __launch_bounds__(256) mse_compose_kernel(const MseHead *heads, const typename MseTraits<T>::D *deltas,
-                                                          uint64_t children, uint64_t span, MseHead *pheads,
-                                                          typename MseTraits<T>::D *pdeltas, ChainGuard guard) {
-    if (!chain_admits(guard)) return;
+// One CTA of 256 threads composes parent `group`.  The children are read through L2 (__ldcg): in
+// the one-launch form other CTAs wrote them, and they are published by a fence and a counter.
+// `s_rows` holds STAGE maps' increment rows; the children are staged STAGE at a time.
+template <typename T, int STAGE>
+__device__ __forceinline__ void compose_group(const MseHead *heads, const typename MseTraits<T>::D *deltas,
+                                              uint64_t children, uint64_t span, uint64_t group, MseHead *pheads,
+                                              typename MseTraits<T>::D *pdeltas, typename MseTraits<T>::D *s_rows) {
     using Tr = MseTraits<T>;
     using D = typename Tr::D;
     constexpr int W = Tr::W;
     constexpr int ROW = W * 2;  // increment words per map
-    const uint64_t c0 = (uint64_t)blockIdx.x * kFanout;
+    const uint64_t c0 = group * kFanout;
     const int count = (int)(c0 + kFanout < children ? kFanout : children - c0);
     __shared__ MseHead s_heads[kFanout];
-    __shared__ D s_rows[kStageMaps * ROW];
     __shared__ int s_khi, s_flags;
     __shared__ unsigned s_fault;
     const int tid = threadIdx.x, lane = tid & 31;
-    if (tid < count) s_heads[tid] = heads[c0 + tid];
+    if (tid < count) {
+        const uint4 hv = __ldcg(reinterpret_cast<const uint4 *>(heads + c0 + tid));
+        memcpy(&s_heads[tid], &hv, sizeof(MseHead));
+    }
     __syncthreads();
     if (tid < 32) {  // parent head: union of the flags, highest window top, earliest fault
         int khi = INT_MIN, flags = kHeadZero;
@@ -792,15 +819,16 @@ __global__ void __launch_bounds__(256) mse_compose_kernel(const MseHead *heads, 
     bh.flags = flags;
     bh.fault = s_fault;
     bh.k_lo = (flags & kHeadZero) ? 0 : max(s_khi - (W - 1), Tr::KMIN);
-    if (tid == 0) pheads[blockIdx.x] = bh;
+    if (tid == 0) pheads[group] = bh;
     if (flags & kHeadZero) return;  // uniform across the CTA
     const int k = bh.k_lo + tid;
     uint64_t acc[2] = {0, 0};
     bool valid = !(flags & kHeadFault);
-    for (int g = 0; g < count; g += kStageMaps) {
-        const int in_stage = min(kStageMaps, count - g);
+    for (int g = 0; g < count; g += STAGE) {
+        const int in_stage = min(STAGE, count - g);
         __syncthreads();  // the previous stage has been consumed
-        for (int i = tid; i < in_stage * ROW; i += 256) s_rows[i] = deltas[(c0 + g) * ROW + i];
+#pragma unroll 4
+        for (int i = tid; i < in_stage * ROW; i += 256) s_rows[i] = __ldcg(deltas + (c0 + g) * ROW + i);
         __syncthreads();
         if (tid < W && valid) {
             for (int c = 0; c < in_stage; ++c) {
@@ -819,10 +847,20 @@ __global__ void __launch_bounds__(256) mse_compose_kernel(const MseHead *heads, 
         }
     }
     if (tid < W) {
-        D *out = pdeltas + ((size_t)blockIdx.x * W + tid) * 2;
+        D *out = pdeltas + ((size_t)group * W + tid) * 2;
         out[0] = valid ? sat_d<T>(acc[0]) : no_map<T>();
         out[1] = valid ? sat_d<T>(acc[1]) : no_map<T>();
     }
+}
+
+// Phase 2 of the three-launch form: one CTA per parent.
+template <typename T>
+__global__ void __launch_bounds__(256) mse_compose_kernel(const MseHead *heads, const typename MseTraits<T>::D *deltas,
+                                                          uint64_t children, uint64_t span, MseHead *pheads,
+                                                          typename MseTraits<T>::D *pdeltas, ChainGuard guard) {
+    if (!chain_admits(guard)) return;
+    __shared__ typename MseTraits<T>::D s_rows[kStageMaps * MseTraits<T>::W * 2];
+    compose_group<T, kStageMaps>(heads, deltas, children, span, blockIdx.x, pheads, pdeltas, s_rows);
 }
 
 // One map at the binade of the state: x -> x + D[x mod 2].  `ok` is false when the map cannot
@@ -840,7 +878,7 @@ __device__ __forceinline__ MapStep map_at(const MseHead &h, const typename MseTr
     if (h.flags & kHeadFault) { m.ok = false; return m; }
     if ((h.flags & kHeadZero) || k > h.k_lo + Tr::W - 1) return m;  // identity: every square < half an ulp
     if (k < h.k_lo) { m.ok = false; return m; }
-    const typename Tr::D a = row[(size_t)(k - h.k_lo) * 2], b = row[(size_t)(k - h.k_lo) * 2 + 1];
+    const typename Tr::D a = __ldcg(row + (size_t)(k - h.k_lo) * 2), b = __ldcg(row + (size_t)(k - h.k_lo) * 2 + 1);
     if (a == no_map<T>() || b == no_map<T>()) { m.ok = false; return m; }
     m.d0 = a;
     m.d1 = b;
@@ -859,8 +897,10 @@ __device__ __forceinline__ unsigned apply_maps(const MseHead *heads, const typen
     int k;
     state_of<T>(s, x, k);
     MapStep m{0, 0, false};
-    if ((unsigned)lane < avail) {
-        const MseHead h = heads[first + lane];
+    if ((unsigned)lane < avail) {  // through L2: in the one-launch form other CTAs wrote the maps
+        const uint4 hv = __ldcg(reinterpret_cast<const uint4 *>(heads + first + lane));
+        MseHead h;
+        memcpy(&h, &hv, sizeof(h));
         m = map_at<T>(h, deltas + (first + lane) * (size_t)Tr::W * 2, k);
     }
 #pragma unroll
@@ -922,55 +962,108 @@ __device__ __forceinline__ typename WalkAcc<T>::U walk_increment(typename Fmt<T>
     return (m + half) >> d;
 }
 
-// The walker runs with one thread per chunk element (one CTA of CHUNK threads).
-template <typename T>
+// Readiness of the maps in the one-launch form (strict_mse_onepass_kernel); a null block_ctas
+// means the three-launch form, where every map is complete before the walk starts.  The
+// counters live in the workspace and are zeroed before each launch.
+struct MseSync {
+    unsigned *block_ctas;    // per block: chunk CTAs that have published their chunk maps
+    unsigned *block_ready;   // per block: its composed map is published
+    unsigned *super_blocks;  // per superblock: blocks whose composed map is published
+    unsigned *super_ready;   // per superblock: its composed map is published
+    unsigned chunks_per_cta; // chunks a publishing CTA covers
+};
+
+__device__ __forceinline__ unsigned load_flag(const unsigned *p) { return *(volatile const unsigned *)p; }
+
+// Chunk CTAs of the one-launch form take several groups of kChunkWarps chunks each (all in one
+// block) and publish once: a publication (a fence and a counter round trip) holds the CTA's slot
+// for about a microsecond, too long to pay once per group.  With an SGD node riding along, one
+// group per CTA keeps the SGD CTAs short and well interleaved.
+constexpr int kGroupsPerCta = 4;
+static_assert((kFanout / kChunkWarps) % kGroupsPerCta == 0, "a chunk CTA's groups lie in one block");
+
+// publishing chunk CTAs of block b in the one-launch form
+__device__ __forceinline__ unsigned block_ctas_onepass(uint64_t chunks, uint64_t b, unsigned per_cta) {
+    const uint64_t c = min((uint64_t)kFanout, chunks - b * kFanout);
+    return (unsigned)((c + per_cta - 1) / per_cta);
+}
+
+// The ordered walk of a segment, one CTA of NT threads; a chunk is resolved with CHUNK / NT
+// consecutive elements per thread.  In the one-launch form it runs beside the CTAs that build
+// the maps: it reads a map only after its publication flag (a bounded wait at the chunk level;
+// a coarser map that is not published yet is passed over for a finer one), and it learns of a
+// Subtract/Multiply fault from the faulting chunk's head when it reaches it.
+template <typename T, int NT>
 __device__ __forceinline__ void mse_walk(
     const T *prediction, const T *target, uint64_t n, const MseHead *heads0, const typename MseTraits<T>::D *deltas0,
     const MseHead *heads1, const typename MseTraits<T>::D *deltas1, const MseHead *heads2,
     const typename MseTraits<T>::D *deltas2, uint64_t chunks, uint64_t blocks, uint64_t supers, uint64_t base,
-    uint64_t total, T denominator, int policy, const T *carry_in, T *carry_out, T *out, unsigned long long *status) {
+    uint64_t total, T denominator, int policy, const T *carry_in, T *carry_out, T *out, unsigned long long *status,
+    const MseSync &sync) {
     using Tr = MseTraits<T>;
     using F = Fmt<T>;
     using U = typename WalkAcc<T>::U;
     constexpr U SAT = WalkAcc<T>::SAT;
-    constexpr int THREADS = Tr::CHUNK, WARPS = THREADS / 32;
+    constexpr int E = Tr::CHUNK / NT, WARPS = NT / 32;
+    static_assert(E * NT == Tr::CHUNK && WARPS * 32 == NT, "walker shape");
     constexpr U TOP = (U)2 << Tr::P;  // a state at or above this has left its binade
-    __shared__ typename F::Bits sq[THREADS];
+    constexpr unsigned FULL = 0xffffffffu;
+    __shared__ typename F::Bits sq[Tr::CHUNK];
     __shared__ T s_sum;
     __shared__ uint64_t s_g;    // elements [0, s_g) of the segment are summed into s_sum
     __shared__ uint64_t s_arg;  // chunk to resolve, or ~0 when the walk is done
-    __shared__ int s_done;      // 2: overflow recorded
+    __shared__ uint64_t s_end;  // the walk stops in front of this element (the first Subtract/Multiply fault)
+    __shared__ int s_done;      // 2: overflow recorded, 3: a wait gave up
     __shared__ unsigned s_pos, s_stop[2];
     __shared__ U s_warp_sum[32];
 
-    // Every Subtract/Multiply fault is already in the status word; the walk stops in front of
-    // the earliest one, so only earlier Adds can still report (their events are smaller).  The
-    // segment holds global elements [base, base + n); a fault in front of it stops it at once.
-    const unsigned long long st0 = read_status(status);
-    uint64_t stop = n;
-    if (st0 != kStatusOk) {
-        const uint64_t first = (st0 >> 3) / 3;
-        stop = first < base ? 0 : (first - base < n ? first - base : n);
-    }
+    // The walk stops in front of the earliest Subtract/Multiply fault, so only earlier Adds can
+    // still report (their events are smaller).  The segment holds global elements
+    // [base, base + n); a fault already recorded in front of it stops it at once.
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-
     if (tid == 0) {
+        const unsigned long long st0 = read_status(status);
+        uint64_t stop = n;
+        if (st0 != kStatusOk && (st0 & 7) != kWatchdog) {
+            const uint64_t first = (st0 >> 3) / 3;
+            stop = first < base ? 0 : (first - base < n ? first - base : n);
+        }
+        s_end = stop;
         s_sum = carry_in ? *carry_in : T(0);
         s_g = 0;
         s_done = 0;
     }
     if (tid < 32) s_warp_sum[tid] = 0;
     __syncthreads();
+    const bool onepass = sync.block_ctas != nullptr;
     for (;;) {
         if (warp == 0) {  // maps as far as they reach; then the chunk to resolve, if any
             const MseHead *lh[kLevels] = {heads0, heads1, heads2};
             const typename Tr::D *ld[kLevels] = {deltas0, deltas1, deltas2};
             const uint64_t count[kLevels] = {chunks, blocks, supers};
+            const uint64_t stop = s_end;
             T s = s_sum;
             uint64_t g = s_g, arg = ~0ull;
             uint64_t fail_g = ~0ull;  // a scan at level fail_level stopped at element fail_g
             int fail_level = kLevels;
-            while (g < stop) {
+            bool gave_up = false;
+            // one-launch form: wait (bounded) until the chunk maps of block b are published
+            auto wait_block = [&](uint64_t b) {
+                if (lane == 0) {
+                    const unsigned need = block_ctas_onepass(chunks, b, sync.chunks_per_cta);
+                    const unsigned long long t0 = global_ns();
+                    while (load_flag(sync.block_ctas + b) < need) {
+                        if (global_ns() - t0 > kWaitLimitNs) {
+                            gave_up = true;
+                            break;
+                        }
+                        __nanosleep(256);
+                    }
+                }
+                gave_up = __shfl_sync(FULL, (int)gave_up, 0) != 0;
+                __threadfence();
+            };
+            while (g < stop && !gave_up) {
                 bool advanced = false;
                 for (int l = kLevels - 1; l >= 0 && !advanced; --l) {
                     const uint64_t span = (uint64_t)Tr::CHUNK << (6 * l);  // kFanout = 2^6
@@ -980,7 +1073,26 @@ __device__ __forceinline__ void mse_walk(
                     uint64_t lim = stop == n ? count[l] : stop / span;
                     if (l + 1 < kLevels) lim = min(lim, (i / kFanout + 1) * kFanout);  // inside the parent
                     if (i >= lim) continue;
-                    const unsigned avail = (unsigned)min((uint64_t)32, lim - i);
+                    unsigned avail = (unsigned)min((uint64_t)32, lim - i);
+                    if (onepass) {  // only published maps (a leading run of them)
+                        bool ok = true;
+                        if ((unsigned)lane < avail) {
+                            const uint64_t j = i + lane;
+                            ok = l == 0   ? load_flag(sync.block_ctas + j / kFanout) >= block_ctas_onepass(chunks, j / kFanout, sync.chunks_per_cta)
+                                 : l == 1 ? load_flag(sync.block_ready + j) != 0
+                                          : load_flag(sync.super_ready + j) != 0;
+                        }
+                        const unsigned late = __ballot_sync(FULL, !ok);
+                        unsigned ready = late ? (unsigned)(__ffs((int)late) - 1) : 32u;
+                        if (!ready) {
+                            if (l > 0) continue;  // a finer level may be published already
+                            wait_block(i / kFanout);  // the chunks of one block are published together
+                            if (gave_up) break;
+                            ready = avail;
+                        }
+                        avail = min(avail, ready);
+                        __threadfence();  // the maps behind the flags are visible to the loads below
+                    }
                     const unsigned m = apply_maps<T>(lh[l], ld[l], i, avail, s, lane);
                     g = min(g + m * span, n);
                     if (m < avail) {
@@ -989,26 +1101,43 @@ __device__ __forceinline__ void mse_walk(
                     }
                     advanced = m > 0;
                 }
-                if (!advanced) {
+                if (!advanced && !gave_up) {
                     arg = g / Tr::CHUNK;  // this chunk needs the element-by-element resolution
+                    if (onepass) wait_block(arg / kFanout);  // its head is read below
                     break;
                 }
             }
             if (lane == 0) {
                 s_sum = s;
                 s_g = g;
-                s_arg = arg;
+                s_arg = gave_up ? ~0ull : arg;
+                if (gave_up) {
+                    record_fault(status, 0, kWatchdog);
+                    s_done = 3;
+                }
+                if (!gave_up && arg != ~0ull) {  // a fault in the chunk to resolve ends the walk there
+                    const uint4 hv = __ldcg(reinterpret_cast<const uint4 *>(heads0 + arg));
+                    MseHead h;
+                    memcpy(&h, &hv, sizeof(h));
+                    if (h.flags & kHeadFault) s_end = min(s_end, arg * Tr::CHUNK + h.fault);
+                }
             }
         }
         __syncthreads();
         if (s_arg == ~0ull) break;
 
-        // ---- resolve one chunk: thread t owns element t (all fault-free in front of `stop`)
+        // ---- resolve one chunk: thread t owns elements [t E, t E + E) (all fault-free in front
+        // of the stop)
+        const uint64_t stop = s_end;
         const uint64_t i0 = s_arg * Tr::CHUNK;
         const unsigned len = (unsigned)((i0 + Tr::CHUNK < stop ? i0 + Tr::CHUNK : stop) - i0);
-        if ((unsigned)tid < len) {
-            const T d = F::sub(prediction[i0 + tid], target[i0 + tid]);
-            sq[tid] = F::bits(F::mul(d, d));
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+            const unsigned c = tid + e * NT;
+            if (c < len) {
+                const T d = F::sub(prediction[i0 + c], target[i0 + c]);
+                sq[c] = F::bits(F::mul(d, d));
+            }
         }
         if (tid == 0) {
             s_pos = 0;
@@ -1024,11 +1153,21 @@ __device__ __forceinline__ void mse_walk(
             int k;
             state_of<T>(s_sum, x64, k);
             const U x = (U)x64;  // below 2^(P+1)
-            const bool active = (unsigned)tid >= pos && (unsigned)tid < len;
-            bool tie = false;
-            const U inc = active ? walk_increment<T>(sq[tid], k, tie) : (U)0;
-            // inclusive prefix over the threads (element order)
-            U incl = inc;
+            U c[E];              // inclusive prefix of this thread's increments
+            bool tie[E];
+            U run = 0;
+#pragma unroll
+            for (int e = 0; e < E; ++e) {
+                const unsigned idx = tid * E + e;
+                const bool active = idx >= pos && idx < len;
+                bool t = false;
+                const U inc = active ? walk_increment<T>(sq[idx], k, t) : (U)0;
+                tie[e] = active && t;
+                run = sat_add<U>(run, inc, SAT);
+                c[e] = run;
+            }
+            // exclusive prefix of the thread totals (element order)
+            U incl = run;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
                 const U v = shfl_up_x(incl, o);
@@ -1036,7 +1175,6 @@ __device__ __forceinline__ void mse_walk(
             }
             if (lane == 31) s_warp_sum[warp] = incl;
             __syncthreads();
-            // warps in front: every warp scans the warp totals itself (no extra barrier)
             U wsum = lane < WARPS ? s_warp_sum[lane] : (U)0;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
@@ -1047,17 +1185,32 @@ __device__ __forceinline__ void mse_walk(
             U before = shfl_up_x(incl, 1);
             if (lane == 0) before = 0;
             before = sat_add<U>(before, warp_before, SAT);
-            // the state after this element (clamped): the first element that reaches TOP, or the
-            // first tie, stops the run
-            const U after = sat_add<U>(sat_add<U>(x, before, SAT), inc, SAT);
-            if (active && (tie || after >= TOP)) atomicMin(&s_stop[it], (unsigned)tid);
+            const U start = sat_add<U>(x, before, SAT);  // the state in front of this thread's elements
+            // the first element that reaches TOP, or the first tie, stops the run
+            unsigned mine = len;
+#pragma unroll
+            for (int e = E - 1; e >= 0; --e) {
+                const unsigned idx = tid * E + e;
+                if (idx >= pos && idx < len && (tie[e] || sat_add<U>(start, c[e], SAT) >= TOP)) mine = idx;
+            }
+            if (mine < len) atomicMin(&s_stop[it], mine);
             __syncthreads();
             const unsigned cut = s_stop[it];
             // the owner of `cut` (the last thread when nothing stops) publishes the state there,
             // adds that element exactly, and moves the cursor
-            if ((cut < len && (unsigned)tid == cut) || (cut == len && tid == THREADS - 1)) {
-                // below TOP: nothing in front of `cut` left the binade
-                const U r = cut < len ? x + before : after;
+            const unsigned owner = cut < len ? cut / E : NT - 1;
+            if ((unsigned)tid == owner) {
+                U r;  // below TOP: nothing in front of `cut` left the binade
+                if (cut < len) {
+                    const int e = (int)(cut - tid * E);
+                    U prev = 0;
+#pragma unroll
+                    for (int q = 0; q < E; ++q)
+                        if (q + 1 == e) prev = c[q];
+                    r = sat_add<U>(start, prev, SAT);
+                } else {
+                    r = sat_add<U>(start, run, SAT);
+                }
                 T s = value_of<T>((uint64_t)r, k);
                 if (cut < len) {
                     const T t = F::add(s, F::value(sq[cut]));
@@ -1082,8 +1235,9 @@ __device__ __forceinline__ void mse_walk(
         if (s_done == 2) break;
     }
     if (tid == 0) {
+        if (s_done == 3) return;  // a wait gave up: the status word says so
         if (carry_out) *carry_out = s_sum;  // the running sum handed to the next segment
-        if (!out || s_done == 2 || stop < n || fault_precedes(status, total * 3)) return;
+        if (!out || s_done == 2 || s_end < n || fault_precedes(status, total * 3)) return;
         T mean;
         const unsigned kind = checked_div<T>(s_sum, denominator, policy, mean);
         if (kind) {
@@ -1104,16 +1258,19 @@ __device__ __forceinline__ void mse_walk(
     prediction, target, n, heads0, deltas0, heads1, deltas1, heads2, deltas2, chunks, blocks, supers, base, total, \
         denominator, policy, carry_in, carry_out, out, status
 
-template <typename T> __global__ void __launch_bounds__(1024) mse_walk_kernel(PCU_MSE_WALK_PARAMS, ChainGuard guard) {
-    if (chain_admits(guard)) mse_walk<T>(PCU_MSE_WALK_ARGS);
+constexpr int kWalkThreads = 32 * kChunkWarps;  // the walker's CTA (also a chunk CTA's shape)
+
+template <typename T>
+__global__ void __launch_bounds__(kWalkThreads) mse_walk_kernel(PCU_MSE_WALK_PARAMS, ChainGuard guard) {
+    if (chain_admits(guard)) mse_walk<T, kWalkThreads>(PCU_MSE_WALK_ARGS, MseSync{});
 }
 
 // CTA 0 walks; the other CTAs stream an SGD node's elements meanwhile (the walker is latency
 // bound and holds one SM).
 template <typename T>
-__global__ void __launch_bounds__(1024) mse_walk_sgd_kernel(PCU_MSE_WALK_PARAMS, SgdRider<T> rider) {
+__global__ void __launch_bounds__(kWalkThreads) mse_walk_sgd_kernel(PCU_MSE_WALK_PARAMS, SgdRider<T> rider) {
     if (blockIdx.x == 0) {
-        mse_walk<T>(PCU_MSE_WALK_ARGS);
+        mse_walk<T, kWalkThreads>(PCU_MSE_WALK_ARGS, MseSync{});
         return;
     }
     sgd_range<T>(rider, 0, rider.n, (uint64_t)(blockIdx.x - 1) * blockDim.x + threadIdx.x,
@@ -1123,6 +1280,77 @@ __global__ void __launch_bounds__(1024) mse_walk_sgd_kernel(PCU_MSE_WALK_PARAMS,
 // An SGD share on its own (the part a segment's chunk warps do not carry).
 template <typename T> __global__ void __launch_bounds__(256) sgd_share_kernel(SgdRider<T> rider) {
     sgd_range<T>(rider, 0, rider.n, (uint64_t)blockIdx.x * blockDim.x + threadIdx.x, (uint64_t)gridDim.x * blockDim.x);
+}
+
+// ---- the one-launch form (binary32): CTA 0 walks while the other CTAs build the chunk maps.
+// The last chunk CTA of a block composes the block map, and the last block of a superblock the
+// superblock map; each publication is a fence followed by a counter or a flag.  Only CTA 0 ever
+// waits (bounded), and only on CTAs that wait for nothing, so the launch always completes: CTA 0
+// is dispatched first and holds one slot, and every other CTA runs to completion.  The walk
+// trails the chunk CTAs by about a block, so it ends shortly after the last chunk instead of
+// running alone for ~0.1 ms after them.
+template <typename T, bool RIDE, int G>
+__global__ void __launch_bounds__(32 * kChunkWarps, MseTraits<T>::MIN_BLOCKS)
+mse_onepass_kernel(const T *prediction, const T *target, uint64_t n, bool vec, int policy, uint64_t chunks,
+                   uint64_t blocks, uint64_t supers, uint64_t ahead, MseHead *h0, typename MseTraits<T>::D *d0,
+                   MseHead *h1, typename MseTraits<T>::D *d1, MseHead *h2, typename MseTraits<T>::D *d2,
+                   MseSync sync, T denominator, T *out, unsigned long long *status, SgdRider<T> rider,
+                   ChainGuard guard) {
+    using Tr = MseTraits<T>;
+    if constexpr (!RIDE)
+        if (!chain_admits(guard)) return;  // the whole launch, walker included
+    if (blockIdx.x == 0) {
+        mse_walk<T, kWalkThreads>(prediction, target, n, h0, d0, h1, d1, h2, d2, chunks, blocks, supers, 0, n,
+                                  denominator, policy, nullptr, nullptr, out, status, sync);
+        return;
+    }
+    const uint64_t b = blockIdx.x - 1;
+    if (sgd_cta<RIDE>(b)) {
+        sgd_cta_work<T>(b, rider);
+        return;
+    }
+    constexpr uint64_t kPerCta = (uint64_t)kChunkWarps * G;
+    const uint64_t cta = chunk_cta<RIDE>(b);
+    if (cta * kPerCta >= chunks) return;  // past the last chunk: part of no block
+    // the chunk warps' slots; once the chunks are done, the staging area of a composition (all
+    // kFanout children at once)
+    __shared__ __align__(16) unsigned char s_slots[kChunkWarps * kSlotBytes<T>];
+    static_assert(kChunkWarps * kSlotBytes<T> >= (size_t)kFanout * Tr::W * 2 * sizeof(typename Tr::D), "staging");
+#pragma unroll 1
+    for (int q = 0; q < G; ++q)  // each group prefetches the next one into L2 (one group: the next wave's)
+        chunk_maps<T>(cta * G + q, prediction, target, n, 0, vec, policy, chunks,
+                      G == 1 ? ahead : (q + 1 < G ? (uint64_t)kChunkWarps : 0), h0, d0, status, s_slots);
+    // Publish this CTA's chunk maps: the barrier orders every thread's writes before thread 0,
+    // whose device-scope fence (cumulative over them) precedes the count.  The last CTA of a
+    // block fences after seeing the count, before its threads read the maps through L2.
+    __shared__ unsigned s_last;
+    __syncthreads();
+    const uint64_t blk = cta / (kFanout / kPerCta);
+    if (threadIdx.x == 0) {
+        __threadfence();
+        s_last = atomicAdd(sync.block_ctas + blk, 1u) + 1 == block_ctas_onepass(chunks, blk, (unsigned)kPerCta);
+        if (s_last) __threadfence();
+    }
+    __syncthreads();
+    if (!s_last) return;
+    compose_group<T, kFanout>(h0, d0, chunks, Tr::CHUNK, blk, h1, d1, reinterpret_cast<typename Tr::D *>(s_slots));
+    __syncthreads();
+    const uint64_t sb = blk / kFanout;
+    if (threadIdx.x == 0) {
+        __threadfence();
+        atomicExch(sync.block_ready + blk, 1u);
+        s_last = atomicAdd(sync.super_blocks + sb, 1u) + 1 == min((uint64_t)kFanout, blocks - sb * kFanout);
+        if (s_last) __threadfence();
+    }
+    __syncthreads();
+    if (!s_last) return;
+    compose_group<T, kFanout>(h1, d1, blocks, (uint64_t)Tr::CHUNK << 6, sb, h2, d2,
+                              reinterpret_cast<typename Tr::D *>(s_slots));
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        atomicExch(sync.super_ready + sb, 1u);
+    }
 }
 
 // binary32/binary64 encoding of an element count, nearest-even (constants/constants.rs:18-27)
@@ -1156,7 +1384,7 @@ template <typename T> T count_value(uint64_t n) {
 // Workspace: per level (chunk, block, superblock) the map heads, then the increment rows.
 template <typename T> struct MseLayout {
     uint64_t count[kLevels];
-    size_t heads_off[kLevels], deltas_off[kLevels], bytes;
+    size_t heads_off[kLevels], deltas_off[kLevels], sync_off, sync_bytes, bytes;
     explicit MseLayout(uint64_t n) {
         using Tr = MseTraits<T>;
         auto up = [](size_t v) { return (v + 255) / 256 * 256; };
@@ -1170,17 +1398,24 @@ template <typename T> struct MseLayout {
             deltas_off[l] = off;
             off += up(count[l] * row);
         }
+        // the one-launch form's publication counters: per block two words, per superblock two
+        sync_off = off;
+        sync_bytes = up((2 * count[1] + 2 * count[2]) * sizeof(unsigned));
+        off += sync_bytes;
         bytes = off;
     }
 };
 
 // The chunk kernel's grid when it carries SGD, and how many units (chunk warps or SGD CTAs)
 // carry it.
-inline uint64_t chunk_grid(uint64_t chunks, bool ride) {
-    const uint64_t ctas = (chunks + kChunkWarps - 1) / kChunkWarps;
+// (chunks_per_cta: kChunkWarps, or more for the one-launch form without SGD)
+inline uint64_t chunk_grid(uint64_t chunks, bool ride, uint64_t chunks_per_cta = kChunkWarps) {
+    const uint64_t ctas = (chunks + chunks_per_cta - 1) / chunks_per_cta;
     return ride ? ctas + (ctas + kSgdPeriod - 2) / (kSgdPeriod - 1) + kSgdPeriod : ctas;
 }
-inline uint64_t sgd_units(uint64_t chunks) { return chunk_grid(chunks, true) / kSgdPeriod; }
+inline uint64_t sgd_units(uint64_t chunks, uint64_t chunks_per_cta = kChunkWarps) {
+    return chunk_grid(chunks, true, chunks_per_cta) / kSgdPeriod;
+}
 
 // Phases 1 and 2 of a segment (global elements [base, base + n)): chunk maps, then block and
 // superblock maps.  `sgd` (if not null and not empty) rides on the chunk kernel, per_unit
@@ -1242,7 +1477,7 @@ int walk_mse(int policy, const T *p, const T *t, uint64_t n, uint64_t base, uint
              T *carry_out, T *out, void *workspace, size_t workspace_bytes, unsigned long long *status,
              cudaStream_t stream, const SgdRider<T> *sgd = nullptr, const ChainGuard &guard = ChainGuard{}) {
     using D = typename MseTraits<T>::D;
-    constexpr unsigned THREADS = MseTraits<T>::CHUNK;
+    constexpr unsigned THREADS = kWalkThreads;
     MseLayout<T> lay(n);
     if (n && (!workspace || workspace_bytes < lay.bytes)) return PCU_B200_ERROR_WORKSPACE;
     char *ws = reinterpret_cast<char *>(workspace);
@@ -1264,13 +1499,62 @@ int walk_mse(int policy, const T *p, const T *t, uint64_t n, uint64_t base, uint
     return pcu_host::launch_status();
 }
 
+// The one-launch form of a whole reduction (binary32): the publication counters are zeroed, then
+// one launch builds the maps and walks them.  `sgd` (if not null and not empty) rides along.
+template <typename T>
+int onepass_mse(int policy, const T *p, const T *t, T *out, uint64_t n, void *workspace, size_t workspace_bytes,
+                unsigned long long *status, cudaStream_t stream, const SgdRider<T> *sgd, const ChainGuard &guard) {
+    MseLayout<T> lay(n);
+    if (!workspace || workspace_bytes < lay.bytes) return PCU_B200_ERROR_WORKSPACE;
+    if (lay.count[0] > 0x7fffffffull * kChunkWarps) return PCU_B200_ERROR_SIZE_OVERFLOW;
+    const bool ride = sgd && sgd->n;
+    char *ws = reinterpret_cast<char *>(workspace);
+    cudaError_t e = cudaMemsetAsync(ws + lay.sync_off, 0, lay.sync_bytes, stream);
+    if (e != cudaSuccess) return pcu_host::set_cuda_error(e);
+    const bool vec = pcu_host::aligned(p, 16) && pcu_host::aligned(t, 16);
+    static int resident[2][64] = {};  // chunk warps resident at once, per variant and device
+    int device = 0;
+    cudaGetDevice(&device);
+    const bool cached = device >= 0 && device < 64;
+    int ahead = cached ? resident[ride][device] : 0;
+    if (!ahead) {
+        int per_sm = 0;
+        e = ride ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mse_onepass_kernel<T, true, 1>, kWalkThreads, 0)
+                 : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mse_onepass_kernel<T, false, kGroupsPerCta>,
+                                                                 kWalkThreads, 0);
+        if (e != cudaSuccess) return pcu_host::set_cuda_error(e);
+        ahead = per_sm * kChunkWarps * pcu_host::sm_count();
+        if (cached) resident[ride][device] = ahead;
+    }
+    using D = typename MseTraits<T>::D;
+    auto H = [&](int l) { return reinterpret_cast<MseHead *>(ws + lay.heads_off[l]); };
+    auto R = [&](int l) { return reinterpret_cast<D *>(ws + lay.deltas_off[l]); };
+    unsigned *u = reinterpret_cast<unsigned *>(ws + lay.sync_off);
+    const unsigned per_cta = ride ? kChunkWarps : kChunkWarps * kGroupsPerCta;
+    MseSync sync{u, u + lay.count[1], u + 2 * lay.count[1], u + 2 * lay.count[1] + lay.count[2], per_cta};
+    const unsigned grid = (unsigned)(1 + chunk_grid(lay.count[0], ride, per_cta));
+    if (ride)
+        mse_onepass_kernel<T, true, 1><<<grid, kWalkThreads, 0, stream>>>(
+            p, t, n, vec, policy, lay.count[0], lay.count[1], lay.count[2], (uint64_t)ahead, H(0), R(0), H(1), R(1),
+            H(2), R(2), sync, count_value<T>(n), out, status, *sgd, guard);
+    else
+        mse_onepass_kernel<T, false, kGroupsPerCta><<<grid, kWalkThreads, 0, stream>>>(
+            p, t, n, vec, policy, lay.count[0], lay.count[1], lay.count[2], (uint64_t)ahead, H(0), R(0), H(1), R(1),
+            H(2), R(2), sync, count_value<T>(n), out, status, SgdRider<T>{}, guard);
+    return pcu_host::launch_status();
+}
+
 template <typename T>
 int run_mse(int policy, const T *p, const T *t, T *out, uint64_t n, void *workspace, size_t workspace_bytes,
             unsigned long long *status, cudaStream_t stream, const ChainGuard &guard) {
-    int rc = prepare_mse<T>(policy, p, t, n, 0, workspace, workspace_bytes, status, stream, nullptr, guard);
-    if (rc) return rc;
-    return walk_mse<T>(policy, p, t, n, 0, n, nullptr, nullptr, out, workspace, workspace_bytes, status, stream,
-                       nullptr, chain_follow(guard));
+    if constexpr (sizeof(T) == 4) {
+        return onepass_mse<T>(policy, p, t, out, n, workspace, workspace_bytes, status, stream, nullptr, guard);
+    } else {  // binary64: three launches (its chunk maps and composition stage do not fit one CTA's memory)
+        int rc = prepare_mse<T>(policy, p, t, n, 0, workspace, workspace_bytes, status, stream, nullptr, guard);
+        if (rc) return rc;
+        return walk_mse<T>(policy, p, t, n, 0, n, nullptr, nullptr, out, workspace, workspace_bytes, status, stream,
+                           nullptr, chain_follow(guard));
+    }
 }
 
 // ---- MSE + SGD in one pass.  The SGD node's elements go to the chunk kernel's SGD CTAs, up to
@@ -1321,11 +1605,22 @@ int run_mse_sgd(int policy, const T *p, const T *t, T *loss, uint64_t n, void *w
                 unsigned long long *mse_status, const SgdRider<T> &sgd, cudaStream_t stream) {
     MseLayout<T> lay(n);
     SgdRider<T> head, tail;
-    split_sgd<T>(sgd, sgd_units(lay.count[0]), head, tail);
-    int rc = prepare_mse<T>(policy, p, t, n, 0, workspace, workspace_bytes, mse_status, stream, &head);
-    if (rc) return rc;
-    return walk_mse<T>(policy, p, t, n, 0, n, nullptr, nullptr, loss, workspace, workspace_bytes, mse_status, stream,
-                       &tail);
+    split_sgd<T>(sgd, sgd_units(lay.count[0]), head, tail);  // riding along: one group per chunk CTA
+    if constexpr (sizeof(T) == 4) {
+        int rc = onepass_mse<T>(policy, p, t, loss, n, workspace, workspace_bytes, mse_status, stream, &head,
+                                ChainGuard{});
+        if (rc || !tail.n) return rc;
+        const uint64_t per_cta = 256ull * (16 / sizeof(T)) * kSgdTrip;
+        const uint64_t cap = 8ull * pcu_host::sm_count();
+        const uint64_t want = (tail.n + per_cta - 1) / per_cta;
+        sgd_share_kernel<T><<<(unsigned)(want < cap ? want : cap), 256, 0, stream>>>(tail);
+        return pcu_host::launch_status();
+    } else {
+        int rc = prepare_mse<T>(policy, p, t, n, 0, workspace, workspace_bytes, mse_status, stream, &head);
+        if (rc) return rc;
+        return walk_mse<T>(policy, p, t, n, 0, n, nullptr, nullptr, loss, workspace, workspace_bytes, mse_status,
+                           stream, &tail);
+    }
 }
 
 // A segment's phases 1 and 2 with an SGD share on the chunk warps; what they cannot carry runs
