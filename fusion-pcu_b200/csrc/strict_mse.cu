@@ -48,6 +48,7 @@
 //     fault an Add of nonnegative finite squares can raise is overflow (fault_domain.rs:207-214);
 //     a map is never applied when its result would leave the binade, so overflow is always met
 //     by the exact add.  Then the checked divide.
+#include <algorithm>
 #include <cstring>
 #include <type_traits>
 
@@ -316,25 +317,32 @@ template <typename T> struct SgdRider {
 // streams a block of SGD elements, the others are chunk CTAs.  The chunk warps are bound by
 // integer issue and the SGD CTAs by HBM, so an SM holding both keeps both busy (an SGD slice
 // inside every chunk warp instead stalls that warp's integer work on memory).
-constexpr int kSgdPeriod = 4;
+#ifndef PCU_SGD_PERIOD
+#define PCU_SGD_PERIOD 4
+#endif
+constexpr int kSgdPeriod = PCU_SGD_PERIOD;
 constexpr int kSgdTrip = 2;  // 16-byte vectors per thread in flight
+#ifndef PCU_SGD_CTA_TRIP
+#define PCU_SGD_CTA_TRIP 2
+#endif
+constexpr int kSgdCtaTrip = PCU_SGD_CTA_TRIP;  // in the SGD CTAs of a chunk launch
 // elements of one SGD CTA trip: the per-CTA share is a multiple of it
-template <typename T> constexpr uint64_t sgd_unit() { return 32ull * kChunkWarps * (16 / sizeof(T)) * kSgdTrip; }
+template <typename T> constexpr uint64_t sgd_unit() { return 32ull * kChunkWarps * (16 / sizeof(T)) * kSgdCtaTrip; }
 
 // Elements [s0, s1) of a rider over `lanes` threads (this one is `lane`), s0 a multiple of the
 // vector width.  Every thread takes its elements in increasing order and stops at its first
 // fault: its later events cannot be the minimum.
-template <typename T>
+template <typename T, int kTrip = kSgdTrip>
 __device__ __forceinline__ void sgd_range(const SgdRider<T> &r, uint64_t s0, uint64_t s1, uint64_t lane,
                                           uint64_t lanes) {
     using VT = typename std::conditional<sizeof(T) == 4, float4, double2>::type;
     constexpr int VW = 16 / sizeof(T);
     const uint64_t vend = r.vec ? s0 + (s1 - s0) / VW * VW : s0;
     const uint64_t nv = (vend - s0) / VW;
-    for (uint64_t j0 = lane; j0 < nv; j0 += lanes * kSgdTrip) {
-        VT a[kSgdTrip], b[kSgdTrip];
+    for (uint64_t j0 = lane; j0 < nv; j0 += lanes * kTrip) {
+        VT a[kTrip], b[kTrip];
 #pragma unroll
-        for (int u = 0; u < kSgdTrip; ++u) {
+        for (int u = 0; u < kTrip; ++u) {
             const uint64_t j = j0 + u * lanes;
             if (j < nv) {
                 a[u] = __ldcs(reinterpret_cast<const VT *>(r.weights + s0) + j);
@@ -342,7 +350,7 @@ __device__ __forceinline__ void sgd_range(const SgdRider<T> &r, uint64_t s0, uin
             }
         }
 #pragma unroll
-        for (int u = 0; u < kSgdTrip; ++u) {
+        for (int u = 0; u < kTrip; ++u) {
             const uint64_t j = j0 + u * lanes;
             if (j >= nv) break;
             VT o;
@@ -729,15 +737,114 @@ __device__ __forceinline__ void chunk_maps(uint64_t cta, const T *prediction, co
 
 // Which CTAs of a chunk launch carry the SGD node (every kSgdPeriod-th when it rides along), and
 // the chunk-CTA number of the others.
-template <bool RIDE> __device__ __forceinline__ bool sgd_cta(uint64_t b) {
-    return RIDE && b % kSgdPeriod == kSgdPeriod - 1;
+// Within every period of P CTAs of a launch that carries SGD, the last S are SGD CTAs.
+template <bool RIDE, int P, int S> __device__ __forceinline__ bool sgd_cta(uint64_t b) {
+    return RIDE && b % P >= (uint64_t)(P - S);
 }
-template <bool RIDE> __device__ __forceinline__ uint64_t chunk_cta(uint64_t b) { return RIDE ? b - b / kSgdPeriod : b; }
+template <bool RIDE, int P, int S> __device__ __forceinline__ uint64_t chunk_cta(uint64_t b) {
+    return RIDE ? (b / P) * (P - S) + b % P : b;
+}
 
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((unsigned)__cvta_generic_to_shared(smem)),
+                 "l"(gmem)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N> __device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// An SGD CTA's block [s0, s1): like sgd_range over the CTA's threads, but the operands come in
+// through cp.async copies into `smem` (kSgdStages stages of kSgdTrip vectors of each operand per
+// thread) instead of registers, so twice the bytes are in flight without costing the chunk
+// code's register budget.  Each thread reads back only its own copies (cp.async.wait_group makes
+// them visible to it), so no barrier is needed; every copy is drained before the thread leaves.
+constexpr int kSgdStages = 2;
+static_assert(kSgdStages * 2 * kSgdTrip * 32 * kChunkWarps * 16 <= kChunkWarps * 1024 * 4, "SGD stages fit the slots");
 template <typename T>
-__device__ __forceinline__ void sgd_cta_work(uint64_t b, const SgdRider<T> &rider) {
-    const uint64_t s0 = (b / kSgdPeriod) * rider.per_unit;
-    if (s0 < rider.n) sgd_range<T>(rider, s0, min(s0 + rider.per_unit, rider.n), threadIdx.x, blockDim.x);
+__device__ __forceinline__ void sgd_range_async(const SgdRider<T> &r, uint64_t s0, uint64_t s1, unsigned char *smem) {
+    using VT = typename std::conditional<sizeof(T) == 4, float4, double2>::type;
+    constexpr int VW = 16 / sizeof(T);
+    const unsigned tid = threadIdx.x, nt = blockDim.x;
+    if (!r.vec) {
+        sgd_range<T>(r, s0, s1, tid, nt);
+        return;
+    }
+    const uint64_t vend = s0 + (s1 - s0) / VW * VW;
+    const uint64_t nv = (vend - s0) / VW;
+    VT *buf = reinterpret_cast<VT *>(smem);  // [stage][operand][u][thread]
+    auto slot = [&](int st, int op, int u) { return buf + ((size_t)(st * 2 + op) * kSgdTrip + u) * nt + tid; };
+    const VT *wv = reinterpret_cast<const VT *>(r.weights + s0), *gv = reinterpret_cast<const VT *>(r.gradient + s0);
+    const uint64_t step = (uint64_t)nt * kSgdTrip;  // vectors per stage of the CTA
+    auto issue = [&](int st, uint64_t j0) {
+#pragma unroll
+        for (int u = 0; u < kSgdTrip; ++u) {
+            const uint64_t j = j0 + (uint64_t)u * nt;
+            if (j < nv) {
+                cp_async16(slot(st, 0, u), wv + j);
+                cp_async16(slot(st, 1, u), gv + j);
+            }
+        }
+        cp_async_commit();  // (an empty group keeps the counting uniform)
+    };
+#pragma unroll
+    for (int st = 0; st < kSgdStages; ++st) issue(st, tid + (uint64_t)st * step);
+    bool stopped = false;
+    int st = 0;
+    for (uint64_t j0 = tid; j0 < nv && !stopped; j0 += step) {
+        cp_async_wait<kSgdStages - 1>();  // the oldest stage has landed
+#pragma unroll
+        for (int u = 0; u < kSgdTrip; ++u) {
+            const uint64_t j = j0 + (uint64_t)u * nt;
+            if (j >= nv || stopped) break;
+            const VT a = *slot(st, 0, u), b = *slot(st, 1, u);
+            VT o;
+            const bool done = sgd_fast<T, VW>(reinterpret_cast<const T *>(&a), reinterpret_cast<const T *>(&b),
+                                              r.rate, r.policy, reinterpret_cast<T *>(&o));
+#pragma unroll
+            for (int e = 0; e < VW && !done; ++e) {
+                unsigned step_k;
+                const unsigned kind = checked_sgd<T>(reinterpret_cast<const T *>(&a)[e],
+                                                     reinterpret_cast<const T *>(&b)[e], r.rate, r.policy,
+                                                     reinterpret_cast<T *>(&o)[e], step_k);
+                if (kind) {  // the elements in front of it are still written, as one at a time would
+#pragma unroll
+                    for (int q = 0; q < e; ++q) r.out[s0 + j * VW + q] = reinterpret_cast<const T *>(&o)[q];
+                    record_fault(r.status, (r.base + s0 + j * VW + e) * 2 + step_k, kind);
+                    stopped = true;
+                    break;
+                }
+            }
+            if (!stopped) __stcs(reinterpret_cast<VT *>(r.out + s0) + j, o);
+        }
+        if (!stopped) issue(st, j0 + (uint64_t)kSgdStages * step);  // refill this stage
+        st ^= 1;
+    }
+    cp_async_wait<0>();  // nothing may land in shared memory after the thread has gone
+    if (stopped) return;
+    for (uint64_t i = vend + tid; i < s1; i += nt) {
+        T o;
+        unsigned step_k;
+        const unsigned kind = checked_sgd<T>(r.weights[i], r.gradient[i], r.rate, r.policy, o, step_k);
+        if (kind) {
+            record_fault(r.status, (r.base + i) * 2 + step_k, kind);
+            return;
+        }
+        r.out[i] = o;
+    }
+}
+
+// ASYNC: the operands through cp.async (the one-launch kernel: 1.07 -> 1.01 ms for 2^28 F32 MSE +
+// SGD); otherwise through registers (measured faster in the three-launch chunk kernel).
+template <typename T, int P, int S, bool ASYNC>
+__device__ __forceinline__ void sgd_cta_work(uint64_t b, const SgdRider<T> &rider, unsigned char *smem) {
+    const uint64_t s0 = ((b / P) * S + (b % P - (P - S))) * rider.per_unit;
+    if (s0 >= rider.n) return;
+    if (ASYNC)
+        sgd_range_async<T>(rider, s0, min(s0 + rider.per_unit, rider.n), smem);
+    else
+        sgd_range<T, kSgdCtaTrip>(rider, s0, min(s0 + rider.per_unit, rider.n), threadIdx.x, blockDim.x);
 }
 
 // Phase 1 of the three-launch form: chunk maps (and the riding SGD CTAs).
@@ -750,11 +857,12 @@ mse_chunk_kernel(const T *prediction, const T *target, uint64_t n, uint64_t base
     if constexpr (!RIDE)
         if (!chain_admits(guard)) return;
     __shared__ __align__(16) unsigned char s_slots[kChunkWarps * kSlotBytes<T>];
-    if (sgd_cta<RIDE>(blockIdx.x)) {  // an SGD CTA (its own status word)
-        sgd_cta_work<T>(blockIdx.x, rider);
+    if (sgd_cta<RIDE, kSgdPeriod, 1>(blockIdx.x)) {  // an SGD CTA (its own status word)
+        sgd_cta_work<T, kSgdPeriod, 1, false>(blockIdx.x, rider, s_slots);
         return;
     }
-    chunk_maps<T>(chunk_cta<RIDE>(blockIdx.x), prediction, target, n, base, vec, policy, chunks, ahead, heads, deltas,
+    chunk_maps<T>(chunk_cta<RIDE, kSgdPeriod, 1>(blockIdx.x), prediction, target, n, base, vec, policy, chunks, ahead,
+                  heads, deltas,
                   status, s_slots);
 }
 
@@ -973,13 +1081,39 @@ struct MseSync {
     unsigned chunks_per_cta; // chunks a publishing CTA covers
 };
 
-__device__ __forceinline__ unsigned load_flag(const unsigned *p) { return *(volatile const unsigned *)p; }
+// Publication primitives of the one-launch form: a counter add that releases everything the CTA
+// wrote before it (ordered by a preceding barrier) and acquires what earlier adders released; a
+// flag store that releases; a flag load that acquires.
+__device__ __forceinline__ unsigned add_acq_rel(unsigned *p, unsigned v) {
+    unsigned old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+__device__ __forceinline__ void store_release(unsigned *p, unsigned v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned load_flag(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
 
 // Chunk CTAs of the one-launch form take several groups of kChunkWarps chunks each (all in one
 // block) and publish once: a publication (a fence and a counter round trip) holds the CTA's slot
 // for about a microsecond, too long to pay once per group.  With an SGD node riding along, one
 // group per CTA keeps the SGD CTAs short and well interleaved.
 constexpr int kGroupsPerCta = 4;
+#ifndef PCU_MSE_RIDE_GROUPS
+#define PCU_MSE_RIDE_GROUPS 1
+#endif
+constexpr int kRideGroupsPerCta = PCU_MSE_RIDE_GROUPS;  // with an SGD node riding along
+#ifndef PCU_MSE_RIDE_PERIOD
+#define PCU_MSE_RIDE_PERIOD 4
+#endif
+#ifndef PCU_MSE_RIDE_SGD
+#define PCU_MSE_RIDE_SGD 1
+#endif
+constexpr int kRidePeriod = PCU_MSE_RIDE_PERIOD, kRideSgd = PCU_MSE_RIDE_SGD;  // S SGD CTAs in every P
 static_assert((kFanout / kChunkWarps) % kGroupsPerCta == 0, "a chunk CTA's groups lie in one block");
 
 // publishing chunk CTAs of block b in the one-launch form
@@ -1304,53 +1438,46 @@ mse_onepass_kernel(const T *prediction, const T *target, uint64_t n, bool vec, i
                                   denominator, policy, nullptr, nullptr, out, status, sync);
         return;
     }
+    // the chunk warps' slots; once the chunks are done, the staging area of a composition (all
+    // kFanout children at once); in an SGD CTA, its copy stages
+    __shared__ __align__(16) unsigned char s_slots[kChunkWarps * kSlotBytes<T>];
     const uint64_t b = blockIdx.x - 1;
-    if (sgd_cta<RIDE>(b)) {
-        sgd_cta_work<T>(b, rider);
+    if (sgd_cta<RIDE, kRidePeriod, kRideSgd>(b)) {
+        sgd_cta_work<T, kRidePeriod, kRideSgd, true>(b, rider, s_slots);
         return;
     }
     constexpr uint64_t kPerCta = (uint64_t)kChunkWarps * G;
-    const uint64_t cta = chunk_cta<RIDE>(b);
+    const uint64_t cta = chunk_cta<RIDE, kRidePeriod, kRideSgd>(b);
     if (cta * kPerCta >= chunks) return;  // past the last chunk: part of no block
-    // the chunk warps' slots; once the chunks are done, the staging area of a composition (all
-    // kFanout children at once)
-    __shared__ __align__(16) unsigned char s_slots[kChunkWarps * kSlotBytes<T>];
     static_assert(kChunkWarps * kSlotBytes<T> >= (size_t)kFanout * Tr::W * 2 * sizeof(typename Tr::D), "staging");
 #pragma unroll 1
-    for (int q = 0; q < G; ++q)  // each group prefetches the next one into L2 (one group: the next wave's)
+    for (int q = 0; q < G; ++q)  // a group prefetches the next one into L2; the last group, the first
+        // group of the CTA that takes this slot one wave later (`ahead` chunks on)
         chunk_maps<T>(cta * G + q, prediction, target, n, 0, vec, policy, chunks,
-                      G == 1 ? ahead : (q + 1 < G ? (uint64_t)kChunkWarps : 0), h0, d0, status, s_slots);
+                      q + 1 < G ? (uint64_t)kChunkWarps : ahead, h0, d0, status, s_slots);
     // Publish this CTA's chunk maps: the barrier orders every thread's writes before thread 0,
-    // whose device-scope fence (cumulative over them) precedes the count.  The last CTA of a
-    // block fences after seeing the count, before its threads read the maps through L2.
+    // whose acquire-release count releases them (cumulatively); the last CTA of a block acquires
+    // the others' maps with the same count, and its threads read them after the barrier.
     __shared__ unsigned s_last;
     __syncthreads();
     const uint64_t blk = cta / (kFanout / kPerCta);
-    if (threadIdx.x == 0) {
-        __threadfence();
-        s_last = atomicAdd(sync.block_ctas + blk, 1u) + 1 == block_ctas_onepass(chunks, blk, (unsigned)kPerCta);
-        if (s_last) __threadfence();
-    }
+    if (threadIdx.x == 0)
+        s_last = add_acq_rel(sync.block_ctas + blk, 1u) + 1 == block_ctas_onepass(chunks, blk, (unsigned)kPerCta);
     __syncthreads();
     if (!s_last) return;
     compose_group<T, kFanout>(h0, d0, chunks, Tr::CHUNK, blk, h1, d1, reinterpret_cast<typename Tr::D *>(s_slots));
     __syncthreads();
     const uint64_t sb = blk / kFanout;
     if (threadIdx.x == 0) {
-        __threadfence();
-        atomicExch(sync.block_ready + blk, 1u);
-        s_last = atomicAdd(sync.super_blocks + sb, 1u) + 1 == min((uint64_t)kFanout, blocks - sb * kFanout);
-        if (s_last) __threadfence();
+        store_release(sync.block_ready + blk, 1u);
+        s_last = add_acq_rel(sync.super_blocks + sb, 1u) + 1 == min((uint64_t)kFanout, blocks - sb * kFanout);
     }
     __syncthreads();
     if (!s_last) return;
     compose_group<T, kFanout>(h1, d1, blocks, (uint64_t)Tr::CHUNK << 6, sb, h2, d2,
                               reinterpret_cast<typename Tr::D *>(s_slots));
     __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        atomicExch(sync.super_ready + sb, 1u);
-    }
+    if (threadIdx.x == 0) store_release(sync.super_ready + sb, 1u);
 }
 
 // binary32/binary64 encoding of an element count, nearest-even (constants/constants.rs:18-27)
@@ -1409,12 +1536,13 @@ template <typename T> struct MseLayout {
 // The chunk kernel's grid when it carries SGD, and how many units (chunk warps or SGD CTAs)
 // carry it.
 // (chunks_per_cta: kChunkWarps, or more for the one-launch form without SGD)
-inline uint64_t chunk_grid(uint64_t chunks, bool ride, uint64_t chunks_per_cta = kChunkWarps) {
+inline uint64_t chunk_grid(uint64_t chunks, bool ride, uint64_t chunks_per_cta = kChunkWarps, int P = kSgdPeriod,
+                           int S = 1) {
     const uint64_t ctas = (chunks + chunks_per_cta - 1) / chunks_per_cta;
-    return ride ? ctas + (ctas + kSgdPeriod - 2) / (kSgdPeriod - 1) + kSgdPeriod : ctas;
+    return ride ? (ctas + (P - S) - 1) / (P - S) * P : ctas;
 }
-inline uint64_t sgd_units(uint64_t chunks, uint64_t chunks_per_cta = kChunkWarps) {
-    return chunk_grid(chunks, true, chunks_per_cta) / kSgdPeriod;
+inline uint64_t sgd_units(uint64_t chunks, uint64_t chunks_per_cta = kChunkWarps, int P = kSgdPeriod, int S = 1) {
+    return chunk_grid(chunks, true, chunks_per_cta, P, S) / P * S;
 }
 
 // Phases 1 and 2 of a segment (global elements [base, base + n)): chunk maps, then block and
@@ -1519,22 +1647,27 @@ int onepass_mse(int policy, const T *p, const T *t, T *out, uint64_t n, void *wo
     int ahead = cached ? resident[ride][device] : 0;
     if (!ahead) {
         int per_sm = 0;
-        e = ride ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mse_onepass_kernel<T, true, 1>, kWalkThreads, 0)
+        e = ride ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mse_onepass_kernel<T, true, kRideGroupsPerCta>,
+                                                                 kWalkThreads, 0)
                  : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mse_onepass_kernel<T, false, kGroupsPerCta>,
                                                                  kWalkThreads, 0);
         if (e != cudaSuccess) return pcu_host::set_cuda_error(e);
-        ahead = per_sm * kChunkWarps * pcu_host::sm_count();
+        // chunk CTAs resident at once (the walker holds one slot; SGD CTAs hold 1 in kSgdPeriod)
+        int64_t ctas = (int64_t)per_sm * pcu_host::sm_count() - 1;
+        if (ride) ctas = ctas * (kRidePeriod - kRideSgd) / kRidePeriod;
+        const int g = ride ? kRideGroupsPerCta : kGroupsPerCta;
+        ahead = (int)std::max<int64_t>(1, ctas * g * kChunkWarps - (int64_t)(g - 1) * kChunkWarps);
         if (cached) resident[ride][device] = ahead;
     }
     using D = typename MseTraits<T>::D;
     auto H = [&](int l) { return reinterpret_cast<MseHead *>(ws + lay.heads_off[l]); };
     auto R = [&](int l) { return reinterpret_cast<D *>(ws + lay.deltas_off[l]); };
     unsigned *u = reinterpret_cast<unsigned *>(ws + lay.sync_off);
-    const unsigned per_cta = ride ? kChunkWarps : kChunkWarps * kGroupsPerCta;
+    const unsigned per_cta = kChunkWarps * (ride ? kRideGroupsPerCta : kGroupsPerCta);
     MseSync sync{u, u + lay.count[1], u + 2 * lay.count[1], u + 2 * lay.count[1] + lay.count[2], per_cta};
-    const unsigned grid = (unsigned)(1 + chunk_grid(lay.count[0], ride, per_cta));
+    const unsigned grid = (unsigned)(1 + chunk_grid(lay.count[0], ride, per_cta, kRidePeriod, kRideSgd));
     if (ride)
-        mse_onepass_kernel<T, true, 1><<<grid, kWalkThreads, 0, stream>>>(
+        mse_onepass_kernel<T, true, kRideGroupsPerCta><<<grid, kWalkThreads, 0, stream>>>(
             p, t, n, vec, policy, lay.count[0], lay.count[1], lay.count[2], (uint64_t)ahead, H(0), R(0), H(1), R(1),
             H(2), R(2), sync, count_value<T>(n), out, status, *sgd, guard);
     else
@@ -1605,7 +1738,10 @@ int run_mse_sgd(int policy, const T *p, const T *t, T *loss, uint64_t n, void *w
                 unsigned long long *mse_status, const SgdRider<T> &sgd, cudaStream_t stream) {
     MseLayout<T> lay(n);
     SgdRider<T> head, tail;
-    split_sgd<T>(sgd, sgd_units(lay.count[0]), head, tail);  // riding along: one group per chunk CTA
+    split_sgd<T>(sgd,
+                 sizeof(T) == 4 ? sgd_units(lay.count[0], kChunkWarps * kRideGroupsPerCta, kRidePeriod, kRideSgd)
+                                : sgd_units(lay.count[0]),
+                 head, tail);
     if constexpr (sizeof(T) == 4) {
         int rc = onepass_mse<T>(policy, p, t, loss, n, workspace, workspace_bytes, mse_status, stream, &head,
                                 ChainGuard{});
