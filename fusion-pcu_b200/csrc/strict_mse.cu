@@ -1102,7 +1102,8 @@ __device__ __forceinline__ unsigned load_flag(const unsigned *p) {
 // block) and publish once: a publication (a fence and a counter round trip) holds the CTA's slot
 // for about a microsecond, too long to pay once per group.  With an SGD node riding along, one
 // group per CTA keeps the SGD CTAs short and well interleaved.
-constexpr int kGroupsPerCta = 4;
+constexpr int kGroupsPerCta = 4;  // when there are at least kManyWaves waves of such CTAs (else 1)
+constexpr int kManyWaves = 6;
 #ifndef PCU_MSE_RIDE_GROUPS
 #define PCU_MSE_RIDE_GROUPS 1
 #endif
@@ -1640,40 +1641,47 @@ int onepass_mse(int policy, const T *p, const T *t, T *out, uint64_t n, void *wo
     cudaError_t e = cudaMemsetAsync(ws + lay.sync_off, 0, lay.sync_bytes, stream);
     if (e != cudaSuccess) return pcu_host::set_cuda_error(e);
     const bool vec = pcu_host::aligned(p, 16) && pcu_host::aligned(t, 16);
-    static int resident[2][64] = {};  // chunk warps resident at once, per variant and device
+    static int resident[64] = {};  // CTAs of the one-launch kernel resident at once, per device
     int device = 0;
     cudaGetDevice(&device);
     const bool cached = device >= 0 && device < 64;
-    int ahead = cached ? resident[ride][device] : 0;
-    if (!ahead) {
+    int slots = cached ? resident[device] : 0;
+    if (!slots) {  // every variant has the same footprint: 64 registers and the same shared memory
         int per_sm = 0;
-        e = ride ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mse_onepass_kernel<T, true, kRideGroupsPerCta>,
-                                                                 kWalkThreads, 0)
-                 : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mse_onepass_kernel<T, false, kGroupsPerCta>,
-                                                                 kWalkThreads, 0);
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mse_onepass_kernel<T, false, kGroupsPerCta>,
+                                                          kWalkThreads, 0);
         if (e != cudaSuccess) return pcu_host::set_cuda_error(e);
-        // chunk CTAs resident at once (the walker holds one slot; SGD CTAs hold 1 in kSgdPeriod)
-        int64_t ctas = (int64_t)per_sm * pcu_host::sm_count() - 1;
-        if (ride) ctas = ctas * (kRidePeriod - kRideSgd) / kRidePeriod;
-        const int g = ride ? kRideGroupsPerCta : kGroupsPerCta;
-        ahead = (int)std::max<int64_t>(1, ctas * g * kChunkWarps - (int64_t)(g - 1) * kChunkWarps);
-        if (cached) resident[ride][device] = ahead;
+        slots = std::max(2, per_sm * pcu_host::sm_count());
+        if (cached) resident[device] = slots;
     }
+    // chunk CTAs resident at once (the walker holds one slot; SGD CTAs hold S in every P)
+    int64_t ctas = slots - 1;
+    if (ride) ctas = ctas * (kRidePeriod - kRideSgd) / kRidePeriod;
+    // several groups per chunk CTA only when there are enough waves of them (the last wave runs
+    // partly empty), never with an SGD node riding along
+    const int g = ride ? kRideGroupsPerCta
+                       : (lay.count[0] >= (uint64_t)kManyWaves * ctas * kChunkWarps * kGroupsPerCta ? kGroupsPerCta : 1);
+    // the first group of the CTA that takes this slot one wave later
+    const uint64_t ahead = (uint64_t)std::max<int64_t>(1, ctas * g * kChunkWarps - (int64_t)(g - 1) * kChunkWarps);
     using D = typename MseTraits<T>::D;
     auto H = [&](int l) { return reinterpret_cast<MseHead *>(ws + lay.heads_off[l]); };
     auto R = [&](int l) { return reinterpret_cast<D *>(ws + lay.deltas_off[l]); };
     unsigned *u = reinterpret_cast<unsigned *>(ws + lay.sync_off);
-    const unsigned per_cta = kChunkWarps * (ride ? kRideGroupsPerCta : kGroupsPerCta);
+    const unsigned per_cta = kChunkWarps * g;
     MseSync sync{u, u + lay.count[1], u + 2 * lay.count[1], u + 2 * lay.count[1] + lay.count[2], per_cta};
     const unsigned grid = (unsigned)(1 + chunk_grid(lay.count[0], ride, per_cta, kRidePeriod, kRideSgd));
     if (ride)
         mse_onepass_kernel<T, true, kRideGroupsPerCta><<<grid, kWalkThreads, 0, stream>>>(
-            p, t, n, vec, policy, lay.count[0], lay.count[1], lay.count[2], (uint64_t)ahead, H(0), R(0), H(1), R(1),
-            H(2), R(2), sync, count_value<T>(n), out, status, *sgd, guard);
-    else
+            p, t, n, vec, policy, lay.count[0], lay.count[1], lay.count[2], ahead, H(0), R(0), H(1), R(1), H(2), R(2),
+            sync, count_value<T>(n), out, status, *sgd, guard);
+    else if (g == kGroupsPerCta)
         mse_onepass_kernel<T, false, kGroupsPerCta><<<grid, kWalkThreads, 0, stream>>>(
-            p, t, n, vec, policy, lay.count[0], lay.count[1], lay.count[2], (uint64_t)ahead, H(0), R(0), H(1), R(1),
-            H(2), R(2), sync, count_value<T>(n), out, status, SgdRider<T>{}, guard);
+            p, t, n, vec, policy, lay.count[0], lay.count[1], lay.count[2], ahead, H(0), R(0), H(1), R(1), H(2), R(2),
+            sync, count_value<T>(n), out, status, SgdRider<T>{}, guard);
+    else
+        mse_onepass_kernel<T, false, 1><<<grid, kWalkThreads, 0, stream>>>(
+            p, t, n, vec, policy, lay.count[0], lay.count[1], lay.count[2], ahead, H(0), R(0), H(1), R(1), H(2), R(2),
+            sync, count_value<T>(n), out, status, SgdRider<T>{}, guard);
     return pcu_host::launch_status();
 }
 

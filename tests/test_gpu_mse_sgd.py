@@ -136,3 +136,27 @@ def test_fused_segments_match_oracle(width):
     first = oracle.sgd_location(sgd_st)[0]
     _, ok_out = oracle.sgd(w[:first], g[:first], RATE)
     assert np.array_equal(bits(to_host(upd[:first])), bits(ok_out))
+
+
+def test_large_mse_and_fused_match_oracle():
+    """2^27 + 3 elements: the one-launch MSE then gives each chunk CTA several groups of chunks
+    (one publication per 32 chunks), a path only large reductions take; the fused call carries an
+    SGD node of the same size."""
+    import torch
+
+    n = (1 << 27) + 3
+    p, t, w, g = _data(32, n, n, seed=271)
+    mse_st, mse_out = oracle.mse(p, t)
+    sgd_st, sgd_out = oracle.sgd(w, g, RATE)
+    assert mse_st == sgd_st == oracle.STATUS_OK
+    pd, td = to_device(p), to_device(t)
+    status = pcu.new_status()
+    loss = pcu.strict_mse(pd, td, status=status)
+    torch.cuda.synchronize()
+    assert status_word(status) == oracle.STATUS_OK
+    assert bits(to_host(loss).reshape(1))[0] == bits(mse_out)[0]
+    del p, t
+    ms, loss2, ss, upd = _fused(*(a for a in (to_host(pd), to_host(td), w, g)))
+    assert ms == ss == oracle.STATUS_OK
+    assert loss2 == bits(mse_out)[0]
+    assert np.array_equal(upd, bits(sgd_out))
