@@ -17,7 +17,8 @@ import numpy as np
 
 __all__ = [
     "ProviderUnavailable", "TensorError", "ArithmeticFault", "CompoundArithmeticFault", "ProviderFailure",
-    "library", "POLICY", "OPS", "STATUS_OK", "new_status", "decode_status", "strict_matmul", "strict_sgd",
+    "library", "POLICY", "OPS", "STATUS_OK", "new_status", "decode_status", "strict_matmul", "strict_matmul_host",
+    "matmul_host_scratch", "strict_sgd",
     "strict_mse", "mse_workspace", "strict_mse_segment_prepare", "strict_mse_segment_walk", "strict_mse_sgd",
     "strict_mse_sgd_segment_prepare", "checked_binary", "checked_relu", "checked_relu_backward", "matmul_fault", "sgd_fault",
     "mse_fault", "element_fault",
@@ -88,6 +89,9 @@ def _declare(L):
     L.pcu_b200_strict_matmul_workspace_size.argtypes = [u64, u64, u64]
     L.pcu_b200_strict_matmul_workspace_size.restype = sz
     L.pcu_b200_strict_matmul.argtypes = [i32, i32, vp, vp, vp, u64, u64, u64, u64, u64, i32, i32, vp, sz, vp, vp]
+    L.pcu_b200_strict_matmul_host_scratch_size.argtypes = [i32, u64, u64, u64]
+    L.pcu_b200_strict_matmul_host_scratch_size.restype = sz
+    L.pcu_b200_strict_matmul_host.argtypes = [i32, i32, vp, vp, vp, u64, u64, u64, vp, sz, vp, vp]
     L.pcu_b200_strict_sgd.argtypes = [i32, i32, vp, vp, vp, u64, u32, vp, vp]
     L.pcu_b200_strict_mse_workspace_size.argtypes = [i32, u64]
     L.pcu_b200_strict_mse_workspace_size.restype = sz
@@ -209,7 +213,8 @@ def strict_matmul(left, right, transpose_left=False, transpose_right=False, poli
                   workspace=None, stream=None):
     torch = _torch()
     assert left.dim() == 2 and right.dim() == 2 and left.dtype == right.dtype
-    assert left.stride(1) == 1 and right.stride(1) == 1, "operands must be row-major"
+    assert (left.numel() == 0 or left.stride(1) == 1) and (right.numel() == 0 or right.stride(1) == 1), \
+        "operands must be row-major"
     rows, inner = (left.shape[1], left.shape[0]) if transpose_left else (left.shape[0], left.shape[1])
     inner2, cols = (right.shape[1], right.shape[0]) if transpose_right else (right.shape[0], right.shape[1])
     if inner != inner2:
@@ -223,10 +228,42 @@ def strict_matmul(left, right, transpose_left=False, transpose_right=False, poli
     if workspace is None or workspace.numel() < need:
         workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=left.device)
     _check(L.pcu_b200_strict_matmul(_dtype_code(left), policy, _ptr(left), _ptr(right), _ptr(out), rows, inner,
-                                    cols, left.stride(0), right.stride(0), int(transpose_left),
+                                    cols, max(left.stride(0), left.shape[1]), max(right.stride(0), right.shape[1]),
+                                    int(transpose_left),
                                     int(transpose_right), _ptr(workspace), workspace.numel(), _ptr(status),
                                     _stream(stream)))
     return out
+
+
+def matmul_host_scratch(left, right, device=None):
+    """A device scratch sized for strict_matmul_host over host operands `left` (rows x inner) and
+    `right` (inner x columns)."""
+    torch = _torch()
+    need = library().pcu_b200_strict_matmul_host_scratch_size(_dtype_code(left), left.shape[0], left.shape[1],
+                                                               right.shape[1])
+    return torch.empty(need, dtype=torch.uint8, device=device or torch.device("cuda", torch.cuda.current_device()))
+
+
+def strict_matmul_host(left, right, policy=0, out=None, status=None, scratch=None, stream=None):
+    """C = A . B with A, B and C in host memory (page-locked for overlap), uploads and read-backs
+    pipelined with the arithmetic by row blocks.  `status` is a host int64 tensor of one element
+    (the unsigned word's bits).  Asynchronous: synchronise the stream before reading the results."""
+    torch = _torch()
+    assert left.device.type == "cpu" and right.device.type == "cpu" and left.dtype == right.dtype
+    assert left.dim() == 2 and right.dim() == 2 and left.is_contiguous() and right.is_contiguous()
+    rows, inner = left.shape
+    if right.shape[0] != inner:
+        raise ValueError(f"MatMulShape {tuple(left.shape)} {tuple(right.shape)}")
+    if out is None:
+        out = torch.empty((rows, right.shape[1]), dtype=left.dtype).pin_memory()
+    if status is None:
+        status = torch.empty(1, dtype=torch.int64).pin_memory()
+    if scratch is None:
+        scratch = matmul_host_scratch(left, right)
+    _check(library().pcu_b200_strict_matmul_host(_dtype_code(left), policy, _ptr(left), _ptr(right), _ptr(out), rows,
+                                                 inner, right.shape[1], _ptr(scratch), scratch.numel(), _ptr(status),
+                                                 _stream(stream)))
+    return out, status
 
 
 def strict_sgd(weights, gradient, rate, policy=0, out=None, status=None, stream=None):

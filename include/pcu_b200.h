@@ -136,6 +136,23 @@ int pcu_b200_strict_matmul_static_scratch(int dtype, int policy, const void *lef
                                           uint64_t right_stride, int transpose_left, int transpose_right,
                                           uint64_t *status, void *stream);
 
+/* Strict MatMul with its operands and result in HOST memory: the host-boundary form of the node
+ * (the reference's pending upload, tensor/pending_upload/pending_upload.rs:115-190, the node's
+ * kernel and the read of its output).  Row-major, untransposed operands with dense rows:
+ * left is rows x inner, right is inner x columns, out is rows x columns.  The rows of out are
+ * computed in blocks so that the uploads of A and the read-backs of C overlap the arithmetic
+ * (two copy streams of this library, ordered after the work already on `stream`, and joined
+ * back into it); with page-locked host memory they run concurrently, with pageable memory they
+ * serialise.  Results and the status word are exactly those of pcu_b200_strict_matmul on the
+ * same operands; the status word goes to *status_host (host memory).  All writes to host memory
+ * are asynchronous: synchronise `stream` before reading out or *status_host.  The device scratch
+ * holds B, two row blocks of A and C, and the workspace:
+ * pcu_b200_strict_matmul_host_scratch_size bytes. */
+size_t pcu_b200_strict_matmul_host_scratch_size(int dtype, uint64_t rows, uint64_t inner, uint64_t columns);
+int pcu_b200_strict_matmul_host(int dtype, int policy, const void *left, const void *right, void *out, uint64_t rows,
+                                uint64_t inner, uint64_t columns, void *device_scratch, size_t scratch_bytes,
+                                uint64_t *status_host, void *stream);
+
 /* ------------------------------------------------------------------ strict SGD */
 
 /* out[i] = weights[i] - rate * gradient[i] with the multiply and the subtract separately
