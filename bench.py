@@ -352,11 +352,13 @@ def mse_sgd(torch, pcu, device, stream, hbm_gbs, args, rank, world):
     w, g_, p, t = block(11), block(12), block(13), block(14)
     out_w = torch.empty_like(w)
     loss = torch.empty((), dtype=torch.float32, device=device)
-    s1, s2 = pcu.new_status(device=device), pcu.new_status(device=device)
+    s12 = pcu.new_status(2, device=device)  # the two nodes' words, all-reduced together
+    s1, s2 = s12[0:1], s12[1:2]
     if world > 1:
         smse = sharded.ShardedMse(p, t, e0, n)
         rider = {"weights": w, "gradient": g_, "rate": 0.01, "first_index": e0, "out": out_w, "status": s2}
-        fused_call = lambda: (smse.run(s1, stream=stream, sgd=rider), sharded.all_reduce_min_status(s2))  # noqa
+        fused_call = lambda: (smse.run(s1, stream=stream, sgd=rider, reduce_status=False),  # noqa: E731
+                              sharded.all_reduce_min_status(s12))
         mse_call = lambda: smse.run(s1, stream=stream)  # noqa: E731
         sgd_call = lambda: (sharded.strict_sgd_block(w, g_, 0.01, e0, s2, out=out_w, stream=stream),  # noqa: E731
                             sharded.all_reduce_min_status(s2))

@@ -20,7 +20,7 @@ __all__ = [
     "library", "POLICY", "OPS", "STATUS_OK", "new_status", "decode_status", "strict_matmul", "strict_matmul_host",
     "matmul_host_scratch", "strict_sgd",
     "strict_mse", "mse_workspace", "strict_mse_segment_prepare", "strict_mse_segment_walk", "strict_mse_sgd",
-    "strict_mse_sgd_segment_prepare", "checked_binary", "checked_relu", "checked_relu_backward", "matmul_fault", "sgd_fault",
+    "strict_mse_sgd_segment_prepare", "strict_mse_sgd_segment", "checked_binary", "checked_relu", "checked_relu_backward", "matmul_fault", "sgd_fault",
     "mse_fault", "element_fault",
 ]
 
@@ -101,6 +101,8 @@ def _declare(L):
     L.pcu_b200_strict_mse_sgd.argtypes = [i32, i32, vp, vp, vp, u64, vp, sz, vp, vp, vp, vp, u64, u32, vp, vp]
     L.pcu_b200_strict_mse_sgd_segment_prepare.argtypes = [i32, i32, vp, vp, u64, u64, vp, sz, vp, vp, vp, vp, u64,
                                                           u64, u32, vp, vp]
+    L.pcu_b200_strict_mse_sgd_segment.argtypes = [i32, i32, vp, vp, u64, u64, u64, vp, vp, vp, vp, sz, vp, vp, vp, vp,
+                                                  u64, u64, u32, vp, vp]
     L.pcu_b200_checked_binary.argtypes = [i32, i32, i32, vp, vp, vp, u64, i32, i32, vp, vp]
     L.pcu_b200_checked_relu.argtypes = [i32, i32, vp, vp, u64, vp, vp]
     L.pcu_b200_checked_relu_backward.argtypes = [i32, i32, vp, vp, vp, u64, vp, vp]
@@ -377,6 +379,26 @@ def strict_mse_sgd_segment_prepare(prediction, target, first_index, weights, gra
         _ptr(workspace), workspace.numel(), _ptr(mse_status), _ptr(weights), _ptr(gradient), _ptr(updated),
         weights.numel(), sgd_first_index, _rate_bits(rate), _ptr(sgd_status), _stream(stream)))
     return mse_status, workspace, updated
+
+
+def strict_mse_sgd_segment(prediction, target, first_index, total_count, carry_in, carry_out, workspace, mse_status,
+                           policy=0, out=None, sgd=None, stream=None):
+    """A whole MSE segment in one call (one launch for binary32): maps and the walk from `carry_in`
+    (a device scalar, None = +0); the running sum after it goes to `carry_out`, the checked mean
+    to `out` for the last segment.  `sgd`: optionally an SGD block carried along, a dict with
+    weights, gradient, rate, first_index, out and status."""
+    assert prediction.is_contiguous() and target.is_contiguous() and prediction.numel() == target.numel()
+    if sgd is None:
+        w = g = upd = None
+        n_sgd, sgd_first, rate_bits, sgd_status = 0, 0, _rate_bits(0.0), new_status(device=prediction.device)
+    else:
+        w, g, upd, sgd_status = sgd["weights"], sgd["gradient"], sgd["out"], sgd["status"]
+        n_sgd, sgd_first, rate_bits = w.numel(), sgd["first_index"], _rate_bits(sgd["rate"])
+    _check(library().pcu_b200_strict_mse_sgd_segment(
+        _dtype_code(prediction), policy, _ptr(prediction), _ptr(target), prediction.numel(), first_index, total_count,
+        _ptr(carry_in), _ptr(carry_out), _ptr(out), _ptr(workspace), workspace.numel(), _ptr(mse_status), _ptr(w),
+        _ptr(g), _ptr(upd), n_sgd, sgd_first, rate_bits, _ptr(sgd_status), _stream(stream)))
+    return out
 
 
 def checked_binary(op, left, right, policy=0, left_uniform=False, right_uniform=False, out=None, status=None,

@@ -1430,13 +1430,13 @@ mse_onepass_kernel(const T *prediction, const T *target, uint64_t n, bool vec, i
                    uint64_t blocks, uint64_t supers, uint64_t ahead, MseHead *h0, typename MseTraits<T>::D *d0,
                    MseHead *h1, typename MseTraits<T>::D *d1, MseHead *h2, typename MseTraits<T>::D *d2,
                    MseSync sync, T denominator, T *out, unsigned long long *status, SgdRider<T> rider,
-                   ChainGuard guard) {
+                   ChainGuard guard, uint64_t base, uint64_t total, const T *carry_in, T *carry_out) {
     using Tr = MseTraits<T>;
     if constexpr (!RIDE)
         if (!chain_admits(guard)) return;  // the whole launch, walker included
     if (blockIdx.x == 0) {
-        mse_walk<T, kWalkThreads>(prediction, target, n, h0, d0, h1, d1, h2, d2, chunks, blocks, supers, 0, n,
-                                  denominator, policy, nullptr, nullptr, out, status, sync);
+        mse_walk<T, kWalkThreads>(prediction, target, n, h0, d0, h1, d1, h2, d2, chunks, blocks, supers, base, total,
+                                  denominator, policy, carry_in, carry_out, out, status, sync);
         return;
     }
     // the chunk warps' slots; once the chunks are done, the staging area of a composition (all
@@ -1454,7 +1454,7 @@ mse_onepass_kernel(const T *prediction, const T *target, uint64_t n, bool vec, i
 #pragma unroll 1
     for (int q = 0; q < G; ++q)  // a group prefetches the next one into L2; the last group, the first
         // group of the CTA that takes this slot one wave later (`ahead` chunks on)
-        chunk_maps<T>(cta * G + q, prediction, target, n, 0, vec, policy, chunks,
+        chunk_maps<T>(cta * G + q, prediction, target, n, base, vec, policy, chunks,
                       q + 1 < G ? (uint64_t)kChunkWarps : ahead, h0, d0, status, s_slots);
     // Publish this CTA's chunk maps: the barrier orders every thread's writes before thread 0,
     // whose acquire-release count releases them (cumulatively); the last CTA of a block acquires
@@ -1632,7 +1632,9 @@ int walk_mse(int policy, const T *p, const T *t, uint64_t n, uint64_t base, uint
 // one launch builds the maps and walks them.  `sgd` (if not null and not empty) rides along.
 template <typename T>
 int onepass_mse(int policy, const T *p, const T *t, T *out, uint64_t n, void *workspace, size_t workspace_bytes,
-                unsigned long long *status, cudaStream_t stream, const SgdRider<T> *sgd, const ChainGuard &guard) {
+                unsigned long long *status, cudaStream_t stream, const SgdRider<T> *sgd, const ChainGuard &guard,
+                uint64_t base = 0, uint64_t total = 0, const T *carry_in = nullptr, T *carry_out = nullptr) {
+    if (!total) total = n;  // a whole reduction unless a segment [base, base + n) of `total`
     MseLayout<T> lay(n);
     if (!workspace || workspace_bytes < lay.bytes) return PCU_B200_ERROR_WORKSPACE;
     if (lay.count[0] > 0x7fffffffull * kChunkWarps) return PCU_B200_ERROR_SIZE_OVERFLOW;
@@ -1673,15 +1675,15 @@ int onepass_mse(int policy, const T *p, const T *t, T *out, uint64_t n, void *wo
     if (ride)
         mse_onepass_kernel<T, true, kRideGroupsPerCta><<<grid, kWalkThreads, 0, stream>>>(
             p, t, n, vec, policy, lay.count[0], lay.count[1], lay.count[2], ahead, H(0), R(0), H(1), R(1), H(2), R(2),
-            sync, count_value<T>(n), out, status, *sgd, guard);
+            sync, count_value<T>(total), out, status, *sgd, guard, base, total, carry_in, carry_out);
     else if (g == kGroupsPerCta)
         mse_onepass_kernel<T, false, kGroupsPerCta><<<grid, kWalkThreads, 0, stream>>>(
             p, t, n, vec, policy, lay.count[0], lay.count[1], lay.count[2], ahead, H(0), R(0), H(1), R(1), H(2), R(2),
-            sync, count_value<T>(n), out, status, SgdRider<T>{}, guard);
+            sync, count_value<T>(total), out, status, SgdRider<T>{}, guard, base, total, carry_in, carry_out);
     else
         mse_onepass_kernel<T, false, 1><<<grid, kWalkThreads, 0, stream>>>(
             p, t, n, vec, policy, lay.count[0], lay.count[1], lay.count[2], ahead, H(0), R(0), H(1), R(1), H(2), R(2),
-            sync, count_value<T>(n), out, status, SgdRider<T>{}, guard);
+            sync, count_value<T>(total), out, status, SgdRider<T>{}, guard, base, total, carry_in, carry_out);
     return pcu_host::launch_status();
 }
 
@@ -1914,4 +1916,66 @@ extern "C" int pcu_b200_strict_mse_sgd_segment_prepare(int dtype, int policy, co
                                         pcu::make_rider<double>(policy, weights, gradient, updated, sgd_count,
                                                                 sgd_first_index, rate_bits_f32, ss),
                                         s);
+}
+
+// A whole segment in one call: its maps, and the walk from *carry_in, in one launch for binary32
+// (three for binary64).  `sgd` as in pcu_b200_strict_mse_sgd_segment_prepare.
+namespace pcu {
+template <typename T>
+int run_mse_sgd_segment(int policy, const T *p, const T *t, uint64_t n, uint64_t base, uint64_t total, const T *carry_in,
+                        T *carry_out, T *out, void *workspace, size_t workspace_bytes, unsigned long long *mse_status,
+                        const SgdRider<T> &sgd, cudaStream_t stream) {
+    MseLayout<T> lay(n);
+    if (!workspace || workspace_bytes < lay.bytes) return PCU_B200_ERROR_WORKSPACE;
+    if constexpr (sizeof(T) == 4) {
+        if (n) {
+            SgdRider<T> head, tail;
+            split_sgd<T>(sgd, sgd_units(lay.count[0], kChunkWarps * kRideGroupsPerCta, kRidePeriod, kRideSgd), head,
+                         tail);
+            int rc = onepass_mse<T>(policy, p, t, out, n, workspace, workspace_bytes, mse_status, stream, &head,
+                                    ChainGuard{}, base, total, carry_in, carry_out);
+            if (rc || !tail.n) return rc;
+            const uint64_t per_cta = 256ull * (16 / sizeof(T)) * kSgdTrip;
+            const uint64_t cap = 8ull * pcu_host::sm_count();
+            const uint64_t want = (tail.n + per_cta - 1) / per_cta;
+            sgd_share_kernel<T><<<(unsigned)(want < cap ? want : cap), 256, 0, stream>>>(tail);
+            return pcu_host::launch_status();
+        }
+    }
+    int rc = prepare_mse_sgd<T>(policy, p, t, n, base, workspace, workspace_bytes, mse_status, sgd, stream);
+    if (rc) return rc;
+    return walk_mse<T>(policy, p, t, n, base, total, carry_in, carry_out, out, workspace, workspace_bytes, mse_status,
+                       stream);
+}
+}  // namespace pcu
+
+extern "C" int pcu_b200_strict_mse_sgd_segment(int dtype, int policy, const void *prediction, const void *target,
+                                               uint64_t mse_count, uint64_t mse_first_index, uint64_t total_count,
+                                               const void *carry_in, void *carry_out, void *out, void *workspace,
+                                               size_t workspace_bytes, uint64_t *mse_status, const void *weights,
+                                               const void *gradient, void *updated, uint64_t sgd_count,
+                                               uint64_t sgd_first_index, uint32_t rate_bits_f32, uint64_t *sgd_status,
+                                               void *stream) {
+    if ((dtype != PCU_B200_F32 && dtype != PCU_B200_F64) || policy < 0 || policy > 2 || !mse_status)
+        return PCU_B200_ERROR_INVALID_ARGUMENT;
+    if (mse_count && (!prediction || !target)) return PCU_B200_ERROR_INVALID_ARGUMENT;
+    if (!valid_sgd_args(dtype, sgd_count, weights, gradient, updated, rate_bits_f32, sgd_status))
+        return PCU_B200_ERROR_INVALID_ARGUMENT;
+    if (total_count > (1ull << 58) || mse_first_index > total_count || mse_count > total_count - mse_first_index)
+        return PCU_B200_ERROR_SIZE_OVERFLOW;
+    if (out && (total_count == 0 || mse_first_index + mse_count != total_count)) return PCU_B200_ERROR_INVALID_ARGUMENT;
+    if (sgd_count > (1ull << 59) || sgd_first_index > (1ull << 59) - sgd_count) return PCU_B200_ERROR_SIZE_OVERFLOW;
+    auto *ms = reinterpret_cast<unsigned long long *>(mse_status);
+    auto *ss = reinterpret_cast<unsigned long long *>(sgd_status);
+    cudaStream_t s = pcu_host::as_stream(stream);
+    if (dtype == PCU_B200_F32)
+        return pcu::run_mse_sgd_segment<float>(
+            policy, (const float *)prediction, (const float *)target, mse_count, mse_first_index, total_count,
+            (const float *)carry_in, (float *)carry_out, (float *)out, workspace, workspace_bytes, ms,
+            pcu::make_rider<float>(policy, weights, gradient, updated, sgd_count, sgd_first_index, rate_bits_f32, ss),
+            s);
+    return pcu::run_mse_sgd_segment<double>(
+        policy, (const double *)prediction, (const double *)target, mse_count, mse_first_index, total_count,
+        (const double *)carry_in, (double *)carry_out, (double *)out, workspace, workspace_bytes, ms,
+        pcu::make_rider<double>(policy, weights, gradient, updated, sgd_count, sgd_first_index, rate_bits_f32, ss), s);
 }

@@ -121,8 +121,15 @@ class ShardedMse:
     def run(self, status, stream=None, reduce_status=True, sgd=None):
         """`sgd`: optionally an independent strict SGD block carried by the bandwidth-bound phase,
         a dict with weights, gradient, rate, first_index (its global first element), out and
-        status (its own word, global events; not all-reduced here)."""
-        if sgd is None:
+        status (its own word, global events; not all-reduced here).
+
+        The first segment's running sum starts at +0, so its rank walks at once, in the same
+        launch as its maps; the others build their maps at once and walk when the carry arrives."""
+        first = dist.get_rank(self.group) == 0
+        if first:
+            pcu.strict_mse_sgd_segment(self.p, self.t, self.first, self.total, None, self.carry, self.workspace, status,
+                                       self.policy, out=self.mean if self.last else None, sgd=sgd, stream=stream)
+        elif sgd is None:
             pcu.strict_mse_segment_prepare(self.p, self.t, self.first, self.policy, status=status,
                                            workspace=self.workspace, stream=stream)
         else:
@@ -130,11 +137,11 @@ class ShardedMse:
                                                sgd["rate"], sgd["first_index"], self.policy, updated=sgd["out"],
                                                mse_status=status, sgd_status=sgd["status"],
                                                workspace=self.workspace, stream=stream)
-        self.carry.zero_()
 
         def walk(carry):
-            pcu.strict_mse_segment_walk(self.p, self.t, self.first, self.total, carry, self.workspace, status,
-                                        self.policy, out=self.mean if self.last else None, stream=stream)
+            if not first:
+                pcu.strict_mse_segment_walk(self.p, self.t, self.first, self.total, carry, self.workspace, status,
+                                            self.policy, out=self.mean if self.last else None, stream=stream)
 
         ordered_handoff(self.carry, walk, self.group)
         dist.broadcast(self.mean, src=_ranks(self.group)[-1], group=self.group)

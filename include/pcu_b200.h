@@ -226,6 +226,19 @@ int pcu_b200_strict_mse_sgd_segment_prepare(int dtype, int policy, const void *p
                                             uint64_t sgd_first_index, uint32_t rate_bits_f32,
                                             uint64_t *sgd_status, void *stream);
 
+/* A whole segment in one call: pcu_b200_strict_mse_sgd_segment_prepare followed by
+ * pcu_b200_strict_mse_segment_walk (same arguments and results), in one launch for binary32, so
+ * the walk runs beside the segment's bandwidth-bound work.  Useful for the first segment of a
+ * split reduction, whose running sum starts at carry_in = NULL (+0): it needs no hand-off before
+ * it can walk.  sgd_count may be 0 (weights, gradient, updated then unused; sgd_status still
+ * required).  No counterpart in the reference. */
+int pcu_b200_strict_mse_sgd_segment(int dtype, int policy, const void *prediction, const void *target,
+                                    uint64_t mse_count, uint64_t mse_first_index, uint64_t total_count,
+                                    const void *carry_in, void *carry_out, void *out, void *workspace,
+                                    size_t workspace_bytes, uint64_t *mse_status, const void *weights,
+                                    const void *gradient, void *updated, uint64_t sgd_count, uint64_t sgd_first_index,
+                                    uint32_t rate_bits_f32, uint64_t *sgd_status, void *stream);
+
 /* ------------------------------------------------------------------ checked elementwise */
 
 /* out[i] = op(left[i], right[i]); a nonzero *_uniform flag broadcasts element 0 of that

@@ -160,3 +160,47 @@ def test_large_mse_and_fused_match_oracle():
     assert ms == ss == oracle.STATUS_OK
     assert loss2 == bits(mse_out)[0]
     assert np.array_equal(upd, bits(sgd_out))
+
+
+@pytest.mark.parametrize("width", [32, 64])
+@pytest.mark.parametrize("case", ["clean", "mse_fault_first_segment", "mse_fault_later", "sgd_fault"])
+def test_one_call_first_segment_then_walks(width, case):
+    """The first segment in one call (pcu_b200_strict_mse_sgd_segment: maps and walk together,
+    from +0), the others prepared and walked with the carried sum, SGD blocks riding along: the
+    split reduction must give the oracle's mean and first faults."""
+    import torch
+
+    n_mse, n_sgd = 5 * 8192 + 321, 120007
+    p, t, w, g = _data(width, n_mse, n_sgd, seed=311 + width)
+    if case == "mse_fault_first_segment":
+        p[7000] = np.nan
+    elif case == "mse_fault_later":
+        t[30000] = np.inf
+    elif case == "sgd_fault":
+        g[100] = np.inf
+    mse_st, mse_out = oracle.mse(p, t)
+    sgd_st, sgd_out = oracle.sgd(w, g, RATE)
+    pd, td, wd, gd = (to_device(a) for a in (p, t, w, g))
+    upd = torch.empty_like(wd)
+    ms, ss = pcu.new_status(), pcu.new_status()
+    carry = torch.zeros((), dtype=pd.dtype, device="cuda")
+    mean = torch.zeros((), dtype=pd.dtype, device="cuda")
+    mse_edges, sgd_edges = [0, 9000, 8192 * 3 + 7, n_mse], [0, 50000, 50001, n_sgd]
+    for k, ((a, b), (c, d)) in enumerate(zip(zip(mse_edges, mse_edges[1:]), zip(sgd_edges, sgd_edges[1:]))):
+        ps, ts = pd[a:b].contiguous(), td[a:b].contiguous()
+        ws = pcu.mse_workspace(ps)
+        rider = {"weights": wd[c:d], "gradient": gd[c:d], "rate": RATE, "first_index": c, "out": upd[c:d],
+                 "status": ss}
+        if k == 0:
+            pcu.strict_mse_sgd_segment(ps, ts, a, n_mse, None, carry, ws, ms, sgd=rider)
+        else:
+            pcu.strict_mse_sgd_segment_prepare(ps, ts, a, wd[c:d], gd[c:d], RATE, c, updated=upd[c:d],
+                                               mse_status=ms, sgd_status=ss, workspace=ws)
+            pcu.strict_mse_segment_walk(ps, ts, a, n_mse, carry, ws, ms, out=mean if b == n_mse else None)
+    torch.cuda.synchronize()
+    assert status_word(ms) == mse_st, (hex(status_word(ms)), hex(mse_st))
+    assert status_word(ss) == sgd_st
+    if mse_st == oracle.STATUS_OK:
+        assert bits(to_host(mean).reshape(1))[0] == bits(mse_out)[0]
+    if sgd_st == oracle.STATUS_OK:
+        assert np.array_equal(bits(to_host(upd)), bits(sgd_out))
