@@ -43,7 +43,8 @@ def _run_device(a, b, policy=0):
     return to_host(out), status_word(status)
 
 
-@pytest.mark.parametrize("shape", [(100, 50, 70), (4100, 64, 96), (6150, 32, 40), (9000, 16, 24), (3000, 0, 5)])
+@pytest.mark.parametrize("shape", [(100, 50, 70), (4100, 64, 96), (6150, 32, 40), (9000, 16, 24), (3000, 0, 5),
+                                   (4200, 40, 2100), (4096, 8, 4096)])
 @pytest.mark.parametrize("pinned", [True, False])
 def test_host_matmul_matches_device_call(shape, pinned):
     rows, inner, cols = shape
@@ -66,9 +67,11 @@ def test_host_matmul_small_against_oracle():
     assert np.array_equal(bits(got), bits(want))
 
 
-@pytest.mark.parametrize("where", ["late_block", "b_column", "two_blocks"])
+@pytest.mark.parametrize("where", ["late_block", "b_column", "two_blocks", "first_block_last_columns",
+                                   "first_block_two_column_pieces"])
 def test_host_matmul_first_fault_matches_device_call(where):
-    rows, inner, cols = 9000, 24, 40  # four blocks of 2250 rows
+    # four row blocks of 2250 rows; the first is computed in four column pieces of 528 columns
+    rows, inner, cols = 9000, 24, 2100
     rng = np.random.default_rng(77)
     a = dyadic_uniform(rng, (rows, inner), 32)
     b = dyadic_uniform(rng, (inner, cols), 32)
@@ -76,10 +79,17 @@ def test_host_matmul_first_fault_matches_device_call(where):
         a[5000, 7] = np.nan
     elif where == "b_column":
         b[3, 11] = np.inf
-    else:
+    elif where == "two_blocks":
         a[8000, 2] = np.nan
         a[2500, 20] = np.float32(3e38)
         b[20, :] = np.float32(4.0)
+    elif where == "first_block_last_columns":  # only the last column piece of the first block
+        b[9, 1900] = np.nan
+        a[:, 9] = np.float32(0.5)
+    else:  # a fault in piece 3 at row 3 against one in piece 1 at row 7: the row decides
+        b[4, 1700] = np.inf
+        a[:3, 4] = 0.0
+        b[11, 600] = np.nan
     got, st = _run_host(a, b)
     _, st_d = _run_device(a, b)
     assert st == st_d != oracle.STATUS_OK, (hex(st), hex(st_d))
