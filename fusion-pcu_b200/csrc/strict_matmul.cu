@@ -608,6 +608,10 @@ int run_matmul(int policy, const T *left, const T *right, T *out, uint64_t rows,
         tma = tr ? make_map<T>(&mb, right, inner, columns, ldb, S::BK, S::BN, true)
                  : make_map<T>(&mb, right, columns, inner, ldb, S::BN, S::BK, false);
     }
+    // An output of a few 128-wide tiles would leave most SMs idle (a 256 x 256 product is 4
+    // CTAs); the 16 x 16-tile kernel spreads it over many CTAs instead.
+    const uint64_t tiles = ((rows + S::BM - 1) / S::BM) * ((columns + S::BN - 1) / S::BN);
+    if (tiles * 4 < (uint64_t)pcu_host::sm_count()) tma = false;
     if (tma && (rows + S::BM - 1) / S::BM <= 65535) {
         if (!tl && !tr) return launch_tma<T, true, false>(ma, mb, p, stream);
         if (!tl && tr) return launch_tma<T, true, true>(ma, mb, p, stream);
