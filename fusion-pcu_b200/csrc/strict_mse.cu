@@ -1004,28 +1004,35 @@ __device__ __forceinline__ unsigned apply_maps(const MseHead *heads, const typen
     uint64_t x;
     int k;
     state_of<T>(s, x, k);
-    MapStep m{0, 0, false};
+    // A map that cannot be used (and a lane past `avail`) carries the increment 2^(P+2) on both
+    // parities: any chain through it ends above the binade, so no separate flag is needed.  The
+    // chain of up to 32 valid maps (each below 2^(P+1)) and poisons stays below 2^(P+7): 32-bit
+    // arithmetic for binary32.
+    using V = typename std::conditional<sizeof(T) == 4, uint32_t, uint64_t>::type;
+    constexpr V POISON = (V)1 << (Tr::P + 2);
+    V d0 = POISON, d1 = POISON;
     if ((unsigned)lane < avail) {  // through L2: in the one-launch form other CTAs wrote the maps
         const uint4 hv = __ldcg(reinterpret_cast<const uint4 *>(heads + first + lane));
         MseHead h;
         memcpy(&h, &hv, sizeof(h));
-        m = map_at<T>(h, deltas + (first + lane) * (size_t)Tr::W * 2, k);
+        const MapStep m = map_at<T>(h, deltas + (first + lane) * (size_t)Tr::W * 2, k);
+        if (m.ok) {
+            d0 = (V)m.d0;
+            d1 = (V)m.d1;
+        }
     }
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-        const unsigned long long l0 = __shfl_up_sync(0xffffffffu, (unsigned long long)m.d0, o);
-        const unsigned long long l1 = __shfl_up_sync(0xffffffffu, (unsigned long long)m.d1, o);
-        const bool lok = __shfl_up_sync(0xffffffffu, (int)m.ok, o) != 0;
+        const V l0 = shfl_up_x(d0, o), l1 = shfl_up_x(d1, o);
         if (lane >= o) {
-            const uint64_t n0 = l0 + (((0 + l0) & 1) ? m.d1 : m.d0);
-            const uint64_t n1 = l1 + (((1 + l1) & 1) ? m.d1 : m.d0);
-            m.d0 = n0;
-            m.d1 = n1;
-            m.ok = m.ok && lok;
+            const V n0 = l0 + ((l0 & 1) ? d1 : d0);
+            const V n1 = l1 + (((1 + l1) & 1) ? d1 : d0);
+            d0 = n0;
+            d1 = n1;
         }
     }
-    const uint64_t nx = x + ((x & 1) ? m.d1 : m.d0);
-    const bool good = m.ok && nx < (2ull << Tr::P);  // the state only grows: the last one decides
+    const uint64_t nx = x + ((x & 1) ? d1 : d0);
+    const bool good = nx < (2ull << Tr::P);  // the state only grows: the last one decides
     const unsigned bad = __ballot_sync(0xffffffffu, !good);
     const unsigned applied = bad ? (unsigned)(__ffs((int)bad) - 1) : 32u;
     if (applied) s = value_of<T>(__shfl_sync(0xffffffffu, (unsigned long long)nx, (int)applied - 1), k);
@@ -1149,8 +1156,10 @@ __device__ __forceinline__ void mse_walk(
     __shared__ uint64_t s_arg;  // chunk to resolve, or ~0 when the walk is done
     __shared__ uint64_t s_end;  // the walk stops in front of this element (the first Subtract/Multiply fault)
     __shared__ int s_done;      // 2: overflow recorded, 3: a wait gave up
-    __shared__ unsigned s_pos, s_stop[2];
+    __shared__ unsigned s_stop[2];
     __shared__ U s_warp_sum[32];
+    __shared__ U s_front[Tr::CHUNK];  // the state in front of each element of the chunk resolved
+    __shared__ U s_after;             // the state after all of them
 
     // The walk stops in front of the earliest Subtract/Multiply fault, so only earlier Adds can
     // still report (their events are smaller).  The segment holds global elements
@@ -1274,19 +1283,18 @@ __device__ __forceinline__ void mse_walk(
                 sq[c] = F::bits(F::mul(d, d));
             }
         }
-        if (tid == 0) {
-            s_pos = 0;
-            s_stop[0] = s_stop[1] = len;
-        }
+        if (tid == 0) s_stop[0] = s_stop[1] = len;
         __syncthreads();
         // Apply every element in front of the first tie or binade crossing at once (a prefix sum
-        // of half-up increments), then add that element exactly; repeat.
-        for (int it = 0;; it ^= 1) {
-            const unsigned pos = s_pos;
-            if (pos >= len) break;
+        // of half-up increments), then add that element exactly; repeat.  Every thread follows
+        // the running sum itself: the states in front of all elements go to shared memory, so
+        // after the cut is known each thread computes the same exact step (two barriers a round).
+        T cur = s_sum;
+        unsigned pos = 0;
+        for (int it = 0; pos < len; it ^= 1) {
             uint64_t x64;
             int k;
-            state_of<T>(s_sum, x64, k);
+            state_of<T>(cur, x64, k);
             const U x = (U)x64;  // below 2^(P+1)
             U c[E];              // inclusive prefix of this thread's increments
             bool tie[E];
@@ -1310,6 +1318,7 @@ __device__ __forceinline__ void mse_walk(
             }
             if (lane == 31) s_warp_sum[warp] = incl;
             __syncthreads();
+            if (tid == 0) s_stop[it ^ 1] = len;  // armed for the next round (its last readers are past)
             U wsum = lane < WARPS ? s_warp_sum[lane] : (U)0;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
@@ -1326,45 +1335,33 @@ __device__ __forceinline__ void mse_walk(
 #pragma unroll
             for (int e = E - 1; e >= 0; --e) {
                 const unsigned idx = tid * E + e;
+                s_front[idx] = e ? sat_add<U>(start, c[e - 1], SAT) : start;
                 if (idx >= pos && idx < len && (tie[e] || sat_add<U>(start, c[e], SAT) >= TOP)) mine = idx;
             }
+            if (tid == NT - 1) s_after = sat_add<U>(start, run, SAT);
             if (mine < len) atomicMin(&s_stop[it], mine);
             __syncthreads();
             const unsigned cut = s_stop[it];
-            // the owner of `cut` (the last thread when nothing stops) publishes the state there,
-            // adds that element exactly, and moves the cursor
-            const unsigned owner = cut < len ? cut / E : NT - 1;
-            if ((unsigned)tid == owner) {
-                U r;  // below TOP: nothing in front of `cut` left the binade
-                if (cut < len) {
-                    const int e = (int)(cut - tid * E);
-                    U prev = 0;
-#pragma unroll
-                    for (int q = 0; q < E; ++q)
-                        if (q + 1 == e) prev = c[q];
-                    r = sat_add<U>(start, prev, SAT);
-                } else {
-                    r = sat_add<U>(start, run, SAT);
-                }
-                T s = value_of<T>((uint64_t)r, k);
-                if (cut < len) {
-                    const T t = F::add(s, F::value(sq[cut]));
-                    if (nonfinite_bits<T>(F::bits(t))) {
+            // below TOP: nothing in front of `cut` left the binade
+            const T sv = value_of<T>((uint64_t)(cut < len ? s_front[cut] : s_after), k);
+            if (cut < len) {
+                const T t = F::add(sv, F::value(sq[cut]));
+                if (nonfinite_bits<T>(F::bits(t))) {
+                    if (tid == 0) {
                         record_fault(status, (base + i0 + cut) * 3 + 2, kOverflow);
                         s_done = 2;
-                        s_pos = len;
-                    } else {
-                        s = t;
-                        s_pos = cut + 1;
                     }
+                    pos = len;
                 } else {
-                    s_pos = len;
+                    cur = t;
+                    pos = cut + 1;
                 }
-                s_sum = s;
-                s_stop[it ^ 1] = len;  // armed for the next iteration
+            } else {
+                cur = sv;
+                pos = len;
             }
-            __syncthreads();
         }
+        if (tid == 0) s_sum = cur;
         if (tid == 0) s_g = s_done == 2 ? stop : i0 + len;
         __syncthreads();
         if (s_done == 2) break;
