@@ -207,7 +207,6 @@ def main():
     a = a_full[r0:r0 + rows_per].contiguous()
     del a_full
     c_local = torch.empty((rows_per, N), dtype=torch.float32, device=device)
-    c_full = torch.empty((N, N), dtype=torch.float32, device=device) if world > 1 else c_local
     status = pcu.new_status(device=device)
     lib = pcu.library()
     ws_bytes = lib.pcu_b200_strict_matmul_workspace_size(rows_per, N, N)
@@ -215,10 +214,14 @@ def main():
 
     sharded = importlib.import_module("fusion-pcu_b200.sharded") if world > 1 else None
 
+    shared_c = sharded.PeerRows(N, N, torch.float32) if world > 1 else None
+
     def step():
         if world > 1:
-            # rank-local rows with global fault events, all-gather of C, global first fault
-            sharded.strict_matmul_rows(a, b, r0, c_local, status, gathered=c_full, workspace=workspace, stream=stream)
+            # this rank's rows with global fault events, written into every rank's C by the same
+            # kernel (peer stores over NVLink); the status all-reduce gives the global first fault
+            # and orders every rank's writes before the next use of C
+            sharded.strict_matmul_rows_allgather(a, b, r0, shared_c, status, workspace=workspace, stream=stream)
             sharded.all_reduce_min_status(status)
         else:
             pcu.strict_matmul(a, b, out=c_local, status=status, workspace=workspace, stream=stream)
@@ -287,6 +290,8 @@ def main():
         secondary = mse_sgd(torch, pcu, device, stream, hbm_gbs, args, rank, world)
 
     if world > 1:
+        torch.cuda.synchronize()
+        shared_c.close()  # barriers inside: no rank frees its C while a peer may still map it
         dist.barrier()
         dist.destroy_process_group()
     if rank != 0:
@@ -301,7 +306,8 @@ def main():
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": "strict checked F32 MatMul 8192^3 (BASELINE configs[1]), dyadic U[-1,1) seeded",
-                   "parallelism": f"row-sharded x{world}" + (" + NCCL all-gather of C" if world > 1 else ""),
+                   "parallelism": f"row-sharded x{world}" + (
+                       " + all-gather of C inside the MatMul kernel (peer stores over NVLink)" if world > 1 else ""),
                    "l2": "inputs (2 x 256 MiB) exceed the 126 MB L2; no flush needed"},
         # every rank copies its A row block and all of B in, its C row block and status out
         "e2e": {"value": FLOPS / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,

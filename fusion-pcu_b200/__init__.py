@@ -92,6 +92,12 @@ def _declare(L):
     L.pcu_b200_strict_matmul_host_scratch_size.argtypes = [i32, u64, u64, u64]
     L.pcu_b200_strict_matmul_host_scratch_size.restype = sz
     L.pcu_b200_strict_matmul_host.argtypes = [i32, i32, vp, vp, vp, u64, u64, u64, vp, sz, vp, vp]
+    L.pcu_b200_strict_matmul_rows_allgather.argtypes = [i32, i32, vp, vp, vp, u64, u64, u64, u64, u64, u64, u64, i32,
+                                                        ctypes.POINTER(vp), i32, vp, sz, vp, vp]
+    L.pcu_b200_peer_alloc.argtypes = [sz, ctypes.POINTER(vp), vp]
+    L.pcu_b200_peer_open.argtypes = [vp, ctypes.POINTER(vp)]
+    L.pcu_b200_peer_close.argtypes = [vp]
+    L.pcu_b200_peer_free.argtypes = [vp]
     L.pcu_b200_strict_sgd.argtypes = [i32, i32, vp, vp, vp, u64, u32, vp, vp]
     L.pcu_b200_strict_mse_workspace_size.argtypes = [i32, u64]
     L.pcu_b200_strict_mse_workspace_size.restype = sz

@@ -48,6 +48,8 @@
 
 namespace pcu {
 
+constexpr int kMaxPeers = 7;  // up to 8 GPUs of one node
+
 template <typename T> struct MatmulParams {
     const T *left;
     const T *right;
@@ -59,7 +61,19 @@ template <typename T> struct MatmulParams {
     unsigned long long *status;
     int vector_out;  // out is 16-byte aligned and columns is a multiple of the 16-byte vector
     ChainGuard guard;  // the node's stage of a guarded chain (empty when not guarded)
+    // A row block of a row-sharded product: every output element also goes to the same place in
+    // each peer's copy of C (peer memory mapped into this process), and events are shifted by
+    // event_base (the block's first cell times inner times 2) to the whole product's ordinals.
+    T *peer_out[kMaxPeers];
+    int npeers;
+    unsigned long long event_base;
 };
+
+// an output element (or 16-byte vector): this device's C and every peer's copy
+template <typename T, typename X> __device__ __forceinline__ void put_out(const MatmulParams<T> &p, uint64_t idx, X v) {
+    *reinterpret_cast<X *>(p.out + idx) = v;
+    for (int q = 0; q < p.npeers; ++q) *reinterpret_cast<X *>(p.peer_out[q] + idx) = v;
+}
 
 // "no nonzero finite element" marker of the exponent prescan (also the memset byte pattern)
 constexpr int kNoExponent = 0x10101010;
@@ -128,7 +142,7 @@ __device__ __forceinline__ T load_b(const MatmulParams<T> &p, uint64_t k, uint64
 template <typename T>
 __device__ __noinline__ void exact_cell(const MatmulParams<T> &p, uint64_t r, uint64_t c) {
     const uint64_t cell = r * p.columns + c;
-    const uint64_t base = cell * p.inner * 2;
+    const uint64_t base = p.event_base + cell * p.inner * 2;
     if (fault_precedes(p.status, base)) return;
     T acc = T(0);
     for (uint64_t k = 0; k < p.inner; ++k) {
@@ -139,7 +153,7 @@ __device__ __noinline__ void exact_cell(const MatmulParams<T> &p, uint64_t r, ui
         if (kind) { record_fault(p.status, base + 2 * k + 1, kind); return; }
         if ((k & 1023) == 1023 && fault_precedes(p.status, base + 2 * k)) return;
     }
-    p.out[cell] = acc;
+    put_out<T, T>(p, cell, acc);
 }
 
 // Does the fast result of cell (r, c) need the exact walk?
@@ -432,12 +446,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                     T *e = reinterpret_cast<T *>(&v);
 #pragma unroll
                     for (int q = 0; q < V; ++q) e[q] = acc[i][jg * V + q];
-                    *reinterpret_cast<VT *>(p.out + r * p.columns + c) = v;
+                    put_out<T, VT>(p, r * p.columns + c, v);
                 } else {
 #pragma unroll
                     for (int q = 0; q < V; ++q) {
                         if (needs_exact(p, acc[i][jg * V + q], rmin[i], cmin[jg * V + q])) exact_cell(p, r, c + q);
-                        else p.out[r * p.columns + c + q] = acc[i][jg * V + q];
+                        else put_out<T, T>(p, r * p.columns + c + q, acc[i][jg * V + q]);
                     }
                 }
             }
@@ -447,10 +461,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint64_t c = n0 + col_of(j);
                 if (c >= p.columns) continue;
                 if (needs_exact(p, acc[i][j], rmin[i], cmin[j])) exact_cell(p, r, c);
-                else p.out[r * p.columns + c] = acc[i][j];
+                else put_out<T, T>(p, r * p.columns + c, acc[i][j]);
             }
         }
     }
+    if (p.npeers) __threadfence_system();  // the peer stores are visible before the kernel ends
 }
 
 // Plain tiled kernel for operands TMA cannot describe (unaligned base or stride): 16x16
@@ -478,7 +493,8 @@ __global__ void __launch_bounds__(256) strict_matmul_generic_kernel(const __grid
     const int rmin = p.row_minexp ? p.row_minexp[r] : 0;
     const int cmin = p.col_minexp ? p.col_minexp[c] : 0;
     if (needs_exact(p, acc, rmin, cmin)) exact_cell(p, r, c);
-    else p.out[r * p.columns + c] = acc;
+    else put_out<T, T>(p, r * p.columns + c, acc);
+    if (p.npeers) __threadfence_system();
 }
 
 }  // namespace pcu
@@ -546,12 +562,16 @@ int launch_tma(const CUtensorMap &ma, const CUtensorMap &mb, const MatmulParams<
 template <typename T>
 int run_matmul(int policy, const T *left, const T *right, T *out, uint64_t rows, uint64_t inner, uint64_t columns,
                uint64_t lda, uint64_t ldb, int tl, int tr, void *workspace, size_t workspace_bytes,
-               unsigned long long *status, cudaStream_t stream, const ChainGuard &guard) {
+               unsigned long long *status, cudaStream_t stream, const ChainGuard &guard,
+               T *const *peer_outs = nullptr, int npeers = 0, unsigned long long event_base = 0) {
     MatmulParams<T> p{left,    right,   out,    rows,
                       inner,   columns, lda,    ldb,
                       tl,      tr,      policy, 0,
                       nullptr, nullptr, status, pcu_host::aligned(out, 16) && columns % (16 / sizeof(T)) == 0,
                       guard};
+    for (int q = 0; q < npeers; ++q) p.peer_out[q] = peer_outs[q];
+    p.npeers = npeers;
+    p.event_base = event_base;
     // the first kernel launched decides the stage's admission, the later ones follow it
     ChainGuard next = guard;
     auto take = [&]() {
@@ -732,4 +752,75 @@ extern "C" int pcu_b200_strict_matmul_static_scratch(int dtype, int policy, cons
     // a previous call left in the shared array never leak into this one.
     return pcu_b200_strict_matmul(dtype, policy, left, right, out, rows, inner, columns, left_stride, right_stride,
                                   transpose_left, transpose_right, scratch, kStaticScratchBytes, status, stream);
+}
+
+// ============================================================================
+// Row-sharded MatMul with the all-gather of C in the same kernel.  Every rank computes its rows
+// of C with the full ordered K loop; the epilogue writes each finished tile into this device's
+// C and, over NVLink, into every peer's C, so the all-gather overlaps the arithmetic tile by
+// tile instead of following it.  The peers' C buffers are mapped with CUDA IPC
+// (pcu_b200_peer_alloc / pcu_b200_peer_open).  Plain stores only: no TMA or bulk copy ever
+// reads or writes peer memory.
+// ============================================================================
+extern "C" int pcu_b200_strict_matmul_rows_allgather(int dtype, int policy, const void *left_rows, const void *right,
+                                                     void *out_full, uint64_t row0, uint64_t rows,
+                                                     uint64_t rows_total, uint64_t inner, uint64_t columns,
+                                                     uint64_t left_stride, uint64_t right_stride, int transpose_right,
+                                                     void *const *peer_outs, int npeers, void *workspace,
+                                                     size_t workspace_bytes, uint64_t *status, void *stream) {
+    if ((dtype != PCU_B200_F32 && dtype != PCU_B200_F64) || policy < 0 || policy > 2 || !status)
+        return PCU_B200_ERROR_INVALID_ARGUMENT;
+    if (npeers < 0 || npeers > kMaxPeers || (npeers && !peer_outs)) return PCU_B200_ERROR_INVALID_ARGUMENT;
+    if (row0 > rows_total || rows > rows_total - row0) return PCU_B200_ERROR_INVALID_ARGUMENT;
+    if (rows == 0 || columns == 0) return PCU_B200_OK;
+    if (!out_full || (inner > 0 && (!left_rows || !right))) return PCU_B200_ERROR_INVALID_ARGUMENT;
+    for (int q = 0; q < npeers; ++q)
+        if (!peer_outs[q]) return PCU_B200_ERROR_INVALID_ARGUMENT;
+    const uint64_t right_row_len = transpose_right ? inner : columns;
+    if (inner > 0 && (left_stride < inner || right_stride < right_row_len)) return PCU_B200_ERROR_INVALID_ARGUMENT;
+    unsigned __int128 events = (unsigned __int128)rows_total * columns;
+    events *= (inner ? inner : 1);
+    events *= 2;
+    if (events > ((unsigned __int128)1 << 60)) return PCU_B200_ERROR_SIZE_OVERFLOW;
+    const size_t elem = dtype == PCU_B200_F64 ? 8 : 4;
+    const unsigned long long event_base = (unsigned long long)row0 * columns * (inner ? inner : 1) * 2;
+    auto *st = reinterpret_cast<unsigned long long *>(status);
+    cudaStream_t s = pcu_host::as_stream(stream);
+    void *peers[kMaxPeers];
+    for (int q = 0; q < npeers; ++q) peers[q] = reinterpret_cast<char *>(peer_outs[q]) + row0 * columns * elem;
+    void *out = reinterpret_cast<char *>(out_full) + row0 * columns * elem;
+    if (dtype == PCU_B200_F32)
+        return run_matmul<float>(policy, (const float *)left_rows, (const float *)right, (float *)out, rows, inner,
+                                 columns, left_stride, right_stride, false, transpose_right != 0, workspace,
+                                 workspace_bytes, st, s, ChainGuard{}, reinterpret_cast<float *const *>(peers), npeers,
+                                 event_base);
+    return run_matmul<double>(policy, (const double *)left_rows, (const double *)right, (double *)out, rows, inner,
+                              columns, left_stride, right_stride, false, transpose_right != 0, workspace,
+                              workspace_bytes, st, s, ChainGuard{}, reinterpret_cast<double *const *>(peers), npeers,
+                              event_base);
+}
+
+extern "C" int pcu_b200_peer_alloc(size_t bytes, void **ptr, void *handle) {
+    if (!ptr || !handle || !bytes) return PCU_B200_ERROR_INVALID_ARGUMENT;
+    cudaError_t e = cudaMalloc(ptr, bytes);
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(reinterpret_cast<cudaIpcMemHandle_t *>(handle), *ptr);
+    return e == cudaSuccess ? PCU_B200_OK : pcu_host::set_cuda_error(e);
+}
+
+extern "C" int pcu_b200_peer_open(const void *handle, void **ptr) {
+    if (!ptr || !handle) return PCU_B200_ERROR_INVALID_ARGUMENT;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    const cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    return e == cudaSuccess ? PCU_B200_OK : pcu_host::set_cuda_error(e);
+}
+
+extern "C" int pcu_b200_peer_close(void *ptr) {
+    const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+    return e == cudaSuccess ? PCU_B200_OK : pcu_host::set_cuda_error(e);
+}
+
+extern "C" int pcu_b200_peer_free(void *ptr) {
+    const cudaError_t e = cudaFree(ptr);
+    return e == cudaSuccess ? PCU_B200_OK : pcu_host::set_cuda_error(e);
 }

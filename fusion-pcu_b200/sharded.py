@@ -102,6 +102,78 @@ def strict_sgd_block(weights, gradient, rate, first_index, status, out=None, pol
     return out
 
 
+class _CudaArray:
+    """A view of raw device memory that torch.as_tensor accepts (__cuda_array_interface__)."""
+
+    def __init__(self, ptr, shape, dtype):
+        typestr = {torch.float32: "<f4", torch.float64: "<f8"}[dtype]
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3}
+
+
+class PeerRows:
+    """A rows x columns matrix of which every rank holds a copy that all ranks write into (CUDA IPC,
+    pcu_b200_peer_alloc / _open): the destination of the fused row-sharded MatMul + all-gather.
+    `local` is this rank's copy (a torch view); `peer_ptrs` the peers' copies mapped here, in rank
+    order without this rank.  Only the provider's own kernels touch the peer copies."""
+
+    def __init__(self, rows, columns, dtype=torch.float32, group=None):
+        import ctypes
+
+        self.group = group
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        L = pcu.library()
+        elem = torch.empty((), dtype=dtype).element_size()
+        ptr, handle = ctypes.c_void_p(), (ctypes.c_ubyte * 64)()
+        pcu._check(L.pcu_b200_peer_alloc(rows * columns * elem, ctypes.byref(ptr), handle))
+        self._ptr = ptr.value
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.peer_ptrs = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                continue
+            hb = (ctypes.c_ubyte * 64).from_buffer_copy(h)
+            q = ctypes.c_void_p()
+            pcu._check(L.pcu_b200_peer_open(hb, ctypes.byref(q)))
+            self.peer_ptrs.append(q.value)
+        self.rows, self.columns, self.dtype = rows, columns, dtype
+        self.local = torch.as_tensor(_CudaArray(self._ptr, (rows, columns), dtype), device="cuda")
+
+    def close(self):
+        """Unmap the peers' copies and free this one (every rank, after its last use)."""
+        L = pcu.library()
+        dist.barrier(group=self.group)
+        for q in self.peer_ptrs:
+            L.pcu_b200_peer_close(q)
+        self.peer_ptrs = []
+        dist.barrier(group=self.group)
+        if self._ptr:
+            L.pcu_b200_peer_free(self._ptr)
+            self._ptr = None
+
+
+def strict_matmul_rows_allgather(left_rows, right, row0, shared, status, transpose_right=False, policy=0,
+                                 workspace=None, stream=None):
+    """Rows [row0, row0 + m) of C = A . op(B) in one kernel with their all-gather: written into
+    `shared.local` and every peer's copy (PeerRows), events global.  Follow with a collective
+    (all_reduce_min_status) before reading C: it orders every rank's call before the read."""
+    import ctypes
+
+    L = pcu.library()
+    rows, inner = left_rows.shape
+    cols = right.shape[0] if transpose_right else right.shape[1]
+    if workspace is None:
+        workspace = torch.empty(max(L.pcu_b200_strict_matmul_workspace_size(rows, inner, cols), 1), dtype=torch.uint8,
+                                device=left_rows.device)
+    peers = (ctypes.c_void_p * max(len(shared.peer_ptrs), 1))(*shared.peer_ptrs)
+    pcu._check(L.pcu_b200_strict_matmul_rows_allgather(
+        pcu._dtype_code(left_rows), policy, pcu._ptr(left_rows), pcu._ptr(right), ctypes.c_void_p(shared._ptr), row0,
+        rows, shared.rows, inner, cols, left_rows.stride(0), right.stride(0), int(transpose_right), peers,
+        len(shared.peer_ptrs), pcu._ptr(workspace), workspace.numel(), pcu._ptr(status), pcu._stream(stream)))
+    return shared.local
+
+
 # ------------------------------------------------------------------------------- MSE
 class ShardedMse:
     """Strict MSE over a tensor split into contiguous segments, one per rank (ordered hand-off).

@@ -153,6 +153,34 @@ int pcu_b200_strict_matmul_host(int dtype, int policy, const void *left, const v
                                 uint64_t inner, uint64_t columns, void *device_scratch, size_t scratch_bytes,
                                 uint64_t *status_host, void *stream);
 
+/* Row-sharded strict MatMul with the all-gather of C in the same kernel.  This rank computes rows
+ * [row0, row0 + rows) of the rows_total x columns product C = A . op(B) (left_rows: this rank's
+ * rows of A, rows x inner with row stride left_stride; right: B as in pcu_b200_strict_matmul,
+ * transpose_right allowed) with the full ordered K loop.  Each finished output tile is written
+ * into out_full (this device's whole C, rows_total x columns, dense) and into every peer's C at
+ * the same place: peer_outs holds npeers (<= 7) device pointers of the peers' C, mapped into this
+ * process with pcu_b200_peer_open.  So the transfer overlaps the arithmetic tile by tile, with
+ * plain NVLink stores (no TMA or bulk copy touches peer memory).  The status word holds the
+ * whole product's event ordinals (cells offset by row0 * columns); the global first fault is the
+ * MIN of all ranks' words.  The kernel ends with a system-scope fence; a peer's rows are complete
+ * in this rank's C once every rank's call has finished, which the caller establishes with a
+ * collective (the status all-reduce) after the call.  No counterpart in the reference (its
+ * strict MatMul runs on one device). */
+int pcu_b200_strict_matmul_rows_allgather(int dtype, int policy, const void *left_rows, const void *right,
+                                          void *out_full, uint64_t row0, uint64_t rows, uint64_t rows_total,
+                                          uint64_t inner, uint64_t columns, uint64_t left_stride,
+                                          uint64_t right_stride, int transpose_right, void *const *peer_outs,
+                                          int npeers, void *workspace, size_t workspace_bytes, uint64_t *status,
+                                          void *stream);
+
+/* CUDA IPC for the buffers peers write into: allocate `bytes` of device memory and its 64-byte
+ * IPC handle; map a peer's buffer from its handle (into this process, on the current device);
+ * unmap; free. */
+int pcu_b200_peer_alloc(size_t bytes, void **ptr, void *handle);
+int pcu_b200_peer_open(const void *handle, void **ptr);
+int pcu_b200_peer_close(void *ptr);
+int pcu_b200_peer_free(void *ptr);
+
 /* ------------------------------------------------------------------ strict SGD */
 
 /* out[i] = weights[i] - rate * gradient[i] with the multiply and the subtract separately

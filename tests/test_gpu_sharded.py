@@ -160,3 +160,78 @@ def test_nccl_sharded_matches_one_device():
         assert mean_bits == bits(mse_out)[0]
     sgd_all = np.concatenate([got[r][3] for r in range(world)])
     assert np.array_equal(sgd_all, bits(sgd_out))
+
+
+def _fused_worker(rank, world, port, queue):
+    """Row-sharded MatMul with the all-gather inside the kernel (peer stores into every rank's C)."""
+    import torch
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    import datetime
+
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    shared = []
+    try:
+        sharded = importlib.import_module("fusion-pcu_b200.sharded")
+        results = []
+        # (m, k, n, fault): a TMA-path product (many 128-wide tiles), a small one (16x16 tiles),
+        # and a fault in a late rank's rows
+        for m, k, n, fault in ((2048, 256, 1536, None), (256, 100, 96, None), (2048, 128, 1024, (1900, 5))):
+            rng = np.random.default_rng(m + k + n)
+            a = dyadic_uniform(rng, (m, k), 32)
+            b = dyadic_uniform(rng, (k, n), 32)
+            if fault:
+                a[fault] = np.nan
+            rows = m // world
+            r0 = rank * rows
+            sh = sharded.PeerRows(m, n, torch.float32)
+            shared.append(sh)
+            sh.local.fill_(-7.0)
+            status = pcu.new_status()
+            sharded.strict_matmul_rows_allgather(to_device(a[r0:r0 + rows]), to_device(b), r0, sh, status)
+            sharded.all_reduce_min_status(status)
+            torch.cuda.synchronize()
+            results.append((status_word(status), bits(to_host(sh.local))))
+        queue.put((rank, results))
+    finally:
+        for sh in shared:
+            sh.close()
+        dist.destroy_process_group()
+
+
+def test_fused_rows_allgather_matches_one_device():
+    import torch
+
+    world = min(torch.cuda.device_count(), 4)
+    if world < 2:
+        pytest.skip("needs 2 or more GPUs")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_fused_worker, args=(r, world, port, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(queue.get(timeout=300) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for case, (m, k, n, fault) in enumerate(((2048, 256, 1536, None), (256, 100, 96, None), (2048, 128, 1024, (1900, 5)))):
+        rng = np.random.default_rng(m + k + n)
+        a = dyadic_uniform(rng, (m, k), 32)
+        b = dyadic_uniform(rng, (k, n), 32)
+        if fault:
+            a[fault] = np.nan
+        status = pcu.new_status()
+        want = pcu.strict_matmul(to_device(a), to_device(b), status=status)
+        torch.cuda.synchronize()
+        want_word = status_word(status)
+        for rank in range(world):
+            word, c_bits = got[rank][case]
+            assert word == want_word, (case, rank, hex(word), hex(want_word))
+            if want_word == pcu.STATUS_OK:  # every rank holds the whole product
+                assert np.array_equal(c_bits, bits(to_host(want))), (case, rank)
