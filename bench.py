@@ -232,11 +232,15 @@ def main():
     word = int(status.cpu().numpy().view(np.uint64)[0])
     assert word == pcu.STATUS_OK, f"unexpected fault {word:#x}"
 
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
+        # the barrier comes after every rank's sampler is running (their start-up times differ),
+        # so that all ranks enter the timed region together: the per-step collective would
+        # otherwise charge the early ranks with waiting for the late ones
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
         start.record(stream)
         for _ in range(args.steps):
             step()

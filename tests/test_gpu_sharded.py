@@ -190,6 +190,8 @@ def _fused_worker(rank, world, port, queue):
             sh = sharded.PeerRows(m, n, torch.float32)
             shared.append(sh)
             sh.local.fill_(-7.0)
+            torch.cuda.synchronize()
+            dist.barrier()  # every rank's C is filled before any peer writes into it
             status = pcu.new_status()
             sharded.strict_matmul_rows_allgather(to_device(a[r0:r0 + rows]), to_device(b), r0, sh, status)
             sharded.all_reduce_min_status(status)
