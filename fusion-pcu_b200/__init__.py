@@ -21,7 +21,7 @@ __all__ = [
     "matmul_host_scratch", "strict_sgd",
     "strict_mse", "mse_workspace", "strict_mse_segment_prepare", "strict_mse_segment_walk", "strict_mse_sgd",
     "strict_mse_sgd_segment_prepare", "strict_mse_sgd_segment", "checked_binary", "checked_relu", "checked_relu_backward", "matmul_fault", "sgd_fault",
-    "mse_fault", "element_fault",
+    "mse_fault", "element_fault", "GuardedChain", "CHAIN_OUTCOMES", "chain_validate", "wait",
 ]
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
@@ -112,6 +112,16 @@ def _declare(L):
     L.pcu_b200_checked_binary.argtypes = [i32, i32, i32, vp, vp, vp, u64, i32, i32, vp, vp]
     L.pcu_b200_checked_relu.argtypes = [i32, i32, vp, vp, u64, vp, vp]
     L.pcu_b200_checked_relu_backward.argtypes = [i32, i32, vp, vp, vp, u64, vp, vp]
+    L.pcu_b200_chain_reset.argtypes = [vp, u32, vp]
+    L.pcu_b200_guarded_strict_matmul.argtypes = [i32, i32, vp, vp, vp, u64, u64, u64, u64, u64, i32, i32, vp, sz, vp,
+                                                 u32, vp]
+    L.pcu_b200_guarded_strict_sgd.argtypes = [i32, i32, vp, vp, vp, u64, u32, vp, u32, vp]
+    L.pcu_b200_guarded_strict_mse.argtypes = [i32, i32, vp, vp, vp, u64, vp, sz, vp, u32, vp]
+    L.pcu_b200_guarded_checked_binary.argtypes = [i32, i32, i32, vp, vp, vp, u64, i32, i32, vp, u32, vp]
+    L.pcu_b200_guarded_checked_relu.argtypes = [i32, i32, vp, vp, u64, vp, u32, vp]
+    L.pcu_b200_guarded_checked_relu_backward.argtypes = [i32, i32, vp, vp, vp, u64, vp, u32, vp]
+    L.pcu_b200_chain_validate.argtypes = [vp, u32, vp, ctypes.POINTER(i32), ctypes.POINTER(u32)]
+    L.pcu_b200_wait.argtypes = [vp, u32]
 
 
 def _torch():
@@ -146,6 +156,16 @@ def _stream(stream):
 
 def _ptr(t):
     return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _node(name, args, status, chain, stream):
+    """pcu_b200_<name>(*args, status, stream); with chain=(records, stage), the guarded form
+    pcu_b200_guarded_<name>(*args, records, stage, stream) as one stage of a GuardedChain."""
+    L = library()
+    if chain is None:
+        return getattr(L, "pcu_b200_" + name)(*args, _ptr(status), _stream(stream))
+    records, stage = chain
+    return getattr(L, "pcu_b200_guarded_" + name)(*args, _ptr(records), int(stage), _stream(stream))
 
 
 def new_status(count=1, device=None, stream=None):
@@ -215,10 +235,11 @@ def element_fault(word, count, value=None):
 
 # ------------------------------------------------------------------ kernel-level calls
 # Each returns the output tensor; faults stay in `status` (device) until the caller reads it,
-# exactly like the reference's one-status-word-per-node protocol.
+# exactly like the reference's one-status-word-per-node protocol.  `chain=GuardedChain.stage(s)`
+# runs the call as stage s of a guarded chain instead (its status word is in the chain's slab).
 
 def strict_matmul(left, right, transpose_left=False, transpose_right=False, policy=0, out=None, status=None,
-                  workspace=None, stream=None):
+                  workspace=None, stream=None, chain=None):
     torch = _torch()
     assert left.dim() == 2 and right.dim() == 2 and left.dtype == right.dtype
     assert (left.numel() == 0 or left.stride(1) == 1) and (right.numel() == 0 or right.stride(1) == 1), \
@@ -230,16 +251,15 @@ def strict_matmul(left, right, transpose_left=False, transpose_right=False, poli
     L = library()
     if out is None:
         out = torch.empty((rows, cols), dtype=left.dtype, device=left.device)
-    if status is None:
+    if status is None and chain is None:
         status = new_status(device=left.device)
     need = L.pcu_b200_strict_matmul_workspace_size(rows, inner, cols)
     if workspace is None or workspace.numel() < need:
         workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=left.device)
-    _check(L.pcu_b200_strict_matmul(_dtype_code(left), policy, _ptr(left), _ptr(right), _ptr(out), rows, inner,
-                                    cols, max(left.stride(0), left.shape[1]), max(right.stride(0), right.shape[1]),
-                                    int(transpose_left),
-                                    int(transpose_right), _ptr(workspace), workspace.numel(), _ptr(status),
-                                    _stream(stream)))
+    _check(_node("strict_matmul", (_dtype_code(left), policy, _ptr(left), _ptr(right), _ptr(out), rows, inner, cols,
+                                   max(left.stride(0), left.shape[1]), max(right.stride(0), right.shape[1]),
+                                   int(transpose_left), int(transpose_right), _ptr(workspace), workspace.numel()),
+                 status, chain, stream))
     return out
 
 
@@ -274,33 +294,33 @@ def strict_matmul_host(left, right, policy=0, out=None, status=None, scratch=Non
     return out, status
 
 
-def strict_sgd(weights, gradient, rate, policy=0, out=None, status=None, stream=None):
+def strict_sgd(weights, gradient, rate, policy=0, out=None, status=None, stream=None, chain=None):
     torch = _torch()
     assert weights.is_contiguous() and gradient.is_contiguous() and weights.numel() == gradient.numel()
     if out is None:
         out = torch.empty_like(weights)
-    if status is None:
+    if status is None and chain is None:
         status = new_status(device=weights.device)
     rate_bits = int(np.array([rate], dtype=np.float32).view(np.uint32)[0])
-    _check(library().pcu_b200_strict_sgd(_dtype_code(weights), policy, _ptr(weights), _ptr(gradient), _ptr(out),
-                                         weights.numel(), rate_bits, _ptr(status), _stream(stream)))
+    _check(_node("strict_sgd", (_dtype_code(weights), policy, _ptr(weights), _ptr(gradient), _ptr(out),
+                                weights.numel(), rate_bits), status, chain, stream))
     return out
 
 
-def strict_mse(prediction, target, policy=0, out=None, status=None, workspace=None, stream=None):
+def strict_mse(prediction, target, policy=0, out=None, status=None, workspace=None, stream=None, chain=None):
     torch = _torch()
     assert prediction.is_contiguous() and target.is_contiguous() and prediction.numel() == target.numel()
     L = library()
     n = prediction.numel()
     if out is None:
         out = torch.empty((), dtype=prediction.dtype, device=prediction.device)
-    if status is None:
+    if status is None and chain is None:
         status = new_status(device=prediction.device)
     need = L.pcu_b200_strict_mse_workspace_size(_dtype_code(prediction), n)
     if workspace is None or workspace.numel() < need:
         workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=prediction.device)
-    _check(L.pcu_b200_strict_mse(_dtype_code(prediction), policy, _ptr(prediction), _ptr(target), _ptr(out), n,
-                                 _ptr(workspace), workspace.numel(), _ptr(status), _stream(stream)))
+    _check(_node("strict_mse", (_dtype_code(prediction), policy, _ptr(prediction), _ptr(target), _ptr(out), n,
+                                _ptr(workspace), workspace.numel()), status, chain, stream))
     return out
 
 
@@ -408,37 +428,103 @@ def strict_mse_sgd_segment(prediction, target, first_index, total_count, carry_i
 
 
 def checked_binary(op, left, right, policy=0, left_uniform=False, right_uniform=False, out=None, status=None,
-                   stream=None):
+                   stream=None, chain=None):
     torch = _torch()
     n = max(1 if left_uniform else left.numel(), 1 if right_uniform else right.numel())
     shape = right.shape if left_uniform else left.shape
     if out is None:
         out = torch.empty(shape, dtype=left.dtype, device=left.device)
-    if status is None:
+    if status is None and chain is None:
         status = new_status(device=left.device)
-    _check(library().pcu_b200_checked_binary(_dtype_code(left), policy, OPS.get(op, op), _ptr(left), _ptr(right),
-                                             _ptr(out), n, int(left_uniform), int(right_uniform), _ptr(status),
-                                             _stream(stream)))
+    _check(_node("checked_binary", (_dtype_code(left), policy, OPS.get(op, op), _ptr(left), _ptr(right), _ptr(out), n,
+                                    int(left_uniform), int(right_uniform)), status, chain, stream))
     return out
 
 
-def checked_relu(x, policy=0, out=None, status=None, stream=None):
+def checked_relu(x, policy=0, out=None, status=None, stream=None, chain=None):
     torch = _torch()
     if out is None:
         out = torch.empty_like(x)
-    if status is None:
+    if status is None and chain is None:
         status = new_status(device=x.device)
-    _check(library().pcu_b200_checked_relu(_dtype_code(x), policy, _ptr(x), _ptr(out), x.numel(), _ptr(status),
-                                           _stream(stream)))
+    _check(_node("checked_relu", (_dtype_code(x), policy, _ptr(x), _ptr(out), x.numel()), status, chain, stream))
     return out
 
 
-def checked_relu_backward(x, upstream, policy=0, out=None, status=None, stream=None):
+def checked_relu_backward(x, upstream, policy=0, out=None, status=None, stream=None, chain=None):
     torch = _torch()
     if out is None:
         out = torch.empty_like(x)
-    if status is None:
+    if status is None and chain is None:
         status = new_status(device=x.device)
-    _check(library().pcu_b200_checked_relu_backward(_dtype_code(x), policy, _ptr(x), _ptr(upstream), _ptr(out),
-                                                    x.numel(), _ptr(status), _stream(stream)))
+    _check(_node("checked_relu_backward", (_dtype_code(x), policy, _ptr(x), _ptr(upstream), _ptr(out), x.numel()),
+                 status, chain, stream))
     return out
+
+
+# ------------------------------------------------------------------ guarded chains
+
+CHAIN_OUTCOMES = {0: "succeeded", 1: "fault", 2: "stage_decode", 3: "unexpected_skip", 4: "executed_after_fault"}
+
+
+def chain_validate(records, extents=None):
+    """Checks a chain's record slab read back to the host (uint64 array, [word, disposition] per
+    stage), as validate_guarded_execution does (Crates/core/runtime/execution/guarded/guarded.rs:
+    107-140).  Returns (outcome, stage), outcome one of CHAIN_OUTCOMES's names; host code only."""
+    recs = np.ascontiguousarray(np.asarray(records, dtype=np.uint64).reshape(-1))
+    if recs.size % 2:
+        raise ValueError("a chain slab holds two words per stage")
+    stages = recs.size // 2
+    ext = None
+    if extents is not None:
+        ext = np.ascontiguousarray(np.asarray(extents, dtype=np.uint64).reshape(-1))
+        if ext.size != stages:
+            raise ValueError("one event extent per stage")
+    outcome, stage = ctypes.c_int(-1), ctypes.c_uint32(0)
+    _check(library().pcu_b200_chain_validate(recs.ctypes.data_as(ctypes.c_void_p), stages,
+                                             ext.ctypes.data_as(ctypes.c_void_p) if ext is not None else None,
+                                             ctypes.byref(outcome), ctypes.byref(stage)))
+    return CHAIN_OUTCOMES[outcome.value], stage.value
+
+
+class GuardedChain:
+    """The record slab of one ordered, stop-on-fault chain of node calls on one stream
+    (Crates/backends/cuda/tensor/guarded/guarded.rs:355-400): [fault word, disposition] per stage.
+    Pass `chain=g.stage(s)` to the node calls in stage order; `validate()` reads the slab once."""
+
+    def __init__(self, stages, device=None):
+        torch = _torch()
+        self.stages = int(stages)
+        self.records = torch.empty(2 * max(self.stages, 1), dtype=torch.int64, device=device or "cuda")
+
+    def reset(self, stream=None):
+        _check(library().pcu_b200_chain_reset(_ptr(self.records), self.stages, _stream(stream)))
+        return self
+
+    def stage(self, s):
+        if not 0 <= s < self.stages:
+            raise IndexError(f"stage {s} of a {self.stages}-stage chain")
+        return (self.records, s)
+
+    def read(self, stream=None):
+        """The slab as uint64 on the host (waits for the stream)."""
+        torch = _torch()
+        s = stream if stream is not None else torch.cuda.current_stream()
+        with torch.cuda.stream(s):
+            host = self.records[:2 * self.stages].cpu()
+        return host.numpy().view(np.uint64)
+
+    def validate(self, extents=None, stream=None):
+        """(outcome, stage, fault word of that stage)."""
+        recs = self.read(stream)
+        outcome, stage = chain_validate(recs, extents)
+        return outcome, stage, int(recs[2 * stage]) if self.stages else STATUS_OK
+
+
+def wait(stream=None, timeout_ms=1000):
+    """True when all work on `stream` has completed within timeout_ms, False if it has not."""
+    rc = library().pcu_b200_wait(_stream(stream), int(timeout_ms))
+    if rc == 6:
+        return False
+    _check(rc)
+    return True

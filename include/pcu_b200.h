@@ -81,6 +81,7 @@ extern "C" {
 #define PCU_B200_ERROR_WORKSPACE 3
 #define PCU_B200_ERROR_CUDA 4
 #define PCU_B200_ERROR_UNSUPPORTED 5
+#define PCU_B200_ERROR_TIMEOUT 6
 
 /* ------------------------------------------------------------------ library */
 
@@ -284,6 +285,84 @@ int pcu_b200_checked_relu(int dtype, int policy, const void *input, void *out, u
  * (scalar_checked_float.rs:634-652). */
 int pcu_b200_checked_relu_backward(int dtype, int policy, const void *input, const void *upstream, void *out,
                                    uint64_t count, uint64_t *status, void *stream);
+
+/* ------------------------------------------------------------------ guarded chains
+ *
+ * An ordered, stop-on-fault chain of node calls on one stream, without a host wait between them.
+ * This replaces the guarded kernel ABI of the reference's owned dispatch, where the status
+ * argument `u64* fault_word` becomes `(u64* chain_records, u32 chain_stage)`
+ * (Crates/backends/cuda/owned_dispatch/guarded/guarded.rs, guarded_source).  It also replaces the
+ * record slab that Crates/backends/cuda/tensor/guarded/guarded.rs:355-400 initialises, submits and
+ * reads back.
+ *
+ * Records: one slab of 2 x stages u64 words.  Record s is [fault word, disposition].
+ *   * The fault word is stage s's status word (sentinel PCU_B200_STATUS_OK).
+ *   * The disposition is PENDING until stage s's first kernel decides it.  Stage s is admitted
+ *     (EXECUTED) when s == 0, or when record s-1 is EXECUTED with a clear fault word.  Otherwise
+ *     it is SKIPPED, and none of its kernels writes anything.
+ *
+ * pcu_b200_guarded_* take the arguments of the unguarded call of the same name, with `status`
+ * replaced by (chain_records, chain_stage).  Stage numbers are the order of submission on the
+ * stream, from 0.  The chain's calls must all be on one stream (or ordered by events).
+ * The host reads the slab back once, after the last stage, and checks it with
+ * pcu_b200_chain_validate. */
+#define PCU_B200_CHAIN_PENDING 0
+#define PCU_B200_CHAIN_EXECUTED 1
+#define PCU_B200_CHAIN_SKIPPED 2
+
+/* Every record to [PCU_B200_STATUS_OK, PENDING], ordered on `stream`. */
+int pcu_b200_chain_reset(uint64_t *chain_records, uint32_t stages, void *stream);
+
+int pcu_b200_guarded_strict_matmul(int dtype, int policy, const void *left, const void *right, void *out,
+                                   uint64_t rows, uint64_t inner, uint64_t columns, uint64_t left_stride,
+                                   uint64_t right_stride, int transpose_left, int transpose_right, void *workspace,
+                                   size_t workspace_bytes, uint64_t *chain_records, uint32_t chain_stage,
+                                   void *stream);
+int pcu_b200_guarded_strict_sgd(int dtype, int policy, const void *weights, const void *gradient, void *out,
+                                uint64_t count, uint32_t rate_bits_f32, uint64_t *chain_records, uint32_t chain_stage,
+                                void *stream);
+int pcu_b200_guarded_strict_mse(int dtype, int policy, const void *prediction, const void *target, void *out,
+                                uint64_t count, void *workspace, size_t workspace_bytes, uint64_t *chain_records,
+                                uint32_t chain_stage, void *stream);
+int pcu_b200_guarded_checked_binary(int dtype, int policy, int op, const void *left, const void *right, void *out,
+                                    uint64_t count, int left_uniform, int right_uniform, uint64_t *chain_records,
+                                    uint32_t chain_stage, void *stream);
+int pcu_b200_guarded_checked_relu(int dtype, int policy, const void *input, void *out, uint64_t count,
+                                  uint64_t *chain_records, uint32_t chain_stage, void *stream);
+int pcu_b200_guarded_checked_relu_backward(int dtype, int policy, const void *input, const void *upstream,
+                                           void *out, uint64_t count, uint64_t *chain_records, uint32_t chain_stage,
+                                           void *stream);
+
+/* Outcomes of pcu_b200_chain_validate (Crates/core/runtime/execution/guarded/guarded.rs:84-140). */
+#define PCU_B200_CHAIN_SUCCEEDED 0           /* every stage executed without a fault */
+#define PCU_B200_CHAIN_FAULT 1               /* *stage: the first faulting stage; every later one skipped */
+#define PCU_B200_CHAIN_STAGE_DECODE 2        /* *stage: a pending or unknown disposition, a fault word on a
+                                                skipped stage, or a fault word no node call writes */
+#define PCU_B200_CHAIN_UNEXPECTED_SKIP 3     /* *stage: skipped although no earlier stage faulted */
+#define PCU_B200_CHAIN_EXECUTED_AFTER_FAULT 4 /* *stage: executed after an earlier fault */
+
+/* Checks a record slab that was read back to HOST memory after the chain completed.  Host
+ * code only; it makes no CUDA call.  Stages are decoded in order, and the first decode error
+ * or order violation is reported, so an earlier fault cannot hide a later bad record.  Only
+ * PCU_B200_CHAIN_SUCCEEDED and PCU_B200_CHAIN_FAULT mean that the outputs may be published.
+ *
+ * A fault word decodes when its kind is one that node calls write: DIVIDE_BY_ZERO, OVERFLOW,
+ * UNDERFLOW or INVALID.  SIGNED_DIVISION_OVERFLOW and a watchdog word are decode errors.
+ * `event_extents` is optional.  When it is given, stage s's event must also be below
+ * event_extents[s]: rows*columns*inner*2 for MatMul, 2n for SGD, 3n+1 for MSE, n for the
+ * elementwise calls.
+ * The return value is PCU_B200_OK or PCU_B200_ERROR_INVALID_ARGUMENT; the outcome goes to
+ * *outcome, and *stage is the stage it names (0 for SUCCEEDED). */
+int pcu_b200_chain_validate(const uint64_t *chain_records, uint32_t stages, const uint64_t *event_extents,
+                            int *outcome, uint32_t *stage);
+
+/* ------------------------------------------------------------------ waiting */
+
+/* Waits until all work submitted to `stream` has completed, for at most timeout_ms
+ * milliseconds.  The other calls of this library never block the host; this one does,
+ * by polling.  Returns PCU_B200_OK when the work has completed, PCU_B200_ERROR_TIMEOUT when
+ * it has not, and PCU_B200_ERROR_CUDA for an error that the stream reports. */
+int pcu_b200_wait(void *stream, uint32_t timeout_ms);
 
 #ifdef __cplusplus
 }
