@@ -122,6 +122,20 @@ def _declare(L):
     L.pcu_b200_guarded_checked_relu_backward.argtypes = [i32, i32, vp, vp, vp, u64, vp, u32, vp]
     L.pcu_b200_chain_validate.argtypes = [vp, u32, vp, ctypes.POINTER(i32), ctypes.POINTER(u32)]
     L.pcu_b200_wait.argtypes = [vp, u32]
+    L.pcu_b200_last_comm_error.restype = i32
+    L.pcu_b200_comm_unique_id.argtypes = [vp]
+    L.pcu_b200_comm_init.argtypes = [vp, i32, i32, ctypes.POINTER(vp)]
+    L.pcu_b200_comm_free.argtypes = [vp]
+    L.pcu_b200_comm_abort.argtypes = [vp]
+    L.pcu_b200_comm_status_min.argtypes = [vp, vp, u64, vp]
+    L.pcu_b200_comm_send.argtypes = [vp, vp, sz, i32, vp]
+    L.pcu_b200_comm_recv.argtypes = [vp, vp, sz, i32, vp]
+    L.pcu_b200_comm_broadcast.argtypes = [vp, vp, sz, i32, vp]
+    L.pcu_b200_comm_peer_buffers.argtypes = [vp, sz, ctypes.POINTER(vp), vp]
+    L.pcu_b200_comm_peer_buffers_free.argtypes = [vp, ctypes.POINTER(vp), vp]
+    L.pcu_b200_comm_strict_matmul_rows.argtypes = [vp, i32, i32, vp, vp, ctypes.POINTER(vp), u64, u64, u64, u64, u64,
+                                                   u64, u64, i32, vp, sz, vp, vp]
+    L.pcu_b200_comm_strict_mse.argtypes = [vp, i32, i32, vp, vp, u64, u64, u64, vp, vp, vp, sz, vp, vp]
 
 
 def _torch():
@@ -136,7 +150,8 @@ def _check(rc):
     if rc != 0:
         L = library()
         msg = L.pcu_b200_error_string(rc).decode()
-        raise ProviderFailure(f"pcu_b200 error {rc}: {msg} (cuda error {L.pcu_b200_last_cuda_error()})")
+        raise ProviderFailure(f"pcu_b200 error {rc}: {msg} (cuda error {L.pcu_b200_last_cuda_error()}, "
+                              f"nccl error {L.pcu_b200_last_comm_error()})")
 
 
 def _dtype_code(t):

@@ -96,6 +96,7 @@ extern "C" const char *pcu_b200_error_string(int code) {
     case PCU_B200_ERROR_CUDA: return "CUDA launch or configuration failure (see pcu_b200_last_cuda_error)";
     case PCU_B200_ERROR_UNSUPPORTED: return "unsupported on this device";
     case PCU_B200_ERROR_TIMEOUT: return "the stream's work did not complete within the timeout";
+    case PCU_B200_ERROR_COMM: return "communicator failure (NCCL; see pcu_b200_last_comm_error)";
     default: return "unknown error";
     }
 }

@@ -1,0 +1,286 @@
+// comm.cu -- the exchange steps of the multi-GPU paths behind the C ABI, for a host that has no
+// communicator of its own (one process per GPU):
+//   * the global first fault: an unsigned MIN of the ranks' status words (NCCL's Uint64 MIN is
+//     unsigned, so the no-fault sentinel, all ones, stays the largest word);
+//   * point-to-point hand-offs and broadcasts of device scalars (the running sum of a split MSE);
+//   * the exchange of peer-buffer IPC handles for the row-sharded MatMul whose all-gather is
+//     inside the kernel, and that MatMul with its fault MIN as one call;
+//   * the split strict MSE with its ordered hand-off as one call.
+//
+// NCCL is loaded at run time (dlopen of libnccl.so.2) when the first communicator is made, so the
+// library has no load-time dependency on it.  A process that has already loaded NCCL (through
+// torch.distributed, say) gets that same copy back from dlopen.
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <cstring>
+#include <mutex>
+#include <new>
+#include <type_traits>
+#include <vector>
+
+#include "common.cuh"
+#include "pcu_b200.h"
+
+struct pcu_b200_comm {
+    ncclComm_t comm;
+    int nranks, rank;
+    uint64_t *scratch;  // device words: [0] the unused SGD status of a segment call, [1] barrier
+};
+
+namespace {
+
+constexpr int kMaxRanks = 8;  // one rank per GPU of one node: the row-sharded MatMul takes <= 7 peers
+constexpr size_t kHandleBytes = 64;
+
+struct Nccl {
+    decltype(&ncclGetUniqueId) get_unique_id = nullptr;
+    decltype(&ncclCommInitRank) init_rank = nullptr;
+    decltype(&ncclCommDestroy) destroy = nullptr;
+    decltype(&ncclCommAbort) abort = nullptr;
+    decltype(&ncclAllReduce) all_reduce = nullptr;
+    decltype(&ncclAllGather) all_gather = nullptr;
+    decltype(&ncclBroadcast) broadcast = nullptr;
+    decltype(&ncclSend) send = nullptr;
+    decltype(&ncclRecv) recv = nullptr;
+    bool ok = false;
+};
+
+const Nccl &nccl() {
+    static Nccl n;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_LOCAL);
+        if (!h) return;
+        bool all = true;
+        auto bind = [&](auto &fn, const char *name) {
+            fn = reinterpret_cast<std::remove_reference_t<decltype(fn)>>(dlsym(h, name));
+            all = all && fn != nullptr;
+        };
+        bind(n.get_unique_id, "ncclGetUniqueId");
+        bind(n.init_rank, "ncclCommInitRank");
+        bind(n.destroy, "ncclCommDestroy");
+        bind(n.abort, "ncclCommAbort");
+        bind(n.all_reduce, "ncclAllReduce");
+        bind(n.all_gather, "ncclAllGather");
+        bind(n.broadcast, "ncclBroadcast");
+        bind(n.send, "ncclSend");
+        bind(n.recv, "ncclRecv");
+        n.ok = all;
+    });
+    return n;
+}
+
+thread_local int g_last_comm_error = 0;
+
+int comm_status(ncclResult_t r) {
+    if (r == ncclSuccess) return PCU_B200_OK;
+    g_last_comm_error = (int)r;
+    return PCU_B200_ERROR_COMM;
+}
+
+int cuda_status(cudaError_t e) { return e == cudaSuccess ? PCU_B200_OK : pcu_host::set_cuda_error(e); }
+
+bool usable(const pcu_b200_comm *c) { return c && c->comm; }
+
+// Every rank reaches this point before any goes on (host and device): a one-word all-reduce,
+// then a wait for it.
+int barrier(pcu_b200_comm *c, cudaStream_t s) {
+    int rc = comm_status(nccl().all_reduce(c->scratch + 1, c->scratch + 1, 1, ncclUint64, ncclMin, c->comm, s));
+    if (rc) return rc;
+    return cuda_status(cudaStreamSynchronize(s));
+}
+
+}  // namespace
+
+extern "C" int pcu_b200_last_comm_error(void) { return g_last_comm_error; }
+
+extern "C" int pcu_b200_comm_unique_id(void *id) {
+    if (!id) return PCU_B200_ERROR_INVALID_ARGUMENT;
+    const Nccl &n = nccl();
+    if (!n.ok) return PCU_B200_ERROR_UNSUPPORTED;
+    ncclUniqueId u;
+    if (int rc = comm_status(n.get_unique_id(&u))) return rc;
+    static_assert(sizeof(u) == PCU_B200_COMM_ID_BYTES, "NCCL unique id size");
+    memcpy(id, &u, sizeof(u));
+    return PCU_B200_OK;
+}
+
+extern "C" int pcu_b200_comm_init(const void *id, int nranks, int rank, pcu_b200_comm **comm) {
+    if (!comm) return PCU_B200_ERROR_INVALID_ARGUMENT;
+    *comm = nullptr;
+    if (!id || nranks < 1 || nranks > kMaxRanks || rank < 0 || rank >= nranks) return PCU_B200_ERROR_INVALID_ARGUMENT;
+    const Nccl &n = nccl();
+    if (!n.ok) return PCU_B200_ERROR_UNSUPPORTED;
+    auto *c = new (std::nothrow) pcu_b200_comm{};
+    if (!c) return PCU_B200_ERROR_INVALID_ARGUMENT;
+    c->nranks = nranks;
+    c->rank = rank;
+    int rc = cuda_status(cudaMalloc(reinterpret_cast<void **>(&c->scratch), 2 * sizeof(uint64_t)));
+    if (!rc) rc = cuda_status(cudaMemset(c->scratch, 0xff, 2 * sizeof(uint64_t)));
+    ncclUniqueId u;
+    memcpy(&u, id, sizeof(u));
+    if (!rc) rc = comm_status(n.init_rank(&c->comm, nranks, u, rank));
+    if (rc) {
+        if (c->scratch) cudaFree(c->scratch);
+        delete c;
+        return rc;
+    }
+    *comm = c;
+    return PCU_B200_OK;
+}
+
+extern "C" int pcu_b200_comm_free(pcu_b200_comm *comm) {
+    if (!comm) return PCU_B200_OK;
+    int rc = comm->comm ? comm_status(nccl().destroy(comm->comm)) : PCU_B200_OK;
+    if (comm->scratch) cudaFree(comm->scratch);
+    delete comm;
+    return rc;
+}
+
+extern "C" int pcu_b200_comm_abort(pcu_b200_comm *comm) {
+    if (!comm) return PCU_B200_OK;
+    int rc = comm->comm ? comm_status(nccl().abort(comm->comm)) : PCU_B200_OK;
+    if (comm->scratch) cudaFree(comm->scratch);
+    delete comm;
+    return rc;
+}
+
+extern "C" int pcu_b200_comm_status_min(pcu_b200_comm *comm, uint64_t *status, uint64_t count, void *stream) {
+    if (!usable(comm) || (count && !status)) return PCU_B200_ERROR_INVALID_ARGUMENT;
+    if (count == 0) return PCU_B200_OK;
+    return comm_status(nccl().all_reduce(status, status, count, ncclUint64, ncclMin, comm->comm,
+                                         pcu_host::as_stream(stream)));
+}
+
+extern "C" int pcu_b200_comm_send(pcu_b200_comm *comm, const void *buffer, size_t bytes, int peer, void *stream) {
+    if (!usable(comm) || peer < 0 || peer >= comm->nranks || peer == comm->rank || (bytes && !buffer))
+        return PCU_B200_ERROR_INVALID_ARGUMENT;
+    return comm_status(nccl().send(buffer, bytes, ncclUint8, peer, comm->comm, pcu_host::as_stream(stream)));
+}
+
+extern "C" int pcu_b200_comm_recv(pcu_b200_comm *comm, void *buffer, size_t bytes, int peer, void *stream) {
+    if (!usable(comm) || peer < 0 || peer >= comm->nranks || peer == comm->rank || (bytes && !buffer))
+        return PCU_B200_ERROR_INVALID_ARGUMENT;
+    return comm_status(nccl().recv(buffer, bytes, ncclUint8, peer, comm->comm, pcu_host::as_stream(stream)));
+}
+
+extern "C" int pcu_b200_comm_broadcast(pcu_b200_comm *comm, void *buffer, size_t bytes, int root, void *stream) {
+    if (!usable(comm) || root < 0 || root >= comm->nranks || (bytes && !buffer))
+        return PCU_B200_ERROR_INVALID_ARGUMENT;
+    return comm_status(
+        nccl().broadcast(buffer, buffer, bytes, ncclUint8, root, comm->comm, pcu_host::as_stream(stream)));
+}
+
+// Each rank allocates its buffer with an IPC handle; the handles are all-gathered through a
+// device staging array; each rank maps the others'.  Blocks until every rank has its mappings.
+extern "C" int pcu_b200_comm_peer_buffers(pcu_b200_comm *comm, size_t bytes, void **buffers, void *stream) {
+    if (!usable(comm) || !bytes || !buffers) return PCU_B200_ERROR_INVALID_ARGUMENT;
+    const int n = comm->nranks, me = comm->rank;
+    cudaStream_t s = pcu_host::as_stream(stream);
+    for (int r = 0; r < n; ++r) buffers[r] = nullptr;
+    unsigned char handle[kHandleBytes];
+    int rc = pcu_b200_peer_alloc(bytes, &buffers[me], handle);
+    if (rc) return rc;
+    unsigned char *staging = nullptr;
+    std::vector<unsigned char> all(n * kHandleBytes);
+    rc = cuda_status(cudaMalloc(reinterpret_cast<void **>(&staging), n * kHandleBytes));
+    if (!rc) rc = cuda_status(cudaMemcpyAsync(staging + me * kHandleBytes, handle, kHandleBytes, cudaMemcpyHostToDevice, s));
+    if (!rc)
+        rc = comm_status(nccl().all_gather(staging + me * kHandleBytes, staging, kHandleBytes, ncclUint8, comm->comm, s));
+    if (!rc) rc = cuda_status(cudaMemcpyAsync(all.data(), staging, all.size(), cudaMemcpyDeviceToHost, s));
+    if (!rc) rc = cuda_status(cudaStreamSynchronize(s));
+    if (staging) cudaFree(staging);
+    for (int r = 0; r < n && !rc; ++r)
+        if (r != me) rc = pcu_b200_peer_open(all.data() + r * kHandleBytes, &buffers[r]);
+    if (rc) {
+        for (int r = 0; r < n; ++r)
+            if (r != me && buffers[r]) pcu_b200_peer_close(buffers[r]);
+        pcu_b200_peer_free(buffers[me]);
+        for (int r = 0; r < n; ++r) buffers[r] = nullptr;
+    }
+    return rc;
+}
+
+// Unmap the peers' buffers, wait until every rank has done so, then free this rank's own.
+extern "C" int pcu_b200_comm_peer_buffers_free(pcu_b200_comm *comm, void **buffers, void *stream) {
+    if (!usable(comm) || !buffers) return PCU_B200_ERROR_INVALID_ARGUMENT;
+    const int me = comm->rank;
+    cudaStream_t s = pcu_host::as_stream(stream);
+    int rc = cuda_status(cudaStreamSynchronize(s));
+    for (int r = 0; r < comm->nranks; ++r)
+        if (r != me && buffers[r]) {
+            const int e = pcu_b200_peer_close(buffers[r]);
+            rc = rc ? rc : e;
+            buffers[r] = nullptr;
+        }
+    const int b = barrier(comm, s);
+    rc = rc ? rc : b;
+    if (buffers[me]) {
+        const int e = pcu_b200_peer_free(buffers[me]);
+        rc = rc ? rc : e;
+        buffers[me] = nullptr;
+    }
+    return rc;
+}
+
+// Rows [row0, row0 + rows) of C = A . op(B) with the all-gather of C in the kernel
+// (pcu_b200_strict_matmul_rows_allgather into buffers[rank] and every peer's buffer), then the
+// status MIN that orders every rank's stores before C is read.
+extern "C" int pcu_b200_comm_strict_matmul_rows(pcu_b200_comm *comm, int dtype, int policy, const void *left_rows,
+                                                const void *right, void *const *buffers, uint64_t row0, uint64_t rows,
+                                                uint64_t rows_total, uint64_t inner, uint64_t columns,
+                                                uint64_t left_stride, uint64_t right_stride, int transpose_right,
+                                                void *workspace, size_t workspace_bytes, uint64_t *status,
+                                                void *stream) {
+    if (!usable(comm) || !buffers || !status) return PCU_B200_ERROR_INVALID_ARGUMENT;
+    void *peers[kMaxRanks - 1];
+    int np = 0;
+    for (int r = 0; r < comm->nranks; ++r)
+        if (r != comm->rank) peers[np++] = buffers[r];
+    int rc = pcu_b200_strict_matmul_rows_allgather(dtype, policy, left_rows, right, buffers[comm->rank], row0, rows,
+                                                   rows_total, inner, columns, left_stride, right_stride,
+                                                   transpose_right, peers, np, workspace, workspace_bytes, status,
+                                                   stream);
+    if (rc) return rc;
+    return pcu_b200_comm_status_min(comm, status, 1, stream);
+}
+
+// A strict MSE over total_count elements split into contiguous segments, rank r holding the
+// global elements [first_index, first_index + count): rank 0 maps and walks its segment in one
+// launch; every other rank builds its maps at once, receives the running sum from rank r - 1,
+// walks and sends it on to rank r + 1.  The last rank's mean is broadcast to out on every rank,
+// and the status words are combined by MIN.
+extern "C" int pcu_b200_comm_strict_mse(pcu_b200_comm *comm, int dtype, int policy, const void *prediction,
+                                        const void *target, uint64_t count, uint64_t first_index, uint64_t total_count,
+                                        void *carry, void *out, void *workspace, size_t workspace_bytes,
+                                        uint64_t *status, void *stream) {
+    if (!usable(comm) || !carry || !out || !status || (dtype != PCU_B200_F32 && dtype != PCU_B200_F64))
+        return PCU_B200_ERROR_INVALID_ARGUMENT;
+    if (count == 0 || first_index > total_count || count > total_count - first_index)
+        return PCU_B200_ERROR_INVALID_ARGUMENT;
+    const int me = comm->rank, last = comm->nranks - 1;
+    const size_t elem = dtype == PCU_B200_F32 ? 4 : 8;
+    const bool tail = first_index + count == total_count;
+    cudaStream_t s = pcu_host::as_stream(stream);
+    int rc;
+    if (me == 0) {
+        rc = cuda_status(cudaMemsetAsync(comm->scratch, 0xff, sizeof(uint64_t), s));
+        if (!rc)
+            rc = pcu_b200_strict_mse_sgd_segment(dtype, policy, prediction, target, count, first_index, total_count,
+                                                 nullptr, carry, tail ? out : nullptr, workspace, workspace_bytes,
+                                                 status, nullptr, nullptr, nullptr, 0, 0, 0, comm->scratch, stream);
+    } else {
+        rc = pcu_b200_strict_mse_segment_prepare(dtype, policy, prediction, target, count, first_index, workspace,
+                                                 workspace_bytes, status, stream);
+        if (!rc) rc = pcu_b200_comm_recv(comm, carry, elem, me - 1, stream);
+        if (!rc)
+            rc = pcu_b200_strict_mse_segment_walk(dtype, policy, prediction, target, count, first_index, total_count,
+                                                  carry, carry, tail ? out : nullptr, workspace, workspace_bytes,
+                                                  status, stream);
+    }
+    if (!rc && me < last) rc = pcu_b200_comm_send(comm, carry, elem, me + 1, stream);
+    if (!rc) rc = pcu_b200_comm_broadcast(comm, out, elem, last, stream);
+    if (!rc) rc = pcu_b200_comm_status_min(comm, status, 1, stream);
+    return rc;
+}

@@ -364,6 +364,79 @@ int pcu_b200_chain_validate(const uint64_t *chain_records, uint32_t stages, cons
  * it has not, and PCU_B200_ERROR_CUDA for an error that the stream reports. */
 int pcu_b200_wait(void *stream, uint32_t timeout_ms);
 
+/* ------------------------------------------------------------------ multi-GPU exchange steps
+ *
+ * A communicator over the ranks of one job, one process per GPU (at most 8, one node), for a
+ * host that has none of its own.  It carries the exchange steps of the split paths:
+ *   * the global first fault, an unsigned MIN of the ranks' status words;
+ *   * the running-sum hand-off of a split MSE;
+ *   * the exchange of peer-buffer handles for the row-sharded MatMul.
+ * The all-gather of that MatMul's C happens inside the MatMul kernel.  None of this has a
+ * counterpart in the reference, whose strict path runs on one device.
+ *
+ * NCCL is loaded at run time (dlopen of libnccl.so.2) by the first call here.  The library has
+ * no load-time dependency on it, and a process that already loaded NCCL reuses that copy.
+ *   * PCU_B200_ERROR_UNSUPPORTED: NCCL could not be loaded.
+ *   * PCU_B200_ERROR_COMM: NCCL returned an error; pcu_b200_last_comm_error gives its code.
+ *
+ * Every rank makes the same collective calls in the same order.  The calls enqueue work on
+ * `stream` and return without waiting, except pcu_b200_comm_init (which waits for every rank to
+ * join) and the two peer-buffer calls.  A call that fails on one rank returns before its
+ * collective and leaves the other ranks waiting in theirs.  The host then bounds its wait with
+ * pcu_b200_wait and aborts the communicator on every rank with pcu_b200_comm_abort. */
+#define PCU_B200_ERROR_COMM 7
+#define PCU_B200_COMM_ID_BYTES 128
+typedef struct pcu_b200_comm pcu_b200_comm;
+
+int pcu_b200_last_comm_error(void);
+
+/* Rank 0 makes the id (PCU_B200_COMM_ID_BYTES bytes); the host hands it to every rank, which
+ * then calls init on its own GPU (the current device) with the job's rank count and its rank. */
+int pcu_b200_comm_unique_id(void *id);
+int pcu_b200_comm_init(const void *id, int nranks, int rank, pcu_b200_comm **comm);
+int pcu_b200_comm_free(pcu_b200_comm *comm);
+int pcu_b200_comm_abort(pcu_b200_comm *comm);
+
+/* status[0..count) becomes the unsigned MIN over ranks, on every rank (all-reduce).  The status
+ * words must carry global events, as every split call here writes them. */
+int pcu_b200_comm_status_min(pcu_b200_comm *comm, uint64_t *status, uint64_t count, void *stream);
+
+/* Device bytes to or from one peer (a matching send and recv), and a broadcast from `root`. */
+int pcu_b200_comm_send(pcu_b200_comm *comm, const void *buffer, size_t bytes, int peer, void *stream);
+int pcu_b200_comm_recv(pcu_b200_comm *comm, void *buffer, size_t bytes, int peer, void *stream);
+int pcu_b200_comm_broadcast(pcu_b200_comm *comm, void *buffer, size_t bytes, int root, void *stream);
+
+/* Collective.  Every rank allocates `bytes` of device memory that the others map with CUDA IPC.
+ * buffers[r] (nranks entries) is rank r's buffer as this process sees it; buffers[rank] is this
+ * rank's own.  Returns once this rank has mapped every peer.  _free unmaps the peers, waits for
+ * every rank to do the same, and frees this rank's buffer. */
+int pcu_b200_comm_peer_buffers(pcu_b200_comm *comm, size_t bytes, void **buffers, void *stream);
+int pcu_b200_comm_peer_buffers_free(pcu_b200_comm *comm, void **buffers, void *stream);
+
+/* The row-sharded strict MatMul in one call.  It runs pcu_b200_strict_matmul_rows_allgather for
+ * rows [row0, row0 + rows) into buffers[rank] and every peer's buffer (buffers from
+ * pcu_b200_comm_peer_buffers, rows_total x columns each), then the status MIN.  When the work on
+ * `stream` is done, every rank's buffers[rank] holds all of C and `status` holds the global
+ * first fault.  C must not be read on any rank after the next call has been made on another. */
+int pcu_b200_comm_strict_matmul_rows(pcu_b200_comm *comm, int dtype, int policy, const void *left_rows,
+                                     const void *right, void *const *buffers, uint64_t row0, uint64_t rows,
+                                     uint64_t rows_total, uint64_t inner, uint64_t columns, uint64_t left_stride,
+                                     uint64_t right_stride, int transpose_right, void *workspace,
+                                     size_t workspace_bytes, uint64_t *status, void *stream);
+
+/* A strict MSE over total_count elements split into contiguous, non-empty segments in rank
+ * order.  Rank r holds the global elements [first_index, first_index + count), and the last rank
+ * ends at total_count.
+ *   * Rank 0 builds its maps and walks them in one launch.
+ *   * Every other rank builds its maps at once, receives the running sum from rank r - 1 into
+ *     `carry` (a device scalar), walks, and sends the sum on to rank r + 1.
+ * The checked mean is broadcast into out[0] on every rank, and `status` becomes the global first
+ * fault.  The result equals pcu_b200_strict_mse over the whole tensor.  The workspace is
+ * pcu_b200_strict_mse_workspace_size(dtype, count). */
+int pcu_b200_comm_strict_mse(pcu_b200_comm *comm, int dtype, int policy, const void *prediction, const void *target,
+                             uint64_t count, uint64_t first_index, uint64_t total_count, void *carry, void *out,
+                             void *workspace, size_t workspace_bytes, uint64_t *status, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
