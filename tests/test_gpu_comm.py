@@ -161,3 +161,49 @@ def test_communicator_split_paths_match_one_device():
             assert word == want_word, (case, rank, hex(word), hex(want_word))
             if want_word == OK:
                 assert out_bits == want_bits == int(bits(out_o)[0]), (case, rank)
+
+
+def test_one_rank_communicator_matches_one_device():
+    """A communicator of one rank (runs on one GPU): NCCL loaded at run time, the status MIN and
+    broadcast as identities, the peer-buffer exchange with no peers, the row-sharded MatMul as the
+    whole product and the split MSE as one segment, then abort."""
+    import torch
+
+    cm = importlib.import_module("fusion-pcu_b200.comm")
+    pcu = importlib.import_module("fusion-pcu_b200")
+    comm = cm.Communicator(cm.Communicator.unique_id(), 1, 0)
+    try:
+        words = np.array([OK, (7 << 3) | 4], dtype=np.uint64)
+        st = torch.from_numpy(words.view(np.int64).copy()).cuda()
+        comm.status_min(st)
+        x = torch.arange(5, dtype=torch.float64, device="cuda")
+        comm.broadcast(x, 0)
+        torch.cuda.synchronize()
+        assert list(st.cpu().numpy().view(np.uint64)) == list(words)
+        assert np.array_equal(to_host(x), np.arange(5.0))
+        for case in (0, 1, 3, 5):
+            a, b = _mm_inputs(case)
+            ad, bd = to_device(a), to_device(b)
+            shared = comm.peer_matrix(a.shape[0], b.shape[1], ad.dtype)
+            status = pcu.new_status()
+            comm.strict_matmul_rows(ad, bd, 0, shared, status)
+            want_status = pcu.new_status()
+            want = pcu.strict_matmul(ad, bd, status=want_status)
+            torch.cuda.synchronize()
+            assert status_word(status) == status_word(want_status), case
+            if status_word(status) == OK:
+                assert np.array_equal(bits(to_host(shared.local)), bits(to_host(want))), case
+            shared.close()
+        for case in range(len(MSE_CASES)):
+            p, t = _mse_inputs(case)
+            pd, td = to_device(p), to_device(t)
+            out = torch.zeros((), dtype=pd.dtype, device="cuda")
+            status = pcu.new_status()
+            comm.strict_mse(pd, td, 0, p.size, out, status)
+            torch.cuda.synchronize()
+            st_o, out_o = oracle.mse(p, t)
+            assert status_word(status) == st_o, case
+            if st_o == OK:
+                assert int(bits(to_host(out).reshape(1))[0]) == int(bits(out_o)[0]), case
+    finally:
+        comm.abort()
