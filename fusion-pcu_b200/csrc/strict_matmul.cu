@@ -49,9 +49,6 @@
 namespace pcu {
 
 constexpr int kMaxPeers = 7;  // up to 8 GPUs of one node
-#ifndef PCU_MM_PEER_FENCE
-#define PCU_MM_PEER_FENCE 1
-#endif
 
 template <typename T> struct MatmulParams {
     const T *left;
@@ -468,7 +465,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     }
-    if (PCU_MM_PEER_FENCE && p.npeers) __threadfence_system();  // the peer stores are visible before the kernel ends
+    if (p.npeers) __threadfence_system();  // the peer stores are visible before the kernel ends
 }
 
 // Plain tiled kernel for operands TMA cannot describe (unaligned base or stride): 16x16
@@ -497,7 +494,7 @@ __global__ void __launch_bounds__(256) strict_matmul_generic_kernel(const __grid
     const int cmin = p.col_minexp ? p.col_minexp[c] : 0;
     if (needs_exact(p, acc, rmin, cmin)) exact_cell(p, r, c);
     else put_out<T, T>(p, r * p.columns + c, acc);
-    if (PCU_MM_PEER_FENCE && p.npeers) __threadfence_system();
+    if (p.npeers) __threadfence_system();
 }
 
 }  // namespace pcu
