@@ -246,19 +246,20 @@ def test_matmul_1024_full(provider, width):
     _matmul_case(provider, a, b, False, True, 0, fast_oracle=True)
 
 
-def test_matmul_8192_sampled_cells(provider):
-    """BASELINE config 2 at full size: 512 random cells re-derived by the soft-float law."""
+@pytest.mark.parametrize("m,k,n", [(8192, 8192, 8192), (2048, 2048, 2048), (4096, 4096, 4096), (8192, 1024, 16384)])
+def test_matmul_sweep_sampled_cells(provider, m, k, n):
+    """BASELINE config 2 at full size (the square sweep and the 8192x1024 . 1024x16384 case):
+    512 random cells of each product re-derived by the soft-float law."""
     import torch
 
-    rng = np.random.default_rng(8192)
-    n = 8192
-    a = dyadic_uniform(rng, (n, n), 32)
-    b = dyadic_uniform(rng, (n, n), 32)
+    rng = np.random.default_rng(8192 if (m, k, n) == (8192, 8192, 8192) else m + 3 * k + 7 * n)
+    a = dyadic_uniform(rng, (m, k), 32)
+    b = dyadic_uniform(rng, (k, n), 32)
     status = provider.new_status()
     out = provider.strict_matmul(to_device(a), to_device(b), status=status)
     torch.cuda.synchronize()
     assert status_word(status) == provider.STATUS_OK
-    cells = rng.choice(n * n, size=512, replace=False).astype(np.uint64)
+    cells = rng.choice(m * n, size=512, replace=False).astype(np.uint64)
     s_o, vals = oracle.matmul_cells(a, b, cells)
     assert s_o == oracle.STATUS_OK
     got = to_host(out).reshape(-1)[cells.astype(np.int64)]
