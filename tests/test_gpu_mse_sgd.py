@@ -204,3 +204,32 @@ def test_one_call_first_segment_then_walks(width, case):
         assert bits(to_host(mean).reshape(1))[0] == bits(mse_out)[0]
     if sgd_st == oracle.STATUS_OK:
         assert np.array_equal(bits(to_host(upd)), bits(sgd_out))
+
+
+def test_bench_workload_matches_oracle():
+    """BASELINE configuration 5 exactly as bench.py times it: 2^28 binary32 elements per array,
+    drawn on the device by the bench's generator (seeds 11..14: weights, gradient, prediction,
+    target; k * 2^-23 with k uniform in [-2^23, 2^23)), lr = f32(0.01).  The fused call's mean and
+    updated weights equal the oracle's bit for bit."""
+    import torch
+
+    n = 1 << 28
+
+    def block(seed):
+        gen = torch.Generator(device="cuda")
+        gen.manual_seed(seed)
+        k = torch.randint(-(1 << 23), 1 << 23, (n,), generator=gen, device="cuda", dtype=torch.int32)
+        return k.to(torch.float32) * (2.0 ** -23)
+
+    w, g, p, t = block(11), block(12), block(13), block(14)
+    ms, ss = pcu.new_status(), pcu.new_status()
+    loss, upd = pcu.strict_mse_sgd(p, t, w, g, RATE, mse_status=ms, sgd_status=ss)
+    torch.cuda.synchronize()
+    assert status_word(ms) == status_word(ss) == oracle.STATUS_OK
+    loss_bits, upd_bits = bits(to_host(loss).reshape(1))[0], bits(to_host(upd))
+    del upd
+    mse_st, mse_out = oracle.mse(to_host(p), to_host(t))
+    assert mse_st == oracle.STATUS_OK and loss_bits == bits(mse_out)[0]
+    del p, t
+    sgd_st, sgd_out = oracle.sgd(to_host(w), to_host(g), RATE)
+    assert sgd_st == oracle.STATUS_OK and np.array_equal(upd_bits, bits(sgd_out))
