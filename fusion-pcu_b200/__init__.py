@@ -92,8 +92,13 @@ def _declare(L):
     L.pcu_b200_strict_matmul_host_scratch_size.argtypes = [i32, u64, u64, u64]
     L.pcu_b200_strict_matmul_host_scratch_size.restype = sz
     L.pcu_b200_strict_matmul_host.argtypes = [i32, i32, vp, vp, vp, u64, u64, u64, vp, sz, vp, vp]
+    L.pcu_b200_issue_probe_ops.argtypes = [i32, u64]
+    L.pcu_b200_issue_probe_ops.restype = u64
+    L.pcu_b200_issue_probe.argtypes = [i32, u64, vp]
+    L.pcu_b200_peer_rows_bytes.argtypes = [i32, u64, u64]
+    L.pcu_b200_peer_rows_bytes.restype = sz
     L.pcu_b200_strict_matmul_rows_allgather.argtypes = [i32, i32, vp, vp, vp, u64, u64, u64, u64, u64, u64, u64, i32,
-                                                        ctypes.POINTER(vp), i32, vp, sz, vp, vp]
+                                                        ctypes.POINTER(vp), i32, i32, u64, vp, sz, vp, vp]
     L.pcu_b200_peer_alloc.argtypes = [sz, ctypes.POINTER(vp), vp]
     L.pcu_b200_peer_open.argtypes = [vp, ctypes.POINTER(vp)]
     L.pcu_b200_peer_close.argtypes = [vp]

@@ -16,7 +16,7 @@ CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(ROOT, "_build", "provider")
 LIBRARY = os.path.join(HERE, "libpcu_b200.so")
 SOURCES = ["abi.cu", "streaming.cu", "strict_matmul.cu", "strict_mse.cu", "tensor_graph.cu", "host_staging.cu",
-           "comm.cu"]
+           "comm.cu", "calibrate.cu"]
 HEADERS = ["checked_law.cuh", "common.cuh", "provider.h"]
 
 NVCC = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"

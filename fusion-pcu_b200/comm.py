@@ -104,10 +104,10 @@ class PeerMatrix:
 
     def __init__(self, comm, rows, columns, dtype, stream=None):
         self.comm, self.rows, self.columns, self.dtype = comm, rows, columns, dtype
-        elem = torch.empty((), dtype=dtype).element_size()
+        L = pcu.library()
         self.buffers = (ctypes.c_void_p * comm.nranks)()
-        pcu._check(pcu.library().pcu_b200_comm_peer_buffers(comm._c, rows * columns * elem, self.buffers,
-                                                             pcu._stream(stream)))
+        nbytes = L.pcu_b200_peer_rows_bytes(0 if dtype == torch.float32 else 1, rows, columns)
+        pcu._check(L.pcu_b200_comm_peer_buffers(comm._c, nbytes, self.buffers, pcu._stream(stream)))
         self.local = torch.as_tensor(_cuda_array(self.buffers[comm.rank], (rows, columns), dtype), device="cuda")
 
     def close(self, stream=None):

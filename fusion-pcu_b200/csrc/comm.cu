@@ -17,6 +17,7 @@
 #include <mutex>
 #include <new>
 #include <type_traits>
+#include <utility>
 #include <vector>
 
 #include "common.cuh"
@@ -26,6 +27,10 @@ struct pcu_b200_comm {
     ncclComm_t comm;
     int nranks, rank;
     uint64_t *scratch;  // device words: [0] the unused SGD status of a segment call, [1] barrier
+    // Calls made so far on each set of peer buffers (keyed by this rank's buffer): the call
+    // number of the row-sharded MatMul's write-side order.  Every rank makes the same calls, so
+    // the counts agree across ranks.
+    std::vector<std::pair<void *, uint64_t>> calls;
 };
 
 namespace {
@@ -198,7 +203,9 @@ extern "C" int pcu_b200_comm_peer_buffers(pcu_b200_comm *comm, size_t bytes, voi
             if (r != me && buffers[r]) pcu_b200_peer_close(buffers[r]);
         pcu_b200_peer_free(buffers[me]);
         for (int r = 0; r < n; ++r) buffers[r] = nullptr;
+        return rc;
     }
+    comm->calls.emplace_back(buffers[me], 0);
     return rc;
 }
 
@@ -216,6 +223,11 @@ extern "C" int pcu_b200_comm_peer_buffers_free(pcu_b200_comm *comm, void **buffe
         }
     const int b = barrier(comm, s);
     rc = rc ? rc : b;
+    for (size_t i = 0; i < comm->calls.size(); ++i)
+        if (comm->calls[i].first == buffers[me]) {
+            comm->calls.erase(comm->calls.begin() + i);
+            break;
+        }
     if (buffers[me]) {
         const int e = pcu_b200_peer_free(buffers[me]);
         rc = rc ? rc : e;
@@ -226,7 +238,8 @@ extern "C" int pcu_b200_comm_peer_buffers_free(pcu_b200_comm *comm, void **buffe
 
 // Rows [row0, row0 + rows) of C = A . op(B) with the all-gather of C in the kernel
 // (pcu_b200_strict_matmul_rows_allgather into buffers[rank] and every peer's buffer), then the
-// status MIN that orders every rank's stores before C is read.
+// status MIN that orders every rank's stores before C is read.  The call number on this buffer
+// set orders the stores after the peers' reads of the previous call's C.
 extern "C" int pcu_b200_comm_strict_matmul_rows(pcu_b200_comm *comm, int dtype, int policy, const void *left_rows,
                                                 const void *right, void *const *buffers, uint64_t row0, uint64_t rows,
                                                 uint64_t rows_total, uint64_t inner, uint64_t columns,
@@ -234,15 +247,20 @@ extern "C" int pcu_b200_comm_strict_matmul_rows(pcu_b200_comm *comm, int dtype, 
                                                 void *workspace, size_t workspace_bytes, uint64_t *status,
                                                 void *stream) {
     if (!usable(comm) || !buffers || !status) return PCU_B200_ERROR_INVALID_ARGUMENT;
+    uint64_t *calls = nullptr;
+    for (auto &entry : comm->calls)
+        if (entry.first == buffers[comm->rank]) calls = &entry.second;
+    if (!calls) return PCU_B200_ERROR_INVALID_ARGUMENT;  // not a buffer set of this communicator
     void *peers[kMaxRanks - 1];
     int np = 0;
     for (int r = 0; r < comm->nranks; ++r)
         if (r != comm->rank) peers[np++] = buffers[r];
     int rc = pcu_b200_strict_matmul_rows_allgather(dtype, policy, left_rows, right, buffers[comm->rank], row0, rows,
                                                    rows_total, inner, columns, left_stride, right_stride,
-                                                   transpose_right, peers, np, workspace, workspace_bytes, status,
-                                                   stream);
+                                                   transpose_right, peers, np, comm->rank, *calls + 1, workspace,
+                                                   workspace_bytes, status, stream);
     if (rc) return rc;
+    ++*calls;
     return pcu_b200_comm_status_min(comm, status, 1, stream);
 }
 

@@ -73,6 +73,9 @@ __device__ __forceinline__ unsigned long long global_ns() {
 // Every device-side wait in this library gives up after this long and reports
 // kWatchdog in the status word instead of spinning forever.
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+// Waits on another GPU's progress (a peer process entering the same call) allow for host-side
+// skew between the ranks' processes as well, so they give up later.
+constexpr unsigned long long kPeerWaitLimitNs = 10000000000ull;
 
 }  // namespace pcu
 

@@ -30,6 +30,7 @@
 
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 #include "pcu_b200.h"
@@ -67,12 +68,58 @@ template <typename T> struct MatmulParams {
     T *peer_out[kMaxPeers];
     int npeers;
     unsigned long long event_base;
+    // Write-after-read order of the peer stores (the "entered" words of the peer buffers):
+    // every CTA stores `epoch` into signal[q], this rank's word in peer q's flag block, when it
+    // starts; before its first peer store it waits until await_[q], peer q's word in this rank's
+    // block, has reached `epoch`, i.e. until peer q's kernel of the same call has started and so
+    // every earlier kernel on that peer's stream (the readers of its C) has finished.
+    unsigned long long *signal[kMaxPeers];
+    const unsigned long long *await_[kMaxPeers];
+    unsigned long long epoch;
+    // CTA schedule: the launch covers linear tiles [tile_first, tile_first + gridDim.x / split)
+    // of a tiles_m x tiles_n grid of (16 * Tile<T>::TM) x BN tiles, visited in the grouped
+    // order; with split 2 each CTA computes one half (BM rows) of a tile.
+    unsigned tiles_m, tiles_n, tile_first;
+    int split;
 };
 
-// an output element (or 16-byte vector): this device's C and every peer's copy
-template <typename T, typename X> __device__ __forceinline__ void put_out(const MatmulParams<T> &p, uint64_t idx, X v) {
+// an output element (or 16-byte vector): this device's C and the first np peers' copies
+template <typename T, typename X>
+__device__ __forceinline__ void put_out(const MatmulParams<T> &p, int np, uint64_t idx, X v) {
     *reinterpret_cast<X *>(p.out + idx) = v;
-    for (int q = 0; q < p.npeers; ++q) *reinterpret_cast<X *>(p.peer_out[q] + idx) = v;
+    for (int q = 0; q < np; ++q) *reinterpret_cast<X *>(p.peer_out[q] + idx) = v;
+}
+
+// Every CTA of a row-sharded call announces, in each peer's flag block, that this rank has
+// entered call `epoch` (one thread; plain system-scope stores over NVLink).
+template <typename T> __device__ __forceinline__ void announce_entry(const MatmulParams<T> &p) {
+    if (!p.npeers || threadIdx.x != 0) return;
+    for (int q = 0; q < p.npeers; ++q)
+        asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p.signal[q]), "l"(p.epoch) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long load_acquire_sys(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Thread 0: how many peers this CTA may store into.  It waits (bounded) until every peer has
+// entered this call; a peer that has not within kPeerWaitLimitNs gets no stores, and the
+// status word records kWatchdog (event 0), which also tells later CTAs not to wait again.
+template <typename T> __device__ __noinline__ int peers_entered(const MatmulParams<T> &p) {
+    constexpr unsigned long long kGaveUp = (0ull << 3) | kWatchdog;
+    const unsigned long long t0 = global_ns();
+    for (int q = 0; q < p.npeers; ++q) {
+        while (load_acquire_sys(p.await_[q]) < p.epoch) {
+            if (read_status(p.status) == kGaveUp || global_ns() - t0 > kPeerWaitLimitNs) {
+                record_fault(p.status, 0, kWatchdog);
+                return 0;
+            }
+            __nanosleep(256);
+        }
+    }
+    return p.npeers;
 }
 
 // "no nonzero finite element" marker of the exponent prescan (also the memset byte pattern)
@@ -140,7 +187,7 @@ __device__ __forceinline__ T load_b(const MatmulParams<T> &p, uint64_t k, uint64
 
 // Exact ordered walk of one cell with the checked law; records its first fault.
 template <typename T>
-__device__ __noinline__ void exact_cell(const MatmulParams<T> &p, uint64_t r, uint64_t c) {
+__device__ __noinline__ void exact_cell(const MatmulParams<T> &p, int np, uint64_t r, uint64_t c) {
     const uint64_t cell = r * p.columns + c;
     const uint64_t base = p.event_base + cell * p.inner * 2;
     if (fault_precedes(p.status, base)) return;
@@ -153,7 +200,7 @@ __device__ __noinline__ void exact_cell(const MatmulParams<T> &p, uint64_t r, ui
         if (kind) { record_fault(p.status, base + 2 * k + 1, kind); return; }
         if ((k & 1023) == 1023 && fault_precedes(p.status, base + 2 * k)) return;
     }
-    put_out<T, T>(p, cell, acc);
+    put_out<T, T>(p, np, cell, acc);
 }
 
 // Does the fast result of cell (r, c) need the exact walk?
@@ -224,9 +271,11 @@ template <typename T, int V> struct SVec;
 template <> struct SVec<float, 4> { using type = float4; };
 template <> struct SVec<double, 2> { using type = double2; };
 
-template <typename T> struct TileShape {
+// TM_ rows of cells per thread: Tile<T>::TM for whole tiles, half of it for the half tiles that
+// fill the last wave of a launch (the tile's BM rows then take two CTAs).
+template <typename T, int TM_ = Tile<T>::TM> struct TileShape {
     static constexpr int V = 16 / sizeof(T);  // elements per 16-byte fragment
-    static constexpr int TM = Tile<T>::TM, TN = Tile<T>::TN, BK = Tile<T>::BK, STAGES = Tile<T>::STAGES;
+    static constexpr int TM = TM_, TN = Tile<T>::TN, BK = Tile<T>::BK, STAGES = Tile<T>::STAGES;
     static constexpr int BM = 16 * TM, BN = 16 * TN;
     static constexpr int A_BYTES = BM * BK * (int)sizeof(T);
     static constexpr int B_BYTES = BN * BK * (int)sizeof(T);
@@ -247,34 +296,37 @@ static_assert(kLookahead >= 1 && kLookahead < 4, "lookahead must leave a slot fr
 
 // A_KMAJOR: op(A) rows are contiguous in k (left not transposed).
 // B_KMAJOR: op(B) columns are contiguous in k (right transposed).
-template <typename T, bool A_KMAJOR, bool B_KMAJOR>
+// TMv: rows of cells per thread (Tile<T>::TM, or half of it for half tiles).
+template <typename T, bool A_KMAJOR, bool B_KMAJOR, int TMv>
 __global__ void __launch_bounds__(kThreads, 1)
     strict_matmul_tma_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                              const __grid_constant__ MatmulParams<T> p) {
-    using S = TileShape<T>;
+    using S = TileShape<T, TMv>;
     constexpr int V = S::V, TM = S::TM, TN = S::TN, BK = S::BK, BM = S::BM, BN = S::BN, STAGES = S::STAGES;
     using VT = typename SVec<T, V>::type;
     using F = Fmt<T>;
 
     if (!chain_admits(p.guard)) return;  // the whole CTA, before any barrier or copy
+    announce_entry(p);
     extern __shared__ unsigned char smem_raw[];
     const uintptr_t base = (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023);
     T *const tiles = reinterpret_cast<T *>(base);
     uint64_t *const full = reinterpret_cast<uint64_t *>(base + STAGES * S::STAGE_BYTES);
     uint64_t *const empty = full + STAGES;
     __shared__ int abort_flag;
+    __shared__ int peers_ok;
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     // Tiles in groups of kGroupRows tile rows, column by column inside a group: the CTAs resident
     // at once share a few A row panels and B column panels, which stay in L2 while they are read.
     uint64_t m0, n0;
     {
-        const unsigned tiles_n = gridDim.x, tiles_m = gridDim.y;
-        const unsigned id = blockIdx.y * tiles_n + blockIdx.x;  // launch order
+        const unsigned tiles_n = p.tiles_n, tiles_m = p.tiles_m;
+        const unsigned id = p.tile_first + blockIdx.x / (unsigned)p.split;  // launch order
         const unsigned first_m = id / (kGroupRows * tiles_n) * kGroupRows;
         const unsigned rows_here = min((unsigned)kGroupRows, tiles_m - first_m);
         const unsigned in_group = id - first_m * tiles_n;
-        m0 = (uint64_t)(first_m + in_group % rows_here) * BM;
+        m0 = (uint64_t)(first_m + in_group % rows_here) * (BM * p.split) + (uint64_t)(blockIdx.x % p.split) * BM;
         n0 = (uint64_t)(in_group / rows_here) * BN;
     }
     const int KT = (int)((p.inner + BK - 1) / BK);
@@ -406,6 +458,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
     }
+    // Peer stores wait until every peer has entered this call (row-sharded form only).
+    if (threadIdx.x == 0) peers_ok = p.npeers ? peers_entered(p) : 0;
     // Never leave the CTA with a bulk copy still writing into its shared memory: after a
     // watchdog abort thread 0 waits (bounded) for every copy it issued but nobody folded.
     __syncthreads();
@@ -429,6 +483,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         cmin[j] = (p.col_minexp && c < p.columns) ? p.col_minexp[c] : 0;
     }
     const bool vec_store = !B_KMAJOR && p.vector_out;
+    const int np = peers_ok;
 #pragma unroll
     for (int i = 0; i < TM; ++i) {
         const uint64_t r = m0 + row_of(i);
@@ -446,12 +501,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                     T *e = reinterpret_cast<T *>(&v);
 #pragma unroll
                     for (int q = 0; q < V; ++q) e[q] = acc[i][jg * V + q];
-                    put_out<T, VT>(p, r * p.columns + c, v);
+                    put_out<T, VT>(p, np, r * p.columns + c, v);
                 } else {
 #pragma unroll
                     for (int q = 0; q < V; ++q) {
-                        if (needs_exact(p, acc[i][jg * V + q], rmin[i], cmin[jg * V + q])) exact_cell(p, r, c + q);
-                        else put_out<T, T>(p, r * p.columns + c + q, acc[i][jg * V + q]);
+                        if (needs_exact(p, acc[i][jg * V + q], rmin[i], cmin[jg * V + q])) exact_cell(p, np, r, c + q);
+                        else put_out<T, T>(p, np, r * p.columns + c + q, acc[i][jg * V + q]);
                     }
                 }
             }
@@ -460,12 +515,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; j < TN; ++j) {
                 const uint64_t c = n0 + col_of(j);
                 if (c >= p.columns) continue;
-                if (needs_exact(p, acc[i][j], rmin[i], cmin[j])) exact_cell(p, r, c);
-                else put_out<T, T>(p, r * p.columns + c, acc[i][j]);
+                if (needs_exact(p, acc[i][j], rmin[i], cmin[j])) exact_cell(p, np, r, c);
+                else put_out<T, T>(p, np, r * p.columns + c, acc[i][j]);
             }
         }
     }
-    if (p.npeers) __threadfence_system();  // the peer stores are visible before the kernel ends
+    if (np) __threadfence_system();  // the peer stores are visible before the kernel ends
 }
 
 // Plain tiled kernel for operands TMA cannot describe (unaligned base or stride): 16x16
@@ -473,9 +528,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <typename T>
 __global__ void __launch_bounds__(256) strict_matmul_generic_kernel(const __grid_constant__ MatmulParams<T> p) {
     if (!chain_admits(p.guard)) return;  // the whole CTA
+    announce_entry(p);
     using F = Fmt<T>;
     __shared__ T sa[16][17];
     __shared__ T sb[16][17];
+    __shared__ int peers_ok;
     const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
     const uint64_t r = (uint64_t)blockIdx.y * 16 + ty, c = (uint64_t)blockIdx.x * 16 + tx;
     T acc = T(0);
@@ -489,12 +546,15 @@ __global__ void __launch_bounds__(256) strict_matmul_generic_kernel(const __grid
         for (int kk = 0; kk < kk_end; ++kk) acc = F::add(acc, F::mul(sa[ty][kk], sb[kk][tx]));
         __syncthreads();
     }
+    if (threadIdx.x == 0) peers_ok = p.npeers ? peers_entered(p) : 0;
+    __syncthreads();
+    const int np = peers_ok;
     if (r >= p.rows || c >= p.columns) return;
     const int rmin = p.row_minexp ? p.row_minexp[r] : 0;
     const int cmin = p.col_minexp ? p.col_minexp[c] : 0;
-    if (needs_exact(p, acc, rmin, cmin)) exact_cell(p, r, c);
-    else put_out<T, T>(p, r * p.columns + c, acc);
-    if (p.npeers) __threadfence_system();
+    if (needs_exact(p, acc, rmin, cmin)) exact_cell(p, np, r, c);
+    else put_out<T, T>(p, np, r * p.columns + c, acc);
+    if (np) __threadfence_system();
 }
 
 }  // namespace pcu
@@ -538,9 +598,11 @@ bool make_map(CUtensorMap *map, const T *base, uint64_t inner_dim, uint64_t oute
     return r == CUDA_SUCCESS;
 }
 
-template <typename T, bool AK, bool BK>
-int launch_tma(const CUtensorMap &ma, const CUtensorMap &mb, const MatmulParams<T> &p, cudaStream_t stream) {
-    using S = TileShape<T>;
+// One launch of `ctas` CTAs of the TMA kernel with TMv rows of cells per thread.
+template <typename T, bool AK, bool BK, int TMv>
+int launch_tma(const CUtensorMap &ma, const CUtensorMap &mb, const MatmulParams<T> &p, unsigned ctas,
+               cudaStream_t stream) {
+    using S = TileShape<T, TMv>;
     static std::mutex lock;
     static bool configured[64] = {false};
     int device = 0;
@@ -548,30 +610,74 @@ int launch_tma(const CUtensorMap &ma, const CUtensorMap &mb, const MatmulParams<
     {
         std::lock_guard<std::mutex> guard(lock);
         if (device >= 0 && device < 64 && !configured[device]) {
-            cudaError_t e = cudaFuncSetAttribute(strict_matmul_tma_kernel<T, AK, BK>,
+            cudaError_t e = cudaFuncSetAttribute(strict_matmul_tma_kernel<T, AK, BK, TMv>,
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM_BYTES);
             if (e != cudaSuccess) return pcu_host::set_cuda_error(e);
             configured[device] = true;
         }
     }
-    dim3 grid((unsigned)((p.columns + S::BN - 1) / S::BN), (unsigned)((p.rows + S::BM - 1) / S::BM));
-    strict_matmul_tma_kernel<T, AK, BK><<<grid, kThreads, S::SMEM_BYTES, stream>>>(ma, mb, p);
+    strict_matmul_tma_kernel<T, AK, BK, TMv><<<ctas, kThreads, S::SMEM_BYTES, stream>>>(ma, mb, p);
     return pcu_host::launch_status();
 }
+
+// Split of a product's tiles into launches.  The TMA kernel runs one CTA per SM, so T tiles take
+// ceil(T / SMs) waves; when the last wave would be at most half full, its R = T mod SMs tiles
+// run instead as 2R half tiles in a second launch, which takes about half a wave's time (8192 x
+// 8192 rows of 1024 per GPU: 512 tiles = 3 waves + 68 tiles on 148 SMs, so 3.5 wave times
+// instead of 4).  Returns the number of whole tiles of the first launch.
+inline uint64_t whole_tile_launch(uint64_t tiles, uint64_t sms) {
+    if (tiles <= sms) return tiles;
+    const uint64_t rem = tiles % sms;
+    return (rem != 0 && 2 * rem <= sms) ? tiles - rem : tiles;
+}
+
+template <typename T, bool AK, bool BK>
+int launch_tma_split(const CUtensorMap &ma, const CUtensorMap &ma_half, const CUtensorMap &mb, MatmulParams<T> p,
+                     uint64_t whole, uint64_t tiles, ChainGuard tail_guard, cudaStream_t stream) {
+    constexpr int TM = Tile<T>::TM;
+    p.tile_first = 0;
+    p.split = 1;
+    if (whole) {
+        int rc = launch_tma<T, AK, BK, TM>(ma, mb, p, (unsigned)whole, stream);
+        if (rc) return rc;
+        p.guard = tail_guard;
+    }
+    if (whole == tiles) return PCU_B200_OK;
+    p.tile_first = (unsigned)whole;
+    p.split = 2;
+    return launch_tma<T, AK, BK, TM / 2>(ma_half, mb, p, (unsigned)(2 * (tiles - whole)), stream);
+}
+
+// The peers of a row-sharded call: their copies of C (this rank's rows), the flag words this
+// rank announces its entry in, the flag words it waits on, and the call's number.
+template <typename T> struct PeerSet {
+    T *out[kMaxPeers];
+    unsigned long long *signal[kMaxPeers];
+    const unsigned long long *await_[kMaxPeers];
+    int count = 0;
+    unsigned long long epoch = 0;
+};
 
 template <typename T>
 int run_matmul(int policy, const T *left, const T *right, T *out, uint64_t rows, uint64_t inner, uint64_t columns,
                uint64_t lda, uint64_t ldb, int tl, int tr, void *workspace, size_t workspace_bytes,
                unsigned long long *status, cudaStream_t stream, const ChainGuard &guard,
-               T *const *peer_outs = nullptr, int npeers = 0, unsigned long long event_base = 0) {
+               const PeerSet<T> *peers = nullptr, unsigned long long event_base = 0) {
     MatmulParams<T> p{left,    right,   out,    rows,
                       inner,   columns, lda,    ldb,
                       tl,      tr,      policy, 0,
                       nullptr, nullptr, status, pcu_host::aligned(out, 16) && columns % (16 / sizeof(T)) == 0,
                       guard};
-    for (int q = 0; q < npeers; ++q) p.peer_out[q] = peer_outs[q];
-    p.npeers = npeers;
+    p.npeers = peers ? peers->count : 0;
+    for (int q = 0; q < p.npeers; ++q) {
+        p.peer_out[q] = peers->out[q];
+        p.signal[q] = peers->signal[q];
+        p.await_[q] = peers->await_[q];
+    }
+    p.epoch = peers ? peers->epoch : 0;
     p.event_base = event_base;
+    p.tiles_m = p.tiles_n = p.tile_first = 0;
+    p.split = 1;
     // the first kernel launched decides the stage's admission, the later ones follow it
     ChainGuard next = guard;
     auto take = [&]() {
@@ -618,7 +724,8 @@ int run_matmul(int policy, const T *left, const T *right, T *out, uint64_t rows,
     }
     p.guard = take();
     using S = TileShape<T>;
-    CUtensorMap ma, mb;
+    using H = TileShape<T, Tile<T>::TM / 2>;
+    CUtensorMap ma, ma_half, mb;
     bool tma = inner > 0;
     if (tma) {
         tma = tl ? make_map<T>(&ma, left, rows, inner, lda, S::BM, S::BK, false)
@@ -630,13 +737,24 @@ int run_matmul(int policy, const T *left, const T *right, T *out, uint64_t rows,
     }
     // An output of a few 128-wide tiles would leave most SMs idle (a 256 x 256 product is 4
     // CTAs); the 16 x 16-tile kernel spreads it over many CTAs instead.
-    const uint64_t tiles = ((rows + S::BM - 1) / S::BM) * ((columns + S::BN - 1) / S::BN);
-    if (tiles * 4 < (uint64_t)pcu_host::sm_count()) tma = false;
-    if (tma && (rows + S::BM - 1) / S::BM <= 65535) {
-        if (!tl && !tr) return launch_tma<T, true, false>(ma, mb, p, stream);
-        if (!tl && tr) return launch_tma<T, true, true>(ma, mb, p, stream);
-        if (tl && !tr) return launch_tma<T, false, false>(ma, mb, p, stream);
-        return launch_tma<T, false, true>(ma, mb, p, stream);
+    const uint64_t tiles_m = (rows + S::BM - 1) / S::BM, tiles_n = (columns + S::BN - 1) / S::BN;
+    const uint64_t tiles = tiles_m * tiles_n;
+    const uint64_t sms = (uint64_t)pcu_host::sm_count();
+    if (tiles * 4 < sms) tma = false;
+    if (tma && tiles < (1ull << 30)) {
+        uint64_t whole = whole_tile_launch(tiles, sms);
+        if (whole < tiles) {
+            const bool half_map = tl ? make_map<T>(&ma_half, left, rows, inner, lda, H::BM, H::BK, false)
+                                     : make_map<T>(&ma_half, left, inner, rows, lda, H::BK, H::BM, true);
+            if (!half_map) whole = tiles;
+        }
+        p.tiles_m = (unsigned)tiles_m;
+        p.tiles_n = (unsigned)tiles_n;
+        const ChainGuard tail_guard = take();
+        if (!tl && !tr) return launch_tma_split<T, true, false>(ma, ma_half, mb, p, whole, tiles, tail_guard, stream);
+        if (!tl && tr) return launch_tma_split<T, true, true>(ma, ma_half, mb, p, whole, tiles, tail_guard, stream);
+        if (tl && !tr) return launch_tma_split<T, false, false>(ma, ma_half, mb, p, whole, tiles, tail_guard, stream);
+        return launch_tma_split<T, false, true>(ma, ma_half, mb, p, whole, tiles, tail_guard, stream);
     }
     if ((rows + 15) / 16 > 65535) return PCU_B200_ERROR_SIZE_OVERFLOW;
     dim3 grid((unsigned)((columns + 15) / 16), (unsigned)((rows + 15) / 16));
@@ -713,21 +831,51 @@ constexpr size_t kStaticScratchBytes = kStaticScratchInts * sizeof(int);
 
 static __device__ __align__(256) int g_strict_matmul_scratch[kStaticScratchInts];
 
+// The current context's unique id (cuCtxGetId through the runtime's driver entry point; the
+// library does not link the driver at load time).  0 when it cannot be read.
+unsigned long long current_context_id() {
+    static std::once_flag once;
+    static PFN_cuCtxGetCurrent_v4000 get_current = nullptr;
+    static PFN_cuCtxGetId_v12000 get_id = nullptr;
+    std::call_once(once, [] {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(ptr);
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<PFN_cuCtxGetId_v12000>(ptr);
+    });
+    CUcontext ctx = nullptr;
+    unsigned long long id = 0;
+    if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || !ctx || get_id(ctx, &id) != CUDA_SUCCESS)
+        return 0;
+    return id;
+}
+
 // Device address of g_strict_matmul_scratch on the current device.  The first call on each
-// device performs the lookup; later calls reuse it.
+// device performs the lookup (cudaGetSymbolAddress, with that device current); later calls reuse
+// it.  The cache is keyed on the device's context as well: after a device reset the module is
+// loaded again, possibly elsewhere, so a new context gets a new lookup.
 int static_scratch_address(void **address) {
     static std::mutex lock;
     static void *addresses[64] = {nullptr};
+    static unsigned long long contexts[64] = {0};
     int device = 0;
     cudaError_t err = cudaGetDevice(&device);
     if (err != cudaSuccess) return pcu_host::set_cuda_error(err);
     if (device < 0 || device >= 64) return PCU_B200_ERROR_UNSUPPORTED;
+    // 0 until this thread's runtime has made the device's context current; the lookup below does
+    // that, so the id is read again after it
+    const unsigned long long context = current_context_id();
     std::lock_guard<std::mutex> guard(lock);
-    if (!addresses[device]) {
+    if (!addresses[device] || context == 0 || contexts[device] != context) {
         void *ptr = nullptr;
         err = cudaGetSymbolAddress(&ptr, g_strict_matmul_scratch);
         if (err != cudaSuccess) return pcu_host::set_cuda_error(err);
         addresses[device] = ptr;
+        contexts[device] = current_context_id();
     }
     *address = addresses[device];
     return PCU_B200_OK;
@@ -742,8 +890,14 @@ extern "C" int pcu_b200_strict_matmul_static_scratch(int dtype, int policy, cons
                                                      void *stream) {
     if ((dtype != PCU_B200_F32 && dtype != PCU_B200_F64) || policy < 0 || policy > 2 || !status)
         return PCU_B200_ERROR_INVALID_ARGUMENT;
-    if (rows + columns > kStaticScratchMaxExtent || rows > kStaticScratchMaxExtent ||
-        columns > kStaticScratchMaxExtent)
+    // Only a call that computes products under a rejecting policy uses the exponent minima; the
+    // others (empty shapes, inner == 0, AllowGradualUnderflow) need no scratch and no limit.
+    const bool uses_scratch = policy != PCU_B200_ALLOW_GRADUAL_UNDERFLOW && rows > 0 && columns > 0 && inner > 0;
+    if (!uses_scratch)
+        return pcu_b200_strict_matmul(dtype, policy, left, right, out, rows, inner, columns, left_stride,
+                                      right_stride, transpose_left, transpose_right, nullptr, 0, status, stream);
+    if (rows > kStaticScratchMaxExtent || columns > kStaticScratchMaxExtent ||
+        rows + columns > kStaticScratchMaxExtent)
         return PCU_B200_ERROR_WORKSPACE;
     void *scratch = nullptr;
     int rc = static_scratch_address(&scratch);
@@ -758,51 +912,115 @@ extern "C" int pcu_b200_strict_matmul_static_scratch(int dtype, int policy, cons
 // Row-sharded MatMul with the all-gather of C in the same kernel.  Every rank computes its rows
 // of C with the full ordered K loop; the epilogue writes each finished tile into this device's
 // C and, over NVLink, into every peer's C, so the all-gather overlaps the arithmetic tile by
-// tile instead of following it.  The peers' C buffers are mapped with CUDA IPC
+// tile instead of following it.  The peers' buffers are mapped with CUDA IPC
 // (pcu_b200_peer_alloc / pcu_b200_peer_open).  Plain stores only: no TMA or bulk copy ever
 // reads or writes peer memory.
+//
+// Each buffer ends with a flag block (one word per rank): a CTA stores the call number into its
+// own word of every peer's block when it starts, and waits, before its first store into a
+// peer's C, until that peer's word in this rank's block has reached the call number.  A peer's
+// kernel only starts once everything before it on the peer's stream has finished, so no store
+// of this call can overwrite C while the peer is still reading the previous call's result.
 // ============================================================================
+namespace {
+
+struct EntrySignal {
+    unsigned long long *word[kMaxPeers];
+    unsigned long long epoch;
+    int count;
+};
+
+// The entry announcement of a call that has no tile to compute on this rank.
+__global__ void announce_kernel(const __grid_constant__ EntrySignal sig) {
+    if (threadIdx.x < (unsigned)sig.count)
+        asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(sig.word[threadIdx.x]), "l"(sig.epoch) : "memory");
+}
+
+uint64_t peer_flags_offset(size_t elem, uint64_t rows_total, uint64_t columns) {
+    return ((rows_total * columns * elem + 255) / 256) * 256;
+}
+
+}  // namespace
+
+extern "C" size_t pcu_b200_peer_rows_bytes(int dtype, uint64_t rows_total, uint64_t columns) {
+    if (dtype != PCU_B200_F32 && dtype != PCU_B200_F64) return 0;
+    return peer_flags_offset(dtype == PCU_B200_F64 ? 8 : 4, rows_total, columns) + 256;
+}
+
 extern "C" int pcu_b200_strict_matmul_rows_allgather(int dtype, int policy, const void *left_rows, const void *right,
                                                      void *out_full, uint64_t row0, uint64_t rows,
                                                      uint64_t rows_total, uint64_t inner, uint64_t columns,
                                                      uint64_t left_stride, uint64_t right_stride, int transpose_right,
-                                                     void *const *peer_outs, int npeers, void *workspace,
-                                                     size_t workspace_bytes, uint64_t *status, void *stream) {
+                                                     void *const *peer_outs, int npeers, int rank, uint64_t epoch,
+                                                     void *workspace, size_t workspace_bytes, uint64_t *status,
+                                                     void *stream) {
     if ((dtype != PCU_B200_F32 && dtype != PCU_B200_F64) || policy < 0 || policy > 2 || !status)
         return PCU_B200_ERROR_INVALID_ARGUMENT;
     if (npeers < 0 || npeers > kMaxPeers || (npeers && !peer_outs)) return PCU_B200_ERROR_INVALID_ARGUMENT;
+    if (rank < 0 || rank > npeers || (npeers && epoch == 0)) return PCU_B200_ERROR_INVALID_ARGUMENT;
     if (row0 > rows_total || rows > rows_total - row0) return PCU_B200_ERROR_INVALID_ARGUMENT;
-    if (rows == 0 || columns == 0) return PCU_B200_OK;
-    if (!out_full || (inner > 0 && (!left_rows || !right))) return PCU_B200_ERROR_INVALID_ARGUMENT;
+    if (!out_full) return PCU_B200_ERROR_INVALID_ARGUMENT;
     for (int q = 0; q < npeers; ++q)
         if (!peer_outs[q]) return PCU_B200_ERROR_INVALID_ARGUMENT;
+    if (rows > 0 && columns > 0 && inner > 0 && (!left_rows || !right)) return PCU_B200_ERROR_INVALID_ARGUMENT;
     const uint64_t right_row_len = transpose_right ? inner : columns;
-    if (inner > 0 && (left_stride < inner || right_stride < right_row_len)) return PCU_B200_ERROR_INVALID_ARGUMENT;
+    if (rows > 0 && columns > 0 && inner > 0 && (left_stride < inner || right_stride < right_row_len))
+        return PCU_B200_ERROR_INVALID_ARGUMENT;
     unsigned __int128 events = (unsigned __int128)rows_total * columns;
     events *= (inner ? inner : 1);
     events *= 2;
     if (events > ((unsigned __int128)1 << 60)) return PCU_B200_ERROR_SIZE_OVERFLOW;
     const size_t elem = dtype == PCU_B200_F64 ? 8 : 4;
-    const unsigned long long event_base = (unsigned long long)row0 * columns * (inner ? inner : 1) * 2;
+    const uint64_t flags = peer_flags_offset(elem, rows_total, columns);
     auto *st = reinterpret_cast<unsigned long long *>(status);
     cudaStream_t s = pcu_host::as_stream(stream);
-    void *peers[kMaxPeers];
-    for (int q = 0; q < npeers; ++q) peers[q] = reinterpret_cast<char *>(peer_outs[q]) + row0 * columns * elem;
-    void *out = reinterpret_cast<char *>(out_full) + row0 * columns * elem;
-    if (dtype == PCU_B200_F32)
-        return run_matmul<float>(policy, (const float *)left_rows, (const float *)right, (float *)out, rows, inner,
-                                 columns, left_stride, right_stride, false, transpose_right != 0, workspace,
-                                 workspace_bytes, st, s, ChainGuard{}, reinterpret_cast<float *const *>(peers), npeers,
-                                 event_base);
-    return run_matmul<double>(policy, (const double *)left_rows, (const double *)right, (double *)out, rows, inner,
-                              columns, left_stride, right_stride, false, transpose_right != 0, workspace,
-                              workspace_bytes, st, s, ChainGuard{}, reinterpret_cast<double *const *>(peers), npeers,
-                              event_base);
+    if (rows == 0 || columns == 0) {
+        // No tile to store, but the call still counts on every rank: announce it so that peers
+        // waiting on this rank's entry go on.
+        if (!npeers) return PCU_B200_OK;
+        EntrySignal sig{};
+        sig.count = npeers;
+        sig.epoch = epoch;
+        for (int q = 0; q < npeers; ++q)
+            sig.word[q] = reinterpret_cast<unsigned long long *>(static_cast<char *>(peer_outs[q]) + flags) + rank;
+        announce_kernel<<<1, 32, 0, s>>>(sig);
+        return pcu_host::launch_status();
+    }
+    const unsigned long long event_base = (unsigned long long)row0 * columns * (inner ? inner : 1) * 2;
+    auto fill = [&](auto *typed_out) {
+        using T = std::remove_pointer_t<decltype(typed_out)>;
+        PeerSet<T> peers;
+        peers.count = npeers;
+        peers.epoch = epoch;
+        for (int q = 0; q < npeers; ++q) {
+            const int peer_rank = q < rank ? q : q + 1;
+            char *peer = static_cast<char *>(peer_outs[q]);
+            peers.out[q] = reinterpret_cast<T *>(peer + row0 * columns * elem);
+            peers.signal[q] = reinterpret_cast<unsigned long long *>(peer + flags) + rank;
+            peers.await_[q] = reinterpret_cast<const unsigned long long *>(static_cast<char *>(out_full) + flags) +
+                              peer_rank;
+        }
+        return peers;
+    };
+    if (dtype == PCU_B200_F32) {
+        const PeerSet<float> peers = fill(static_cast<float *>(nullptr));
+        float *out = reinterpret_cast<float *>(static_cast<char *>(out_full) + row0 * columns * elem);
+        return run_matmul<float>(policy, (const float *)left_rows, (const float *)right, out, rows, inner, columns,
+                                 left_stride, right_stride, false, transpose_right != 0, workspace, workspace_bytes,
+                                 st, s, ChainGuard{}, &peers, event_base);
+    }
+    const PeerSet<double> peers = fill(static_cast<double *>(nullptr));
+    double *out = reinterpret_cast<double *>(static_cast<char *>(out_full) + row0 * columns * elem);
+    return run_matmul<double>(policy, (const double *)left_rows, (const double *)right, out, rows, inner, columns,
+                              left_stride, right_stride, false, transpose_right != 0, workspace, workspace_bytes, st,
+                              s, ChainGuard{}, &peers, event_base);
 }
 
 extern "C" int pcu_b200_peer_alloc(size_t bytes, void **ptr, void *handle) {
     if (!ptr || !handle || !bytes) return PCU_B200_ERROR_INVALID_ARGUMENT;
     cudaError_t e = cudaMalloc(ptr, bytes);
+    // zero-filled: the flag blocks of the row-sharded all-gather start below every call number
+    if (e == cudaSuccess) e = cudaMemset(*ptr, 0, bytes);
     if (e == cudaSuccess) e = cudaIpcGetMemHandle(reinterpret_cast<cudaIpcMemHandle_t *>(handle), *ptr);
     return e == cudaSuccess ? PCU_B200_OK : pcu_host::set_cuda_error(e);
 }

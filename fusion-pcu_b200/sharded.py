@@ -115,7 +115,9 @@ class PeerRows:
     """A rows x columns matrix of which every rank holds a copy that all ranks write into (CUDA IPC,
     pcu_b200_peer_alloc / _open): the destination of the fused row-sharded MatMul + all-gather.
     `local` is this rank's copy (a torch view); `peer_ptrs` the peers' copies mapped here, in rank
-    order without this rank.  Only the provider's own kernels touch the peer copies."""
+    order without this rank.  Only the provider's own kernels touch the peer copies.  `calls`
+    numbers the MatMuls made into this matrix (the same on every rank): the kernel stores into a
+    peer's copy only once that peer has entered the same call."""
 
     def __init__(self, rows, columns, dtype=torch.float32, group=None):
         import ctypes
@@ -123,9 +125,10 @@ class PeerRows:
         self.group = group
         self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
         L = pcu.library()
-        elem = torch.empty((), dtype=dtype).element_size()
         ptr, handle = ctypes.c_void_p(), (ctypes.c_ubyte * 64)()
-        pcu._check(L.pcu_b200_peer_alloc(rows * columns * elem, ctypes.byref(ptr), handle))
+        code = 0 if dtype == torch.float32 else 1
+        pcu._check(L.pcu_b200_peer_alloc(L.pcu_b200_peer_rows_bytes(code, rows, columns), ctypes.byref(ptr), handle))
+        self.calls = 0
         self._ptr = ptr.value
         handles = [None] * self.world
         dist.all_gather_object(handles, bytes(handle), group=group)
@@ -156,8 +159,12 @@ class PeerRows:
 def strict_matmul_rows_allgather(left_rows, right, row0, shared, status, transpose_right=False, policy=0,
                                  workspace=None, stream=None):
     """Rows [row0, row0 + m) of C = A . op(B) in one kernel with their all-gather: written into
-    `shared.local` and every peer's copy (PeerRows), events global.  Follow with a collective
-    (all_reduce_min_status) before reading C: it orders every rank's call before the read."""
+    `shared.local` and every peer's copy (PeerRows), events global.
+
+    Ordering: follow with a collective (all_reduce_min_status) before reading C; it orders every
+    rank's stores before the read.  The other direction needs nothing from the caller as long as
+    every reader of C runs on `stream` (or is joined into it) before the next call: the kernel
+    stores into a peer's C only after that peer's kernel of the same call has started."""
     import ctypes
 
     L = pcu.library()
@@ -170,7 +177,9 @@ def strict_matmul_rows_allgather(left_rows, right, row0, shared, status, transpo
     pcu._check(L.pcu_b200_strict_matmul_rows_allgather(
         pcu._dtype_code(left_rows), policy, pcu._ptr(left_rows), pcu._ptr(right), ctypes.c_void_p(shared._ptr), row0,
         rows, shared.rows, inner, cols, left_rows.stride(0), right.stride(0), int(transpose_right), peers,
-        len(shared.peer_ptrs), pcu._ptr(workspace), workspace.numel(), pcu._ptr(status), pcu._stream(stream)))
+        len(shared.peer_ptrs), shared.rank, shared.calls + 1, pcu._ptr(workspace), workspace.numel(),
+        pcu._ptr(status), pcu._stream(stream)))
+    shared.calls += 1
     return shared.local
 
 

@@ -48,7 +48,7 @@
 extern "C" {
 #endif
 
-#define PCU_B200_ABI_VERSION 1
+#define PCU_B200_ABI_VERSION 2
 
 /* element types (PcuScalarType::F32 / F64) */
 #define PCU_B200_F32 0
@@ -125,13 +125,17 @@ int pcu_b200_strict_matmul(int dtype, int policy, const void *left, const void *
  * device allocator (in Fusion-PCU every device allocation belongs to the Rust memory-resource
  * pool), or a caller that must keep the call itself free of allocation.  This variant takes no
  * workspace.  Its scratch is a fixed array of device memory inside this library (about 257 KB,
- * held on every GPU that loads the library until the process exits), so it accepts only
- * shapes with rows + columns <= 65536; larger shapes return PCU_B200_ERROR_WORKSPACE.  It calls
- * no cudaMalloc or cudaFree.  The first call on each device looks up the array's device address
- * (cudaGetSymbolAddress); make that first call before any stream capture.  All calls share the
- * one array: each call re-initialises what it reads, but calls whose executions overlap on the
- * GPU (other streams, other host threads) race on it and must be serialised by the caller.
- * Everything else -- arguments, results, status word, errors -- is exactly pcu_b200_strict_matmul. */
+ * held on every GPU that loads the library until the process exits).  A call that uses it (a
+ * non-empty product under IeeeAfterRounding or RejectSubnormalResult) is limited to
+ * rows + columns <= 65536; larger ones return PCU_B200_ERROR_WORKSPACE.  Calls that need no
+ * scratch (empty shapes, inner == 0, AllowGradualUnderflow) have no limit.  It calls no
+ * cudaMalloc or cudaFree.  The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress) and later calls reuse it while the device's context stays the same (a
+ * new context after a device reset gets a new lookup); make that first call before any stream
+ * capture.  All calls share the one array: each call re-initialises what it reads, but calls
+ * whose executions overlap on the GPU (other streams, other host threads) race on it and must be
+ * serialised by the caller.  Everything else -- arguments, results, status word, errors -- is
+ * exactly pcu_b200_strict_matmul. */
 int pcu_b200_strict_matmul_static_scratch(int dtype, int policy, const void *left, const void *right, void *out,
                                           uint64_t rows, uint64_t inner, uint64_t columns, uint64_t left_stride,
                                           uint64_t right_stride, int transpose_left, int transpose_right,
@@ -158,29 +162,51 @@ int pcu_b200_strict_matmul_host(int dtype, int policy, const void *left, const v
  * [row0, row0 + rows) of the rows_total x columns product C = A . op(B) (left_rows: this rank's
  * rows of A, rows x inner with row stride left_stride; right: B as in pcu_b200_strict_matmul,
  * transpose_right allowed) with the full ordered K loop.  Each finished output tile is written
- * into out_full (this device's whole C, rows_total x columns, dense) and into every peer's C at
- * the same place: peer_outs holds npeers (<= 7) device pointers of the peers' C, mapped into this
- * process with pcu_b200_peer_open.  So the transfer overlaps the arithmetic tile by tile, with
- * plain NVLink stores (no TMA or bulk copy touches peer memory).  The status word holds the
- * whole product's event ordinals (cells offset by row0 * columns); the global first fault is the
- * MIN of all ranks' words.  The kernel ends with a system-scope fence; a peer's rows are complete
- * in this rank's C once every rank's call has finished, which the caller establishes with a
- * collective (the status all-reduce) after the call.  No counterpart in the reference (its
- * strict MatMul runs on one device). */
+ * into out_full (this rank's buffer: its whole C, rows_total x columns, dense) and into every
+ * peer's buffer at the same place: peer_outs holds npeers (<= 7) device pointers of the peers'
+ * buffers, in rank order without this rank, mapped into this process with pcu_b200_peer_open.
+ * So the transfer overlaps the arithmetic tile by tile, with plain NVLink stores (no TMA or bulk
+ * copy touches peer memory).  The status word holds the whole product's event ordinals (cells
+ * offset by row0 * columns); the global first fault is the MIN of all ranks' words.
+ *
+ * Buffers: every rank's buffer is pcu_b200_peer_rows_bytes(dtype, rows_total, columns) bytes
+ * from pcu_b200_peer_alloc (zero-filled): C, then a flag block with one word per rank.
+ *
+ * Ordering, both directions:
+ *   - read side: a peer's rows are complete in this rank's C once every rank's call has
+ *     finished, which the caller establishes with a collective after the call (the status MIN);
+ *   - write side: `epoch` numbers the calls on this set of buffers (1, 2, 3, ..., the same on
+ *     every rank) and `rank` is this rank's index (0..npeers).  The kernel records its entry in
+ *     each peer's flag block and stores into a peer's C only after that peer's kernel of the
+ *     same call has started, i.e. after everything the peer queued before it on its stream --
+ *     its readers of the previous call's C -- has finished.  Readers of C on another stream must
+ *     be joined into the calling stream before the next call.  A peer that has not entered the
+ *     call within 10 s gets no stores and the status word records PCU_B200_STATUS_WATCHDOG.
+ *
+ * No counterpart in the reference (its strict MatMul runs on one device). */
+size_t pcu_b200_peer_rows_bytes(int dtype, uint64_t rows_total, uint64_t columns);
 int pcu_b200_strict_matmul_rows_allgather(int dtype, int policy, const void *left_rows, const void *right,
                                           void *out_full, uint64_t row0, uint64_t rows, uint64_t rows_total,
                                           uint64_t inner, uint64_t columns, uint64_t left_stride,
                                           uint64_t right_stride, int transpose_right, void *const *peer_outs,
-                                          int npeers, void *workspace, size_t workspace_bytes, uint64_t *status,
-                                          void *stream);
+                                          int npeers, int rank, uint64_t epoch, void *workspace,
+                                          size_t workspace_bytes, uint64_t *status, void *stream);
 
-/* CUDA IPC for the buffers peers write into: allocate `bytes` of device memory and its 64-byte
- * IPC handle; map a peer's buffer from its handle (into this process, on the current device);
+/* CUDA IPC for the buffers peers write into: allocate `bytes` of zero-filled device memory and
+ * its 64-byte IPC handle; map a peer's buffer from its handle (into this process, on the current device);
  * unmap; free. */
 int pcu_b200_peer_alloc(size_t bytes, void **ptr, void *handle);
 int pcu_b200_peer_open(const void *handle, void **ptr);
 int pcu_b200_peer_close(void *ptr);
 int pcu_b200_peer_free(void *ptr);
+
+/* Measured roofline denominator of the strict MatMul (no counterpart in the reference): the
+ * FP32 or FP64 non-FMA issue rate of this GPU.  pcu_b200_issue_probe launches `iterations`
+ * rounds of independent, separately rounded multiplies and adds on every SM at full occupancy;
+ * time it with CUDA events on `stream`.  pcu_b200_issue_probe_ops is the number of multiplies
+ * plus adds that launch executes on the current device. */
+uint64_t pcu_b200_issue_probe_ops(int dtype, uint64_t iterations);
+int pcu_b200_issue_probe(int dtype, uint64_t iterations, void *stream);
 
 /* ------------------------------------------------------------------ strict SGD */
 
@@ -406,7 +432,8 @@ int pcu_b200_comm_send(pcu_b200_comm *comm, const void *buffer, size_t bytes, in
 int pcu_b200_comm_recv(pcu_b200_comm *comm, void *buffer, size_t bytes, int peer, void *stream);
 int pcu_b200_comm_broadcast(pcu_b200_comm *comm, void *buffer, size_t bytes, int root, void *stream);
 
-/* Collective.  Every rank allocates `bytes` of device memory that the others map with CUDA IPC.
+/* Collective.  Every rank allocates `bytes` of zero-filled device memory that the others map
+ * with CUDA IPC (for a row-sharded MatMul: pcu_b200_peer_rows_bytes(dtype, rows_total, columns)).
  * buffers[r] (nranks entries) is rank r's buffer as this process sees it; buffers[rank] is this
  * rank's own.  Returns once this rank has mapped every peer.  _free unmaps the peers, waits for
  * every rank to do the same, and frees this rank's buffer. */
@@ -415,9 +442,11 @@ int pcu_b200_comm_peer_buffers_free(pcu_b200_comm *comm, void **buffers, void *s
 
 /* The row-sharded strict MatMul in one call.  It runs pcu_b200_strict_matmul_rows_allgather for
  * rows [row0, row0 + rows) into buffers[rank] and every peer's buffer (buffers from
- * pcu_b200_comm_peer_buffers, rows_total x columns each), then the status MIN.  When the work on
- * `stream` is done, every rank's buffers[rank] holds all of C and `status` holds the global
- * first fault.  C must not be read on any rank after the next call has been made on another. */
+ * pcu_b200_comm_peer_buffers, pcu_b200_peer_rows_bytes each), then the status MIN.  When the
+ * work on `stream` is done, every rank's buffers[rank] holds all of C and `status` holds the
+ * global first fault.  The communicator numbers the calls on each buffer set, so the next
+ * call's stores into a rank's C wait until that rank's stream has reached the call: readers of C
+ * queued on `stream` before the next call are never overwritten. */
 int pcu_b200_comm_strict_matmul_rows(pcu_b200_comm *comm, int dtype, int policy, const void *left_rows,
                                      const void *right, void *const *buffers, uint64_t row0, uint64_t rows,
                                      uint64_t rows_total, uint64_t inner, uint64_t columns, uint64_t left_stride,

@@ -61,7 +61,18 @@ def test_host_validation_rejects_bad_arguments(provider):
                                       big, big, big, big, 0, 0, None, 0, sp, None) == 2
     # empty outputs are a successful no-op
     assert lib.pcu_b200_strict_matmul(0, 0, None, None, None, 0, 5, 5, 5, 5, 0, 0, None, 0, sp, None) == 0
-    assert lib.pcu_b200_abi_version() == 1
+    assert lib.pcu_b200_abi_version() == 2
+    # row-sharded all-gather: the rank must index the peer list, and a call with peers needs a
+    # call number (the write-side order of the peer stores)
+    peers = (ctypes.c_void_p * 1)(16)
+    dev = ctypes.c_void_p(256)
+    for rank, epoch in ((2, 1), (-1, 1), (0, 0)):
+        assert lib.pcu_b200_strict_matmul_rows_allgather(0, 0, dev, dev, dev, 0, 4, 8, 4, 4, 4, 4, 0, peers, 1, rank,
+                                                         epoch, None, 0, sp, None) == 1
+    # a buffer of the all-gather is C rounded up to 256 bytes plus a 256-byte flag block
+    assert lib.pcu_b200_peer_rows_bytes(0, 3, 5) == 256 + 256
+    assert lib.pcu_b200_peer_rows_bytes(1, 64, 64) == 64 * 64 * 8 + 256
+    assert lib.pcu_b200_peer_rows_bytes(5, 64, 64) == 0
     assert lib.pcu_b200_error_string(3).decode().startswith("workspace")
 
 

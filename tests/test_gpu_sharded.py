@@ -237,3 +237,81 @@ def test_fused_rows_allgather_matches_one_device():
             assert word == want_word, (case, rank, hex(word), hex(want_word))
             if want_word == pcu.STATUS_OK:  # every rank holds the whole product
                 assert np.array_equal(c_bits, bits(to_host(want))), (case, rank)
+
+
+_RACE_CASE = (2048, 128, 1024, 10)  # m, k, n, back-to-back calls
+
+
+def _race_worker(rank, world, port, queue):
+    """Ten row-sharded calls in a row, each followed by a reader of C on the same stream; rank 0's
+    reader first spins for about a millisecond, long enough for the other ranks' next call to
+    finish its tiles.  Nothing but the library's own ordering keeps their stores out of rank 0's
+    C until its reader is done."""
+    import torch
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    import datetime
+
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    sh = None
+    try:
+        sharded = importlib.import_module("fusion-pcu_b200.sharded")
+        m, k, n, calls = _RACE_CASE
+        rows = m // world
+        r0 = rank * rows
+        b = to_device(dyadic_uniform(np.random.default_rng(900), (k, n), 32))
+        lefts = [to_device(dyadic_uniform(np.random.default_rng(901 + i), (m, k), 32)[r0:r0 + rows])
+                 for i in range(calls)]
+        sh = sharded.PeerRows(m, n, torch.float32)
+        status = pcu.new_status(calls)
+        torch.cuda.synchronize()
+        dist.barrier()
+        snaps = []
+        for i in range(calls):
+            sharded.strict_matmul_rows_allgather(lefts[i], b, r0, sh, status[i:i + 1])
+            sharded.all_reduce_min_status(status[i:i + 1])
+            if rank == 0:
+                torch.cuda._sleep(2_000_000)
+            snaps.append(sh.local.clone())
+        torch.cuda.synchronize()
+        words = [int(w) & ((1 << 64) - 1) for w in status.cpu().tolist()]
+        queue.put((rank, words, [bits(to_host(s)) for s in snaps]))
+    finally:
+        if sh is not None:
+            sh.close()
+        dist.destroy_process_group()
+
+
+def test_fused_rows_allgather_readers_are_not_overwritten():
+    import torch
+
+    world = min(torch.cuda.device_count(), 4)
+    if world < 2:
+        pytest.skip("needs 2 or more GPUs")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_race_worker, args=(r, world, port, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict((r[0], r[1:]) for r in (queue.get(timeout=300) for _ in range(world)))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    m, k, n, calls = _RACE_CASE
+    b = to_device(dyadic_uniform(np.random.default_rng(900), (k, n), 32))
+    for i in range(calls):
+        a = to_device(dyadic_uniform(np.random.default_rng(901 + i), (m, k), 32))
+        status = pcu.new_status()
+        want = bits(to_host(pcu.strict_matmul(a, b, status=status)))
+        torch.cuda.synchronize()
+        assert status_word(status) == pcu.STATUS_OK
+        for rank in range(world):
+            words, snaps = got[rank]
+            assert words[i] == pcu.STATUS_OK, (rank, i, hex(words[i]))
+            assert np.array_equal(snaps[i], want), (rank, i)

@@ -84,3 +84,31 @@ def test_static_scratch_rejects_shapes_beyond_its_limit(provider):
     assert rc == 3  # PCU_B200_ERROR_WORKSPACE: rows + columns exceeds 65536
     torch.cuda.synchronize()
     assert status_word(status) == provider.STATUS_OK
+
+
+def test_static_scratch_limit_applies_only_when_the_scratch_is_used(provider):
+    """Calls that need no exponent minima (empty shapes, AllowGradualUnderflow) are not limited:
+    they return exactly what the workspace entry point returns."""
+    import torch
+
+    fn = _bind(provider.library())
+    status = provider.new_status()
+    dummy = torch.zeros(16, dtype=torch.float32, device="cuda")
+    # rows == 0: an empty product, whatever the column count
+    assert fn(0, 0, dummy.data_ptr(), dummy.data_ptr(), dummy.data_ptr(), 0, 4, 70000, 4, 70000, 0, 0,
+              status.data_ptr(), torch.cuda.current_stream().cuda_stream) == 0
+    # AllowGradualUnderflow (policy 2) with rows + columns above the limit, twice in a row
+    rng = np.random.default_rng(77)
+    for seed in (0, 1):
+        a = to_device(dyadic_uniform(rng, (65000, 4), 32))
+        b = to_device(dyadic_uniform(rng, (4, 600), 32))
+        ref_status = provider.new_status()
+        ref = provider.strict_matmul(a, b, False, False, 2, status=ref_status)
+        out = torch.empty((65000, 600), dtype=torch.float32, device="cuda")
+        st = provider.new_status()
+        assert _call_static(fn, provider, a, b, out, st, False, False, 2) == 0
+        torch.cuda.synchronize()
+        assert status_word(st) == status_word(ref_status) == provider.STATUS_OK
+        assert np.array_equal(bits(to_host(out)), bits(to_host(ref)))
+    torch.cuda.synchronize()
+    assert status_word(status) == provider.STATUS_OK
