@@ -246,6 +246,37 @@ def test_matmul_1024_full(provider, width):
     _matmul_case(provider, a, b, False, True, 0, fast_oracle=True)
 
 
+def _split_launch(m, n, width, sms=148):
+    """True when the product's last wave of 128-row tiles runs as a separate half-tile launch
+    (the schedule of strict_matmul.cu's whole_tile_launch)."""
+    bn = 128 if width == 32 else 64
+    tiles = -(-m // 128) * -(-n // bn)
+    return tiles > sms and tiles % sms != 0 and 2 * (tiles % sms) <= sms
+
+
+@pytest.mark.parametrize("width", [32, 64])
+@pytest.mark.parametrize("tl,tr", [(False, False), (True, False), (False, True), (True, True)])
+def test_matmul_half_tile_tail_launch(provider, width, tl, tr):
+    """Products whose last wave is cut into half tiles (a second launch of 64-row CTAs), the shape of
+    an 8192 x 8192 product's row block on 8 GPUs, and a ragged one whose last tile row ends inside a
+    half; every cell bit-exact and the first fault where the oracle puts it."""
+    import torch
+
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    rng = np.random.default_rng(640 + width + 2 * tl + tr)
+    cols = 8192 if width == 32 else 4096
+    for m, k, n, fault in ((1024, 48, cols, None), (1000, 40, cols - 24, None), (1024, 24, cols, 3)):
+        assert sms != 148 or _split_launch(m, n, width, sms), (m, n)
+        a = dyadic_uniform(rng, (k, m) if tl else (m, k), width)
+        b = dyadic_uniform(rng, (n, k) if tr else (k, n), width)
+        if fault is not None:  # a NaN in op(B)'s last column: its tiles are in the half-tile launch
+            if tr:
+                b[n - 1, fault] = np.nan
+            else:
+                b[fault, n - 1] = np.nan
+        _matmul_case(provider, a, b, tl, tr, 0, fast_oracle=True)
+
+
 @pytest.mark.parametrize("m,k,n", [(8192, 8192, 8192), (2048, 2048, 2048), (4096, 4096, 4096), (8192, 1024, 16384)])
 def test_matmul_sweep_sampled_cells(provider, m, k, n):
     """BASELINE config 2 at full size (the square sweep and the 8192x1024 . 1024x16384 case):
