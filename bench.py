@@ -494,10 +494,11 @@ def mse_sgd(torch, pcu, device, stream, hbm_gbs, args, rank, world):
     s12 = pcu.new_status(2, device=device)  # the two nodes' words, all-reduced together
     s1, s2 = s12[0:1], s12[1:2]
     if world > 1:
+        # device hand-off: the segment walks chain through IPC-mapped blocks and one exchange
+        # kernel leaves both global first faults and the mean on every rank
         smse = sharded.ShardedMse(p, t, e0, n)
         rider = {"weights": w, "gradient": g_, "rate": 0.01, "first_index": e0, "out": out_w, "status": s2}
-        fused_call = lambda: (smse.run(s1, stream=stream, sgd=rider, reduce_status=False),  # noqa: E731
-                              sharded.all_reduce_min_status(s12))
+        fused_call = lambda: smse.run(s1, stream=stream, sgd=rider)  # noqa: E731
         mse_call = lambda: smse.run(s1, stream=stream)  # noqa: E731
         sgd_call = lambda: (sharded.strict_sgd_block(w, g_, 0.01, e0, s2, out=out_w, stream=stream),  # noqa: E731
                             sharded.all_reduce_min_status(s2))
@@ -529,8 +530,8 @@ def mse_sgd(torch, pcu, device, stream, hbm_gbs, args, rank, world):
     gbs = total / (times["fused"] * 1e-3) / 1e9
     result = {"value": gbs, "unit": "GB/s", "elements": n, "ms": times["fused"],
               "scaling": "strong", "parallelism": f"element blocks x{world}" + (
-                  " + ordered MSE hand-off" if world > 1 else ""),
-              "call": "pcu_b200_strict_mse_sgd" + ("_segment_prepare + ordered walks" if world > 1 else ""),
+                  " + ordered MSE hand-off on the device (NVLink stores)" if world > 1 else ""),
+              "call": "pcu_b200_strict_mse_sgd" + ("_split" if world > 1 else ""),
               "separate_ms": times["mse"] + times["sgd"], "mse_ms": times["mse"], "sgd_ms": times["sgd"],
               "separate_gbs": total / ((times["mse"] + times["sgd"]) * 1e-3) / 1e9,
               "sgd_gbs": sgd_bytes / (times["sgd"] * 1e-3) / 1e9,
@@ -541,6 +542,7 @@ def mse_sgd(torch, pcu, device, stream, hbm_gbs, args, rank, world):
         fused_call()
         torch.cuda.synchronize()
         result["parity"] = mse_sgd_parity(torch, pcu, device, smse.mean, out_w, s12, e0, e1, n, rank, world)
+        smse.close()
     return result
 
 

@@ -95,6 +95,9 @@ def _declare(L):
     L.pcu_b200_issue_probe_ops.argtypes = [i32, u64]
     L.pcu_b200_issue_probe_ops.restype = u64
     L.pcu_b200_issue_probe.argtypes = [i32, u64, vp]
+    L.pcu_b200_mse_handoff_bytes.restype = sz
+    L.pcu_b200_strict_mse_sgd_split.argtypes = [i32, i32, vp, vp, u64, u64, u64, vp, vp, sz, vp, vp, vp, vp, u64, u64,
+                                                u32, vp, ctypes.POINTER(vp), i32, i32, u64, vp]
     L.pcu_b200_peer_rows_bytes.argtypes = [i32, u64, u64]
     L.pcu_b200_peer_rows_bytes.restype = sz
     L.pcu_b200_strict_matmul_rows_allgather.argtypes = [i32, i32, vp, vp, vp, u64, u64, u64, u64, u64, u64, u64, i32,
@@ -140,7 +143,7 @@ def _declare(L):
     L.pcu_b200_comm_peer_buffers_free.argtypes = [vp, ctypes.POINTER(vp), vp]
     L.pcu_b200_comm_strict_matmul_rows.argtypes = [vp, i32, i32, vp, vp, ctypes.POINTER(vp), u64, u64, u64, u64, u64,
                                                    u64, u64, i32, vp, sz, vp, vp]
-    L.pcu_b200_comm_strict_mse.argtypes = [vp, i32, i32, vp, vp, u64, u64, u64, vp, vp, vp, sz, vp, vp]
+    L.pcu_b200_comm_strict_mse.argtypes = [vp, i32, i32, vp, vp, u64, u64, u64, vp, vp, sz, vp, vp]
 
 
 def _torch():

@@ -90,11 +90,10 @@ class Communicator:
         assert prediction.is_contiguous() and target.is_contiguous() and prediction.numel() == target.numel()
         if workspace is None:
             workspace = pcu.mse_workspace(prediction)
-        carry = torch.zeros(1, dtype=prediction.dtype, device=prediction.device)
         pcu._check(pcu.library().pcu_b200_comm_strict_mse(
             self._c, pcu._dtype_code(prediction), policy, pcu._ptr(prediction), pcu._ptr(target), prediction.numel(),
-            first_index, total_count, pcu._ptr(carry), pcu._ptr(out), pcu._ptr(workspace), workspace.numel(),
-            pcu._ptr(status), pcu._stream(stream)))
+            first_index, total_count, pcu._ptr(out), pcu._ptr(workspace), workspace.numel(), pcu._ptr(status),
+            pcu._stream(stream)))
         return out
 
 

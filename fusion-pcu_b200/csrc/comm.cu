@@ -31,6 +31,10 @@ struct pcu_b200_comm {
     // number of the row-sharded MatMul's write-side order.  Every rank makes the same calls, so
     // the counts agree across ranks.
     std::vector<std::pair<void *, uint64_t>> calls;
+    // The split strict MSE's hand-off blocks (every rank's, mapped here), made by the first
+    // pcu_b200_comm_strict_mse call, and the number of such calls.
+    void *handoff[8];
+    uint64_t mse_calls;
 };
 
 namespace {
@@ -135,8 +139,22 @@ extern "C" int pcu_b200_comm_init(const void *id, int nranks, int rank, pcu_b200
     return PCU_B200_OK;
 }
 
+// The hand-off blocks without a collective (free and abort): unmap the peers', free this rank's.
+static void drop_handoff(pcu_b200_comm *c) {
+    if (!c->handoff[c->rank]) return;
+    for (int r = 0; r < c->nranks; ++r)
+        if (r != c->rank && c->handoff[r]) pcu_b200_peer_close(c->handoff[r]);
+    pcu_b200_peer_free(c->handoff[c->rank]);
+    for (int r = 0; r < c->nranks; ++r) c->handoff[r] = nullptr;
+}
+
 extern "C" int pcu_b200_comm_free(pcu_b200_comm *comm) {
     if (!comm) return PCU_B200_OK;
+    if (comm->handoff[comm->rank]) {
+        // every rank unmaps before any frees: the barrier of the peer-buffer release
+        const int rc = pcu_b200_comm_peer_buffers_free(comm, comm->handoff, nullptr);
+        if (rc) drop_handoff(comm);
+    }
     int rc = comm->comm ? comm_status(nccl().destroy(comm->comm)) : PCU_B200_OK;
     if (comm->scratch) cudaFree(comm->scratch);
     delete comm;
@@ -146,6 +164,7 @@ extern "C" int pcu_b200_comm_free(pcu_b200_comm *comm) {
 extern "C" int pcu_b200_comm_abort(pcu_b200_comm *comm) {
     if (!comm) return PCU_B200_OK;
     int rc = comm->comm ? comm_status(nccl().abort(comm->comm)) : PCU_B200_OK;
+    drop_handoff(comm);
     if (comm->scratch) cudaFree(comm->scratch);
     delete comm;
     return rc;
@@ -265,40 +284,26 @@ extern "C" int pcu_b200_comm_strict_matmul_rows(pcu_b200_comm *comm, int dtype, 
 }
 
 // A strict MSE over total_count elements split into contiguous segments, rank r holding the
-// global elements [first_index, first_index + count): rank 0 maps and walks its segment in one
-// launch; every other rank builds its maps at once, receives the running sum from rank r - 1,
-// walks and sends it on to rank r + 1.  The last rank's mean is broadcast to out on every rank,
-// and the status words are combined by MIN.
+// global elements [first_index, first_index + count), through pcu_b200_strict_mse_sgd_split: the
+// running sum goes from rank to rank on the device (IPC-mapped hand-off blocks, made by the
+// first call, which is collective like every call here), and a one-warp exchange leaves the
+// mean and the MIN of the status words on every rank.  No NCCL call after the first.
 extern "C" int pcu_b200_comm_strict_mse(pcu_b200_comm *comm, int dtype, int policy, const void *prediction,
                                         const void *target, uint64_t count, uint64_t first_index, uint64_t total_count,
-                                        void *carry, void *out, void *workspace, size_t workspace_bytes,
-                                        uint64_t *status, void *stream) {
-    if (!usable(comm) || !carry || !out || !status || (dtype != PCU_B200_F32 && dtype != PCU_B200_F64))
+                                        void *out, void *workspace, size_t workspace_bytes, uint64_t *status,
+                                        void *stream) {
+    if (!usable(comm) || !out || !status || (dtype != PCU_B200_F32 && dtype != PCU_B200_F64))
         return PCU_B200_ERROR_INVALID_ARGUMENT;
     if (count == 0 || first_index > total_count || count > total_count - first_index)
         return PCU_B200_ERROR_INVALID_ARGUMENT;
-    const int me = comm->rank, last = comm->nranks - 1;
-    const size_t elem = dtype == PCU_B200_F32 ? 4 : 8;
-    const bool tail = first_index + count == total_count;
-    cudaStream_t s = pcu_host::as_stream(stream);
-    int rc;
-    if (me == 0) {
-        rc = cuda_status(cudaMemsetAsync(comm->scratch, 0xff, sizeof(uint64_t), s));
-        if (!rc)
-            rc = pcu_b200_strict_mse_sgd_segment(dtype, policy, prediction, target, count, first_index, total_count,
-                                                 nullptr, carry, tail ? out : nullptr, workspace, workspace_bytes,
-                                                 status, nullptr, nullptr, nullptr, 0, 0, 0, comm->scratch, stream);
-    } else {
-        rc = pcu_b200_strict_mse_segment_prepare(dtype, policy, prediction, target, count, first_index, workspace,
-                                                 workspace_bytes, status, stream);
-        if (!rc) rc = pcu_b200_comm_recv(comm, carry, elem, me - 1, stream);
-        if (!rc)
-            rc = pcu_b200_strict_mse_segment_walk(dtype, policy, prediction, target, count, first_index, total_count,
-                                                  carry, carry, tail ? out : nullptr, workspace, workspace_bytes,
-                                                  status, stream);
+    if (!comm->handoff[comm->rank]) {
+        const int rc = pcu_b200_comm_peer_buffers(comm, pcu_b200_mse_handoff_bytes(), comm->handoff, stream);
+        if (rc) return rc;
     }
-    if (!rc && me < last) rc = pcu_b200_comm_send(comm, carry, elem, me + 1, stream);
-    if (!rc) rc = pcu_b200_comm_broadcast(comm, out, elem, last, stream);
-    if (!rc) rc = pcu_b200_comm_status_min(comm, status, 1, stream);
+    const int rc = pcu_b200_strict_mse_sgd_split(dtype, policy, prediction, target, count, first_index, total_count,
+                                                 out, workspace, workspace_bytes, status, nullptr, nullptr, nullptr, 0,
+                                                 0, 0x3f800000u, nullptr, comm->handoff, comm->rank, comm->nranks,
+                                                 comm->mse_calls + 1, stream);
+    if (!rc) ++comm->mse_calls;
     return rc;
 }

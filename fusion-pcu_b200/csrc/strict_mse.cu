@@ -1130,6 +1130,26 @@ __device__ __forceinline__ unsigned block_ctas_onepass(uint64_t chunks, uint64_t
     return (unsigned)((c + per_cta - 1) / per_cta);
 }
 
+// The device-side hand-off of a split reduction's running sum between ranks (one GPU each):
+// the walker of rank r > 0 waits (bounded) until rank r - 1 has stored the call's carry into this
+// rank's hand-off block (in_flag reaches `epoch`), and the walker of rank r < last stores its own
+// into rank r + 1's block (the value, then out_flag = epoch, a system-scope release over
+// NVLink).  Both null: a carry from, and to, this device's own memory in stream order.
+struct CarryLink {
+    const unsigned long long *in_flag;
+    unsigned long long *out_flag;
+    unsigned long long epoch;
+};
+
+__device__ __forceinline__ unsigned long long load_acquire_sys_u64(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void store_release_sys_u64(unsigned long long *p, unsigned long long v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
 // The ordered walk of a segment, one CTA of NT threads; a chunk is resolved with CHUNK / NT
 // consecutive elements per thread.  In the one-launch form it runs beside the CTAs that build
 // the maps: it reads a map only after its publication flag (a bounded wait at the chunk level;
@@ -1141,7 +1161,7 @@ __device__ __forceinline__ void mse_walk(
     const MseHead *heads1, const typename MseTraits<T>::D *deltas1, const MseHead *heads2,
     const typename MseTraits<T>::D *deltas2, uint64_t chunks, uint64_t blocks, uint64_t supers, uint64_t base,
     uint64_t total, T denominator, int policy, const T *carry_in, T *carry_out, T *out, unsigned long long *status,
-    const MseSync &sync) {
+    const MseSync &sync, const CarryLink &link) {
     using Tr = MseTraits<T>;
     using F = Fmt<T>;
     using U = typename WalkAcc<T>::U;
@@ -1166,16 +1186,27 @@ __device__ __forceinline__ void mse_walk(
     // [base, base + n); a fault already recorded in front of it stops it at once.
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (tid == 0) {
+        s_done = 0;
+        if (link.in_flag) {  // the previous rank's running sum, over NVLink (bounded wait)
+            const unsigned long long t0 = global_ns();
+            while (load_acquire_sys_u64(link.in_flag) < link.epoch) {
+                if (global_ns() - t0 > kPeerWaitLimitNs) {
+                    record_fault(status, 0, kWatchdog);
+                    s_done = 3;
+                    break;
+                }
+                __nanosleep(512);
+            }
+        }
         const unsigned long long st0 = read_status(status);
-        uint64_t stop = n;
+        uint64_t stop = s_done == 3 ? 0 : n;
         if (st0 != kStatusOk && (st0 & 7) != kWatchdog) {
             const uint64_t first = (st0 >> 3) / 3;
             stop = first < base ? 0 : (first - base < n ? first - base : n);
         }
         s_end = stop;
-        s_sum = carry_in ? *carry_in : T(0);
+        s_sum = carry_in ? *(volatile const T *)carry_in : T(0);
         s_g = 0;
-        s_done = 0;
     }
     if (tid < 32) s_warp_sum[tid] = 0;
     __syncthreads();
@@ -1367,8 +1398,12 @@ __device__ __forceinline__ void mse_walk(
         if (s_done == 2) break;
     }
     if (tid == 0) {
+        if (s_done != 3 && carry_out) *carry_out = s_sum;  // the running sum handed to the next segment
+        if (link.out_flag) {  // published even after a give-up: the next rank must not wait for it
+            __threadfence_system();
+            store_release_sys_u64(link.out_flag, link.epoch);
+        }
         if (s_done == 3) return;  // a wait gave up: the status word says so
-        if (carry_out) *carry_out = s_sum;  // the running sum handed to the next segment
         if (!out || s_done == 2 || s_end < n || fault_precedes(status, total * 3)) return;
         T mean;
         const unsigned kind = checked_div<T>(s_sum, denominator, policy, mean);
@@ -1393,16 +1428,17 @@ __device__ __forceinline__ void mse_walk(
 constexpr int kWalkThreads = 32 * kChunkWarps;  // the walker's CTA (also a chunk CTA's shape)
 
 template <typename T>
-__global__ void __launch_bounds__(kWalkThreads) mse_walk_kernel(PCU_MSE_WALK_PARAMS, ChainGuard guard) {
-    if (chain_admits(guard)) mse_walk<T, kWalkThreads>(PCU_MSE_WALK_ARGS, MseSync{});
+__global__ void __launch_bounds__(kWalkThreads) mse_walk_kernel(PCU_MSE_WALK_PARAMS, ChainGuard guard, CarryLink link) {
+    if (chain_admits(guard)) mse_walk<T, kWalkThreads>(PCU_MSE_WALK_ARGS, MseSync{}, link);
 }
 
 // CTA 0 walks; the other CTAs stream an SGD node's elements meanwhile (the walker is latency
 // bound and holds one SM).
 template <typename T>
-__global__ void __launch_bounds__(kWalkThreads) mse_walk_sgd_kernel(PCU_MSE_WALK_PARAMS, SgdRider<T> rider) {
+__global__ void __launch_bounds__(kWalkThreads) mse_walk_sgd_kernel(PCU_MSE_WALK_PARAMS, SgdRider<T> rider,
+                                                                      CarryLink link) {
     if (blockIdx.x == 0) {
-        mse_walk<T, kWalkThreads>(PCU_MSE_WALK_ARGS, MseSync{});
+        mse_walk<T, kWalkThreads>(PCU_MSE_WALK_ARGS, MseSync{}, link);
         return;
     }
     sgd_range<T>(rider, 0, rider.n, (uint64_t)(blockIdx.x - 1) * blockDim.x + threadIdx.x,
@@ -1427,13 +1463,13 @@ mse_onepass_kernel(const T *prediction, const T *target, uint64_t n, bool vec, i
                    uint64_t blocks, uint64_t supers, uint64_t ahead, MseHead *h0, typename MseTraits<T>::D *d0,
                    MseHead *h1, typename MseTraits<T>::D *d1, MseHead *h2, typename MseTraits<T>::D *d2,
                    MseSync sync, T denominator, T *out, unsigned long long *status, SgdRider<T> rider,
-                   ChainGuard guard, uint64_t base, uint64_t total, const T *carry_in, T *carry_out) {
+                   ChainGuard guard, uint64_t base, uint64_t total, const T *carry_in, T *carry_out, CarryLink link) {
     using Tr = MseTraits<T>;
     if constexpr (!RIDE)
         if (!chain_admits(guard)) return;  // the whole launch, walker included
     if (blockIdx.x == 0) {
         mse_walk<T, kWalkThreads>(prediction, target, n, h0, d0, h1, d1, h2, d2, chunks, blocks, supers, base, total,
-                                  denominator, policy, carry_in, carry_out, out, status, sync);
+                                  denominator, policy, carry_in, carry_out, out, status, sync, link);
         return;
     }
     // the chunk warps' slots; once the chunks are done, the staging area of a composition (all
@@ -1601,7 +1637,8 @@ int prepare_mse(int policy, const T *p, const T *t, uint64_t n, uint64_t base, v
 template <typename T>
 int walk_mse(int policy, const T *p, const T *t, uint64_t n, uint64_t base, uint64_t total, const T *carry_in,
              T *carry_out, T *out, void *workspace, size_t workspace_bytes, unsigned long long *status,
-             cudaStream_t stream, const SgdRider<T> *sgd = nullptr, const ChainGuard &guard = ChainGuard{}) {
+             cudaStream_t stream, const SgdRider<T> *sgd = nullptr, const ChainGuard &guard = ChainGuard{},
+             const CarryLink &link = CarryLink{}) {
     using D = typename MseTraits<T>::D;
     constexpr unsigned THREADS = kWalkThreads;
     MseLayout<T> lay(n);
@@ -1616,11 +1653,11 @@ int walk_mse(int policy, const T *p, const T *t, uint64_t n, uint64_t base, uint
         const unsigned extra = (unsigned)(want < cap ? want : cap);
         mse_walk_sgd_kernel<T><<<1 + extra, THREADS, 0, stream>>>(
             p, t, n, H(0), R(0), H(1), R(1), H(2), R(2), lay.count[0], lay.count[1], lay.count[2], base, total,
-            count_value<T>(total), policy, carry_in, carry_out, out, status, *sgd);
+            count_value<T>(total), policy, carry_in, carry_out, out, status, *sgd, link);
     } else {
         mse_walk_kernel<T><<<1, THREADS, 0, stream>>>(p, t, n, H(0), R(0), H(1), R(1), H(2), R(2), lay.count[0],
                                                       lay.count[1], lay.count[2], base, total, count_value<T>(total),
-                                                      policy, carry_in, carry_out, out, status, guard);
+                                                      policy, carry_in, carry_out, out, status, guard, link);
     }
     return pcu_host::launch_status();
 }
@@ -1630,7 +1667,8 @@ int walk_mse(int policy, const T *p, const T *t, uint64_t n, uint64_t base, uint
 template <typename T>
 int onepass_mse(int policy, const T *p, const T *t, T *out, uint64_t n, void *workspace, size_t workspace_bytes,
                 unsigned long long *status, cudaStream_t stream, const SgdRider<T> *sgd, const ChainGuard &guard,
-                uint64_t base = 0, uint64_t total = 0, const T *carry_in = nullptr, T *carry_out = nullptr) {
+                uint64_t base = 0, uint64_t total = 0, const T *carry_in = nullptr, T *carry_out = nullptr,
+                const CarryLink &link = CarryLink{}) {
     if (!total) total = n;  // a whole reduction unless a segment [base, base + n) of `total`
     MseLayout<T> lay(n);
     if (!workspace || workspace_bytes < lay.bytes) return PCU_B200_ERROR_WORKSPACE;
@@ -1672,15 +1710,17 @@ int onepass_mse(int policy, const T *p, const T *t, T *out, uint64_t n, void *wo
     if (ride)
         mse_onepass_kernel<T, true, kRideGroupsPerCta><<<grid, kWalkThreads, 0, stream>>>(
             p, t, n, vec, policy, lay.count[0], lay.count[1], lay.count[2], ahead, H(0), R(0), H(1), R(1), H(2), R(2),
-            sync, count_value<T>(total), out, status, *sgd, guard, base, total, carry_in, carry_out);
+            sync, count_value<T>(total), out, status, *sgd, guard, base, total, carry_in, carry_out, link);
     else if (g == kGroupsPerCta)
         mse_onepass_kernel<T, false, kGroupsPerCta><<<grid, kWalkThreads, 0, stream>>>(
             p, t, n, vec, policy, lay.count[0], lay.count[1], lay.count[2], ahead, H(0), R(0), H(1), R(1), H(2), R(2),
-            sync, count_value<T>(total), out, status, SgdRider<T>{}, guard, base, total, carry_in, carry_out);
+            sync, count_value<T>(total), out, status, SgdRider<T>{}, guard, base, total, carry_in, carry_out,
+            link);
     else
         mse_onepass_kernel<T, false, 1><<<grid, kWalkThreads, 0, stream>>>(
             p, t, n, vec, policy, lay.count[0], lay.count[1], lay.count[2], ahead, H(0), R(0), H(1), R(1), H(2), R(2),
-            sync, count_value<T>(total), out, status, SgdRider<T>{}, guard, base, total, carry_in, carry_out);
+            sync, count_value<T>(total), out, status, SgdRider<T>{}, guard, base, total, carry_in, carry_out,
+            link);
     return pcu_host::launch_status();
 }
 
@@ -1921,7 +1961,7 @@ namespace pcu {
 template <typename T>
 int run_mse_sgd_segment(int policy, const T *p, const T *t, uint64_t n, uint64_t base, uint64_t total, const T *carry_in,
                         T *carry_out, T *out, void *workspace, size_t workspace_bytes, unsigned long long *mse_status,
-                        const SgdRider<T> &sgd, cudaStream_t stream) {
+                        const SgdRider<T> &sgd, cudaStream_t stream, const CarryLink &link = CarryLink{}) {
     MseLayout<T> lay(n);
     if (!workspace || workspace_bytes < lay.bytes) return PCU_B200_ERROR_WORKSPACE;
     if constexpr (sizeof(T) == 4) {
@@ -1930,7 +1970,7 @@ int run_mse_sgd_segment(int policy, const T *p, const T *t, uint64_t n, uint64_t
             split_sgd<T>(sgd, sgd_units(lay.count[0], kChunkWarps * kRideGroupsPerCta, kRidePeriod, kRideSgd), head,
                          tail);
             int rc = onepass_mse<T>(policy, p, t, out, n, workspace, workspace_bytes, mse_status, stream, &head,
-                                    ChainGuard{}, base, total, carry_in, carry_out);
+                                    ChainGuard{}, base, total, carry_in, carry_out, link);
             if (rc || !tail.n) return rc;
             const uint64_t per_cta = 256ull * (16 / sizeof(T)) * kSgdTrip;
             const uint64_t cap = 8ull * pcu_host::sm_count();
@@ -1942,7 +1982,7 @@ int run_mse_sgd_segment(int policy, const T *p, const T *t, uint64_t n, uint64_t
     int rc = prepare_mse_sgd<T>(policy, p, t, n, base, workspace, workspace_bytes, mse_status, sgd, stream);
     if (rc) return rc;
     return walk_mse<T>(policy, p, t, n, base, total, carry_in, carry_out, out, workspace, workspace_bytes, mse_status,
-                       stream);
+                       stream, nullptr, ChainGuard{}, link);
 }
 }  // namespace pcu
 
@@ -1975,4 +2015,170 @@ extern "C" int pcu_b200_strict_mse_sgd_segment(int dtype, int policy, const void
         policy, (const double *)prediction, (const double *)target, mse_count, mse_first_index, total_count,
         (const double *)carry_in, (double *)carry_out, (double *)out, workspace, workspace_bytes, ms,
         pcu::make_rider<double>(policy, weights, gradient, updated, sgd_count, sgd_first_index, rate_bits_f32, ss), s);
+}
+
+// ============================================================================
+// The split strict MSE with every exchange on the device (one process per GPU).
+//
+// Every rank's hand-off block (pcu_b200_peer_alloc, zero-filled, mapped into every peer with
+// pcu_b200_peer_open) holds the carry slot its predecessor stores into, and two banks of
+// exchange slots, one per rank, selected by the call number's parity.  A call is one launch of
+// the segment (maps and walk together for binary32) whose walker waits for the carry from rank
+// r - 1 and stores its own into rank r + 1's block, then mse_exchange_kernel: it stores this
+// rank's MSE and SGD words (and, on the last rank, the mean) into every peer's slot, waits for
+// every peer's slot of the same call, and leaves the MIN of all ranks' words and the mean on
+// this rank.  A rank's store of call e + 2 into a peer's bank can only follow that peer's exit
+// from call e (it needs the peer's call e + 1 slot first), so two banks never mix calls.
+// ============================================================================
+namespace {
+
+constexpr int kHandoffRanks = 8;
+
+struct HandoffSlot {
+    unsigned long long mse, sgd, mean, epoch;
+};
+
+struct HandoffBlock {
+    unsigned long long carry;        // the running sum's bits (binary32 in the low half)
+    unsigned long long carry_epoch;  // call number of `carry`
+    unsigned long long pad[6];
+    HandoffSlot slot[2][kHandoffRanks];
+};
+
+struct ExchangeArgs {
+    HandoffBlock *blocks[kHandoffRanks];  // as this process sees them; blocks[rank] is its own
+    unsigned long long *mse_status, *sgd_status;  // sgd_status may be null
+    void *mean;                                   // this rank's mean output
+    unsigned long long epoch;
+    int rank, nranks, mean_bytes;
+};
+
+__global__ void __launch_bounds__(32) mse_exchange_kernel(const __grid_constant__ ExchangeArgs a) {
+    using pcu::load_acquire_sys_u64;
+    using pcu::store_release_sys_u64;
+    const int q = threadIdx.x, last = a.nranks - 1;
+    const int bank = (int)(a.epoch & 1);
+    const unsigned long long mse = *(volatile unsigned long long *)a.mse_status;
+    const unsigned long long sgd = a.sgd_status ? *(volatile unsigned long long *)a.sgd_status : ~0ull;
+    unsigned long long mean = 0;
+    if (a.rank == last)
+        mean = a.mean_bytes == 8 ? *(volatile unsigned long long *)a.mean : *(volatile unsigned *)a.mean;
+    const bool peer = q < a.nranks && q != a.rank;
+    if (peer) {
+        HandoffSlot *dst = &a.blocks[q]->slot[bank][a.rank];
+        dst->mse = mse;
+        dst->sgd = sgd;
+        dst->mean = mean;
+        __threadfence_system();
+        store_release_sys_u64(&dst->epoch, a.epoch);
+    }
+    bool ok = true;
+    unsigned long long m_mse = mse, m_sgd = sgd, peer_mean = 0;
+    if (peer) {
+        const HandoffSlot *src = &a.blocks[a.rank]->slot[bank][q];
+        const unsigned long long t0 = pcu::global_ns();
+        while (load_acquire_sys_u64(&src->epoch) < a.epoch) {
+            if (pcu::global_ns() - t0 > pcu::kPeerWaitLimitNs) {
+                ok = false;
+                break;
+            }
+            __nanosleep(256);
+        }
+        if (ok) {
+            const unsigned long long pm = *(volatile const unsigned long long *)&src->mse;
+            const unsigned long long ps = *(volatile const unsigned long long *)&src->sgd;
+            m_mse = pm < m_mse ? pm : m_mse;
+            m_sgd = ps < m_sgd ? ps : m_sgd;
+            peer_mean = *(volatile const unsigned long long *)&src->mean;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        const unsigned long long om = __shfl_xor_sync(0xffffffffu, m_mse, o);
+        const unsigned long long os = __shfl_xor_sync(0xffffffffu, m_sgd, o);
+        m_mse = om < m_mse ? om : m_mse;
+        m_sgd = os < m_sgd ? os : m_sgd;
+    }
+    const bool all_ok = __all_sync(0xffffffffu, ok);
+    if (q == 0) {
+        constexpr unsigned long long kGaveUp = (0ull << 3) | pcu::kWatchdog;
+        *a.mse_status = all_ok ? m_mse : kGaveUp;
+        if (a.sgd_status) *a.sgd_status = m_sgd;
+    }
+    if (q == last && peer && ok) {  // the mean comes from the last rank
+        if (a.mean_bytes == 8) *(unsigned long long *)a.mean = peer_mean;
+        else *(unsigned *)a.mean = (unsigned)peer_mean;
+    }
+}
+
+}  // namespace
+
+extern "C" size_t pcu_b200_mse_handoff_bytes(void) { return (sizeof(HandoffBlock) + 255) / 256 * 256; }
+
+extern "C" int pcu_b200_strict_mse_sgd_split(int dtype, int policy, const void *prediction, const void *target,
+                                             uint64_t mse_count, uint64_t mse_first_index, uint64_t total_count,
+                                             void *mean_out, void *workspace, size_t workspace_bytes,
+                                             uint64_t *mse_status, const void *weights, const void *gradient,
+                                             void *updated, uint64_t sgd_count, uint64_t sgd_first_index,
+                                             uint32_t rate_bits_f32, uint64_t *sgd_status, void *const *blocks,
+                                             int rank, int nranks, uint64_t epoch, void *stream) {
+    if ((dtype != PCU_B200_F32 && dtype != PCU_B200_F64) || policy < 0 || policy > 2 || !mse_status || !mean_out)
+        return PCU_B200_ERROR_INVALID_ARGUMENT;
+    if (nranks < 1 || nranks > kHandoffRanks || rank < 0 || rank >= nranks || !blocks || epoch == 0)
+        return PCU_B200_ERROR_INVALID_ARGUMENT;
+    for (int r = 0; r < nranks; ++r)
+        if (!blocks[r]) return PCU_B200_ERROR_INVALID_ARGUMENT;
+    if (mse_count && (!prediction || !target)) return PCU_B200_ERROR_INVALID_ARGUMENT;
+    if (sgd_count && !sgd_status) return PCU_B200_ERROR_INVALID_ARGUMENT;
+    if (sgd_count && !valid_sgd_args(dtype, sgd_count, weights, gradient, updated, rate_bits_f32, sgd_status))
+        return PCU_B200_ERROR_INVALID_ARGUMENT;
+    if (total_count == 0 || total_count > (1ull << 58) || mse_first_index > total_count ||
+        mse_count > total_count - mse_first_index)
+        return PCU_B200_ERROR_SIZE_OVERFLOW;
+    if ((rank == nranks - 1) != (mse_first_index + mse_count == total_count)) return PCU_B200_ERROR_INVALID_ARGUMENT;
+    if (sgd_count > (1ull << 59) || sgd_first_index > (1ull << 59) - sgd_count) return PCU_B200_ERROR_SIZE_OVERFLOW;
+    auto *ms = reinterpret_cast<unsigned long long *>(mse_status);
+    auto *ss = reinterpret_cast<unsigned long long *>(sgd_status);
+    cudaStream_t s = pcu_host::as_stream(stream);
+    auto *mine = static_cast<HandoffBlock *>(blocks[rank]);
+    pcu::CarryLink link{};
+    link.epoch = epoch;
+    const void *carry_in = nullptr;
+    void *carry_out = nullptr;
+    if (rank > 0) {
+        carry_in = &mine->carry;
+        link.in_flag = &mine->carry_epoch;
+    }
+    if (rank < nranks - 1) {
+        auto *next = static_cast<HandoffBlock *>(blocks[rank + 1]);
+        carry_out = &next->carry;
+        link.out_flag = &next->carry_epoch;
+    }
+    void *out = rank == nranks - 1 ? mean_out : nullptr;
+    int rc;
+    if (dtype == PCU_B200_F32)
+        rc = pcu::run_mse_sgd_segment<float>(
+            policy, (const float *)prediction, (const float *)target, mse_count, mse_first_index, total_count,
+            (const float *)carry_in, (float *)carry_out, (float *)out, workspace, workspace_bytes, ms,
+            pcu::make_rider<float>(policy, weights, gradient, updated, sgd_count, sgd_first_index, rate_bits_f32, ss),
+            s, link);
+    else
+        rc = pcu::run_mse_sgd_segment<double>(
+            policy, (const double *)prediction, (const double *)target, mse_count, mse_first_index, total_count,
+            (const double *)carry_in, (double *)carry_out, (double *)out, workspace, workspace_bytes, ms,
+            pcu::make_rider<double>(policy, weights, gradient, updated, sgd_count, sgd_first_index, rate_bits_f32,
+                                    ss),
+            s, link);
+    if (rc || nranks == 1) return rc;
+    ExchangeArgs a{};
+    for (int r = 0; r < nranks; ++r) a.blocks[r] = static_cast<HandoffBlock *>(blocks[r]);
+    a.mse_status = ms;
+    a.sgd_status = ss;
+    a.mean = mean_out;
+    a.epoch = epoch;
+    a.rank = rank;
+    a.nranks = nranks;
+    a.mean_bytes = dtype == PCU_B200_F64 ? 8 : 4;
+    mse_exchange_kernel<<<1, 32, 0, s>>>(a);
+    return pcu_host::launch_status();
 }

@@ -111,6 +111,39 @@ class _CudaArray:
                                          "version": 3}
 
 
+def _map_peer_buffer(nbytes, group):
+    """Allocate `nbytes` of zero-filled device memory with an IPC handle on every rank and map every
+    peer's: (this rank's pointer, every rank's pointer in rank order as this process sees it)."""
+    import ctypes
+
+    L = pcu.library()
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    ptr, handle = ctypes.c_void_p(), (ctypes.c_ubyte * 64)()
+    pcu._check(L.pcu_b200_peer_alloc(nbytes, ctypes.byref(ptr), handle))
+    handles = [None] * world
+    dist.all_gather_object(handles, bytes(handle), group=group)
+    ptrs = []
+    for r, h in enumerate(handles):
+        if r == rank:
+            ptrs.append(ptr.value)
+            continue
+        q = ctypes.c_void_p()
+        pcu._check(L.pcu_b200_peer_open((ctypes.c_ubyte * 64).from_buffer_copy(h), ctypes.byref(q)))
+        ptrs.append(q.value)
+    return ptr.value, ptrs
+
+
+def _unmap_peer_buffer(own, ptrs, group):
+    """Unmap the peers' buffers, wait for every rank to do the same, free this rank's own."""
+    L = pcu.library()
+    dist.barrier(group=group)
+    for q in ptrs:
+        if q != own:
+            L.pcu_b200_peer_close(q)
+    dist.barrier(group=group)
+    L.pcu_b200_peer_free(own)
+
+
 class PeerRows:
     """A rows x columns matrix of which every rank holds a copy that all ranks write into (CUDA IPC,
     pcu_b200_peer_alloc / _open): the destination of the fused row-sharded MatMul + all-gather.
@@ -189,23 +222,61 @@ class ShardedMse:
 
     prediction/target: this rank's segment, the global elements [first_index, first_index + n)
     of `total`.  run() returns the mean (a device scalar, the same on every rank) and leaves the
-    all-reduced first fault in `status`."""
+    global first fault in `status`.
 
-    def __init__(self, prediction, target, first_index, total, policy=0, group=None):
+    handoff="device" (the default on GPUs): pcu_b200_strict_mse_sgd_split -- every rank's segment
+    is one launch whose walker takes the running sum from rank r - 1 and hands its own to rank
+    r + 1 through IPC-mapped hand-off blocks, and a one-warp exchange leaves the MIN of the status
+    words and the mean on every rank; no NCCL call and no host round trip.  handoff="nccl": the
+    same hand-off with torch.distributed send/recv, broadcast and all-reduce (any backend)."""
+
+    def __init__(self, prediction, target, first_index, total, policy=0, group=None, handoff="device"):
         self.p, self.t = prediction, target
         self.first, self.total, self.policy, self.group = first_index, total, policy, group
         self.workspace = pcu.mse_workspace(prediction)
         self.carry = torch.zeros(1, dtype=prediction.dtype, device=prediction.device)
         self.mean = torch.zeros(1, dtype=prediction.dtype, device=prediction.device)
         self.last = first_index + prediction.numel() == total
+        self.handoff = handoff
+        self.calls = 0
+        if handoff == "device":
+            self._own, self._blocks = _map_peer_buffer(pcu.library().pcu_b200_mse_handoff_bytes(), group)
+
+    def close(self):
+        """Release the hand-off blocks (every rank, after its last call)."""
+        if self.handoff == "device" and self._own:
+            _unmap_peer_buffer(self._own, self._blocks, self.group)
+            self._own = None
+
+    def _run_device(self, status, stream, sgd):
+        import ctypes
+
+        L = pcu.library()
+        rank, world = dist.get_rank(self.group), dist.get_world_size(self.group)
+        blocks = (ctypes.c_void_p * world)(*self._blocks)
+        if sgd is None:
+            sgd_args = (None, None, None, 0, 0, 0, None)
+        else:
+            rate_bits = int(np.array([sgd["rate"]], dtype=np.float32).view(np.uint32)[0])
+            sgd_args = (pcu._ptr(sgd["weights"]), pcu._ptr(sgd["gradient"]), pcu._ptr(sgd["out"]),
+                        sgd["weights"].numel(), sgd["first_index"], rate_bits, pcu._ptr(sgd["status"]))
+        pcu._check(L.pcu_b200_strict_mse_sgd_split(
+            pcu._dtype_code(self.p), self.policy, pcu._ptr(self.p), pcu._ptr(self.t), self.p.numel(), self.first,
+            self.total, pcu._ptr(self.mean), pcu._ptr(self.workspace), self.workspace.numel(), pcu._ptr(status),
+            *sgd_args, blocks, rank, world, self.calls + 1, pcu._stream(stream)))
+        self.calls += 1
+        return self.mean.reshape(())
 
     def run(self, status, stream=None, reduce_status=True, sgd=None):
         """`sgd`: optionally an independent strict SGD block carried by the bandwidth-bound phase,
         a dict with weights, gradient, rate, first_index (its global first element), out and
-        status (its own word, global events; not all-reduced here).
+        status (its own word, global events; MIN-reduced with the MSE's in the device hand-off,
+        left to the caller in the NCCL one).
 
         The first segment's running sum starts at +0, so its rank walks at once, in the same
         launch as its maps; the others build their maps at once and walk when the carry arrives."""
+        if self.handoff == "device":
+            return self._run_device(status, stream, sgd)
         first = dist.get_rank(self.group) == 0
         if first:
             pcu.strict_mse_sgd_segment(self.p, self.t, self.first, self.total, None, self.carry, self.workspace, status,

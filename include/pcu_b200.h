@@ -294,6 +294,32 @@ int pcu_b200_strict_mse_sgd_segment(int dtype, int policy, const void *predictio
                                     const void *gradient, void *updated, uint64_t sgd_count, uint64_t sgd_first_index,
                                     uint32_t rate_bits_f32, uint64_t *sgd_status, void *stream);
 
+/* The split strict MSE (with an optional independent strict SGD node riding along) with every
+ * exchange on the device: one process per GPU of one node, nranks <= 8, rank r holding the
+ * global elements [mse_first_index, mse_first_index + mse_count) of a total_count-element
+ * reduction, the segments in rank order (rank nranks - 1 holds the last one).
+ *   - blocks: nranks device pointers in rank order, each rank's hand-off block
+ *     (pcu_b200_mse_handoff_bytes bytes from pcu_b200_peer_alloc, mapped here with
+ *     pcu_b200_peer_open; blocks[rank] is this rank's own);
+ *   - epoch numbers the calls on this set of blocks (1, 2, 3, ..., the same on every rank).
+ * The segment's maps and walk run as one launch (binary32; three for binary64).  The walker of
+ * rank r > 0 waits until rank r - 1 has stored its running sum into this rank's block, and
+ * rank r < nranks - 1 stores its own into rank r + 1's (plain NVLink stores and a release flag:
+ * no NCCL, no host round trip).  Then a one-warp exchange stores this rank's words into every
+ * peer's block and waits for theirs.  When the work on `stream` is done, on every rank:
+ * *mse_status and *sgd_status hold the MIN over ranks (the global first faults; words carry
+ * global events), *mean_out holds the mean (binary32/64 as dtype).  A device wait that gives up
+ * (10 s) leaves PCU_B200_STATUS_WATCHDOG in *mse_status.  The SGD node ([sgd_first_index,
+ * sgd_first_index + sgd_count) of its own tensor) is as in pcu_b200_strict_mse_sgd_segment.
+ * No counterpart in the reference (its strict MSE runs on one lane of one device). */
+size_t pcu_b200_mse_handoff_bytes(void);
+int pcu_b200_strict_mse_sgd_split(int dtype, int policy, const void *prediction, const void *target,
+                                  uint64_t mse_count, uint64_t mse_first_index, uint64_t total_count, void *mean_out,
+                                  void *workspace, size_t workspace_bytes, uint64_t *mse_status, const void *weights,
+                                  const void *gradient, void *updated, uint64_t sgd_count, uint64_t sgd_first_index,
+                                  uint32_t rate_bits_f32, uint64_t *sgd_status, void *const *blocks, int rank,
+                                  int nranks, uint64_t epoch, void *stream);
+
 /* ------------------------------------------------------------------ checked elementwise */
 
 /* out[i] = op(left[i], right[i]); a nonzero *_uniform flag broadcasts element 0 of that
@@ -453,18 +479,17 @@ int pcu_b200_comm_strict_matmul_rows(pcu_b200_comm *comm, int dtype, int policy,
                                      uint64_t right_stride, int transpose_right, void *workspace,
                                      size_t workspace_bytes, uint64_t *status, void *stream);
 
-/* A strict MSE over total_count elements split into contiguous, non-empty segments in rank
- * order.  Rank r holds the global elements [first_index, first_index + count), and the last rank
- * ends at total_count.
- *   * Rank 0 builds its maps and walks them in one launch.
- *   * Every other rank builds its maps at once, receives the running sum from rank r - 1 into
- *     `carry` (a device scalar), walks, and sends the sum on to rank r + 1.
- * The checked mean is broadcast into out[0] on every rank, and `status` becomes the global first
- * fault.  The result equals pcu_b200_strict_mse over the whole tensor.  The workspace is
- * pcu_b200_strict_mse_workspace_size(dtype, count). */
+/* The split strict MSE in one call: rank r holds the global elements [first_index, first_index +
+ * count) of a total_count-element reduction, the segments in rank order.  It runs
+ * pcu_b200_strict_mse_sgd_split: the running sum goes from rank to rank on the device through
+ * IPC-mapped hand-off blocks that the first call makes (collectively, like every call here, and
+ * kept until the communicator is freed), and a one-warp exchange leaves the mean in *out and the
+ * global first fault in *status on every rank.  No NCCL call after the first.  The segments are
+ * non-empty and the last rank's ends at total_count; the result equals pcu_b200_strict_mse over
+ * the whole tensor.  The workspace is pcu_b200_strict_mse_workspace_size(dtype, count). */
 int pcu_b200_comm_strict_mse(pcu_b200_comm *comm, int dtype, int policy, const void *prediction, const void *target,
-                             uint64_t count, uint64_t first_index, uint64_t total_count, void *carry, void *out,
-                             void *workspace, size_t workspace_bytes, uint64_t *status, void *stream);
+                             uint64_t count, uint64_t first_index, uint64_t total_count, void *out, void *workspace,
+                             size_t workspace_bytes, uint64_t *status, void *stream);
 
 #ifdef __cplusplus
 }

@@ -31,6 +31,6 @@ def test_arguments_are_checked_first(provider):
     assert lib.pcu_b200_comm_peer_buffers_free(None, bufs, None) == 1
     assert lib.pcu_b200_comm_strict_matmul_rows(None, 0, 0, None, None, bufs, 0, 1, 1, 1, 1, 1, 1, 0, None, 0, None,
                                                 None) == 1
-    assert lib.pcu_b200_comm_strict_mse(None, 0, 0, None, None, 1, 0, 1, None, None, None, 0, None, None) == 1
+    assert lib.pcu_b200_comm_strict_mse(None, 0, 0, None, None, 1, 0, 1, None, None, 0, None, None) == 1
     assert lib.pcu_b200_error_string(7).decode().startswith("communicator failure")
     assert lib.pcu_b200_last_comm_error() == 0

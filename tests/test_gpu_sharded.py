@@ -116,11 +116,28 @@ def _nccl_worker(rank, world, port, queue):
         sgd_out = sharded.strict_sgd_block(to_device(p[e0:e1]), to_device(t[e0:e1]), 0.25, e0, st2)
         sharded.all_reduce_min_status(st2)
         st3 = pcu.new_status()
-        mse = sharded.ShardedMse(to_device(p[e0:e1]), to_device(t[e0:e1]), e0, e)
+        mse = sharded.ShardedMse(to_device(p[e0:e1]), to_device(t[e0:e1]), e0, e, handoff="nccl")
         mean = mse.run(st3)
         torch.cuda.synchronize()
+        # the device hand-off on the same segments: twice in a row (the exchange banks alternate)
+        # and then with an SGD node riding along, whose word is MIN-reduced with the MSE's
+        dev = sharded.ShardedMse(to_device(p[e0:e1]), to_device(t[e0:e1]), e0, e)
+        dev_words, dev_means = [], []
+        for _ in range(2):
+            st4 = pcu.new_status()
+            dev_means.append(bits(to_host(dev.run(st4)).reshape(1))[0])
+            torch.cuda.synchronize()
+            dev_words.append(status_word(st4))
+        st5, st6 = pcu.new_status(), pcu.new_status()
+        w_out = torch.empty(e1 - e0, dtype=torch.float32, device="cuda")
+        rider = {"weights": to_device(p[e0:e1]), "gradient": to_device(t[e0:e1]), "rate": 0.25, "first_index": e0,
+                 "out": w_out, "status": st6}
+        dev_means.append(bits(to_host(dev.run(st5, sgd=rider)).reshape(1))[0])
+        torch.cuda.synchronize()
+        dev_words += [status_word(st5), status_word(st6)]
+        dev.close()
         queue.put((rank, mm_word, mm_bits, status_word(st2), bits(to_host(sgd_out)), status_word(st3),
-                   bits(to_host(mean).reshape(1))[0]))
+                   bits(to_host(mean).reshape(1))[0], dev_words, dev_means, bits(to_host(w_out))))
     finally:
         dist.destroy_process_group()
 
@@ -154,12 +171,16 @@ def test_nccl_sharded_matches_one_device():
     sgd_st, sgd_out = oracle.sgd(p, t, 0.25)
     mse_st, mse_out = oracle.mse(p, t)
     for rank in range(world):
-        mm_word, _, sgd_word, sgd_bits, mse_word, mean_bits = got[rank]
+        mm_word, _, sgd_word, sgd_bits, mse_word, mean_bits, dev_words, dev_means, _ = got[rank]
         assert mm_word == mm_st
         assert sgd_word == sgd_st and mse_word == mse_st
         assert mean_bits == bits(mse_out)[0]
+        assert dev_words == [mse_st, mse_st, mse_st, sgd_st], (rank, [hex(w) for w in dev_words])
+        assert all(m == bits(mse_out)[0] for m in dev_means), rank
     sgd_all = np.concatenate([got[r][3] for r in range(world)])
     assert np.array_equal(sgd_all, bits(sgd_out))
+    rider_all = np.concatenate([got[r][8] for r in range(world)])
+    assert np.array_equal(rider_all, bits(sgd_out))
 
 
 def _fused_worker(rank, world, port, queue):
@@ -315,3 +336,86 @@ def test_fused_rows_allgather_readers_are_not_overwritten():
             words, snaps = got[rank]
             assert words[i] == pcu.STATUS_OK, (rank, i, hex(words[i]))
             assert np.array_equal(snaps[i], want), (rank, i)
+
+
+def _mse_cases(world):
+    """(width, p, t) cases for the device hand-off: clean, a NaN in the last segment, squares whose
+    running sum overflows only once the carry from the earlier segments is added, and faults in
+    the first and the last segment (the first one wins)."""
+    e = 3 * 8192 + 515
+    out = []
+    for width in (32, 64):
+        rng = np.random.default_rng(4000 + width)
+        p, t = dyadic_uniform(rng, e, width), dyadic_uniform(rng, e, width)
+        out.append((width, "clean", p, t))
+        q = p.copy()
+        q[e - 7] = np.nan
+        out.append((width, "nan_last", q, t))
+        # one huge square at the end of segment 0 and one at the start of segment 1: each is
+        # finite, their sum is not, so rank 1's walk overflows on the carried sum
+        sharded = importlib.import_module("fusion-pcu_b200.sharded")
+        b1 = sharded.shard_bounds(e, 0, world, align=4)[1]
+        big = 1.5e19 if width == 32 else 1e154
+        q, r = p.copy(), t.copy()
+        q[b1 - 1:b1 + 1] = big
+        r[b1 - 1:b1 + 1] = 0
+        out.append((width, "overflow_by_carry", q, r))
+        q = p.copy()
+        q[5] = np.inf
+        q[e - 3] = np.nan
+        out.append((width, "first_wins", q, t))
+    return out
+
+
+def _device_mse_worker(rank, world, port, queue):
+    import torch
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    import datetime
+
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        sharded = importlib.import_module("fusion-pcu_b200.sharded")
+        results = []
+        for width, name, p, t in _mse_cases(world):
+            e = p.size
+            e0, e1 = sharded.shard_bounds(e, rank, world, align=4)
+            mse = sharded.ShardedMse(to_device(p[e0:e1]), to_device(t[e0:e1]), e0, e)
+            st = pcu.new_status()
+            mean = mse.run(st)
+            torch.cuda.synchronize()
+            results.append((status_word(st), bits(to_host(mean).reshape(1))[0]))
+            mse.close()
+        queue.put((rank, results))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_device_mse_handoff_faults_match_one_device():
+    import torch
+
+    world = min(torch.cuda.device_count(), 4)
+    if world < 2:
+        pytest.skip("needs 2 or more GPUs")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_device_mse_worker, args=(r, world, port, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(queue.get(timeout=300) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for i, (width, name, p, t) in enumerate(_mse_cases(world)):
+        st_o, out_o = oracle.mse(p, t)
+        for rank in range(world):
+            word, mean_bits = got[rank][i]
+            assert word == st_o, (name, width, rank, oracle.decode(word), oracle.decode(st_o))
+            if st_o == oracle.STATUS_OK:
+                assert mean_bits == bits(out_o)[0], (name, width, rank)

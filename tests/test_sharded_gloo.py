@@ -167,3 +167,59 @@ def test_sharded_faults_and_mse_handoff_match_one_pass(world):
         assert results[rank]["matmul"] == exp["matmul"], rank
         assert results[rank]["sgd"] == exp["sgd"], rank
         assert results[rank]["mse"] == exp["mse"], rank
+
+
+def _lost_rank_worker(rank, world, port, queue):
+    """Rank 1 leaves before the MSE hand-off (an exception between steps); the others must end with
+    an error from their next exchange within the process group's short timeout, not hang."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    import time
+
+    t0 = time.time()
+    try:
+        if rank == 1:
+            raise RuntimeError("rank 1 lost")
+        carry = torch.zeros(1, dtype=torch.int64)
+        sharded.ordered_handoff(carry, lambda c: c.add_(1))
+        mean = torch.zeros(1, dtype=torch.int64)
+        dist.broadcast(mean, src=world - 1)
+        status = torch.full((1,), -1, dtype=torch.int64)
+        sharded.all_reduce_min_status(status)
+        queue.put((rank, "completed", time.time() - t0))
+    except RuntimeError as e:
+        queue.put((rank, "error" if rank != 1 else "lost", time.time() - t0))
+        del e
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:  # noqa: BLE001 - the group is already broken
+            pass
+
+
+def test_lost_rank_ends_the_handoff_with_an_error():
+    import torch.multiprocessing as mp
+
+    world = 3
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_lost_rank_worker, args=(r, world, port, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict((r, (what, dt)) for r, what, dt in (queue.get(timeout=120) for _ in range(world)))
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert results[1][0] == "lost"
+    for rank in (0, 2):
+        what, dt = results[rank]
+        assert what == "error", (rank, what)
+        assert dt < 60, (rank, dt)
