@@ -354,18 +354,29 @@ def main():
         torch.cuda.synchronize()
         dist.barrier()
 
-    # ---- end to end through the host-boundary call (pcu_b200_strict_matmul_host): A's rows and
-    # B from page-locked host memory, C's rows and the status word back to it, every step; the
-    # uploads and read-backs overlap the arithmetic by row blocks inside the call
+    # ---- end to end from page-locked host memory, every step: A's rows and B go up, C's rows and
+    # the status word come back.  N = 1: the host-boundary call (pcu_b200_strict_matmul_host, B
+    # uploaded in column pieces, A and C by row blocks, all overlapped with the arithmetic).
+    # N > 1: each rank uploads its rows of A and only its 1/N slice of B's rows; the slices are
+    # all-gathered over NVLink and pcu_b200_strict_matmul_host_left computes the rank's rows.
     a_h = a.cpu().pin_memory()
-    b_h = b.cpu().pin_memory()
+    k0, k1 = rank * N // world, (rank + 1) * N // world
+    b_h = b[k0:k1].cpu().pin_memory()
     c_h = torch.empty((rows_per, N), dtype=torch.float32).pin_memory()
     s_h = torch.empty(1, dtype=torch.int64).pin_memory()
     del workspace
-    host_scratch = pcu.matmul_host_scratch(a_h, b_h, device=device)
+    if world == 1:
+        host_scratch = pcu.matmul_host_scratch(a_h, b_h, device=device)
 
-    def e2e_step():
-        pcu.strict_matmul_host(a_h, b_h, out=c_h, status=s_h, scratch=host_scratch, stream=stream)
+        def e2e_step():
+            pcu.strict_matmul_host(a_h, b_h, out=c_h, status=s_h, scratch=host_scratch, stream=stream)
+    else:
+        b_gathered = torch.empty((N, N), dtype=torch.float32, device=device)
+        host_scratch = torch.empty(lib.pcu_b200_strict_matmul_host_left_scratch_size(0, rows_per, N, N),
+                                   dtype=torch.uint8, device=device)
+
+        def e2e_step():
+            sharded.strict_matmul_rows_host(a_h, b_h, k0, b_gathered, c_h, s_h, scratch=host_scratch, stream=stream)
 
     e2e_step()
     torch.cuda.synchronize()
@@ -374,6 +385,8 @@ def main():
     e2e_ms = time_calls(torch, e2e_step, args.steps, stream, warm=0)
     assert int(s_h.numpy().view(np.uint64)[0]) == pcu.STATUS_OK
     del host_scratch, a_h, b_h, c_h
+    if world > 1:
+        del b_gathered
 
     times = torch.tensor([ms, kernel_ms, e2e_ms, fused_ms or 0.0], dtype=torch.float64, device=device)
     if world > 1:
@@ -412,11 +425,15 @@ def main():
                    "parallelism": f"row-sharded x{world}" + (
                        " + all-gather of C inside the MatMul kernel (peer stores over NVLink)" if world > 1 else ""),
                    "l2": "inputs (2 x 256 MiB) exceed the 126 MB L2; no flush needed"},
-        # every rank copies its A row block and all of B in, its C row block and status out
+        # per rank: its rows of A and its slice of B's rows in, its rows of C and its status out
         "e2e": {"value": FLOPS / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
-                "h2d_bytes_per_step": (rows_per + N) * N * 4, "d2h_bytes_per_step": rows_per * N * 4 + 8,
-                "call": "pcu_b200_strict_matmul_host (page-locked host buffers; uploads and read-backs "
-                        "overlapped with the arithmetic by row blocks)"},
+                "h2d_bytes_per_step": (rows_per + N // world) * N * 4, "d2h_bytes_per_step": rows_per * N * 4 + 8,
+                "bytes_per": "rank",
+                "call": ("pcu_b200_strict_matmul_host (page-locked host buffers; uploads and read-backs "
+                         "overlapped with the arithmetic by row blocks)") if world == 1 else
+                        ("each rank: its rows of A and 1/N of B's rows up from page-locked memory, B's slices "
+                         "all-gathered over NVLink (NCCL), pcu_b200_strict_matmul_host_left for its rows of C, "
+                         "C's rows and the status word back")},
         "roofline": {"bound": "fp32-issue", "achieved": kernel_tflops, "peak": peak_tflops, "unit": "TFLOP/s",
                      "frac": kernel_tflops / peak_tflops,
                      "peak_source": f"{sms} SMs x 128 FP32 lanes x sm_max_mhz {sm_max_mhz} ({peak_src}); "

@@ -18,7 +18,7 @@ import numpy as np
 __all__ = [
     "ProviderUnavailable", "TensorError", "ArithmeticFault", "CompoundArithmeticFault", "ProviderFailure",
     "library", "POLICY", "OPS", "STATUS_OK", "new_status", "decode_status", "strict_matmul", "strict_matmul_host",
-    "matmul_host_scratch", "strict_sgd",
+    "matmul_host_scratch", "strict_matmul_host_left", "strict_sgd",
     "strict_mse", "mse_workspace", "strict_mse_segment_prepare", "strict_mse_segment_walk", "strict_mse_sgd",
     "strict_mse_sgd_segment_prepare", "strict_mse_sgd_segment", "checked_binary", "checked_relu", "checked_relu_backward", "matmul_fault", "sgd_fault",
     "mse_fault", "element_fault", "GuardedChain", "CHAIN_OUTCOMES", "chain_validate", "wait",
@@ -92,6 +92,9 @@ def _declare(L):
     L.pcu_b200_strict_matmul_host_scratch_size.argtypes = [i32, u64, u64, u64]
     L.pcu_b200_strict_matmul_host_scratch_size.restype = sz
     L.pcu_b200_strict_matmul_host.argtypes = [i32, i32, vp, vp, vp, u64, u64, u64, vp, sz, vp, vp]
+    L.pcu_b200_strict_matmul_host_left_scratch_size.argtypes = [i32, u64, u64, u64]
+    L.pcu_b200_strict_matmul_host_left_scratch_size.restype = sz
+    L.pcu_b200_strict_matmul_host_left.argtypes = [i32, i32, vp, vp, u64, vp, u64, u64, u64, vp, sz, vp, vp]
     L.pcu_b200_issue_probe_ops.argtypes = [i32, u64]
     L.pcu_b200_issue_probe_ops.restype = u64
     L.pcu_b200_issue_probe.argtypes = [i32, u64, vp]
@@ -314,6 +317,31 @@ def strict_matmul_host(left, right, policy=0, out=None, status=None, scratch=Non
     _check(library().pcu_b200_strict_matmul_host(_dtype_code(left), policy, _ptr(left), _ptr(right), _ptr(out), rows,
                                                  inner, right.shape[1], _ptr(scratch), scratch.numel(), _ptr(status),
                                                  _stream(stream)))
+    return out, status
+
+
+def strict_matmul_host_left(left, right, policy=0, out=None, status=None, scratch=None, stream=None):
+    """C = A . B with A and C in host memory and B already on the device (row-major, unit column
+    stride): A's rows go up and C's rows come back by row blocks, overlapped with the arithmetic.
+    `status` is a host int64 tensor of one element.  Asynchronous, as strict_matmul_host."""
+    torch = _torch()
+    assert left.device.type == "cpu" and right.device.type == "cuda" and left.dtype == right.dtype
+    assert left.dim() == 2 and right.dim() == 2 and left.is_contiguous() and right.stride(1) == 1
+    rows, inner = left.shape
+    if right.shape[0] != inner:
+        raise ValueError(f"MatMulShape {tuple(left.shape)} {tuple(right.shape)}")
+    cols = right.shape[1]
+    L = library()
+    if out is None:
+        out = torch.empty((rows, cols), dtype=left.dtype).pin_memory()
+    if status is None:
+        status = torch.empty(1, dtype=torch.int64).pin_memory()
+    if scratch is None:
+        need = L.pcu_b200_strict_matmul_host_left_scratch_size(_dtype_code(left), rows, inner, cols)
+        scratch = torch.empty(need, dtype=torch.uint8, device=right.device)
+    _check(L.pcu_b200_strict_matmul_host_left(_dtype_code(left), policy, _ptr(left), _ptr(right),
+                                              max(right.stride(0), cols), _ptr(out), rows, inner, cols, _ptr(scratch),
+                                              scratch.numel(), _ptr(status), _stream(stream)))
     return out, status
 
 

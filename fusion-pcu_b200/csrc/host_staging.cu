@@ -83,18 +83,20 @@ int staging_for_device(Staging **out) {
     return PCU_B200_OK;
 }
 
+// Device scratch of a host-boundary call: B (unless it is already on the device), two row blocks
+// of A and of C, the MatMul workspace and the status words.
 struct HostLayout {
     int blocks;
     uint64_t block_rows;
     size_t b_off, a_off[2], c_off[2], ws_off, st_off, ws_bytes, bytes;
-    HostLayout(size_t elem, uint64_t rows, uint64_t inner, uint64_t columns) {
+    HostLayout(size_t elem, uint64_t rows, uint64_t inner, uint64_t columns, bool right_on_device = false) {
         auto up = [](size_t v) { return (v + 255) / 256 * 256; };
         blocks = (int)(rows / kRowsPerBlockMin);
         blocks = blocks < 1 ? 1 : (blocks > 4 ? 4 : blocks);
         block_rows = (rows + blocks - 1) / blocks;
         size_t off = 0;
         b_off = off;
-        off += up(inner * columns * elem);
+        if (!right_on_device) off += up(inner * columns * elem);
         const int buffers = blocks > 1 ? 2 : 1;
         for (int i = 0; i < 2; ++i) {
             a_off[i] = off;
@@ -124,9 +126,18 @@ extern "C" size_t pcu_b200_strict_matmul_host_scratch_size(int dtype, uint64_t r
     return HostLayout(dtype == PCU_B200_F64 ? 8 : 4, rows, inner, columns).bytes;
 }
 
-extern "C" int pcu_b200_strict_matmul_host(int dtype, int policy, const void *left, const void *right, void *out,
-                                           uint64_t rows, uint64_t inner, uint64_t columns, void *device_scratch,
-                                           size_t scratch_bytes, uint64_t *status_host, void *stream) {
+extern "C" size_t pcu_b200_strict_matmul_host_left_scratch_size(int dtype, uint64_t rows, uint64_t inner,
+                                                                uint64_t columns) {
+    return HostLayout(dtype == PCU_B200_F64 ? 8 : 4, rows, inner, columns, true).bytes;
+}
+
+namespace {
+
+// Both host-boundary forms: `right` in host memory (dense rows, uploaded here) or, with
+// right_on_device, already on the device with row stride right_stride.
+int run_host(int dtype, int policy, const void *left, const void *right, bool right_on_device, uint64_t right_stride,
+             void *out, uint64_t rows, uint64_t inner, uint64_t columns, void *device_scratch, size_t scratch_bytes,
+             uint64_t *status_host, void *stream) {
     if ((dtype != PCU_B200_F32 && dtype != PCU_B200_F64) || policy < 0 || policy > 2 || !status_host)
         return PCU_B200_ERROR_INVALID_ARGUMENT;
     if (rows == 0 || columns == 0) {
@@ -134,12 +145,13 @@ extern "C" int pcu_b200_strict_matmul_host(int dtype, int policy, const void *le
         return PCU_B200_OK;
     }
     if (!out || (inner > 0 && (!left || !right))) return PCU_B200_ERROR_INVALID_ARGUMENT;
+    if (right_on_device && inner > 0 && right_stride < columns) return PCU_B200_ERROR_INVALID_ARGUMENT;
     unsigned __int128 events = (unsigned __int128)rows * columns;
     events *= (inner ? inner : 1);
     events *= 2;
     if (events > ((unsigned __int128)1 << 60)) return PCU_B200_ERROR_SIZE_OVERFLOW;
     const size_t elem = dtype == PCU_B200_F64 ? 8 : 4;
-    const HostLayout lay(elem, rows, inner, columns);
+    const HostLayout lay(elem, rows, inner, columns, right_on_device);
     if (!device_scratch || scratch_bytes < lay.bytes) return PCU_B200_ERROR_WORKSPACE;
     std::lock_guard<std::mutex> guard(g_staging_lock);  // the event pool is shared per device
     Staging *stg = nullptr;
@@ -165,7 +177,11 @@ extern "C" int pcu_b200_strict_matmul_host(int dtype, int policy, const void *le
     const uint64_t align = 16 / elem;
     uint64_t sub_cols = (columns + kFirstSplit - 1) / kFirstSplit;
     sub_cols = (sub_cols + align - 1) / align * align;
-    const int split = (lay.blocks > 1 && inner > 0 && sub_cols >= 512) ? (int)((columns + sub_cols - 1) / sub_cols) : 1;
+    const int split = (!right_on_device && lay.blocks > 1 && inner > 0 && sub_cols >= 512)
+                          ? (int)((columns + sub_cols - 1) / sub_cols)
+                          : 1;
+    const char *b_dev = right_on_device ? reinterpret_cast<const char *>(right) : base + lay.b_off;
+    const uint64_t ldb = right_on_device ? right_stride : columns;
     Pieces pieces{};
     int words = 0;
 
@@ -185,7 +201,7 @@ extern "C" int pcu_b200_strict_matmul_host(int dtype, int policy, const void *le
             return rc;
         if ((rc = check(cudaEventRecord(ev_a(i), stg->up)))) return rc;
         if (i == 0) {  // B, in column blocks of `sub_cols` (the whole of B at once when split == 1)
-            for (int j = 0; j < split && inner > 0; ++j) {
+            for (int j = 0; j < split && inner > 0 && !right_on_device; ++j) {
                 const uint64_t c0 = (uint64_t)j * sub_cols, nc = split == 1 ? columns : std::min(sub_cols, columns - c0);
                 if ((rc = check(cudaMemcpy2DAsync(base + lay.b_off + c0 * elem, pitch,
                                                   reinterpret_cast<const char *>(right) + c0 * elem, pitch, nc * elem,
@@ -193,7 +209,7 @@ extern "C" int pcu_b200_strict_matmul_host(int dtype, int policy, const void *le
                     return rc;
                 if ((rc = check(cudaEventRecord(ev_bj(j), stg->up)))) return rc;
             }
-            if (inner == 0 && (rc = check(cudaEventRecord(ev_bj(0), stg->up)))) return rc;
+            if ((inner == 0 || right_on_device) && (rc = check(cudaEventRecord(ev_bj(0), stg->up)))) return rc;
         }
         // the block's product: after its rows of A, B (or its columns), and the read-back of this
         // C buffer two blocks back
@@ -205,8 +221,8 @@ extern "C" int pcu_b200_strict_matmul_host(int dtype, int policy, const void *le
             if (i == 0 && (rc = check(cudaStreamWaitEvent(s, ev_bj(parts == 1 ? 0 : j), 0)))) return rc;
             char *dcj = dc + (size_t)j * lay.block_rows * sub_cols * elem;  // dense nr x nc
             if ((rc = pcu_b200_status_reset(st + words, 1, s))) return rc;
-            rc = pcu::strict_matmul(dtype, policy, da, base + lay.b_off + c0 * elem, dcj, nr, inner, nc, inner, columns,
-                                    0, 0, base + lay.ws_off, lay.ws_bytes, st + words, s, pcu::ChainGuard{});
+            rc = pcu::strict_matmul(dtype, policy, da, b_dev + c0 * elem, dcj, nr, inner, nc, inner, ldb, 0, 0,
+                                    base + lay.ws_off, lay.ws_bytes, st + words, s, pcu::ChainGuard{});
             if (rc) return rc;
             pieces.row0[words] = r0;
             pieces.col0[words] = c0;
@@ -229,4 +245,21 @@ extern "C" int pcu_b200_strict_matmul_host(int dtype, int policy, const void *le
                                           inner, reinterpret_cast<unsigned long long *>(st + kMaxWords));
     if ((rc = pcu_host::launch_status())) return rc;
     return check(cudaMemcpyAsync(status_host, st + kMaxWords, sizeof(uint64_t), cudaMemcpyDeviceToHost, s));
+}
+
+}  // namespace
+
+extern "C" int pcu_b200_strict_matmul_host(int dtype, int policy, const void *left, const void *right, void *out,
+                                           uint64_t rows, uint64_t inner, uint64_t columns, void *device_scratch,
+                                           size_t scratch_bytes, uint64_t *status_host, void *stream) {
+    return run_host(dtype, policy, left, right, false, columns, out, rows, inner, columns, device_scratch,
+                    scratch_bytes, status_host, stream);
+}
+
+extern "C" int pcu_b200_strict_matmul_host_left(int dtype, int policy, const void *left, const void *right,
+                                                uint64_t right_stride, void *out, uint64_t rows, uint64_t inner,
+                                                uint64_t columns, void *device_scratch, size_t scratch_bytes,
+                                                uint64_t *status_host, void *stream) {
+    return run_host(dtype, policy, left, right, true, right_stride, out, rows, inner, columns, device_scratch,
+                    scratch_bytes, status_host, stream);
 }

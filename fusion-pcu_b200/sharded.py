@@ -94,6 +94,21 @@ def strict_matmul_rows(left_rows, right, row0, out_local, status, gathered=None,
     return out_local
 
 
+def strict_matmul_rows_host(left_rows, right_rows, k0, right_device, out_rows, status, scratch=None, stream=None,
+                            group=None, policy=0):
+    """The row-sharded product end to end from host memory: this rank's rows of A (host,
+    left_rows) and its slice of B's rows [k0, k0 + len) (host, right_rows) go up, the slices are
+    all-gathered over NVLink into `right_device` (the whole of B on every rank), and the rank's
+    rows of C come back to `out_rows` (host) with its status word (rank-local events) in `status`
+    (a host int64 tensor).  Every rank uploads its own slice of B only, so the PCIe traffic of the
+    whole job is A + B in and C out, each once.  B's row count must divide evenly by the ranks."""
+    k1 = k0 + right_rows.shape[0]
+    right_device[k0:k1].copy_(right_rows, non_blocking=True)
+    dist.all_gather_into_tensor(right_device, right_device[k0:k1], group=group)
+    return pcu.strict_matmul_host_left(left_rows, right_device, policy, out=out_rows, status=status, scratch=scratch,
+                                       stream=stream)
+
+
 # ------------------------------------------------------------------------------- SGD
 def strict_sgd_block(weights, gradient, rate, first_index, status, out=None, policy=0, stream=None):
     """SGD on this rank's element block [first_index, first_index + n) with global events."""

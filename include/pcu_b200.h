@@ -158,6 +158,20 @@ int pcu_b200_strict_matmul_host(int dtype, int policy, const void *left, const v
                                 uint64_t inner, uint64_t columns, void *device_scratch, size_t scratch_bytes,
                                 uint64_t *status_host, void *stream);
 
+/* The host-boundary form with B already on the device: left (rows x inner, dense rows) and out
+ * (rows x columns) in host memory, right on the device (inner x columns, row stride right_stride
+ * elements).  The rows of A go up and the rows of C come back by row blocks, overlapped with the
+ * arithmetic as in pcu_b200_strict_matmul_host; results and status word are exactly those of
+ * pcu_b200_strict_matmul.  The row-sharded end-to-end step uses it: each rank uploads its rows of
+ * A and a slice of B's rows, the slices are all-gathered over NVLink into a device B, and this
+ * call computes the rank's rows.  Device scratch: pcu_b200_strict_matmul_host_left_scratch_size
+ * bytes (two row blocks of A and C, the workspace and the status words).  No counterpart in the
+ * reference. */
+size_t pcu_b200_strict_matmul_host_left_scratch_size(int dtype, uint64_t rows, uint64_t inner, uint64_t columns);
+int pcu_b200_strict_matmul_host_left(int dtype, int policy, const void *left, const void *right, uint64_t right_stride,
+                                     void *out, uint64_t rows, uint64_t inner, uint64_t columns, void *device_scratch,
+                                     size_t scratch_bytes, uint64_t *status_host, void *stream);
+
 /* Row-sharded strict MatMul with the all-gather of C in the same kernel.  This rank computes rows
  * [row0, row0 + rows) of the rows_total x columns product C = A . op(B) (left_rows: this rank's
  * rows of A, rows x inner with row stride left_stride; right: B as in pcu_b200_strict_matmul,

@@ -93,3 +93,30 @@ def test_host_matmul_first_fault_matches_device_call(where):
     got, st = _run_host(a, b)
     _, st_d = _run_device(a, b)
     assert st == st_d != oracle.STATUS_OK, (hex(st), hex(st_d))
+
+
+@pytest.mark.parametrize("shape", [(1024, 96, 8192), (4100, 64, 96), (9000, 24, 2100), (3000, 0, 5)])
+@pytest.mark.parametrize("strided", [False, True])
+def test_host_left_matches_device_call(shape, strided):
+    """pcu_b200_strict_matmul_host_left: A and C in host memory, B already on the device (dense or
+    with a row stride wider than its columns); the result and status word of the device call."""
+    import torch
+
+    rows, inner, cols = shape
+    rng = np.random.default_rng(rows + 3 * inner + 7 * cols)
+    a = dyadic_uniform(rng, (rows, inner), 32)
+    b = dyadic_uniform(rng, (inner, cols), 32)
+    if inner:
+        a[rows - 1, inner // 2] = np.nan if rows > 4000 else a[rows - 1, inner // 2]
+    bd = to_device(b)
+    if strided:
+        wide = torch.zeros((inner, cols + 8), dtype=torch.float32, device="cuda")
+        wide[:, :cols] = bd
+        bd = wide[:, :cols]
+    out, st = pcu.strict_matmul_host_left(_host(a, True), bd)
+    torch.cuda.synchronize()
+    got, word = out.numpy(), int(st.numpy().view(np.uint64)[0])
+    want, st_d = _run_device(a, b)
+    assert word == st_d, (hex(word), hex(st_d))
+    if st_d == oracle.STATUS_OK:
+        assert np.array_equal(bits(got), bits(want))
