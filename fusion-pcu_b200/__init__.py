@@ -326,7 +326,7 @@ def strict_matmul_host_left(left, right, policy=0, out=None, status=None, scratc
     `status` is a host int64 tensor of one element.  Asynchronous, as strict_matmul_host."""
     torch = _torch()
     assert left.device.type == "cpu" and right.device.type == "cuda" and left.dtype == right.dtype
-    assert left.dim() == 2 and right.dim() == 2 and left.is_contiguous() and right.stride(1) == 1
+    assert left.dim() == 2 and right.dim() == 2 and left.is_contiguous() and (right.numel() == 0 or right.stride(1) == 1)
     rows, inner = left.shape
     if right.shape[0] != inner:
         raise ValueError(f"MatMulShape {tuple(left.shape)} {tuple(right.shape)}")
