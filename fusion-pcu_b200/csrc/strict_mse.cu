@@ -535,8 +535,10 @@ __device__ __forceinline__ void chunk_maps(uint64_t cta, const T *prediction, co
             for (int e = 0; e < V; ++e) {
                 const T qs_ = F::mul(F::value((B)qf[r * V + e]), scale);  // q / 2^L0, exact
                 const T t = add_rz(qs_, magic);                          // 2^P + floor(q / 2^L0)
-                const bool exact = F::sub(t, magic) == qs_;  // nothing of q below 2^L0
-                const Fix tb = (Fix)F::bits(t) | (exact ? (Fix)0 : STICKY);
+                // floor(q / 2^L0) - q / 2^L0, exact: +0 when nothing of q lies below 2^L0, negative
+                // otherwise, so its sign bit is the sticky flag (FP pipe, no compare or select)
+                const T frac = F::sub(F::sub(t, magic), qs_);
+                const Fix tb = (Fix)F::bits(t) | ((Fix)F::bits(frac) & STICKY);
                 qf[r * V + e] = tb;
                 X[r] ^= tb;
             }
@@ -615,16 +617,31 @@ __device__ __forceinline__ void chunk_maps(uint64_t cta, const T *prediction, co
     // (a state in a normal binade is at least 2^P ulps, so a larger sum always leaves it); the
     // sums only grow as j falls, so the failing j form a prefix.
     uint64_t S[NW];
-#pragma unroll
-    for (int w = NW - 1; w >= 0; --w) {
-        uint64_t s = cnt[w];
+    if constexpr (NW == 1) {
+        // one word (binary32): a 32-bit scan saturated at 2^30, far above the 2^P that decides
+        // usability, so no saturated sum is ever taken for a usable one
+        constexpr unsigned SAT32 = 1u << 30;
+        unsigned s = (unsigned)cnt[0];
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
-            const uint64_t v = shfl_down_x(s, o);
-            if (lane + o < 32) s = min(s + sat_shl(v, o, Tr::SAT), (uint64_t)Tr::SAT);
+            const unsigned v = __shfl_down_sync(FULL, s, o);
+            const unsigned sh = v >= (SAT32 >> o) ? SAT32 : v << o;
+            if (lane + o < 32) s = min(s + sh, SAT32);
         }
-        if (w + 1 < NW) s = min(s + sat_shl(shfl_x(S[w + 1 < NW ? w + 1 : w], 0), 32 - lane, Tr::SAT), (uint64_t)Tr::SAT);
-        S[w] = s;
+        S[0] = s >= SAT32 ? Tr::SAT : s;
+    } else {
+#pragma unroll
+        for (int w = NW - 1; w >= 0; --w) {
+            uint64_t s = cnt[w];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint64_t v = shfl_down_x(s, o);
+                if (lane + o < 32) s = min(s + sat_shl(v, o, Tr::SAT), (uint64_t)Tr::SAT);
+            }
+            if (w + 1 < NW)
+                s = min(s + sat_shl(shfl_x(S[w + 1 < NW ? w + 1 : w], 0), 32 - lane, Tr::SAT), (uint64_t)Tr::SAT);
+            S[w] = s;
+        }
     }
     uint64_t cprev[NW];  // cnt[b - 1] for b = 32 w + lane
     int fail_max = 0;
@@ -652,13 +669,21 @@ __device__ __forceinline__ void chunk_maps(uint64_t cta, const T *prediction, co
     Tie *tl = reinterpret_cast<Tie *>(slots + (size_t)warp * kSlotBytes<T>);
     if (!(head.flags & kHeadFault) && jmin <= W) {
         const Fix threshold = (Fix)1 << (jmin - 1), lowmask = threshold - 1;
+        // a word (MARK | Q, STICKY when q has bits below 2^L0) can be a tie iff it has neither the
+        // sticky flag nor a set bit under 2^(jmin - 1): one AND per element (MARK lies above the
+        // mask).  A zero Q passes too; such rare rows are re-checked exactly below.
+        const Fix may_mask = STICKY | lowmask;
 #pragma unroll 1
         for (int r = 0; r < ROWS; ++r) {
             Fix Q[V];
 #pragma unroll
             for (int v = 0; v < (int)(V * sizeof(Fix) / 16); ++v)
                 reinterpret_cast<uint4 *>(Q)[v] = reinterpret_cast<const uint4 *>(qs + CM::index(r, lane, 0))[v];
-            bool row_may = false;  // a nonzero Q, nothing of q below 2^L0, lowest set bit >= jmin - 1
+            bool row_may = false;
+#pragma unroll
+            for (int e = 0; e < V; ++e) row_may |= (Q[e] & may_mask) == 0;
+            if (!__any_sync(FULL, row_may)) continue;
+            row_may = false;  // the exact test: a nonzero Q, not sticky, lowest set bit >= jmin - 1
 #pragma unroll
             for (int e = 0; e < V; ++e) {
                 const Fix q = Q[e] & LOW;
