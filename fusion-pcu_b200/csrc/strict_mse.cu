@@ -173,6 +173,11 @@ template <typename X> __device__ __forceinline__ X shfl_down_x(X v, int o) {
     else return __shfl_down_sync(0xffffffffu, (unsigned long long)v, o);
 }
 
+template <typename X> __device__ __forceinline__ X shfl_xor_x(X v, int o) {
+    if constexpr (sizeof(X) == 4) return __shfl_xor_sync(0xffffffffu, (unsigned)v, o);
+    else return __shfl_xor_sync(0xffffffffu, (unsigned long long)v, o);
+}
+
 template <typename X> __device__ __forceinline__ X shfl_x(X v, int src) {
     if constexpr (sizeof(X) == 4) return __shfl_sync(0xffffffffu, (unsigned)v, src);
     else return __shfl_sync(0xffffffffu, (unsigned long long)v, src);
@@ -410,7 +415,7 @@ __device__ __forceinline__ void chunk_maps(uint64_t cta, const T *prediction, co
 
     // per warp, in `slots` (kChunkWarps x kSlotBytes<T> bytes of shared memory): the chunk's
     // fixed-point squares, then (in place) its ties in element order
-    __shared__ Fix s_lane_ex[kChunkWarps][ROWS][32];  // exclusive prefix XOR in front of (row, lane)
+    __shared__ Fix s_lane_ex[kChunkWarps][ROWS][32];  // per (row, lane): the XOR of its Q words
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint64_t chunk = cta * kChunkWarps + warp;
@@ -576,24 +581,11 @@ __device__ __forceinline__ void chunk_maps(uint64_t cta, const T *prediction, co
 #pragma unroll
         for (int v = 0; v < (int)(V * sizeof(Fix) / 16); ++v)
             reinterpret_cast<uint4 *>(qs + CM::index(r, lane, 0))[v] = reinterpret_cast<const uint4 *>(&qf[r * V])[v];
-    // ---- exclusive prefix XOR of R = Q ^ (Q << 1) in element order, per row across the lanes
-    // (XOR is linear: a row's R total is R of the row's XOR)
-    {
-        Fix total = 0;
+    // ---- the XOR of each row's Q words per lane: the prefix XOR of R = Q ^ (Q << 1) that the tie
+    // listing needs is formed from it only for rows that hold a tie (XOR is linear: R of a XOR is
+    // the XOR of the Rs)
 #pragma unroll
-        for (int r = 0; r < ROWS; ++r) {
-            const Fix xr = X[r] & LOW;
-            const Fix row = xr ^ (xr << 1);
-            Fix incl = row;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const Fix v = shfl_up_x(incl, o);
-                if (lane >= o) incl ^= v;
-            }
-            s_lane_ex[warp][r][lane] = total ^ incl ^ row;  // rows before r, then lanes before this one
-            total ^= shfl_x(incl, 31);
-        }
-    }
+    for (int r = 0; r < ROWS; ++r) s_lane_ex[warp][r][lane] = X[r] & LOW;
     // ---- per-bit population counts of the chunk: Harley-Seal vertical counters per lane, then
     // a warp bit-transpose per counter plane leaves the count of bit 32 w + b in lane b, word w
     uint64_t cnt[NW];
@@ -690,10 +682,25 @@ __device__ __forceinline__ void chunk_maps(uint64_t cta, const T *prediction, co
                 row_may |= q != 0 && (q & lowmask) == 0 && !(Q[e] & STICKY);
             }
             if (!__any_sync(FULL, row_may)) continue;
+            // exclusive prefix XOR of R in front of (r, lane): R of every lane's words of the rows
+            // before r, then an exclusive scan over the lanes of this row
+            Fix earlier = 0;
+#pragma unroll 1
+            for (int r2 = 0; r2 < r; ++r2) earlier ^= s_lane_ex[warp][r2][lane];
+#pragma unroll
+            for (int o = 16; o; o >>= 1) earlier ^= shfl_xor_x(earlier, o);
+            const Fix xr = s_lane_ex[warp][r][lane];
+            const Fix rrow = xr ^ (xr << 1);
+            Fix incl = rrow;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const Fix v = shfl_up_x(incl, o);
+                if (lane >= o) incl ^= v;
+            }
             unsigned mask = 0;   // bit e: element (r, lane, e) is a tie
             uint64_t code = 0;   // byte e: its j (6 bits) and parities (2 bits)
             if (row_may) {
-                Fix prefix = s_lane_ex[warp][r][lane];
+                Fix prefix = (earlier ^ (earlier << 1)) ^ incl ^ rrow;
 #pragma unroll
                 for (int e = 0; e < V; ++e) {
                     const Fix q = Q[e] & LOW;
