@@ -18,7 +18,7 @@ import numpy as np
 __all__ = [
     "ProviderUnavailable", "TensorError", "ArithmeticFault", "CompoundArithmeticFault", "ProviderFailure",
     "library", "POLICY", "OPS", "STATUS_OK", "new_status", "decode_status", "strict_matmul", "strict_matmul_host",
-    "matmul_host_scratch", "strict_matmul_host_left", "strict_sgd",
+    "matmul_host_scratch", "strict_matmul_host_left", "strict_matmul_epilogue", "EpilogueStage", "strict_sgd",
     "strict_mse", "mse_workspace", "strict_mse_segment_prepare", "strict_mse_segment_walk", "strict_mse_sgd",
     "strict_mse_sgd_segment_prepare", "strict_mse_sgd_segment", "checked_binary", "checked_relu", "checked_relu_backward", "matmul_fault", "sgd_fault",
     "mse_fault", "element_fault", "GuardedChain", "CHAIN_OUTCOMES", "chain_validate", "wait",
@@ -64,6 +64,14 @@ class CompoundArithmeticFault(TensorError):
         self.step, self.kind = step, kind
 
 
+class EpilogueStage(ctypes.Structure):
+    """pcu_b200_epilogue_stage: one elementwise node fused into a MatMul's epilogue."""
+    _fields_ = [("op", ctypes.c_int), ("operand", ctypes.c_void_p), ("operand_uniform", ctypes.c_int),
+                ("operand_left", ctypes.c_int), ("out", ctypes.c_void_p), ("status", ctypes.c_void_p)]
+
+
+EPILOGUE_OPS = {"add": 0, "sub": 1, "mul": 2, "div": 3, "relu": 4, "relu_backward": 5}
+
 _lib = None
 
 
@@ -91,6 +99,8 @@ def _declare(L):
     L.pcu_b200_strict_matmul.argtypes = [i32, i32, vp, vp, vp, u64, u64, u64, u64, u64, i32, i32, vp, sz, vp, vp]
     L.pcu_b200_strict_matmul_host_scratch_size.argtypes = [i32, u64, u64, u64]
     L.pcu_b200_strict_matmul_host_scratch_size.restype = sz
+    L.pcu_b200_strict_matmul_epilogue.argtypes = [i32, i32, vp, vp, vp, u64, u64, u64, u64, u64, i32, i32,
+                                                  ctypes.POINTER(EpilogueStage), i32, vp, sz, vp, vp]
     L.pcu_b200_strict_matmul_host.argtypes = [i32, i32, vp, vp, vp, u64, u64, u64, vp, sz, vp, vp]
     L.pcu_b200_strict_matmul_host_left_scratch_size.argtypes = [i32, u64, u64, u64]
     L.pcu_b200_strict_matmul_host_left_scratch_size.restype = sz
@@ -286,6 +296,41 @@ def strict_matmul(left, right, transpose_left=False, transpose_right=False, poli
                                    max(left.stride(0), left.shape[1]), max(right.stride(0), right.shape[1]),
                                    int(transpose_left), int(transpose_right), _ptr(workspace), workspace.numel()),
                  status, chain, stream))
+    return out
+
+
+def strict_matmul_epilogue(left, right, stages, transpose_left=False, transpose_right=False, policy=0, out=None,
+                           status=None, workspace=None, stream=None):
+    """op(left) . op(right) with elementwise nodes fused into the epilogue (at most two).  `stages`
+    is a list of dicts: op ("add", "sub", "mul", "div", "relu", "relu_backward"), operand (a tensor
+    shaped like the product, or one element for a uniform operand; none for relu), operand_left
+    (the operand is the node's left argument: for relu_backward, the forward input x), out and
+    status (the node's own output and status word).  Returns the MatMul's own output."""
+    torch = _torch()
+    rows, inner = (left.shape[1], left.shape[0]) if transpose_left else (left.shape[0], left.shape[1])
+    cols = right.shape[0] if transpose_right else right.shape[1]
+    L = library()
+    if out is None:
+        out = torch.empty((rows, cols), dtype=left.dtype, device=left.device)
+    if status is None:
+        status = new_status(device=left.device)
+    need = L.pcu_b200_strict_matmul_workspace_size(rows, inner, cols)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=left.device)
+    arr = (EpilogueStage * max(len(stages), 1))()
+    for k, st in enumerate(stages):
+        operand = st.get("operand")
+        arr[k].op = EPILOGUE_OPS[st["op"]]
+        arr[k].operand = operand.data_ptr() if operand is not None else None
+        arr[k].operand_uniform = int(operand is not None and operand.numel() == 1 and rows * cols > 1)
+        arr[k].operand_left = int(st.get("operand_left", False))
+        arr[k].out = st["out"].data_ptr()
+        arr[k].status = st["status"].data_ptr()
+    _check(L.pcu_b200_strict_matmul_epilogue(_dtype_code(left), policy, _ptr(left), _ptr(right), _ptr(out), rows,
+                                             inner, cols, max(left.stride(0), left.shape[1]),
+                                             max(right.stride(0), right.shape[1]), int(transpose_left),
+                                             int(transpose_right), arr, len(stages), _ptr(workspace),
+                                             workspace.numel(), _ptr(status), _stream(stream)))
     return out
 
 

@@ -7,13 +7,14 @@
 #include <cstdint>
 
 #include "common.cuh"
+#include "pcu_b200.h"
 
 namespace pcu {
 
 int strict_matmul(int dtype, int policy, const void *left, const void *right, void *out, uint64_t rows,
                   uint64_t inner, uint64_t columns, uint64_t left_stride, uint64_t right_stride, int transpose_left,
                   int transpose_right, void *workspace, size_t workspace_bytes, uint64_t *status, void *stream,
-                  const ChainGuard &guard);
+                  const ChainGuard &guard, const pcu_b200_epilogue_stage *stages = nullptr, int stage_count = 0);
 int strict_sgd(int dtype, int policy, const void *weights, const void *gradient, void *out, uint64_t count,
                uint32_t rate_bits_f32, uint64_t *status, void *stream, const ChainGuard &guard);
 int strict_mse(int dtype, int policy, const void *prediction, const void *target, void *out, uint64_t count,

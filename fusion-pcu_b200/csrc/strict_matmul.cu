@@ -51,6 +51,23 @@ namespace pcu {
 
 constexpr int kMaxPeers = 7;  // up to 8 GPUs of one node
 
+// Elementwise stages fused into the MatMul's epilogue (pcu_b200_strict_matmul_epilogue): stage s
+// takes the previous value (the MatMul's result for stage 0) and, for a checked binary op or
+// ReLU-backward, one more operand laid out like the output (or one uniform element), writes its
+// own output and records its first fault, with the element-index events of an elementwise
+// node, in its own status word.  A cell whose MatMul (or earlier stage) faulted runs no later
+// stage: that node's fault is reported before any of theirs.
+constexpr int kMaxEpilogue = PCU_B200_EPILOGUE_MAX;
+template <typename T> struct EpilogueParams {
+    int count;
+    int op[kMaxEpilogue];            // PCU_B200_ADD..DIV, PCU_B200_EPILOGUE_RELU, _RELU_BACKWARD
+    const T *operand[kMaxEpilogue];  // binary op or ReLU-backward: the other argument
+    int uniform[kMaxEpilogue];       // the operand is one element, used for every cell
+    int operand_left[kMaxEpilogue];  // the operand is the left argument: op(operand, value)
+    T *out[kMaxEpilogue];
+    unsigned long long *status[kMaxEpilogue];
+};
+
 template <typename T> struct MatmulParams {
     const T *left;
     const T *right;
@@ -81,13 +98,43 @@ template <typename T> struct MatmulParams {
     // order; with split 2 each CTA computes one half (BM rows) of a tile.
     unsigned tiles_m, tiles_n, tile_first;
     int split;
+    EpilogueParams<T> epi;  // fused elementwise stages (count 0: none)
 };
 
-// an output element (or 16-byte vector): this device's C and the first np peers' copies
+// The fused stages of one output cell (out of line: only products with an epilogue reach it).
+template <typename T> __device__ __noinline__ void epilogue_cell(const MatmulParams<T> &p, uint64_t idx, T v) {
+    for (int s = 0; s < p.epi.count; ++s) {
+        const int op = p.epi.op[s];
+        T o;
+        unsigned kind;
+        if (op == PCU_B200_EPILOGUE_RELU) {
+            kind = checked_relu<T>(v, p.policy, o);
+        } else {
+            const T w = p.epi.operand[s][p.epi.uniform[s] ? 0 : idx];
+            const T a = p.epi.operand_left[s] ? w : v, b = p.epi.operand_left[s] ? v : w;
+            kind = op == PCU_B200_EPILOGUE_RELU_BACKWARD ? checked_relu_backward<T>(a, b, p.policy, o)
+                                                         : checked_binary<T>(op, a, b, p.policy, o);
+        }
+        if (kind) {
+            record_fault(p.epi.status[s], idx, kind);
+            return;
+        }
+        p.epi.out[s][idx] = o;
+        v = o;
+    }
+}
+
+// an output element (or 16-byte vector): this device's C and the first np peers' copies, then
+// the fused stages, if any
 template <typename T, typename X>
 __device__ __forceinline__ void put_out(const MatmulParams<T> &p, int np, uint64_t idx, X v) {
     *reinterpret_cast<X *>(p.out + idx) = v;
     for (int q = 0; q < np; ++q) *reinterpret_cast<X *>(p.peer_out[q] + idx) = v;
+    if (p.epi.count) {
+        constexpr int kCells = sizeof(X) / sizeof(T);
+#pragma unroll
+        for (int q = 0; q < kCells; ++q) epilogue_cell<T>(p, idx + q, reinterpret_cast<const T *>(&v)[q]);
+    }
 }
 
 // Every CTA of a row-sharded call announces, in each peer's flag block, that this rank has
@@ -662,7 +709,8 @@ template <typename T>
 int run_matmul(int policy, const T *left, const T *right, T *out, uint64_t rows, uint64_t inner, uint64_t columns,
                uint64_t lda, uint64_t ldb, int tl, int tr, void *workspace, size_t workspace_bytes,
                unsigned long long *status, cudaStream_t stream, const ChainGuard &guard,
-               const PeerSet<T> *peers = nullptr, unsigned long long event_base = 0) {
+               const PeerSet<T> *peers = nullptr, unsigned long long event_base = 0,
+               const EpilogueParams<T> *epi = nullptr) {
     MatmulParams<T> p{left,    right,   out,    rows,
                       inner,   columns, lda,    ldb,
                       tl,      tr,      policy, 0,
@@ -678,6 +726,7 @@ int run_matmul(int policy, const T *left, const T *right, T *out, uint64_t rows,
     p.event_base = event_base;
     p.tiles_m = p.tiles_n = p.tile_first = 0;
     p.split = 1;
+    p.epi = epi ? *epi : EpilogueParams<T>{};
     // the first kernel launched decides the stage's admission, the later ones follow it
     ChainGuard next = guard;
     auto take = [&]() {
@@ -769,12 +818,41 @@ extern "C" size_t pcu_b200_strict_matmul_workspace_size(uint64_t rows, uint64_t 
     return ((rows * 4 + 255) / 256) * 256 + ((columns * 4 + 255) / 256) * 256;
 }
 
+namespace {
+
+template <typename T> EpilogueParams<T> epilogue_params(const pcu_b200_epilogue_stage *stages, int count) {
+    EpilogueParams<T> e{};
+    e.count = count;
+    for (int i = 0; i < count; ++i) {
+        e.op[i] = stages[i].op;
+        e.operand[i] = static_cast<const T *>(stages[i].operand);
+        e.uniform[i] = stages[i].operand_uniform != 0;
+        e.operand_left[i] = stages[i].operand_left != 0;
+        e.out[i] = static_cast<T *>(stages[i].out);
+        e.status[i] = reinterpret_cast<unsigned long long *>(stages[i].status);
+    }
+    return e;
+}
+
+}  // namespace
+
 int pcu::strict_matmul(int dtype, int policy, const void *left, const void *right, void *out, uint64_t rows,
                        uint64_t inner, uint64_t columns, uint64_t left_stride, uint64_t right_stride,
                        int transpose_left, int transpose_right, void *workspace, size_t workspace_bytes,
-                       uint64_t *status, void *stream, const ChainGuard &guard) {
+                       uint64_t *status, void *stream, const ChainGuard &guard,
+                       const pcu_b200_epilogue_stage *stages, int stage_count) {
     if ((dtype != PCU_B200_F32 && dtype != PCU_B200_F64) || policy < 0 || policy > 2 || !status)
         return PCU_B200_ERROR_INVALID_ARGUMENT;
+    if (stage_count < 0 || stage_count > kMaxEpilogue || (stage_count && (!stages || guard.disp)))
+        return PCU_B200_ERROR_INVALID_ARGUMENT;
+    for (int i = 0; i < stage_count; ++i) {
+        const pcu_b200_epilogue_stage &st = stages[i];
+        const bool binary = st.op >= PCU_B200_ADD && st.op <= PCU_B200_DIV;
+        if (!binary && st.op != PCU_B200_EPILOGUE_RELU && st.op != PCU_B200_EPILOGUE_RELU_BACKWARD)
+            return PCU_B200_ERROR_INVALID_ARGUMENT;
+        if (!st.status || ((rows && columns) && (!st.out || (st.op != PCU_B200_EPILOGUE_RELU && !st.operand))))
+            return PCU_B200_ERROR_INVALID_ARGUMENT;
+    }
     if (rows == 0 || columns == 0) return chain_decide_only(guard, pcu_host::as_stream(stream));
     if (!out || (inner > 0 && (!left || !right))) return PCU_B200_ERROR_INVALID_ARGUMENT;
     // left is rows x inner (or inner x rows); right is inner x columns (or columns x inner)
@@ -789,13 +867,27 @@ int pcu::strict_matmul(int dtype, int policy, const void *left, const void *righ
     if (events > ((unsigned __int128)1 << 60)) return PCU_B200_ERROR_SIZE_OVERFLOW;
     auto *st = reinterpret_cast<unsigned long long *>(status);
     cudaStream_t s = pcu_host::as_stream(stream);
-    if (dtype == PCU_B200_F32)
+    if (dtype == PCU_B200_F32) {
+        const EpilogueParams<float> epi = epilogue_params<float>(stages, stage_count);
         return run_matmul<float>(policy, (const float *)left, (const float *)right, (float *)out, rows, inner, columns,
                                  left_stride, right_stride, transpose_left != 0, transpose_right != 0, workspace,
-                                 workspace_bytes, st, s, guard);
+                                 workspace_bytes, st, s, guard, nullptr, 0, stage_count ? &epi : nullptr);
+    }
+    const EpilogueParams<double> epi = epilogue_params<double>(stages, stage_count);
     return run_matmul<double>(policy, (const double *)left, (const double *)right, (double *)out, rows, inner,
                               columns, left_stride, right_stride, transpose_left != 0, transpose_right != 0,
-                              workspace, workspace_bytes, st, s, guard);
+                              workspace, workspace_bytes, st, s, guard, nullptr, 0, stage_count ? &epi : nullptr);
+}
+
+extern "C" int pcu_b200_strict_matmul_epilogue(int dtype, int policy, const void *left, const void *right, void *out,
+                                               uint64_t rows, uint64_t inner, uint64_t columns, uint64_t left_stride,
+                                               uint64_t right_stride, int transpose_left, int transpose_right,
+                                               const pcu_b200_epilogue_stage *stages, int stage_count,
+                                               void *workspace, size_t workspace_bytes, uint64_t *status,
+                                               void *stream) {
+    return pcu::strict_matmul(dtype, policy, left, right, out, rows, inner, columns, left_stride, right_stride,
+                              transpose_left, transpose_right, workspace, workspace_bytes, status, stream,
+                              ChainGuard{}, stages, stage_count);
 }
 
 extern "C" int pcu_b200_strict_matmul(int dtype, int policy, const void *left, const void *right, void *out,

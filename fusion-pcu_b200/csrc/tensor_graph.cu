@@ -301,6 +301,9 @@ struct pcu_b200_prepared {
     uint64_t *status = nullptr;     // per node id
     uint64_t *disp = nullptr;       // per node id: guarded-chain disposition (pending 0, executed 1, skipped 2)
     std::vector<int32_t> stages;    // the planned nodes that launch work, in plan order
+    // Per stage: how many of the stages right after a MatMul run in its epilogue in the chained
+    // mode (pcu_b200_strict_matmul_epilogue); 0 for every other stage.
+    std::vector<int> fused;
     void *workspace = nullptr;
     size_t workspace_bytes = 0;
     size_t elem = 4;
@@ -374,6 +377,70 @@ int decode(const pcu_b200_prepared &p, int32_t id, uint64_t word, pcu_b200_tenso
         break;
     }
     return e->code;
+}
+
+// The epilogue form of MatMul stage i with its p.fused[i] following stages.
+int launch_fused(pcu_b200_prepared &p, size_t i, void *stream) {
+    const int32_t id = p.stages[i];
+    const Node &n = p.graph.nodes[id];
+    pcu_b200_epilogue_stage st[PCU_B200_EPILOGUE_MAX] = {};
+    int32_t value = id;  // the node whose result the next stage takes
+    for (int k = 0; k < p.fused[i]; ++k) {
+        const int32_t sid = p.stages[i + 1 + k];
+        const Node &f = p.graph.nodes[sid];
+        if (f.op == PCU_B200_NODE_RELU) {
+            st[k].op = PCU_B200_EPILOGUE_RELU;
+        } else {
+            const bool value_left = f.left == value;
+            const int32_t other = value_left ? f.right : f.left;
+            st[k].op = f.op == PCU_B200_NODE_RELU_BACKWARD ? PCU_B200_EPILOGUE_RELU_BACKWARD : f.op - PCU_B200_NODE_ADD;
+            st[k].operand = p.buffers[other];
+            st[k].operand_uniform = p.graph.nodes[other].op == PCU_B200_NODE_UNIFORM ? 1 : 0;
+            st[k].operand_left = value_left ? 0 : 1;
+        }
+        st[k].out = p.buffers[sid];
+        st[k].status = p.status + sid;
+        value = sid;
+    }
+    const auto &sa = p.graph.nodes[n.left].shape, &sb = p.graph.nodes[n.right].shape;
+    const uint64_t inner = n.tl ? sa[0] : sa[1];
+    return pcu::strict_matmul(p.graph.dtype, p.graph.policy, p.buffers[n.left], p.buffers[n.right], p.buffers[id],
+                              n.shape[0], inner, n.shape[1], sa[1], sb[1], n.tl, n.tr, p.workspace, p.workspace_bytes,
+                              p.status + id, stream, pcu::ChainGuard{}, st, p.fused[i]);
+}
+
+// Which stages the chained mode runs in a MatMul's epilogue: up to PCU_B200_EPILOGUE_MAX stages
+// right after it in plan order, each an elementwise node (checked Add/Sub/Mul/Div, ReLU,
+// ReLU-backward) of the same shape that takes the previous stage's result as exactly one of its
+// operands.  The stages are consecutive, so the first faulting node in graph order is the same
+// as when they run one by one.
+void plan_fusion(pcu_b200_prepared &p) {
+    const auto &nodes = p.graph.nodes;
+    p.fused.assign(p.stages.size(), 0);
+    for (size_t i = 0; i < p.stages.size(); ++i) {
+        const Node &m = nodes[p.stages[i]];
+        if (m.op != PCU_B200_NODE_MATMUL || m.count() == 0) continue;
+        int32_t value = p.stages[i];
+        int k = 0;
+        while (k < PCU_B200_EPILOGUE_MAX && i + 1 + k < p.stages.size()) {
+            const Node &f = nodes[p.stages[i + 1 + k]];
+            bool ok = f.shape == m.shape;
+            if (f.op == PCU_B200_NODE_RELU) {
+                ok = ok && f.left == value;
+            } else if ((f.op >= PCU_B200_NODE_ADD && f.op <= PCU_B200_NODE_DIV) || f.op == PCU_B200_NODE_RELU_BACKWARD) {
+                ok = ok && ((f.left == value) != (f.right == value));
+                const int32_t other = f.left == value ? f.right : f.left;
+                ok = ok && other >= 0 && nodes[other].shape == m.shape && p.buffers[other];
+            } else {
+                ok = false;
+            }
+            if (!ok) break;
+            value = p.stages[i + 1 + k];
+            ++k;
+        }
+        p.fused[i] = k;
+        i += k;
+    }
 }
 
 int launch(pcu_b200_prepared &p, int32_t id, void *stream, const pcu::ChainGuard &guard) {
@@ -614,6 +681,7 @@ extern "C" pcu_b200_prepared *pcu_b200_graph_prepare(const pcu_b200_graph *g, co
     }
     for (int32_t id : p->plan)
         if (g->nodes[id].op != PCU_B200_NODE_INPUT && g->nodes[id].op != PCU_B200_NODE_UNIFORM) p->stages.push_back(id);
+    plan_fusion(*p);
     cudaError_t err = cudaMalloc((void **)&p->status, std::max<size_t>(N, 1) * sizeof(uint64_t));
     if (err == cudaSuccess) err = cudaMalloc((void **)&p->disp, std::max<size_t>(N, 1) * sizeof(uint64_t));
     if (err == cudaSuccess && ws) err = cudaMalloc(&p->workspace, ws);
@@ -664,6 +732,17 @@ int launch_plan(pcu_b200_prepared &p, cudaStream_t s, int32_t &failed, bool guar
         if (err != cudaSuccess) return pcu_host::set_cuda_error(err);
     }
     for (size_t i = 0; i < p.stages.size(); ++i) {
+        // the chained mode runs fusable stages in their MatMul's epilogue; the guarded chain keeps
+        // one kernel per stage (a skipped stage must touch nothing)
+        if (!guarded && p.fused[i]) {
+            rc = launch_fused(p, i, s);
+            if (rc) {
+                failed = p.stages[i];
+                return rc;
+            }
+            i += p.fused[i];
+            continue;
+        }
         rc = launch(p, p.stages[i], s, guarded ? stage_guard(p, i) : pcu::ChainGuard{});
         if (rc) {
             failed = p.stages[i];
@@ -793,6 +872,13 @@ extern "C" int pcu_b200_prepared_execute(pcu_b200_prepared *p, const void *const
         if (int code = decode(*p, id, word, e)) return code;
     }
     return PCU_B200_TENSOR_OK;
+}
+
+extern "C" int pcu_b200_prepared_fused(const pcu_b200_prepared *p, int32_t value) {
+    if (!p) return 0;
+    for (size_t i = 0; i < p->stages.size(); ++i)
+        if (p->stages[i] == value) return p->fused[i];
+    return 0;
 }
 
 extern "C" int pcu_b200_prepared_stage(const pcu_b200_prepared *p, int32_t value, uint64_t *fault_word,

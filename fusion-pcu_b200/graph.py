@@ -81,6 +81,8 @@ def _lib():
         L.pcu_b200_prepared_input_value.restype = i32
         L.pcu_b200_prepared_buffer.argtypes = [vp, i32]
         L.pcu_b200_prepared_buffer.restype = vp
+        L.pcu_b200_prepared_fused.argtypes = [vp, i32]
+        L.pcu_b200_prepared_fused.restype = ctypes.c_int
         L.pcu_b200_prepared_execute.argtypes = [vp, ctypes.POINTER(vp), ctypes.c_int, vp, err]
         L.pcu_b200_prepared_execute.restype = ctypes.c_int
         L.pcu_b200_prepared_read.argtypes = [vp, i32, vp, sz, vp]
@@ -245,6 +247,10 @@ class PreparedGraph:
     def buffer(self, value):
         """Device address of a planned value's buffer (0 if the value is not planned)."""
         return self._L.pcu_b200_prepared_buffer(self._h, value) or 0
+
+    def fused(self, value):
+        """How many of the nodes after MatMul `value` the chained mode runs in its epilogue."""
+        return self._L.pcu_b200_prepared_fused(self._h, value)
 
     def execute(self, inputs=None, wait_each_node=True, stream=None, mode=None):
         """Copy the host `inputs` ({input value: array}) in, run the plan and raise the first fault.

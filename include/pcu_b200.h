@@ -117,6 +117,40 @@ int pcu_b200_strict_matmul(int dtype, int policy, const void *left, const void *
                            uint64_t right_stride, int transpose_left, int transpose_right, void *workspace,
                            size_t workspace_bytes, uint64_t *status, void *stream);
 
+/* Strict MatMul with up to PCU_B200_EPILOGUE_MAX elementwise nodes fused into its epilogue: the
+ * graph's MatMul -> bias Add -> ReLU of a layer, or MatMul -> ReLU-backward of the backward
+ * pass, computed by one kernel.  Stage s applies a checked node to the previous value (the
+ * MatMul's result for stage 0): a checked binary op (PCU_B200_ADD..DIV) with `operand` as its
+ * other argument (an array laid out like out, rows x columns dense, or one element when
+ * operand_uniform; operand_left puts it on the left: op(operand, value)),
+ * PCU_B200_EPILOGUE_RELU, or PCU_B200_EPILOGUE_RELU_BACKWARD (relu_backward(x, dy), see below).
+ * Each stage writes
+ * its own output and records its first fault in its own status word, with the element-index
+ * events of the unfused node (tensor.rs:5657, relu_backward.rs:259-281), so the lowest faulting
+ * node in graph order and its event are exactly those of the unfused sequence: a cell whose
+ * MatMul (or earlier stage) faulted runs no later stage, and an earlier node's fault is always
+ * reported first.  out (the MatMul's own result) is written too.  For
+ * PCU_B200_EPILOGUE_RELU_BACKWARD, operand_left = 1 means operand is the forward input x and the
+ * value is the upstream gradient dy; operand_left = 0 the opposite.  Not for guarded chains.
+ * No counterpart call in the reference, which runs these nodes one by one
+ * (tensor/tensor.rs:4714-4727, 4891-4943). */
+#define PCU_B200_EPILOGUE_MAX 2
+#define PCU_B200_EPILOGUE_RELU 4
+#define PCU_B200_EPILOGUE_RELU_BACKWARD 5
+typedef struct pcu_b200_epilogue_stage {
+    int op;
+    const void *operand;
+    int operand_uniform;
+    int operand_left;
+    void *out;
+    uint64_t *status;
+} pcu_b200_epilogue_stage;
+int pcu_b200_strict_matmul_epilogue(int dtype, int policy, const void *left, const void *right, void *out,
+                                    uint64_t rows, uint64_t inner, uint64_t columns, uint64_t left_stride,
+                                    uint64_t right_stride, int transpose_left, int transpose_right,
+                                    const pcu_b200_epilogue_stage *stages, int stage_count, void *workspace,
+                                    size_t workspace_bytes, uint64_t *status, void *stream);
+
 /* pcu_b200_strict_matmul for callers that cannot allocate device memory.  It has no
  * counterpart in the reference.
  *

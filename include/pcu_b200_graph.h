@@ -116,6 +116,13 @@ void pcu_b200_prepared_free(pcu_b200_prepared *prepared);
 /* Number of graph inputs the plan binds, in capture order, and the value id of input i. */
 int32_t pcu_b200_prepared_input_count(const pcu_b200_prepared *prepared);
 int32_t pcu_b200_prepared_input_value(const pcu_b200_prepared *prepared, int32_t index);
+/* How many of the nodes planned right after MatMul node `value` run in its epilogue in the
+ * chained mode (pcu_b200_strict_matmul_epilogue): elementwise nodes of the same shape (checked
+ * Add/Sub/Mul/Div, ReLU, ReLU-backward) that take the previous node's result as one operand, at
+ * most PCU_B200_EPILOGUE_MAX.  0 for every other node and in the other modes' sense: the
+ * each-node and guarded modes run one kernel per node. */
+int pcu_b200_prepared_fused(const pcu_b200_prepared *p, int32_t value);
+
 /* Device buffer of a planned value (inputs can be written there directly). */
 void *pcu_b200_prepared_buffer(const pcu_b200_prepared *prepared, int32_t value);
 
