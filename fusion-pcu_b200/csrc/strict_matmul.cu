@@ -567,7 +567,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     }
-    if (np) __threadfence_system();  // the peer stores are visible before the kernel ends
+    // No fence after the peer stores: a kernel's writes, to peer memory as to any other, are
+    // visible to everything ordered after its completion, and C is read only after the status
+    // collective that follows this kernel on every rank.  A per-CTA system fence would hold the CTA
+    // (and its SM) until its own stores had crossed NVLink behind those of every CTA finishing at
+    // the same time, instead of letting them drain under the next wave's arithmetic.
 }
 
 // Plain tiled kernel for operands TMA cannot describe (unaligned base or stride): 16x16
@@ -601,7 +605,6 @@ __global__ void __launch_bounds__(256) strict_matmul_generic_kernel(const __grid
     const int cmin = p.col_minexp ? p.col_minexp[c] : 0;
     if (needs_exact(p, acc, rmin, cmin)) exact_cell(p, np, r, c);
     else put_out<T, T>(p, np, r * p.columns + c, acc);
-    if (np) __threadfence_system();
 }
 
 }  // namespace pcu

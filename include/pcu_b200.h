@@ -222,7 +222,8 @@ int pcu_b200_strict_matmul_host_left(int dtype, int policy, const void *left, co
  *
  * Ordering, both directions:
  *   - read side: a peer's rows are complete in this rank's C once every rank's call has
- *     finished, which the caller establishes with a collective after the call (the status MIN);
+ *     finished (a kernel's peer stores are visible to whatever is ordered after its completion),
+ *     which the caller establishes with a collective after the call (the status MIN);
  *   - write side: `epoch` numbers the calls on this set of buffers (1, 2, 3, ..., the same on
  *     every rank) and `rank` is this rank's index (0..npeers).  The kernel records its entry in
  *     each peer's flag block and stores into a peer's C only after that peer's kernel of the
