@@ -183,6 +183,11 @@ def test_nccl_sharded_matches_one_device():
     assert np.array_equal(rider_all, bits(sgd_out))
 
 
+def _FUSED_CASES(world):
+    return ((2048, 256, 1536, None), (256, 100, 96, None), (2048, 128, 1024, (1900, 5)),
+            (1024 * world, 32, 8192, None))
+
+
 def _fused_worker(rank, world, port, queue):
     """Row-sharded MatMul with the all-gather inside the kernel (peer stores into every rank's C)."""
     import torch
@@ -199,8 +204,9 @@ def _fused_worker(rank, world, port, queue):
         sharded = importlib.import_module("fusion-pcu_b200.sharded")
         results = []
         # (m, k, n, fault): a TMA-path product (many 128-wide tiles), a small one (16x16 tiles),
-        # and a fault in a late rank's rows
-        for m, k, n, fault in ((2048, 256, 1536, None), (256, 100, 96, None), (2048, 128, 1024, (1900, 5))):
+        # a fault in a late rank's rows, and rows of 8 x 128 per rank x 8192 columns (512 tiles: the
+        # last wave in half tiles, peer stores from both launches)
+        for m, k, n, fault in _FUSED_CASES(world):
             rng = np.random.default_rng(m + k + n)
             a = dyadic_uniform(rng, (m, k), 32)
             b = dyadic_uniform(rng, (k, n), 32)
@@ -243,7 +249,7 @@ def test_fused_rows_allgather_matches_one_device():
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    for case, (m, k, n, fault) in enumerate(((2048, 256, 1536, None), (256, 100, 96, None), (2048, 128, 1024, (1900, 5)))):
+    for case, (m, k, n, fault) in enumerate(_FUSED_CASES(world)):
         rng = np.random.default_rng(m + k + n)
         a = dyadic_uniform(rng, (m, k), 32)
         b = dyadic_uniform(rng, (k, n), 32)
