@@ -2167,7 +2167,9 @@ extern "C" int pcu_b200_strict_mse_sgd_split(int dtype, int policy, const void *
     if (total_count == 0 || total_count > (1ull << 58) || mse_first_index > total_count ||
         mse_count > total_count - mse_first_index)
         return PCU_B200_ERROR_SIZE_OVERFLOW;
-    if ((rank == nranks - 1) != (mse_first_index + mse_count == total_count)) return PCU_B200_ERROR_INVALID_ARGUMENT;
+    // the last rank's segment ends the reduction (it divides); earlier ones may end there too when
+    // the segments after them are empty
+    if (rank == nranks - 1 && mse_first_index + mse_count != total_count) return PCU_B200_ERROR_INVALID_ARGUMENT;
     if (sgd_count > (1ull << 59) || sgd_first_index > (1ull << 59) - sgd_count) return PCU_B200_ERROR_SIZE_OVERFLOW;
     auto *ms = reinterpret_cast<unsigned long long *>(mse_status);
     auto *ss = reinterpret_cast<unsigned long long *>(sgd_status);

@@ -34,6 +34,18 @@ int main(void) {
           PCU_B200_OK); /* an empty output is a successful no-op */
     CHECK(pcu_b200_guarded_checked_relu(PCU_B200_F32, 0, NULL, NULL, 4, NULL, 0, NULL) ==
           PCU_B200_ERROR_INVALID_ARGUMENT);
+    /* the row-sharded all-gather's buffers: C, then a 256-byte flag block */
+    CHECK(pcu_b200_peer_rows_bytes(PCU_B200_F32, 3, 5) == 512);
+    CHECK(pcu_b200_mse_handoff_bytes() > 0 && pcu_b200_mse_handoff_bytes() % 256 == 0);
+    /* a fused epilogue with more stages than the kernel carries is refused before any work */
+    pcu_b200_epilogue_stage stages[PCU_B200_EPILOGUE_MAX + 1];
+    memset(stages, 0, sizeof(stages));
+    CHECK(pcu_b200_strict_matmul_epilogue(PCU_B200_F32, 0, NULL, NULL, NULL, 4, 4, 4, 4, 4, 0, 0, stages,
+                                          PCU_B200_EPILOGUE_MAX + 1, NULL, 0, &status, NULL) ==
+          PCU_B200_ERROR_INVALID_ARGUMENT);
+    /* the split MSE needs its hand-off blocks and a call number */
+    CHECK(pcu_b200_strict_mse_sgd_split(PCU_B200_F32, 0, NULL, NULL, 4, 0, 4, &status, NULL, 0, &status, NULL, NULL,
+                                        NULL, 0, 0, 0, NULL, NULL, 0, 1, 1, NULL) == PCU_B200_ERROR_INVALID_ARGUMENT);
     pcu_b200_comm *comm = NULL;
     CHECK(pcu_b200_comm_init(NULL, 2, 0, &comm) == PCU_B200_ERROR_INVALID_ARGUMENT && comm == NULL);
     CHECK(pcu_b200_comm_free(NULL) == PCU_B200_OK);
