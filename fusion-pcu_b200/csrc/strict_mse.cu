@@ -1154,8 +1154,6 @@ constexpr int kRideGroupsPerCta = PCU_MSE_RIDE_GROUPS;  // with an SGD node ridi
 #define PCU_MSE_RIDE_SGD 1
 #endif
 constexpr int kRidePeriod = PCU_MSE_RIDE_PERIOD, kRideSgd = PCU_MSE_RIDE_SGD;  // S SGD CTAs in every P
-constexpr uint64_t kTrailDiv = 32;         // 1/32 of a riding SGD node goes to trailing SGD CTAs
-constexpr uint64_t kTrailPerCta = 65536;   // elements per trailing SGD CTA
 static_assert((kFanout / kChunkWarps) % kGroupsPerCta == 0, "a chunk CTA's groups lie in one block");
 
 // publishing chunk CTAs of block b in the one-launch form
@@ -1497,8 +1495,7 @@ mse_onepass_kernel(const T *prediction, const T *target, uint64_t n, bool vec, i
                    uint64_t blocks, uint64_t supers, uint64_t ahead, MseHead *h0, typename MseTraits<T>::D *d0,
                    MseHead *h1, typename MseTraits<T>::D *d1, MseHead *h2, typename MseTraits<T>::D *d2,
                    MseSync sync, T denominator, T *out, unsigned long long *status, SgdRider<T> rider,
-                   ChainGuard guard, uint64_t base, uint64_t total, const T *carry_in, T *carry_out, CarryLink link,
-                   SgdRider<T> trail, uint64_t main_ctas) {
+                   ChainGuard guard, uint64_t base, uint64_t total, const T *carry_in, T *carry_out, CarryLink link) {
     using Tr = MseTraits<T>;
     if constexpr (!RIDE)
         if (!chain_admits(guard)) return;  // the whole launch, walker included
@@ -1511,11 +1508,6 @@ mse_onepass_kernel(const T *prediction, const T *target, uint64_t n, bool vec, i
     // kFanout children at once); in an SGD CTA, its copy stages
     __shared__ __align__(16) unsigned char s_slots[kChunkWarps * kSlotBytes<T>];
     const uint64_t b = blockIdx.x - 1;
-    if (RIDE && b >= main_ctas) {  // trailing SGD CTAs: they run while the last maps are walked
-        const uint64_t s0 = (b - main_ctas) * trail.per_unit;
-        if (s0 < trail.n) sgd_range_async<T>(trail, s0, min(s0 + trail.per_unit, trail.n), s_slots);
-        return;
-    }
     if (sgd_cta<RIDE, kRidePeriod, kRideSgd>(b)) {
         sgd_cta_work<T, kRidePeriod, kRideSgd, true>(b, rider, s_slots);
         return;
@@ -1746,44 +1738,21 @@ int onepass_mse(int policy, const T *p, const T *t, T *out, uint64_t n, void *wo
     unsigned *u = reinterpret_cast<unsigned *>(ws + lay.sync_off);
     const unsigned per_cta = kChunkWarps * g;
     MseSync sync{u, u + lay.count[1], u + 2 * lay.count[1], u + 2 * lay.count[1] + lay.count[2], per_cta};
-    const uint64_t main_ctas = chunk_grid(lay.count[0], ride, per_cta, kRidePeriod, kRideSgd);
-    // With an SGD node riding along, its last 1/kTrailDiv goes to SGD-only CTAs after all chunk
-    // CTAs: they stream while the walker finishes the last maps, which otherwise runs alone.
-    SgdRider<T> head = ride ? *sgd : SgdRider<T>{}, trail{};
-    uint64_t trail_ctas = 0;
-    if (ride) {
-        // the cut is a whole number of SGD units, so the trailing share starts 16-byte aligned
-        const uint64_t at = (head.n - head.n / kTrailDiv) / sgd_unit<T>() * sgd_unit<T>();
-        const uint64_t tn = head.n - at;
-        if (tn && at) {
-            trail = head;
-            trail.vec = head.vec && at % (16 / sizeof(T)) == 0;
-            trail.weights += at;
-            trail.gradient += at;
-            trail.out += at;
-            trail.base += at;
-            trail.n = tn;
-            trail.per_unit = kTrailPerCta;
-            head.n = at;
-            trail_ctas = (tn + kTrailPerCta - 1) / kTrailPerCta;
-        }
-    }
-    const unsigned grid = (unsigned)(1 + main_ctas + trail_ctas);
+    const unsigned grid = (unsigned)(1 + chunk_grid(lay.count[0], ride, per_cta, kRidePeriod, kRideSgd));
     if (ride)
         mse_onepass_kernel<T, true, kRideGroupsPerCta><<<grid, kWalkThreads, 0, stream>>>(
             p, t, n, vec, policy, lay.count[0], lay.count[1], lay.count[2], ahead, H(0), R(0), H(1), R(1), H(2), R(2),
-            sync, count_value<T>(total), out, status, head, guard, base, total, carry_in, carry_out, link, trail,
-            main_ctas);
+            sync, count_value<T>(total), out, status, *sgd, guard, base, total, carry_in, carry_out, link);
     else if (g == kGroupsPerCta)
         mse_onepass_kernel<T, false, kGroupsPerCta><<<grid, kWalkThreads, 0, stream>>>(
             p, t, n, vec, policy, lay.count[0], lay.count[1], lay.count[2], ahead, H(0), R(0), H(1), R(1), H(2), R(2),
             sync, count_value<T>(total), out, status, SgdRider<T>{}, guard, base, total, carry_in, carry_out,
-            link, SgdRider<T>{}, main_ctas);
+            link);
     else
         mse_onepass_kernel<T, false, 1><<<grid, kWalkThreads, 0, stream>>>(
             p, t, n, vec, policy, lay.count[0], lay.count[1], lay.count[2], ahead, H(0), R(0), H(1), R(1), H(2), R(2),
             sync, count_value<T>(total), out, status, SgdRider<T>{}, guard, base, total, carry_in, carry_out,
-            link, SgdRider<T>{}, main_ctas);
+            link);
     return pcu_host::launch_status();
 }
 
