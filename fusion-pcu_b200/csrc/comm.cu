@@ -294,7 +294,8 @@ extern "C" int pcu_b200_comm_strict_mse(pcu_b200_comm *comm, int dtype, int poli
                                         void *stream) {
     if (!usable(comm) || !out || !status || (dtype != PCU_B200_F32 && dtype != PCU_B200_F64))
         return PCU_B200_ERROR_INVALID_ARGUMENT;
-    if (count == 0 || first_index > total_count || count > total_count - first_index)
+    // a rank's segment may be empty (its walk passes the running sum on unchanged)
+    if (total_count == 0 || first_index > total_count || count > total_count - first_index)
         return PCU_B200_ERROR_INVALID_ARGUMENT;
     if (!comm->handoff[comm->rank]) {
         const int rc = pcu_b200_comm_peer_buffers(comm, pcu_b200_mse_handoff_bytes(), comm->handoff, stream);

@@ -533,9 +533,10 @@ int pcu_b200_comm_strict_matmul_rows(pcu_b200_comm *comm, int dtype, int policy,
  * pcu_b200_strict_mse_sgd_split: the running sum goes from rank to rank on the device through
  * IPC-mapped hand-off blocks that the first call makes (collectively, like every call here, and
  * kept until the communicator is freed), and a one-warp exchange leaves the mean in *out and the
- * global first fault in *status on every rank.  No NCCL call after the first.  The segments are
- * non-empty and the last rank's ends at total_count; the result equals pcu_b200_strict_mse over
- * the whole tensor.  The workspace is pcu_b200_strict_mse_workspace_size(dtype, count). */
+ * global first fault in *status on every rank.  No NCCL call after the first.  A segment may be
+ * empty (count 0: the rank passes the running sum on); the last rank's ends at total_count; the
+ * result equals pcu_b200_strict_mse over the whole tensor.  The workspace is
+ * pcu_b200_strict_mse_workspace_size(dtype, count) (at least one byte). */
 int pcu_b200_comm_strict_mse(pcu_b200_comm *comm, int dtype, int policy, const void *prediction, const void *target,
                              uint64_t count, uint64_t first_index, uint64_t total_count, void *out, void *workspace,
                              size_t workspace_bytes, uint64_t *status, void *stream);

@@ -24,7 +24,10 @@ OK = (1 << 64) - 1
 MM_CASES = [(512, 256, 384, 32, None), (512, 256, 384, 32, (400, 7)), (256, 64, 96, 64, None),
             (2048, 128, 1536, 32, None), (2048, 128, 1536, 32, (100, 3)), (1024, 96, 640, 64, (1000, 50))]
 # (elements, width, NaN position in the target or None)
-MSE_CASES = [((1 << 20) + 7, 32, None), ((1 << 20) + 7, 32, 900000), (300001, 64, 1000), (70000, 64, None)]
+# (the last case is shorter than the cuts' 12345-element shift, so every rank after the first gets
+# an empty segment, whatever the number of ranks)
+MSE_CASES = [((1 << 20) + 7, 32, None), ((1 << 20) + 7, 32, 900000), (300001, 64, 1000), (70000, 64, None),
+             (10000, 32, 4000)]
 
 
 def _cuts(n, world):
