@@ -128,15 +128,19 @@ def test_communicator_split_paths_match_one_device():
     procs = [ctx.Process(target=_worker, args=(r, world, uid_queue, queue)) for r in range(world)]
     for p in procs:
         p.start()
+    got = {}
     try:
-        got = dict(queue.get(timeout=300) for _ in range(world))
+        # a rank that fails reports its traceback at once; the others may then wait for it in a
+        # collective, so stop at the first failure instead of waiting for every rank
+        while len(got) < world:
+            rank, res = queue.get(timeout=300)
+            got[rank] = res
+            assert isinstance(res, dict), f"rank {rank} failed:\n{res}"
     finally:
         for p in procs:
-            p.join(timeout=60)
+            p.join(timeout=60 if len(got) == world else 1)
             if p.exitcode is None:
                 p.kill()
-    for rank in range(world):
-        assert isinstance(got[rank], dict), got[rank]
     pcu = importlib.import_module("fusion-pcu_b200")
     for rank in range(world):
         assert list(got[rank]["min"]) == [OK, (1 << 63) | 0x15, (3 << 3) | 3, (9 << 3) | 5]
