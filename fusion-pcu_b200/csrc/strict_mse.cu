@@ -1025,50 +1025,81 @@ __device__ __forceinline__ MapStep map_at(const MseHead &h, const typename MseTr
     return m;
 }
 
-// Warp 0: apply as many of the `avail` (<= 32) consecutive maps starting at `first` as keep the
-// state inside its binade, all at once: lane i loads map first + i at the state's binade, an
-// inclusive scan composes the maps (first L, then R: D[p] = L[p] + R[(p + L[p]) mod 2]), and the
-// leading lanes whose state stays below 2^(P+1) are applied.  Returns how many were applied.
-template <typename T>
-__device__ __forceinline__ unsigned apply_maps(const MseHead *heads, const typename MseTraits<T>::D *deltas,
-                                               uint64_t first, unsigned avail, T &s, int lane) {
-    using Tr = MseTraits<T>;
-    uint64_t x;
-    int k;
-    state_of<T>(s, x, k);
-    // A map that cannot be used (and a lane past `avail`) carries the increment 2^(P+2) on both
-    // parities: any chain through it ends above the binade, so no separate flag is needed.  The
-    // chain of up to 32 valid maps (each below 2^(P+1)) and poisons stays below 2^(P+7): 32-bit
-    // arithmetic for binary32.
+// A map as the walk composes it: the increments (d0, d1) for an even and an odd state.  A map
+// that cannot be used (a fault, a binade outside its window, not published yet, or a thread with
+// no map) carries POISON = 2^(P+2) on both parities, and every composition saturates there: a
+// chain through it ends above the binade, so no separate flag is needed, and a chain of any
+// length stays in 32 bits for binary32.
+template <typename T> struct WalkMap {
     using V = typename std::conditional<sizeof(T) == 4, uint32_t, uint64_t>::type;
-    constexpr V POISON = (V)1 << (Tr::P + 2);
-    V d0 = POISON, d1 = POISON;
-    if ((unsigned)lane < avail) {  // through L2: in the one-launch form other CTAs wrote the maps
-        const uint4 hv = __ldcg(reinterpret_cast<const uint4 *>(heads + first + lane));
-        MseHead h;
-        memcpy(&h, &hv, sizeof(h));
-        const MapStep m = map_at<T>(h, deltas + (first + lane) * (size_t)Tr::W * 2, k);
-        if (m.ok) {
-            d0 = (V)m.d0;
-            d1 = (V)m.d1;
+    static constexpr V POISON = (V)1 << (MseTraits<T>::P + 2);
+    V d0, d1;
+};
+
+// First l, then r: D[p] = l[p] + r[(p + l[p]) mod 2], saturated at POISON (a valid map is below
+// 2^(P+1), so the sum of two is below 2^(P+3)).
+template <typename T> __device__ __forceinline__ WalkMap<T> compose_maps(WalkMap<T> l, WalkMap<T> r) {
+    using V = typename WalkMap<T>::V;
+    const V n0 = l.d0 + ((l.d0 & 1) ? r.d1 : r.d0);
+    const V n1 = l.d1 + ((l.d1 & 1) ? r.d0 : r.d1);
+    return WalkMap<T>{n0 < WalkMap<T>::POISON ? n0 : WalkMap<T>::POISON,
+                      n1 < WalkMap<T>::POISON ? n1 : WalkMap<T>::POISON};
+}
+
+// One round of the walk covers up to NT consecutive maps from the walk's position on, each at
+// the coarsest level its position allows: chunk maps up to the next block boundary, block maps up
+// to the next superblock boundary, superblock maps, and, in front of a stop that is not the end
+// of the segment, block maps and chunk maps again.  So a run that crosses a binade inside a
+// superblock needs one round at each level going down and a single round back up.  Each run of
+// one level is one entry: maps first .. first + (start[e + 1] - start[e]) - 1 of `level`.
+constexpr int kPlanRuns = 5;
+struct WalkPlan {
+    uint64_t first[kPlanRuns];
+    unsigned start[kPlanRuns + 1];  // a round's map j belongs to the entry e with start[e] <= j < start[e + 1]
+    int level[kPlanRuns];
+    int runs;
+};
+
+// Positions are in chunks.  `lim[l]`: maps of level l lie wholly in front of the stop (at the
+// end of the segment the last map of a level, which ends at n, counts).  A map that failed at
+// `fail_c` is replaced by its children: every map inside it is of a finer level.
+__device__ __forceinline__ void plan_walk_round(uint64_t c, const uint64_t lim[kLevels], uint64_t fail_c,
+                                                int fail_level, unsigned cap, WalkPlan &w) {
+    unsigned total = 0;
+    w.runs = 0;
+    auto emit = [&](int l, uint64_t first, uint64_t end) {
+        if (end > first && total < cap) {
+            w.first[w.runs] = first;
+            w.level[w.runs] = l;
+            w.start[w.runs] = total;
+            total += (unsigned)min(end - first, (uint64_t)(cap - total));
+            ++w.runs;
         }
-    }
+    };
+    // up: finer maps until the next coarser map can be used
+    uint64_t p = c;
+    int top = kLevels - 1;
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const V l0 = shfl_up_x(d0, o), l1 = shfl_up_x(d1, o);
-        if (lane >= o) {
-            const V n0 = l0 + ((l0 & 1) ? d1 : d0);
-            const V n1 = l1 + (((1 + l1) & 1) ? d1 : d0);
-            d0 = n0;
-            d1 = n1;
+    for (int l = 0; l + 1 < kLevels; ++l) {
+        if (top < kLevels - 1) break;
+        const int sh = 6 * l, sh1 = 6 * (l + 1);
+        uint64_t q = ((p + (1ull << sh1) - 1) >> sh1) << sh1;  // the next level-(l+1) boundary
+        if (q == p && p == fail_c && fail_level == l + 1) q = p + (1ull << sh1);
+        if ((q >> sh1) >= lim[l + 1]) {
+            top = l;  // no coarser map from q on
+        } else {
+            emit(l, p >> sh, q >> sh);
+            p = q;
         }
     }
-    const uint64_t nx = x + ((x & 1) ? d1 : d0);
-    const bool good = nx < (2ull << Tr::P);  // the state only grows: the last one decides
-    const unsigned bad = __ballot_sync(0xffffffffu, !good);
-    const unsigned applied = bad ? (unsigned)(__ffs((int)bad) - 1) : 32u;
-    if (applied) s = value_of<T>(__shfl_sync(0xffffffffu, (unsigned long long)nx, (int)applied - 1), k);
-    return applied;
+    // down: each level up to its limit, then the finer ones in front of the stop
+#pragma unroll
+    for (int l = kLevels - 1; l >= 0; --l) {
+        if (l > top) continue;
+        emit(l, p >> (6 * l), lim[l]);
+        p = max(p, lim[l] << (6 * l));
+    }
+    w.start[w.runs] = total;
 }
 
 // Prefix sums of half-up increments inside one binade: 32-bit for binary32 (a state is below
@@ -1243,95 +1274,156 @@ __device__ __forceinline__ void mse_walk(
     if (tid < 32) s_warp_sum[tid] = 0;
     __syncthreads();
     const bool onepass = sync.block_ctas != nullptr;
+    using WM = WalkMap<T>;
+    using V = typename WM::V;
+    __shared__ WalkPlan s_plan;
+    __shared__ uint64_t s_fail_c;  // the map at this chunk position failed at level s_fail_level:
+    __shared__ int s_fail_level;   // the next round goes down to its children
+    __shared__ V s_wmap[WARPS][2];
+    __shared__ unsigned s_wbad[WARPS];
+    __shared__ int s_cut_late, s_cut_level;
+    __shared__ MseHead s_cut_head;  // the head of the map at the cut, when it was loaded
+    __shared__ uint64_t s_known_c;  // the chunk to resolve whose head a round loaded (after its flag)
+    __shared__ MseHead s_known_head;
+    if (tid == 0) {
+        s_fail_c = ~0ull;
+        s_fail_level = kLevels;
+        s_known_c = ~0ull;
+    }
+    // one-launch form: wait (bounded) until the chunk maps of block b are published
+    auto wait_block = [&](uint64_t b) {
+        const unsigned need = block_ctas_onepass(chunks, b, sync.chunks_per_cta);
+        const unsigned long long t0 = global_ns();
+        while (load_flag(sync.block_ctas + b) < need) {
+            if (global_ns() - t0 > kWaitLimitNs) return false;
+            __nanosleep(256);
+        }
+        return true;
+    };
     for (;;) {
-        if (warp == 0) {  // maps as far as they reach; then the chunk to resolve, if any
-            const MseHead *lh[kLevels] = {heads0, heads1, heads2};
-            const typename Tr::D *ld[kLevels] = {deltas0, deltas1, deltas2};
-            const uint64_t count[kLevels] = {chunks, blocks, supers};
-            const uint64_t stop = s_end;
-            T s = s_sum;
-            uint64_t g = s_g, arg = ~0ull;
-            uint64_t fail_g = ~0ull;  // a scan at level fail_level stopped at element fail_g
-            int fail_level = kLevels;
-            bool gave_up = false;
-            // one-launch form: wait (bounded) until the chunk maps of block b are published
-            auto wait_block = [&](uint64_t b) {
-                if (lane == 0) {
-                    const unsigned need = block_ctas_onepass(chunks, b, sync.chunks_per_cta);
-                    const unsigned long long t0 = global_ns();
-                    while (load_flag(sync.block_ctas + b) < need) {
-                        if (global_ns() - t0 > kWaitLimitNs) {
-                            gave_up = true;
-                            break;
-                        }
-                        __nanosleep(256);
-                    }
+        // ---- thread 0: the next round's maps, or the chunk to resolve element by element
+        if (tid == 0) {
+            uint64_t arg = ~0ull;
+            s_plan.runs = 0;
+            s_plan.start[0] = 0;
+            const uint64_t g = s_g, stop = s_end;
+            if (s_done == 0 && g < stop) {
+                const uint64_t c = g / Tr::CHUNK;
+                if (c == s_fail_c && s_fail_level == 0) {
+                    arg = c;
+                } else {
+                    const uint64_t lim[kLevels] = {stop == n ? chunks : stop / Tr::CHUNK,
+                                                   stop == n ? blocks : stop / ((uint64_t)Tr::CHUNK << 6),
+                                                   stop == n ? supers : stop / ((uint64_t)Tr::CHUNK << 12)};
+                    plan_walk_round(c, lim, s_fail_c, s_fail_level, NT, s_plan);
+                    if (!s_plan.runs) arg = c;  // the stop lies inside this chunk
                 }
-                gave_up = __shfl_sync(FULL, (int)gave_up, 0) != 0;
-                __threadfence();
-            };
-            while (g < stop && !gave_up) {
-                bool advanced = false;
-                for (int l = kLevels - 1; l >= 0 && !advanced; --l) {
-                    const uint64_t span = (uint64_t)Tr::CHUNK << (6 * l);  // kFanout = 2^6
-                    if (g % span || (g == fail_g && l >= fail_level)) continue;
-                    const uint64_t i = g / span;
-                    // maps lie wholly in front of `stop` (the last one of a level ends at n)
-                    uint64_t lim = stop == n ? count[l] : stop / span;
-                    if (l + 1 < kLevels) lim = min(lim, (i / kFanout + 1) * kFanout);  // inside the parent
-                    if (i >= lim) continue;
-                    unsigned avail = (unsigned)min((uint64_t)32, lim - i);
-                    if (onepass) {  // only published maps (a leading run of them)
-                        bool ok = true;
-                        if ((unsigned)lane < avail) {
-                            const uint64_t j = i + lane;
-                            ok = l == 0   ? load_flag(sync.block_ctas + j / kFanout) >= block_ctas_onepass(chunks, j / kFanout, sync.chunks_per_cta)
-                                 : l == 1 ? load_flag(sync.block_ready + j) != 0
-                                          : load_flag(sync.super_ready + j) != 0;
-                        }
-                        const unsigned late = __ballot_sync(FULL, !ok);
-                        unsigned ready = late ? (unsigned)(__ffs((int)late) - 1) : 32u;
-                        if (!ready) {
-                            if (l > 0) continue;  // a finer level may be published already
-                            wait_block(i / kFanout);  // the chunks of one block are published together
-                            if (gave_up) break;
-                            ready = avail;
-                        }
-                        avail = min(avail, ready);
-                        __threadfence();  // the maps behind the flags are visible to the loads below
-                    }
-                    const unsigned m = apply_maps<T>(lh[l], ld[l], i, avail, s, lane);
-                    g = min(g + m * span, n);
-                    if (m < avail) {
-                        fail_g = g;
-                        fail_level = l;
-                    }
-                    advanced = m > 0;
-                }
-                if (!advanced && !gave_up) {
-                    arg = g / Tr::CHUNK;  // this chunk needs the element-by-element resolution
-                    if (onepass) wait_block(arg / kFanout);  // its head is read below
-                    break;
-                }
-            }
-            if (lane == 0) {
-                s_sum = s;
-                s_g = g;
-                s_arg = gave_up ? ~0ull : arg;
-                if (gave_up) {
+                // its head: from the round that found its map unusable, or read here (in the
+                // one-launch form after its publication)
+                const bool known = arg != ~0ull && arg == s_known_c;
+                if (arg != ~0ull && !known && onepass && !wait_block(arg / kFanout)) {
                     record_fault(status, 0, kWatchdog);
                     s_done = 3;
+                    arg = ~0ull;
                 }
-                if (!gave_up && arg != ~0ull) {  // a fault in the chunk to resolve ends the walk there
-                    const uint4 hv = __ldcg(reinterpret_cast<const uint4 *>(heads0 + arg));
-                    MseHead h;
-                    memcpy(&h, &hv, sizeof(h));
+                if (arg != ~0ull) {  // a fault in the chunk to resolve ends the walk there
+                    MseHead h = s_known_head;
+                    if (!known) {
+                        const uint4 hv = __ldcg(reinterpret_cast<const uint4 *>(heads0 + arg));
+                        memcpy(&h, &hv, sizeof(h));
+                    }
                     if (h.flags & kHeadFault) s_end = min(s_end, arg * Tr::CHUNK + h.fault);
                 }
             }
+            s_arg = arg;
         }
         __syncthreads();
-        if (s_arg == ~0ull) break;
+        if (s_arg == ~0ull && !s_plan.runs) break;  // the walk is done (or a wait gave up)
+        if (s_arg == ~0ull) {
+            // ---- a round of maps: thread j loads map j of the plan at the state's binade (in the
+            // one-launch form only a published one), a CTA-wide inclusive scan composes them in
+            // walk order, and the leading maps whose state stays below 2^(P+1) are applied
+            uint64_t x;
+            int k;
+            state_of<T>(s_sum, x, k);
+            const unsigned count = s_plan.start[s_plan.runs];
+            int l = 0;
+            uint64_t idx = 0;
+            bool late = false;
+            MseHead h{};
+            WM m{WM::POISON, WM::POISON};
+            if ((unsigned)tid < count) {
+                int e = 0;
+                while (e + 1 < s_plan.runs && s_plan.start[e + 1] <= (unsigned)tid) ++e;
+                l = s_plan.level[e];
+                idx = s_plan.first[e] + (tid - s_plan.start[e]);
+                if (onepass)  // the flag's acquire orders this thread's map loads below
+                    late = !(l == 0   ? load_flag(sync.block_ctas + idx / kFanout) >=
+                                          block_ctas_onepass(chunks, idx / kFanout, sync.chunks_per_cta)
+                             : l == 1 ? load_flag(sync.block_ready + idx) != 0
+                                      : load_flag(sync.super_ready + idx) != 0);
+                if (!late) {  // through L2: in the one-launch form other CTAs wrote the maps
+                    const MseHead *heads = l == 0 ? heads0 : l == 1 ? heads1 : heads2;
+                    const typename Tr::D *deltas = l == 0 ? deltas0 : l == 1 ? deltas1 : deltas2;
+                    const uint4 hv = __ldcg(reinterpret_cast<const uint4 *>(heads + idx));
+                    memcpy(&h, &hv, sizeof(h));
+                    const MapStep ms = map_at<T>(h, deltas + idx * (size_t)Tr::W * 2, k);
+                    if (ms.ok) m = WM{(V)ms.d0, (V)ms.d1};
+                }
+            }
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const WM left{shfl_up_x(m.d0, o), shfl_up_x(m.d1, o)};
+                if (lane >= o) m = compose_maps<T>(left, m);
+            }
+            if (lane == 31) {
+                s_wmap[warp][0] = m.d0;
+                s_wmap[warp][1] = m.d1;
+            }
+            __syncthreads();
+            if (warp) {
+                WM front{s_wmap[0][0], s_wmap[0][1]};
+                for (int w = 1; w < warp; ++w) front = compose_maps<T>(front, WM{s_wmap[w][0], s_wmap[w][1]});
+                m = compose_maps<T>(front, m);
+            }
+            const uint64_t nx = x + ((x & 1) ? m.d1 : m.d0);
+            const bool good = (unsigned)tid < count && nx < TOP;  // the state only grows
+            const unsigned bad = __ballot_sync(FULL, !good);
+            if (lane == 0) s_wbad[warp] = bad ? (unsigned)(warp * 32 + __ffs((int)bad) - 1) : (unsigned)NT;
+            __syncthreads();
+            unsigned cut = NT;
+#pragma unroll
+            for (int w = 0; w < WARPS; ++w) cut = min(cut, s_wbad[w]);
+            if (cut && (unsigned)tid == cut - 1) {
+                s_sum = value_of<T>(nx, k);
+                s_g = min((idx + 1) * ((uint64_t)Tr::CHUNK << (6 * l)), n);
+            }
+            if ((unsigned)tid == cut && cut < count) {
+                s_cut_late = late;
+                s_cut_level = l;
+                s_cut_head = h;
+            }
+            __syncthreads();
+            if (tid == 0 && cut < count) {
+                // the map at the cut leaves the binade or cannot be used: its children next (a
+                // chunk's is resolved element by element); not published yet: go on from there,
+                // with its children if it is the first (a finer level may be published already),
+                // or after waiting for a chunk's
+                const uint64_t c = s_g / Tr::CHUNK;
+                if (!s_cut_late || (cut == 0 && s_cut_level > 0)) {
+                    s_fail_c = c;
+                    s_fail_level = s_cut_level;
+                    if (!s_cut_late && s_cut_level == 0) {
+                        s_known_c = c;
+                        s_known_head = s_cut_head;
+                    }
+                } else if (cut == 0 && !wait_block(c / kFanout)) {
+                    record_fault(status, 0, kWatchdog);
+                    s_done = 3;
+                }
+            }
+            continue;  // thread 0 plans the next round; the others wait for it at the barrier
+        }
 
         // ---- resolve one chunk: thread t owns elements [t E, t E + E) (all fault-free in front
         // of the stop)
@@ -1431,10 +1523,9 @@ __device__ __forceinline__ void mse_walk(
     }
     if (tid == 0) {
         if (s_done != 3 && carry_out) *carry_out = s_sum;  // the running sum handed to the next segment
-        if (link.out_flag) {  // published even after a give-up: the next rank must not wait for it
-            __threadfence_system();
+        if (link.out_flag)  // published even after a give-up: the next rank must not wait for it; the
+            // release orders this thread's store of the sum before the flag
             store_release_sys_u64(link.out_flag, link.epoch);
-        }
         if (s_done == 3) return;  // a wait gave up: the status word says so
         if (!out || s_done == 2 || s_end < n || fault_precedes(status, total * 3)) return;
         T mean;
@@ -2101,8 +2192,7 @@ __global__ void __launch_bounds__(32) mse_exchange_kernel(const __grid_constant_
         dst->mse = mse;
         dst->sgd = sgd;
         dst->mean = mean;
-        __threadfence_system();
-        store_release_sys_u64(&dst->epoch, a.epoch);
+        store_release_sys_u64(&dst->epoch, a.epoch);  // the release orders the three stores before it
     }
     bool ok = true;
     unsigned long long m_mse = mse, m_sgd = sgd, peer_mean = 0;

@@ -412,6 +412,24 @@ def test_mse_late_faults(provider, width):
         _mse_case(provider, q, t)
 
 
+@pytest.mark.parametrize("width", [32, 64])
+def test_mse_stop_inside_superblocks(provider, width):
+    """A Subtract fault past the first superblock stops the walk in front of it: the walk takes
+    superblock maps, then block maps and chunk maps up to the fault (and its rounds mix all three
+    levels).  Faults at a superblock boundary, a block boundary, and inside a chunk."""
+    rng = np.random.default_rng(970 + width)
+    chunk = 1024 if width == 32 else 512
+    block, sup = chunk * 64, chunk * 4096
+    n = 3 * sup + 5000
+    p = dyadic_uniform(rng, n, width)
+    t = dyadic_uniform(rng, n, width)
+    for where in (sup + 7 * block + 5 * chunk + 7, 2 * sup, 2 * sup + 3 * block, 3 * sup + 4999):
+        q = p.copy()
+        q[where] = np.nan
+        _mse_case(provider, q, t)
+    _mse_case(provider, p, t)
+
+
 def test_mse_overflow_and_tiny_mean(provider):
     import torch
 
