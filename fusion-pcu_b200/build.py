@@ -17,7 +17,7 @@ BUILD = os.path.join(ROOT, "_build", "provider")
 LIBRARY = os.path.join(HERE, "libpcu_b200.so")
 SOURCES = ["abi.cu", "streaming.cu", "strict_matmul.cu", "strict_mse.cu", "tensor_graph.cu", "host_staging.cu",
            "comm.cu", "calibrate.cu"]
-HEADERS = ["checked_law.cuh", "common.cuh", "provider.h"]
+HEADERS = ["checked_law.cuh", "common.cuh", "mse_walk_plan.h", "provider.h"]
 
 NVCC = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

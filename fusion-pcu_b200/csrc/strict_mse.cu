@@ -53,6 +53,7 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "mse_walk_plan.h"
 #include "pcu_b200.h"
 #include "provider.h"
 
@@ -1046,61 +1047,7 @@ template <typename T> __device__ __forceinline__ WalkMap<T> compose_maps(WalkMap
                       n1 < WalkMap<T>::POISON ? n1 : WalkMap<T>::POISON};
 }
 
-// One round of the walk covers up to NT consecutive maps from the walk's position on, each at
-// the coarsest level its position allows: chunk maps up to the next block boundary, block maps up
-// to the next superblock boundary, superblock maps, and, in front of a stop that is not the end
-// of the segment, block maps and chunk maps again.  So a run that crosses a binade inside a
-// superblock needs one round at each level going down and a single round back up.  Each run of
-// one level is one entry: maps first .. first + (start[e + 1] - start[e]) - 1 of `level`.
-constexpr int kPlanRuns = 5;
-struct WalkPlan {
-    uint64_t first[kPlanRuns];
-    unsigned start[kPlanRuns + 1];  // a round's map j belongs to the entry e with start[e] <= j < start[e + 1]
-    int level[kPlanRuns];
-    int runs;
-};
-
-// Positions are in chunks.  `lim[l]`: maps of level l lie wholly in front of the stop (at the
-// end of the segment the last map of a level, which ends at n, counts).  A map that failed at
-// `fail_c` is replaced by its children: every map inside it is of a finer level.
-__device__ __forceinline__ void plan_walk_round(uint64_t c, const uint64_t lim[kLevels], uint64_t fail_c,
-                                                int fail_level, unsigned cap, WalkPlan &w) {
-    unsigned total = 0;
-    w.runs = 0;
-    auto emit = [&](int l, uint64_t first, uint64_t end) {
-        if (end > first && total < cap) {
-            w.first[w.runs] = first;
-            w.level[w.runs] = l;
-            w.start[w.runs] = total;
-            total += (unsigned)min(end - first, (uint64_t)(cap - total));
-            ++w.runs;
-        }
-    };
-    // up: finer maps until the next coarser map can be used
-    uint64_t p = c;
-    int top = kLevels - 1;
-#pragma unroll
-    for (int l = 0; l + 1 < kLevels; ++l) {
-        if (top < kLevels - 1) break;
-        const int sh = 6 * l, sh1 = 6 * (l + 1);
-        uint64_t q = ((p + (1ull << sh1) - 1) >> sh1) << sh1;  // the next level-(l+1) boundary
-        if (q == p && p == fail_c && fail_level == l + 1) q = p + (1ull << sh1);
-        if ((q >> sh1) >= lim[l + 1]) {
-            top = l;  // no coarser map from q on
-        } else {
-            emit(l, p >> sh, q >> sh);
-            p = q;
-        }
-    }
-    // down: each level up to its limit, then the finer ones in front of the stop
-#pragma unroll
-    for (int l = kLevels - 1; l >= 0; --l) {
-        if (l > top) continue;
-        emit(l, p >> (6 * l), lim[l]);
-        p = max(p, lim[l] << (6 * l));
-    }
-    w.start[w.runs] = total;
-}
+static_assert(kLevels == kPlanLevels, "the walk plan's levels");
 
 // Prefix sums of half-up increments inside one binade: 32-bit for binary32 (a state is below
 // 2^24 and everything is clamped at 2^30), 64-bit for binary64.
