@@ -126,25 +126,54 @@ class _CudaArray:
                                          "version": 3}
 
 
+def _raise_collective(what, failed):
+    """Raise the same ProviderFailure on every rank: the first rank in `failed` ((rank, code) pairs,
+    as every rank received them) could not do `what`."""
+    r, code = failed[0]
+    msg = pcu.library().pcu_b200_error_string(code).decode()
+    raise pcu.ProviderFailure(f"rank {r} could not {what}: pcu_b200 error {code}: {msg}")
+
+
 def _map_peer_buffer(nbytes, group):
     """Allocate `nbytes` of zero-filled device memory with an IPC handle on every rank and map every
-    peer's: (this rank's pointer, every rank's pointer in rank order as this process sees it)."""
+    peer's: (this rank's pointer, every rank's pointer in rank order as this process sees it).
+
+    Collective even when it fails.  Every rank takes part in both exchanges (the handles, then
+    whether each rank mapped every peer's buffer).  If any rank could not allocate its buffer or
+    map a peer's, every rank releases what it holds and raises the same ProviderFailure, so no
+    rank is left waiting in a later collective for one that gave up."""
     import ctypes
 
     L = pcu.library()
     rank, world = dist.get_rank(group), dist.get_world_size(group)
     ptr, handle = ctypes.c_void_p(), (ctypes.c_ubyte * 64)()
-    pcu._check(L.pcu_b200_peer_alloc(nbytes, ctypes.byref(ptr), handle))
-    handles = [None] * world
-    dist.all_gather_object(handles, bytes(handle), group=group)
-    ptrs = []
-    for r, h in enumerate(handles):
+    rc = L.pcu_b200_peer_alloc(nbytes, ctypes.byref(ptr), handle)
+    entries = [None] * world
+    dist.all_gather_object(entries, (rc, bytes(handle)), group=group)
+    failed = [(r, code) for r, (code, _) in enumerate(entries) if code != 0]
+    if failed:
+        if rc == 0:
+            L.pcu_b200_peer_free(ptr.value)  # no peer has mapped it
+        _raise_collective("allocate its peer buffer", failed)
+    ptrs, rc = [], 0
+    for r, (_, h) in enumerate(entries):
         if r == rank:
             ptrs.append(ptr.value)
             continue
         q = ctypes.c_void_p()
-        pcu._check(L.pcu_b200_peer_open((ctypes.c_ubyte * 64).from_buffer_copy(h), ctypes.byref(q)))
-        ptrs.append(q.value)
+        if rc == 0:
+            rc = L.pcu_b200_peer_open((ctypes.c_ubyte * 64).from_buffer_copy(h), ctypes.byref(q))
+        ptrs.append(q.value if rc == 0 else None)
+    codes = [None] * world
+    dist.all_gather_object(codes, rc, group=group)
+    failed = [(r, code) for r, code in enumerate(codes) if code != 0]
+    if failed:
+        for r, q in enumerate(ptrs):
+            if r != rank and q:
+                L.pcu_b200_peer_close(q)
+        dist.barrier(group=group)  # no rank still maps this rank's buffer when it is freed
+        L.pcu_b200_peer_free(ptr.value)
+        _raise_collective("map a peer's buffer", failed)
     return ptr.value, ptrs
 
 
@@ -168,26 +197,13 @@ class PeerRows:
     peer's copy only once that peer has entered the same call."""
 
     def __init__(self, rows, columns, dtype=torch.float32, group=None):
-        import ctypes
-
         self.group = group
         self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
         L = pcu.library()
-        ptr, handle = ctypes.c_void_p(), (ctypes.c_ubyte * 64)()
         code = 0 if dtype == torch.float32 else 1
-        pcu._check(L.pcu_b200_peer_alloc(L.pcu_b200_peer_rows_bytes(code, rows, columns), ctypes.byref(ptr), handle))
+        self._ptr, ptrs = _map_peer_buffer(L.pcu_b200_peer_rows_bytes(code, rows, columns), group)
         self.calls = 0
-        self._ptr = ptr.value
-        handles = [None] * self.world
-        dist.all_gather_object(handles, bytes(handle), group=group)
-        self.peer_ptrs = []
-        for r, h in enumerate(handles):
-            if r == self.rank:
-                continue
-            hb = (ctypes.c_ubyte * 64).from_buffer_copy(h)
-            q = ctypes.c_void_p()
-            pcu._check(L.pcu_b200_peer_open(hb, ctypes.byref(q)))
-            self.peer_ptrs.append(q.value)
+        self.peer_ptrs = [q for r, q in enumerate(ptrs) if r != self.rank]
         self.rows, self.columns, self.dtype = rows, columns, dtype
         self.local = torch.as_tensor(_CudaArray(self._ptr, (rows, columns), dtype), device="cuda")
 

@@ -223,3 +223,101 @@ def test_lost_rank_ends_the_handoff_with_an_error():
         what, dt = results[rank]
         assert what == "error", (rank, what)
         assert dt < 60, (rank, dt)
+
+
+# ------------------------------------------------------------------ peer buffer set-up
+class _FakePeerLibrary:
+    """Stands in for libpcu_b200.so's IPC entry points on CPU ranks: a buffer is an address, its
+    handle carries the address, and a mapping is the address plus an offset.  `fail_alloc` and
+    `fail_open` name the ranks whose allocation or mapping returns an error code."""
+
+    def __init__(self, rank, fail_alloc=(), fail_open=()):
+        self.rank, self.fail_alloc, self.fail_open = rank, set(fail_alloc), set(fail_open)
+        self.live, self.mapped = set(), set()
+
+    def pcu_b200_peer_alloc(self, nbytes, pptr, handle):
+        if self.rank in self.fail_alloc:
+            return 2
+        addr = 0x10000 * (self.rank + 1)
+        pptr._obj.value = addr
+        for i, b in enumerate(addr.to_bytes(8, "little")):
+            handle[i] = b
+        self.live.add(addr)
+        return 0
+
+    def pcu_b200_peer_open(self, handle, pptr):
+        if self.rank in self.fail_open:
+            return 2
+        addr = int.from_bytes(bytes(handle)[:8], "little") + 0x100 * (self.rank + 1)
+        pptr._obj.value = addr
+        self.mapped.add(addr)
+        return 0
+
+    def pcu_b200_peer_close(self, ptr):
+        self.mapped.discard(ptr)
+        return 0
+
+    def pcu_b200_peer_free(self, ptr):
+        self.live.discard(ptr)
+        return 0
+
+    def pcu_b200_error_string(self, rc):
+        return b"CUDA runtime failure"
+
+
+def _peer_buffer_worker(rank, world, port, queue):
+    """Three set-ups in a row on the same ranks: all succeed; one rank cannot allocate; one rank
+    cannot map a peer's buffer.  Each rank reports what it returned or raised and what it still
+    holds."""
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    out = []
+    for fail_alloc, fail_open in (((), ()), ((1,), ()), ((), (0,))):
+        fake = _FakePeerLibrary(rank, fail_alloc, fail_open)
+        sharded.pcu.library = lambda fake=fake: fake
+        try:
+            own, ptrs = sharded._map_peer_buffer(64, None)
+            out.append(("ok", own, ptrs, sorted(fake.live), sorted(fake.mapped)))
+        except sharded.pcu.ProviderFailure as e:
+            out.append(("raised", str(e), None, sorted(fake.live), sorted(fake.mapped)))
+    dist.destroy_process_group()
+    queue.put((rank, out))
+
+
+def test_peer_buffer_setup_fails_on_every_rank_together():
+    """sharded._map_peer_buffer is collective even when it fails: a rank that cannot allocate its
+    buffer, or cannot map a peer's, makes every rank release what it holds and raise the same
+    error, instead of leaving the others waiting in a later collective."""
+    import torch.multiprocessing as mp
+
+    world = 3
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_peer_buffer_worker, args=(r, world, port, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(queue.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank in range(world):
+        ok, alloc_fail, open_fail = results[rank]
+        # all succeed: this rank's own buffer, every peer's mapped at its own address
+        assert ok[0] == "ok"
+        own = 0x10000 * (rank + 1)
+        assert ok[1] == own and ok[2][rank] == own
+        peers = [0x10000 * (r + 1) + 0x100 * (rank + 1) for r in range(world) if r != rank]
+        assert [q for r, q in enumerate(ok[2]) if r != rank] == peers
+        assert ok[3] == [own] and ok[4] == peers
+        # rank 1 cannot allocate: every rank raises naming it and holds nothing
+        assert alloc_fail[0] == "raised" and "rank 1 could not allocate" in alloc_fail[1], alloc_fail
+        assert alloc_fail[3] == [] and alloc_fail[4] == []
+        # rank 0 cannot map: every rank raises naming it, unmaps and frees
+        assert open_fail[0] == "raised" and "rank 0 could not map" in open_fail[1], open_fail
+        assert open_fail[3] == [] and open_fail[4] == []
