@@ -26,7 +26,10 @@
 struct pcu_b200_comm {
     ncclComm_t comm;
     int nranks, rank;
-    uint64_t *scratch;  // device words: [0] the unused SGD status of a segment call, [1] barrier
+    // device memory made with the communicator: words [0] the unused SGD status of a segment
+    // call, [1] barrier, [2] the peer-buffer set-up's agreement; then one staging slot per rank for
+    // the set-up's exchange of IPC handles (a status word, then the handle)
+    uint64_t *scratch;
     // Calls made so far on each set of peer buffers (keyed by this rank's buffer): the call
     // number of the row-sharded MatMul's write-side order.  Every rank makes the same calls, so
     // the counts agree across ranks.
@@ -41,6 +44,9 @@ namespace {
 
 constexpr int kMaxRanks = 8;  // one rank per GPU of one node: the row-sharded MatMul takes <= 7 peers
 constexpr size_t kHandleBytes = 64;
+constexpr size_t kScratchWords = 3;
+constexpr size_t kSlotBytes = 8 + kHandleBytes;
+constexpr size_t kScratchBytes = kScratchWords * 8 + kMaxRanks * kSlotBytes;
 
 struct Nccl {
     decltype(&ncclGetUniqueId) get_unique_id = nullptr;
@@ -125,8 +131,8 @@ extern "C" int pcu_b200_comm_init(const void *id, int nranks, int rank, pcu_b200
     if (!c) return PCU_B200_ERROR_INVALID_ARGUMENT;
     c->nranks = nranks;
     c->rank = rank;
-    int rc = cuda_status(cudaMalloc(reinterpret_cast<void **>(&c->scratch), 2 * sizeof(uint64_t)));
-    if (!rc) rc = cuda_status(cudaMemset(c->scratch, 0xff, 2 * sizeof(uint64_t)));
+    int rc = cuda_status(cudaMalloc(reinterpret_cast<void **>(&c->scratch), kScratchBytes));
+    if (!rc) rc = cuda_status(cudaMemset(c->scratch, 0xff, kScratchBytes));
     ncclUniqueId u;
     memcpy(&u, id, sizeof(u));
     if (!rc) rc = comm_status(n.init_rank(&c->comm, nranks, u, rank));
@@ -196,30 +202,56 @@ extern "C" int pcu_b200_comm_broadcast(pcu_b200_comm *comm, void *buffer, size_t
         nccl().broadcast(buffer, buffer, bytes, ncclUint8, root, comm->comm, pcu_host::as_stream(stream)));
 }
 
-// Each rank allocates its buffer with an IPC handle; the handles are all-gathered through a
-// device staging array; each rank maps the others'.  Blocks until every rank has its mappings.
+// Each rank allocates its buffer with an IPC handle; the handles are all-gathered through the
+// communicator's staging slots; each rank maps the others'.  Blocks until every rank has its
+// mappings.  Collective even when it fails: every rank takes part in the exchange with its
+// allocation's status and in a MAX of the mapping results, so when one rank cannot allocate or map,
+// every rank releases what it holds and returns the same error, and none is left waiting in a
+// later collective.
 extern "C" int pcu_b200_comm_peer_buffers(pcu_b200_comm *comm, size_t bytes, void **buffers, void *stream) {
     if (!usable(comm) || !bytes || !buffers) return PCU_B200_ERROR_INVALID_ARGUMENT;
     const int n = comm->nranks, me = comm->rank;
     cudaStream_t s = pcu_host::as_stream(stream);
     for (int r = 0; r < n; ++r) buffers[r] = nullptr;
-    unsigned char handle[kHandleBytes];
-    int rc = pcu_b200_peer_alloc(bytes, &buffers[me], handle);
-    if (rc) return rc;
-    unsigned char *staging = nullptr;
-    std::vector<unsigned char> all(n * kHandleBytes);
-    rc = cuda_status(cudaMalloc(reinterpret_cast<void **>(&staging), n * kHandleBytes));
-    if (!rc) rc = cuda_status(cudaMemcpyAsync(staging + me * kHandleBytes, handle, kHandleBytes, cudaMemcpyHostToDevice, s));
-    if (!rc)
-        rc = comm_status(nccl().all_gather(staging + me * kHandleBytes, staging, kHandleBytes, ncclUint8, comm->comm, s));
+    unsigned char slot[kSlotBytes] = {};  // this rank's status word, then its handle
+    const uint64_t alloc_rc = (uint64_t)pcu_b200_peer_alloc(bytes, &buffers[me], slot + 8);
+    memcpy(slot, &alloc_rc, 8);
+    unsigned char *staging = reinterpret_cast<unsigned char *>(comm->scratch + kScratchWords);
+    std::vector<unsigned char> all(n * kSlotBytes);
+    int rc = cuda_status(cudaMemcpyAsync(staging + me * kSlotBytes, slot, kSlotBytes, cudaMemcpyHostToDevice, s));
+    const int ex = comm_status(
+        nccl().all_gather(staging + me * kSlotBytes, staging, kSlotBytes, ncclUint8, comm->comm, s));
+    rc = rc ? rc : ex;
     if (!rc) rc = cuda_status(cudaMemcpyAsync(all.data(), staging, all.size(), cudaMemcpyDeviceToHost, s));
     if (!rc) rc = cuda_status(cudaStreamSynchronize(s));
-    if (staging) cudaFree(staging);
-    for (int r = 0; r < n && !rc; ++r)
-        if (r != me) rc = pcu_b200_peer_open(all.data() + r * kHandleBytes, &buffers[r]);
+    for (int r = 0; r < n && !rc; ++r) {  // the first rank that could not allocate, as every rank sees it
+        uint64_t st;
+        memcpy(&st, all.data() + r * kSlotBytes, 8);
+        if (st) rc = (int)st;
+    }
+    if (rc) {
+        if (buffers[me]) pcu_b200_peer_free(buffers[me]);  // no peer has mapped it
+        buffers[me] = nullptr;
+        return rc;
+    }
+    int open_rc = 0;
+    for (int r = 0; r < n && !open_rc; ++r)
+        if (r != me) open_rc = pcu_b200_peer_open(all.data() + r * kSlotBytes + 8, &buffers[r]);
+    uint64_t agreed = (uint64_t)open_rc;
+    rc = cuda_status(cudaMemcpyAsync(comm->scratch + 2, &agreed, 8, cudaMemcpyHostToDevice, s));
+    const int mx = comm_status(nccl().all_reduce(comm->scratch + 2, comm->scratch + 2, 1, ncclUint64, ncclMax,
+                                                 comm->comm, s));
+    rc = rc ? rc : mx;
+    if (!rc) rc = cuda_status(cudaMemcpyAsync(&agreed, comm->scratch + 2, 8, cudaMemcpyDeviceToHost, s));
+    if (!rc) rc = cuda_status(cudaStreamSynchronize(s));
+    // every rank read the same non-zero word: every rank takes the barrier below.  Only a failure of
+    // the exchange itself (a broken context or communicator) is left to this rank alone.
+    const bool together = !rc && agreed;
+    if (together) rc = open_rc ? open_rc : (int)agreed;
     if (rc) {
         for (int r = 0; r < n; ++r)
             if (r != me && buffers[r]) pcu_b200_peer_close(buffers[r]);
+        if (together) barrier(comm, s);  // no rank still maps this rank's buffer when it is freed
         pcu_b200_peer_free(buffers[me]);
         for (int r = 0; r < n; ++r) buffers[r] = nullptr;
         return rc;
