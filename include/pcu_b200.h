@@ -510,8 +510,10 @@ int pcu_b200_comm_broadcast(pcu_b200_comm *comm, void *buffer, size_t bytes, int
 /* Collective.  Every rank allocates `bytes` of zero-filled device memory that the others map
  * with CUDA IPC (for a row-sharded MatMul: pcu_b200_peer_rows_bytes(dtype, rows_total, columns)).
  * buffers[r] (nranks entries) is rank r's buffer as this process sees it; buffers[rank] is this
- * rank's own.  Returns once this rank has mapped every peer.  _free unmaps the peers, waits for
- * every rank to do the same, and frees this rank's buffer. */
+ * rank's own.  Returns once this rank has mapped every peer.  Collective when it fails too: if
+ * any rank cannot allocate its buffer or map a peer's, every rank releases what it holds, leaves
+ * buffers[] null and returns the same error.  _free unmaps the peers, waits for every rank to do
+ * the same, and frees this rank's buffer. */
 int pcu_b200_comm_peer_buffers(pcu_b200_comm *comm, size_t bytes, void **buffers, void *stream);
 int pcu_b200_comm_peer_buffers_free(pcu_b200_comm *comm, void **buffers, void *stream);
 
