@@ -277,6 +277,24 @@ def test_matmul_half_tile_tail_launch(provider, width, tl, tr):
         _matmul_case(provider, a, b, tl, tr, 0, fast_oracle=True)
 
 
+@pytest.mark.parametrize("tl,tr", [(False, False), (True, False), (False, True), (True, True)])
+def test_matmul_narrow_output_on_the_tma_kernel(provider, tl, tr):
+    """Enough row tiles for the TMA kernel but an output only 32 (or 40) columns wide, so every
+    128-column tile is mostly outside the matrix: the per-rank shapes of the 4-layer MLP's last
+    layer column-sharded over 8 GPUs, forward (K = 512 here) and backward (K = 32).  Every cell
+    bit-exact, and a NaN in op(B)'s last column reported where the oracle puts it."""
+    rng = np.random.default_rng(7000 + 2 * tl + tr)
+    for m, k, n, fault in ((8192, 512, 32, None), (8192, 32, 512, None), (8192, 200, 40, 7)):
+        a = dyadic_uniform(rng, (k, m) if tl else (m, k), 32)
+        b = dyadic_uniform(rng, (n, k) if tr else (k, n), 32)
+        if fault is not None:
+            if tr:
+                b[n - 1, fault] = np.nan
+            else:
+                b[fault, n - 1] = np.nan
+        _matmul_case(provider, a, b, tl, tr, 0, fast_oracle=True)
+
+
 @pytest.mark.parametrize("m,k,n", [(8192, 8192, 8192), (2048, 2048, 2048), (4096, 4096, 4096), (8192, 1024, 16384)])
 def test_matmul_sweep_sampled_cells(provider, m, k, n):
     """BASELINE config 2 at full size (the square sweep and the 8192x1024 . 1024x16384 case):
