@@ -101,6 +101,8 @@ def _declare(L):
     L.pcu_b200_strict_matmul_host_scratch_size.restype = sz
     L.pcu_b200_strict_matmul_epilogue.argtypes = [i32, i32, vp, vp, vp, u64, u64, u64, u64, u64, i32, i32,
                                                   ctypes.POINTER(EpilogueStage), i32, vp, sz, vp, vp]
+    L.pcu_b200_strict_matmul_static_scratch.argtypes = [i32, i32, vp, vp, vp, u64, u64, u64, u64, u64, i32, i32, vp,
+                                                        vp]
     L.pcu_b200_strict_matmul_host.argtypes = [i32, i32, vp, vp, vp, u64, u64, u64, vp, sz, vp, vp]
     L.pcu_b200_strict_matmul_host_left_scratch_size.argtypes = [i32, u64, u64, u64]
     L.pcu_b200_strict_matmul_host_left_scratch_size.restype = sz

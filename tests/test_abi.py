@@ -88,3 +88,39 @@ def test_workspace_sizes(provider, rows, inner, columns):
         got = lib.pcu_b200_strict_mse_workspace_size(dtype, 1 << 28)
         assert got >= ((1 << 28) // chunk) * per_chunk and got % 256 == 0
         assert got < ((1 << 28) // chunk) * per_chunk * 1.1
+
+
+def _c_signatures():
+    """(name, return type, parameter count) of every function declared in include/*.h."""
+    sigs = []
+    for header in sorted(os.listdir(os.path.join(ROOT, "include"))):
+        if not header.endswith(".h"):
+            continue
+        text = open(os.path.join(ROOT, "include", header)).read()
+        text = re.sub(r"/\*.*?\*/", " ", text, flags=re.S)
+        text = re.sub(r"//[^\n]*", " ", text)
+        for ret, name, params in re.findall(r"([\w\s\*]+?)\b(pcu_b200_\w+)\s*\(([^;{}]*?)\)\s*;", text, flags=re.S):
+            tokens = ret.replace("*", " * ").split()
+            kind = "pointer" if tokens and tokens[-1] == "*" else (tokens[-1] if tokens else "")
+            count = 0 if params.strip() in ("", "void") else params.count(",") + 1
+            sigs.append((name, kind, count))
+    return sigs
+
+
+def test_ctypes_declarations_match_the_headers(provider):
+    """The Python binding (and the graph layer's, declared on the same library object) gives every
+    entry point with parameters argtypes of the header's length, and a restype wide enough for
+    size_t, uint64_t and pointer results (ctypes would otherwise truncate them to an int)."""
+    import importlib
+
+    L = importlib.import_module("fusion-pcu_b200.graph")._lib()
+    wrong = []
+    for name, kind, count in _c_signatures():
+        fn = getattr(L, name)
+        if count and (fn.argtypes is None or len(fn.argtypes) != count):
+            wrong.append((name, "argtypes", None if fn.argtypes is None else len(fn.argtypes), count))
+        want = {"size_t": (ctypes.c_size_t,), "uint64_t": (ctypes.c_uint64,),
+                "pointer": (ctypes.c_void_p, ctypes.c_char_p)}.get(kind)
+        if want and fn.restype not in want:
+            wrong.append((name, "restype", fn.restype, kind))
+    assert not wrong, wrong
