@@ -102,23 +102,37 @@ def _c_signatures():
         for ret, name, params in re.findall(r"([\w\s\*]+?)\b(pcu_b200_\w+)\s*\(([^;{}]*?)\)\s*;", text, flags=re.S):
             tokens = ret.replace("*", " * ").split()
             kind = "pointer" if tokens and tokens[-1] == "*" else (tokens[-1] if tokens else "")
-            count = 0 if params.strip() in ("", "void") else params.count(",") + 1
-            sigs.append((name, kind, count))
+            plist = [] if params.strip() in ("", "void") else [q.strip() for q in params.split(",")]
+            sigs.append((name, kind, plist))
     return sigs
+
+
+def _param_fits(param, ctype):
+    """A C parameter and its ctypes type agree: a pointer for a pointer, the same width for an
+    integer."""
+    if "*" in param or "[" in param:
+        return ctype in (ctypes.c_void_p, ctypes.c_char_p) or issubclass(ctype, (ctypes._Pointer, ctypes.Array))
+    base = param.replace("const", " ").split()[0]
+    width = {"int": 4, "int32_t": 4, "uint32_t": 4, "uint64_t": 8, "size_t": 8}.get(base)
+    return width is not None and ctypes.sizeof(ctype) == width and issubclass(ctype, ctypes._SimpleCData)
 
 
 def test_ctypes_declarations_match_the_headers(provider):
     """The Python binding (and the graph layer's, declared on the same library object) gives every
-    entry point with parameters argtypes of the header's length, and a restype wide enough for
+    entry point with parameters argtypes of the header's length, each a pointer where the header
+    has a pointer and an integer of the header's width otherwise, and a restype wide enough for
     size_t, uint64_t and pointer results (ctypes would otherwise truncate them to an int)."""
     import importlib
 
     L = importlib.import_module("fusion-pcu_b200.graph")._lib()
     wrong = []
-    for name, kind, count in _c_signatures():
+    for name, kind, params in _c_signatures():
         fn = getattr(L, name)
-        if count and (fn.argtypes is None or len(fn.argtypes) != count):
-            wrong.append((name, "argtypes", None if fn.argtypes is None else len(fn.argtypes), count))
+        if params and (fn.argtypes is None or len(fn.argtypes) != len(params)):
+            wrong.append((name, "argtypes", None if fn.argtypes is None else len(fn.argtypes), len(params)))
+        elif params:
+            wrong += [(name, "parameter", i, q, t) for i, (q, t) in enumerate(zip(params, fn.argtypes))
+                      if not _param_fits(q, t)]
         want = {"size_t": (ctypes.c_size_t,), "uint64_t": (ctypes.c_uint64,),
                 "pointer": (ctypes.c_void_p, ctypes.c_char_p)}.get(kind)
         if want and fn.restype not in want:
